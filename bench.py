@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Benchmark of the base-encoding hot path (one JSON line on rank 0).
+
+Workload (BASELINE metric "encoded vectors/sec at 1/2/4/8 B200 (D=128,M=8,K=256,beam=16)"):
+1,000,000 base vectors per GPU, D=128 float32 (seeded SIFT-like generator, integer values in
+[0, 255]), M=8 codebooks of K=256, beam 16, one ICM sweep, no ILS.  One step = the whole encode
+stage (xC GEMM, beam search, LS, beam MSE, ICM, final MSE) over the GPU's shard, plus the one
+NCCL all-reduce of the per-shard MSE sums when N > 1.  Weak scaling: every GPU encodes its own
+1M-vector shard; codebooks are trained once on rank 0 (seeded residual k-means stand-in for the
+reference's trainer) and broadcast over NCCL.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--n", type=int, default=1_000_000, help="vectors per GPU")
+    p.add_argument("--d", type=int, default=128)
+    p.add_argument("--m", type=int, default=8)
+    p.add_argument("--k", type=int, default=256)
+    p.add_argument("--beam", type=int, default=16)
+    p.add_argument("--icm", type=int, default=1)
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the CPU-baseline sample")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def load_measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def make_codebooks(args, device):
+    """Seeded residual k-means on a 50,000-vector subsample (seed 0): the stand-in for codebooks
+    frozen from the reference's trainer."""
+    from stlq_b200 import synth
+
+    train = synth.sift_like(50_000, d=args.d, seed=0)
+    books = synth.train_rvq(train, args.m, args.k, iters=8, seed=0, device=device)
+    return synth.flatten_books(books)
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 10 or (self.uuid and self.uuid not in parts[1]):
+                    continue
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[6:10]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": float(rows[0][3]),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def cand_flops_per_vector(m, K, beam):
+    """Algorithmic FP32 work of the beam expansion per vector (minimal candidate cost, FMA = 2):
+    beam*K*sum_{L=1}^{m-1}(L^2 + 4L + 5) + 3K for layer 0."""
+    return beam * K * sum(L * L + 4 * L + 5 for L in range(1, m)) + 3 * K
+
+
+def measure_fp32_peak(torch, device):
+    """FP32 SIMT peak measured here: cuBLAS SGEMM with TF32 off, 8192^3, best of 5."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    a = torch.randn(8192, 8192, device=device)
+    b = torch.randn(8192, 8192, device=device)
+    best = 0.0
+    for _ in range(6):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        e.synchronize()
+        best = max(best, 2 * 8192 ** 3 / (s.elapsed_time(e) / 1e3) / 1e12)
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return best
+
+
+def cpu_reference_sample(C, h_vec, X, args, seconds, gpu_codes=None):
+    """The reference's own CPU encoder (oracle/_ref: beam_search.cpp, least_squares.cpp, icm.cpp, ...
+    compiled from its sources) on a bounded sample, with every host thread.  Returns
+    (vectors_per_s, threads, sample_n, code_match or None)."""
+    import oracle
+
+    ref = oracle.Reference(threads=os.cpu_count())
+    P = ref.precomp(h_vec, C)
+    probe = min(len(X), 256)
+    t0 = time.perf_counter()
+    P.encode_base(X[:probe], args.beam, args.icm)
+    rate = probe / max(time.perf_counter() - t0, 1e-6)
+    ns = int(min(len(X), max(probe, rate * seconds)))
+    t0 = time.perf_counter()
+    r = P.encode_base(X[:ns], args.beam, args.icm)
+    dt = time.perf_counter() - t0
+    match = None
+    if gpu_codes is not None:
+        same = (gpu_codes[:ns] == r["B"]).all(1)
+        match = {"frac": float(same.mean()), "vectors": ns, "mismatched": int((~same).sum()),
+                 "reference_final_mse": float(r["final_mse"])}
+    return ns / dt, ref.threads, ns, match, r
+
+
+def run_reference(args):
+    """--impl reference: the reference's own CPU implementation of the path, timed on this box's
+    host cores (rank 0 only)."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+
+    from stlq_b200 import synth
+
+    dev = "cuda" if torch.cuda.is_available() else None
+    C = make_codebooks(args, dev)
+    X = synth.sift_like(min(args.n, 200_000), d=args.d, seed=4)
+    import oracle
+
+    ref = oracle.Reference(threads=os.cpu_count())
+    P = ref.precomp([args.k] * args.m, C)
+    probe = 256
+    t0 = time.perf_counter()
+    P.encode_base(X[:probe], args.beam, args.icm)
+    rate = probe / max(time.perf_counter() - t0, 1e-6)
+    per_step = int(min(len(X), max(probe, rate * args.cpu_seconds / max(args.steps, 1))))
+    for _ in range(min(args.warmup, 1)):
+        P.encode_base(X[:min(per_step, 512)], args.beam, args.icm)
+    times = []
+    for s in range(args.steps):
+        lo = (s * per_step) % max(len(X) - per_step, 1)
+        t0 = time.perf_counter()
+        P.encode_base(X[lo:lo + per_step], args.beam, args.icm)
+        times.append(time.perf_counter() - t0)
+    t = sum(times)
+    value = per_step * args.steps / t
+    line = {
+        "impl": "reference", "metric": "encoded vectors/sec", "value": value, "unit": "vectors/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.n} x D={args.d} f32 (SIFT-like, seed 4), M={args.m}, K={args.k}, "
+                               f"beam={args.beam}, ICM={args.icm}, ILS=0; reference CPU encoder on a "
+                               f"{per_step}-vector sample per step",
+                   "cache": "sample per step"},
+        "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": ref.threads, "kind": "reference",
+                         "sample": f"{per_step} vectors per step x {args.steps} steps; BLAS core {ref.blas_core()}"},
+        "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import stlq_b200
+    from stlq_b200 import synth
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    # Codebooks: trained on rank 0, replicated to every GPU with one NCCL broadcast.
+    H = args.m * args.k
+    if rank == 0:
+        C = torch.from_numpy(make_codebooks(args, device)).to(device)
+    else:
+        C = torch.empty((H, args.d), dtype=torch.float32, device=device)
+    if world > 1:
+        dist.broadcast(C, src=0)
+    C_np = C.cpu().numpy()
+    h_vec = [args.k] * args.m
+    enc = stlq_b200.Encoder(C_np, h_vec, device=local)
+    n = args.n
+    offset = rank * n
+    X_np = synth.sift_like(n, d=args.d, seed=4, start=offset)
+    X = torch.from_numpy(X_np).to(device)
+    B = torch.empty((n, args.m), dtype=torch.uint8, device=device)
+    a = torch.empty((n, args.m), dtype=torch.float32, device=device)
+    cost = torch.empty(n, dtype=torch.float32, device=device)
+    sse = torch.zeros(2, dtype=torch.float64, device=device)
+
+    def step():
+        enc.encode_base_device(X, args.beam, args.icm, 0, 0, True, 38251450, offset, B=B, a=a, cost=cost, sse=sse)
+        if world > 1:
+            dist.all_reduce(sse)  # the one reduce of the per-shard MSE sums
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    enc.sync()
+    barrier()
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop()
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    t = torch.tensor([t_local], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_max = float(t.item())
+    value = world * n * args.steps / t_max
+    total_mse = float(sse[1].item()) / (world * n)
+    launches_per_step = 0
+    slice_v = min((1 << 31) // (H * 4), 65535 * 64)
+    launches_per_step = ((n + slice_v - 1) // slice_v) * 4
+
+    # e2e: the same stage through the host-buffer C-ABI call (pinned host input and outputs;
+    # H2D + encode + D2H inside the timed region, synchronous call, wall clock).
+    e2e = None
+    if not args.no_e2e:
+        Xh = torch.from_numpy(X_np).pin_memory()
+        Bh = torch.empty((n, args.m), dtype=torch.uint8).pin_memory()
+        ah = torch.empty((n, args.m), dtype=torch.float32).pin_memory()
+        ch = torch.empty(n, dtype=torch.float32).pin_memory()
+        out = dict(B=Bh.numpy(), a=ah.numpy(), cost=ch.numpy())
+        for _ in range(max(1, min(args.warmup, 2))):
+            enc.encode_base(Xh.numpy(), args.beam, args.icm, 0, 0, True, 38251450, offset, out=out)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            r = enc.encode_base(Xh.numpy(), args.beam, args.icm, 0, 0, True, 38251450, offset, out=out)
+        te = time.perf_counter() - t0
+        tt = torch.tensor([te], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        te = float(tt.item())
+        e2e = {"value": world * n * args.steps / te, "unit": "vectors/s",
+               "h2d_bytes_per_step": int(X_np.nbytes),
+               "d2h_bytes_per_step": int(n * args.m + n * args.m * 4 + n * 4 + 16),
+               "timing": "wall clock around the synchronous host-buffer call, max over ranks"}
+        assert np.array_equal(r["B"], B.cpu().numpy()), "host and device paths disagree"
+
+    # Dominant kernel (beam search) timed alone on a 262,144-vector slice, CUDA events on the
+    # launching stream, L2 holds none of its 2 GiB xC input between launches.
+    S = min(n, 262_144)
+    xC = enc.xc_gemm(X[:S])
+    xn = enc.xnorm2(X[:S])
+    for _ in range(2):
+        enc.beam_search(xn, xC, args.beam)
+    reps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        enc.beam_search(xn, xC, args.beam)
+    e1.record()
+    torch.cuda.synchronize()
+    beam_s = e0.elapsed_time(e1) / 1e3 / reps
+    # GEMM alone on the same slice.
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(reps):
+        enc.xc_gemm(X[:S])
+    g1.record()
+    torch.cuda.synchronize()
+    gemm_s = g0.elapsed_time(g1) / 1e3 / reps
+    del xC
+
+    cpu = None
+    code_match = None
+    if rank == 0 and not args.no_cpu:
+        try:
+            v, cores, ns, code_match, _ = cpu_reference_sample(C_np, h_vec, X_np, args, args.cpu_seconds,
+                                                               gpu_codes=B.cpu().numpy())
+            cpu = {"value": v, "unit": "vectors/s", "cores": cores, "kind": "reference",
+                   "sample": f"first {ns} vectors of rank 0's shard, same codebooks and settings, "
+                             f"reference CPU encoder (oracle/_ref) with {cores} threads"}
+        except Exception as exc:  # the reference library did not travel or does not load
+            cpu = {"value": None, "unit": "vectors/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"unavailable: {exc}"}
+    if rank == 0:
+        peaks, peaks_src = load_measured_peaks()
+        fp32_peak = measure_fp32_peak(torch, device)
+        F_cand = cand_flops_per_vector(args.m, args.k, args.beam)
+        beam_bytes = S * (4 * H + 4 + args.m)
+        achieved_gbs = beam_bytes / beam_s / 1e9
+        F_gemm = 2 * args.d * H
+        hbm_bytes_vec = 4 * args.d + args.m + 4 * args.m
+        t_gemm = F_gemm / (peaks["bf16_tflops"] * 1e12)
+        t_hbm = hbm_bytes_vec / (peaks["hbm_gbs"] * 1e9)
+        t_cand = F_cand / (fp32_peak * 1e12)
+        line = {
+            "metric": "encoded vectors/sec", "value": value, "unit": "vectors/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded SIFT-like D=128, values 0..255; codebooks: seeded residual k-means)",
+            "config": {"workload": f"{n} x D={args.d} f32 per GPU, M={args.m}, K={args.k}, beam={args.beam}, "
+                                   f"ICM={args.icm}, ILS=0, use_abs, seed 38251450",
+                       "vectors_per_gpu": n, "gemm_mode": "exact",
+                       "cache": "inputs larger than L2 (X 512 MB, xC 2 GiB per slice)",
+                       "parallelism": f"dp{world} (shards of base vectors)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "mse": total_mse,
+            "roofline": {
+                "bound": "hbm", "kernel": "BeamSearchKernel<8>", "achieved": achieved_gbs,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"],
+                "traffic": None, "peak_source": peaks_src,
+                "note": "algorithmic bytes per vector = xC row (4H) + ||x||^2 (4) + codes (M); the kernel is "
+                        "bound by FP32 issue, see simt",
+                "simt": {"achieved": F_cand * S / beam_s / 1e12, "peak": fp32_peak, "unit": "TFLOP/s",
+                         "frac": F_cand * S / beam_s / 1e12 / fp32_peak, "flops_per_vector": F_cand,
+                         "peak_source": "cuBLAS SGEMM (TF32 off) measured in this run"},
+                "beam_ms_per_262144": beam_s * 1e3, "gemm_ms_per_262144": gemm_s * 1e3,
+                "gemm_tflops": F_gemm * S / gemm_s / 1e12,
+                "whole_job_fraction_of_2term_bound": value / world * max(t_gemm, t_hbm),
+                "whole_job_fraction_of_3term_bound": value / world * max(t_gemm, t_hbm, t_cand),
+            },
+            "clocks": clock_info,
+            "cpu_baseline": cpu,
+            "code_match": code_match,
+        }
+        if e2e:
+            line["e2e"] = e2e
+        print(json.dumps(line), flush=True)
+    enc.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+/* stlq_b200: B200-native (sm_100a) base-encoding hot path of STLQ behind a C ABI.
+ *
+ * One encoder handle holds one frozen codebook set on one GPU.  All matrices use the reference's
+ * column-major layout (include/stlq/common/types.h:37-55 in the reference): a d x n matrix is n
+ * columns of d contiguous floats, i.e. vector j starts at X + j*d.  Codes are m x n uint8 (the
+ * reference's FullCode, types.h:22-32): vector j's codes start at B + j*m.  Coefficients are
+ * m x n floats in the same layout.
+ *
+ * Errors: every entry point returns 0 on success or a nonzero STLQ_B200_E* code; the message is
+ * available from stlq_b200_last_error() on the calling thread.  Nothing throws across the ABI.
+ * Thread safety: a handle may be used by one host thread at a time; distinct handles are
+ * independent (one per GPU / per host thread, like the reference's thread_local CUDA sessions).
+ */
+#ifndef STLQ_B200_H_
+#define STLQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct stlq_b200_encoder stlq_b200_encoder;
+
+enum {
+    STLQ_B200_OK = 0,
+    STLQ_B200_EINVAL = 1,   /* bad argument (null pointer, size out of range, unsupported shape) */
+    STLQ_B200_ECUDA = 2,    /* CUDA runtime error */
+    STLQ_B200_ENOMEM = 3,   /* device allocation failed */
+    STLQ_B200_EDEVICE = 4   /* a kernel reported an internal error (bounded wait expired, ...) */
+};
+
+/* How xC = C_all^T X is computed.
+ *   STLQ_B200_GEMM_EXACT  FP32 FMA chains in the order of the reference's CPU BLAS backend
+ *                         (OpenBLAS SkylakeX SGEMM: one chain per 448-deep K block, blocks summed);
+ *                         xC and therefore the codes are bit-identical to the reference's.
+ *   STLQ_B200_GEMM_STRICT tcgen05 tensor cores, 3xTF32 split: FP32-accurate, not bit-identical
+ *                         (the reference's runtime.cuda_mode=strict accuracy class).
+ *   STLQ_B200_GEMM_FAST   tcgen05 tensor cores, 1xTF32 (the reference's TF32 fast mode). */
+enum {
+    STLQ_B200_GEMM_EXACT = 0,
+    STLQ_B200_GEMM_STRICT = 1,
+    STLQ_B200_GEMM_FAST = 2
+};
+
+/* Input element types for X. */
+enum { STLQ_B200_F32 = 0, STLQ_B200_U8 = 1 };
+
+/* Limits of this build. */
+#define STLQ_B200_MAX_M 16      /* codebooks (layers) */
+#define STLQ_B200_MAX_K 256     /* codewords per codebook (uint8 codes) */
+#define STLQ_B200_MAX_BEAM 32   /* beam width */
+
+/* Message for the last failed call on this host thread ("" if none). */
+const char* stlq_b200_last_error(void);
+
+/* Version string of the library ("stlq_b200 <semver> sm_100a"). */
+const char* stlq_b200_version(void);
+
+/* Create an encoder on CUDA device `device`.
+ * Replaces BuildPrecomp (reference: src/quantizer/encoder_precomp.inc:1-53) plus the device
+ * uploads of FullIcmCudaSession::EnsurePrecomp (src/quantizer/icm_cuda_kernels.inc:2100-2150).
+ *   C_all   d x H column-major (H = sum of h_vec), the reference's Precomp::C_all.
+ *   G       optional H x H column-major Gram matrix (the reference's Precomp::G); when NULL it is
+ *           computed on the device as C_all^T C_all in the order selected by gemm_mode.
+ *   invnorm optional H floats (Precomp::invnorm_flat); computed when NULL.
+ * h_vec[l] in [1, 256], m in [1, 16], d >= 1. */
+int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_all, const float* G,
+                     const float* invnorm, int gemm_mode, stlq_b200_encoder** out);
+
+int stlq_b200_destroy(stlq_b200_encoder* enc);
+
+/* Encode n vectors held in HOST memory: the whole EncodeBase stage
+ * (src/quantizer/encoder_encode_base.inc:1-106): xC GEMM, BeamSearchPrefixLS, SolveLeastSquaresAll,
+ * beam MSE, DynamicIcmWithIls{Abs,NoAbs}NoNormal, final MSE.  Host<->device copies are staged
+ * through pinned buffers in slices and overlapped with compute.
+ *   X            d x n, element type x_dtype (STLQ_B200_F32 or STLQ_B200_U8).
+ *   B_out        m x n uint8 codes.          a_out    m x n LS coefficients (may be NULL).
+ *   cost_out     n floats, ICM cost (SampleCost) per vector (may be NULL).
+ *   sse_out      2 doubles (may be NULL): sum over vectors of the clamped squared error after
+ *                the beam and after ICM/ILS (MeanMseFromPrecomp x n, linkage_tools.cpp:170-219).
+ *   sample_id_offset  global id of vector 0 (ILS perturbation stream, icm.cpp:950-960). */
+int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
+                          int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                          uint8_t* B_out, float* a_out, float* cost_out, double* sse_out);
+
+/* Same stage on DEVICE buffers (all pointers on the encoder's device), enqueued on `stream`
+ * (a cudaStream_t; NULL = the legacy default stream).  Asynchronous: returns after enqueueing.
+ * sse_out_dev: 2 doubles on the device (may be NULL). */
+int stlq_b200_encode_base_device(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, int beam,
+                                 int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                 uint64_t sample_id_offset, uint8_t* B_dev, float* a_dev, float* cost_dev,
+                                 double* sse_out_dev, void* stream);
+
+/* ---- Stage-level entry points (device buffers, asynchronous on `stream`) ---- */
+
+/* xC = C_all^T X  (H x n).  Replaces the Gemm call of EncodeBase (encoder_encode_base.inc:33-37)
+ * and StreamKernelProvider::GemmDevice (include/stlq/core/kernel_provider.h:75-100). */
+int stlq_b200_xc_gemm(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* xC_dev,
+                      void* stream);
+
+/* ||x||^2 per vector (ComputeXNorm2, src/quantizer/cost_utils.cpp:88-110), same float order. */
+int stlq_b200_xnorm2(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* xnorm2_dev,
+                     void* stream);
+
+/* BeamSearchPrefixLS (src/quantizer/beam_search.cpp:196-422; declared in
+ * include/stlq/quantizer/beam_search.h:18-22): m x n codes from xC and ||x||^2. */
+int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const float* xC_dev, int64_t n,
+                          int beam, uint8_t* B_dev, void* stream);
+
+/* SolveLeastSquaresAll (src/quantizer/least_squares.cpp:406-560): m x n coefficients. */
+int stlq_b200_solve_ls(stlq_b200_encoder* enc, const float* xC_dev, const uint8_t* B_dev, int64_t n,
+                       float* a_dev, void* stream);
+
+/* DynamicIcmWithIls{Abs,NoAbs}NoNormalCudaDeviceXc (include/stlq/quantizer/icm_cuda.h:70-101;
+ * CPU semantics icm.cpp:89-344, 872-1003).  B_dev is in/out; a_dev and cost_dev are outputs.
+ * The ICM layer orders are drawn on the host with std::mt19937(seed) + std::shuffle, exactly
+ * as the reference does. */
+int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnorm2_dev, int64_t n, int icm_iters,
+                  int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                  uint8_t* B_dev, float* a_dev, float* cost_dev, void* stream);
+
+/* Sum over vectors of MeanMseFromPrecomp's clamped per-vector error, in double, added into
+ * *sse_dev (src/linkage/linkage_tools.cpp:170-219). */
+int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const float* xC_dev,
+                  const uint8_t* B_dev, const float* a_dev, int64_t n, double* sse_dev, void* stream);
+
+/* Block until all work this encoder enqueued on `stream` has finished; returns
+ * STLQ_B200_EDEVICE if a kernel flagged an internal error since the last check. */
+int stlq_b200_sync(stlq_b200_encoder* enc, void* stream);
+
+/* Shape queries. */
+int stlq_b200_dims(const stlq_b200_encoder* enc, int* d, int* m, int* H);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STLQ_B200_H_ */

@@ -1,0 +1,269 @@
+"""Parity checkers for the base-encoding hot path: TEST INFRASTRUCTURE ONLY.
+
+Two CPU implementations, loaded through ctypes:
+
+* ``Oracle`` wraps ``_build/libstlq_oracle.so``, the restatement in ``stlq_oracle.cpp``
+  (codes widened to uint16, so it also covers K > 256).
+* ``Reference`` wraps ``_ref/libstlq_ref.so``, the reference's own hot-path sources compiled by
+  ``Makefile`` (beam_search.cpp, least_squares.cpp, icm.cpp, cost_utils.cpp, ...).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference legs may
+import this package, and only to check or to time the CPU baseline.  The product path
+(``stlq_b200``) never imports it.
+
+All arrays use the reference's column-major layout: a (rows x cols) matrix is a numpy array of
+shape (cols, rows), C-contiguous, so that column j is row j of the numpy array.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libstlq_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libstlq_ref.so")
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_f64p = ctypes.POINTER(ctypes.c_double)
+_i32p = ctypes.POINTER(ctypes.c_int)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+
+
+def build(reference: bool = True) -> None:
+    """Compile the restatement (always) and the reference library (when its sources exist)."""
+    targets = ["oracle"]
+    if reference and os.path.isdir(os.environ.get("STLQ_REF_DIR", "/root/reference")):
+        targets.append("ref")
+    env = dict(os.environ)
+    if "STLQ_REF_DIR" in env:
+        env["REF"] = env["STLQ_REF_DIR"]
+    subprocess.run(["make", "-s", "-C", HERE, "-j8", *targets], check=True, env=env)
+
+
+def _p(a, t):
+    return a.ctypes.data_as(t)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _offsets(h_vec):
+    return np.concatenate([[0], np.cumsum(h_vec)[:-1]]).astype(np.int32)
+
+
+class Oracle:
+    """The CPU restatement (stlq_oracle.cpp)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build(reference=False)
+        self.lib = ctypes.CDLL(path)
+        L = self.lib
+        L.oracle_sse.restype = ctypes.c_double
+        L.oracle_solve_ls_all.restype = ctypes.c_int
+
+    def gemm_xc(self, C_all, X):
+        """xC = C_all^T X.  C_all: (H, d), X: (n, d) -> (n, H)."""
+        C_all, X = _f32(C_all), _f32(X)
+        H, d = C_all.shape
+        n = X.shape[0]
+        out = np.empty((n, H), np.float32)
+        self.lib.oracle_gemm_tn(d, H, n, _p(C_all, _f32p), _p(X, _f32p), _p(out, _f32p))
+        return out
+
+    def xnorm2(self, X):
+        X = _f32(X)
+        out = np.empty(X.shape[0], np.float32)
+        self.lib.oracle_xnorm2(X.shape[1], X.shape[0], _p(X, _f32p), _p(out, _f32p))
+        return out
+
+    def precomp(self, C_all):
+        """(G as (H, H) column-major i.e. G_np[col, row], invnorm (H,))."""
+        C_all = _f32(C_all)
+        H, d = C_all.shape
+        G = np.empty((H, H), np.float32)
+        inv = np.empty(H, np.float32)
+        self.lib.oracle_precomp(d, H, _p(C_all, _f32p), _p(G, _f32p), _p(inv, _f32p))
+        return G, inv
+
+    def beam_search(self, h_vec, G, xnorm2, xC, beam):
+        h = np.asarray(h_vec, np.int32)
+        n, H = xC.shape
+        B = np.empty((n, len(h)), np.uint16)
+        self.lib.oracle_beam_search(len(h), _p(h, _i32p), H, _p(_f32(G), _f32p), n, _p(_f32(xnorm2), _f32p),
+                                    _p(_f32(xC), _f32p), int(beam), _p(B, _u16p))
+        return B
+
+    def solve_ls(self, h_vec, G, xC, B):
+        h = np.asarray(h_vec, np.int32)
+        n, H = xC.shape
+        B = np.ascontiguousarray(B, np.uint16)
+        a = np.empty((n, len(h)), np.float32)
+        fails = self.lib.oracle_solve_ls_all(len(h), _p(h, _i32p), H, _p(_f32(G), _f32p), n, _p(_f32(xC), _f32p),
+                                             _p(B, _u16p), _p(a, _f32p))
+        return a, fails
+
+    def costs(self, h_vec, G, xC, B, a, xnorm2):
+        h = np.asarray(h_vec, np.int32)
+        n, H = xC.shape
+        B = np.ascontiguousarray(B, np.uint16)
+        out = np.empty(n, np.float32)
+        self.lib.oracle_costs(len(h), _p(h, _i32p), H, _p(_f32(G), _f32p), n, _p(_f32(xC), _f32p),
+                              _p(B, _u16p), _p(_f32(a), _f32p), _p(_f32(xnorm2), _f32p), _p(out, _f32p))
+        return out
+
+    def sse(self, h_vec, G, X, xC, B, a):
+        h = np.asarray(h_vec, np.int32)
+        n, H = xC.shape
+        B = np.ascontiguousarray(B, np.uint16)
+        return self.lib.oracle_sse(X.shape[1], len(h), _p(h, _i32p), H, _p(_f32(G), _f32p), n, _p(_f32(X), _f32p),
+                                   _p(_f32(xC), _f32p), _p(B, _u16p), _p(_f32(a), _f32p))
+
+    def icm_orders(self, m, icm_iters, ils_iters, seed):
+        out = np.empty(((ils_iters + 1) * icm_iters * m) or 1, np.int32)
+        self.lib.oracle_icm_orders(m, icm_iters, ils_iters, ctypes.c_uint32(seed), _p(out, _i32p))
+        return out[: (ils_iters + 1) * icm_iters * m].reshape(ils_iters + 1, icm_iters, m)
+
+    def icm(self, h_vec, G, invnorm, xC, xnorm2, B, icm_iters, ils_iters=0, perturb_k=0, use_abs=True,
+            seed=38251450, sample_id_offset=0):
+        """DynamicIcmWithIls*NoNormal.  Returns (B, a, cost); B is copied, not modified."""
+        h = np.asarray(h_vec, np.int32)
+        n, H = xC.shape
+        Bo = np.array(B, np.uint16, copy=True, order="C")
+        a = np.empty((n, len(h)), np.float32)
+        cost = np.empty(n, np.float32)
+        self.lib.oracle_icm(len(h), _p(h, _i32p), H, _p(_f32(G), _f32p), _p(_f32(invnorm), _f32p), n,
+                            _p(_f32(xC), _f32p), _p(_f32(xnorm2), _f32p), int(icm_iters), int(ils_iters),
+                            int(perturb_k), int(bool(use_abs)), ctypes.c_uint32(seed),
+                            ctypes.c_uint64(sample_id_offset), _p(Bo, _u16p), _p(a, _f32p), _p(cost, _f32p))
+        return Bo, a, cost
+
+    def encode_base(self, h_vec, C_all, X, beam, icm_iters, ils_iters=0, perturb_k=0, use_abs=True,
+                    seed=38251450, G=None, invnorm=None):
+        """EncodeBase's stage order (encoder_encode_base.inc:1-106) on the restatement."""
+        if G is None or invnorm is None:
+            G, invnorm = self.precomp(C_all)
+        xC = self.gemm_xc(C_all, X)
+        xn = self.xnorm2(X)
+        B = self.beam_search(h_vec, G, xn, xC, beam)
+        a, _ = self.solve_ls(h_vec, G, xC, B)
+        beam_sse = self.sse(h_vec, G, X, xC, B, a)
+        B, a, cost = self.icm(h_vec, G, invnorm, xC, xn, B, icm_iters, ils_iters, perturb_k, use_abs, seed)
+        final_sse = self.sse(h_vec, G, X, xC, B, a)
+        return dict(B=B, a=a, cost=cost, xC=xC, xnorm2=xn, beam_sse=beam_sse, final_sse=final_sse)
+
+
+class Reference:
+    """The reference's own functions (compiled from its sources by oracle/Makefile)."""
+
+    def __init__(self, path: str = REF_SO, threads: int | None = None):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: build it with `make -C oracle ref` where the reference sources are")
+        self.lib = ctypes.CDLL(path)
+        L = self.lib
+        L.ref_precomp_create.restype = ctypes.c_void_p
+        L.ref_precomp_destroy.argtypes = [ctypes.c_void_p]
+        for f in ("ref_precomp_H", "ref_gemm_xc", "ref_beam_search", "ref_solve_ls", "ref_costs", "ref_mean_mse",
+                  "ref_icm", "ref_encode_base", "ref_precomp_get"):
+            getattr(L, f).argtypes = None
+        L.ref_mean_mse.restype = ctypes.c_float
+        L.ref_blas_core.restype = ctypes.c_char_p
+        self.set_threads(threads or os.cpu_count() or 1)
+
+    def set_threads(self, n: int) -> None:
+        self.threads = int(n)
+        self.lib.ref_set_threads(self.threads)
+
+    def blas_core(self) -> str:
+        return self.lib.ref_blas_core().decode()
+
+    def precomp(self, h_vec, C_all):
+        return RefPrecomp(self, h_vec, C_all)
+
+
+class RefPrecomp:
+    def __init__(self, ref: Reference, h_vec, C_all):
+        self.ref, self.lib = ref, ref.lib
+        self.h_vec = np.asarray(h_vec, np.int32)
+        self.C_all = _f32(C_all)
+        self.H, self.d = self.C_all.shape
+        self.m = len(self.h_vec)
+        self.h = ctypes.c_void_p(self.lib.ref_precomp_create(self.d, self.m, _p(self.h_vec, _i32p),
+                                                             _p(self.C_all, _f32p)))
+
+    def __del__(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            self.lib.ref_precomp_destroy(self.h)
+            self.h = None
+
+    def G_invnorm(self):
+        G = np.empty((self.H, self.H), np.float32)
+        inv = np.empty(self.H, np.float32)
+        self.lib.ref_precomp_get(self.h, _p(G, _f32p), _p(inv, _f32p))
+        return G, inv
+
+    def gemm_xc(self, X):
+        X = _f32(X)
+        out = np.empty((X.shape[0], self.H), np.float32)
+        self.lib.ref_gemm_xc(self.h, _p(X, _f32p), X.shape[0], _p(out, _f32p))
+        return out
+
+    def xnorm2(self, X):
+        X = _f32(X)
+        out = np.empty(X.shape[0], np.float32)
+        self.lib.ref_xnorm2(_p(X, _f32p), X.shape[1], X.shape[0], _p(out, _f32p))
+        return out
+
+    def beam_search(self, X, xC, beam):
+        X = _f32(X)
+        B = np.empty((X.shape[0], self.m), np.uint8)
+        self.lib.ref_beam_search(self.h, _p(X, _f32p), X.shape[0], _p(_f32(xC), _f32p), int(beam), _p(B, _u8p))
+        return B
+
+    def solve_ls(self, xC, B):
+        B = np.ascontiguousarray(B, np.uint8)
+        a = np.empty((B.shape[0], self.m), np.float32)
+        self.lib.ref_solve_ls(self.h, _p(_f32(xC), _f32p), B.shape[0], _p(B, _u8p), _p(a, _f32p))
+        return a
+
+    def costs(self, xC, B, a, xnorm2):
+        B = np.ascontiguousarray(B, np.uint8)
+        out = np.empty(B.shape[0], np.float32)
+        self.lib.ref_costs(self.h, _p(_f32(xC), _f32p), B.shape[0], _p(B, _u8p), _p(_f32(a), _f32p),
+                           _p(_f32(xnorm2), _f32p), _p(out, _f32p))
+        return out
+
+    def mean_mse(self, X, xC, B, a):
+        B = np.ascontiguousarray(B, np.uint8)
+        return float(self.lib.ref_mean_mse(self.h, _p(_f32(X), _f32p), B.shape[0], _p(_f32(xC), _f32p),
+                                           _p(B, _u8p), _p(_f32(a), _f32p)))
+
+    def icm(self, X, xC, B, icm_iters, ils_iters=0, perturb_k=0, use_abs=True, seed=38251450, sample_id_offset=0):
+        Bo = np.array(B, np.uint8, copy=True, order="C")
+        n = Bo.shape[0]
+        a = np.empty((n, self.m), np.float32)
+        cost = np.empty(n, np.float32)
+        self.lib.ref_icm(self.h, _p(_f32(X), _f32p), n, _p(_f32(xC), _f32p), int(icm_iters), int(ils_iters),
+                         int(perturb_k), int(bool(use_abs)), ctypes.c_uint32(seed), ctypes.c_uint64(sample_id_offset),
+                         _p(Bo, _u8p), _p(a, _f32p), _p(cost, _f32p))
+        return Bo, a, cost
+
+    def encode_base(self, X, beam, icm_iters, ils_iters=0, perturb_k=0, use_abs=True, seed=38251450):
+        X = _f32(X)
+        n = X.shape[0]
+        B = np.empty((n, self.m), np.uint8)
+        a = np.empty((n, self.m), np.float32)
+        cost = np.empty(n, np.float32)
+        bm, fm = ctypes.c_float(), ctypes.c_float()
+        t = np.zeros(5, np.float64)
+        rc = self.lib.ref_encode_base(self.h, _p(X, _f32p), n, int(beam), int(icm_iters), int(ils_iters),
+                                      int(perturb_k), int(bool(use_abs)), ctypes.c_uint32(seed), _p(B, _u8p),
+                                      _p(a, _f32p), _p(cost, _f32p), ctypes.byref(bm), ctypes.byref(fm), _p(t, _f64p))
+        if rc != 0:
+            raise RuntimeError(f"ref_encode_base failed: {rc}")
+        return dict(B=B, a=a, cost=cost, beam_mse=bm.value, final_mse=fm.value, t_stages=t)

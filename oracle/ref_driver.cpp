@@ -1,0 +1,249 @@
+// Test infrastructure only (parity checker and CPU baseline); never part of the product path.
+//
+// A thin extern "C" driver around the REFERENCE's own hot-path functions, compiled from the
+// reference sources where they lie (oracle/Makefile lists them).  Python tests and bench.py's
+// reference arm load the resulting oracle/_ref/libstlq_ref.so through ctypes.
+//
+// Every entry point calls the reference's code; the only logic restated here is the glue that
+// the reference keeps in translation units too heavy to compile on their own:
+//   - ref_precomp_create restates BuildPrecomp (src/quantizer/encoder_precomp.inc:1-53)
+//     and calls the reference's stlq::Gemm for G, exactly as BuildPrecomp does.
+//   - ref_encode_base restates the stage order of EncodeBase
+//     (src/quantizer/encoder_encode_base.inc:1-106), CPU branch.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include <omp.h>
+
+#include "stlq/common/types.h"
+#include "stlq/core/blas.h"
+#include "stlq/core/threading.h"
+#include "stlq/linkage/linkage_summary.h"
+#include "stlq/quantizer/beam_search.h"
+#include "stlq/quantizer/cost_utils.h"
+#include "stlq/quantizer/icm.h"
+#include "stlq/quantizer/least_squares.h"
+
+extern "C" char* openblas_get_corename(void);
+
+namespace {
+
+using stlq::ColMajorMatrix;
+using stlq::FullCode;
+using stlq::Precomp;
+
+ColMajorMatrix<float> Wrap(const float* p, int rows, int cols) {
+    ColMajorMatrix<float> m(rows, cols);
+    std::memcpy(m.data.data(), p, sizeof(float) * static_cast<std::size_t>(rows) * cols);
+    return m;
+}
+
+ColMajorMatrix<FullCode> WrapCodes(const std::uint8_t* p, int rows, int cols) {
+    ColMajorMatrix<FullCode> m(rows, cols);
+    std::memcpy(m.data.data(), p, static_cast<std::size_t>(rows) * cols);
+    return m;
+}
+
+double Now() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ref_blas_core(void) { return openblas_get_corename(); }
+
+void ref_set_threads(int n) {
+    omp_set_num_threads(std::max(1, n));
+    stlq::SetOmpDefaultThreads(std::max(1, n));
+    stlq::BlasSetThreads(1);
+}
+
+int ref_max_threads(void) { return omp_get_max_threads(); }
+
+// Restates BuildPrecomp (encoder_precomp.inc:1-53): C_all = concat of books, invnorm, offsets,
+// flat_layer, and G = C_all^T C_all through the reference's stlq::Gemm.
+void* ref_precomp_create(int d, int m, const int* h_vec, const float* C_all) {
+    auto* p = new Precomp();
+    int H = 0;
+    for (int l = 0; l < m; ++l) H += h_vec[l];
+    p->C_all = Wrap(C_all, d, H);
+    p->G = ColMajorMatrix<float>(H, H);
+    p->offsets.resize(m);
+    p->flat_layer.resize(H);
+    p->invnorm_flat.resize(H);
+    p->h_vec.assign(h_vec, h_vec + m);
+    p->H = H;
+    p->m = m;
+    p->d = d;
+    int off = 0;
+    for (int l = 0; l < m; ++l) {
+        p->offsets[l] = off;
+        for (int c = 0; c < h_vec[l]; ++c) {
+            const float* col = p->C_all.Col(off + c);
+            float norm_sq = 0.0f;
+            for (int r = 0; r < d; ++r) norm_sq += col[r] * col[r];
+            p->flat_layer[off + c] = l;
+            p->invnorm_flat[off + c] = norm_sq > 0.0f ? 1.0f / std::sqrt(norm_sq) : 0.0f;
+        }
+        off += h_vec[l];
+    }
+    {
+        stlq::ScopedBlasThreads blas_scope(stlq::OmpMaxThreads());
+        stlq::Gemm(true, false, 1.0f, p->C_all, p->C_all, 0.0f, &p->G);
+    }
+    static std::uint64_t tag = 0;
+    p->build_tag = ++tag;
+    return p;
+}
+
+void ref_precomp_destroy(void* h) { delete static_cast<Precomp*>(h); }
+
+int ref_precomp_H(void* h) { return static_cast<Precomp*>(h)->H; }
+
+void ref_precomp_get(void* h, float* G_out, float* invnorm_out) {
+    const auto* p = static_cast<Precomp*>(h);
+    if (G_out) std::memcpy(G_out, p->G.data.data(), sizeof(float) * p->G.data.size());
+    if (invnorm_out) std::memcpy(invnorm_out, p->invnorm_flat.data(), sizeof(float) * p->H);
+}
+
+// xC = C_all^T X with the reference's Gemm (encoder_encode_base.inc:33-37).
+void ref_gemm_xc(void* h, const float* X, int n, float* xC_out) {
+    const auto* p = static_cast<Precomp*>(h);
+    ColMajorMatrix<float> Xm = Wrap(X, p->d, n);
+    ColMajorMatrix<float> xC(p->H, n);
+    {
+        stlq::ScopedBlasThreads blas_scope(stlq::OmpMaxThreads());
+        stlq::Gemm(true, false, 1.0f, p->C_all, Xm, 0.0f, &xC);
+    }
+    std::memcpy(xC_out, xC.data.data(), sizeof(float) * xC.data.size());
+}
+
+// BeamSearchPrefixLS (beam_search.cpp:196-422).
+void ref_beam_search(void* h, const float* X, int n, const float* xC, int beam, std::uint8_t* B_out) {
+    const auto* p = static_cast<Precomp*>(h);
+    ColMajorMatrix<float> Xm = Wrap(X, p->d, n);
+    ColMajorMatrix<float> xCm = Wrap(xC, p->H, n);
+    ColMajorMatrix<FullCode> B;
+    stlq::BeamSearchPrefixLS(Xm, *p, xCm, std::max(1, beam), &B);
+    std::memcpy(B_out, B.data.data(), B.data.size());
+}
+
+// SolveLeastSquaresAll (least_squares.cpp:406+).
+void ref_solve_ls(void* h, const float* xC, int n, const std::uint8_t* B, float* a_out) {
+    const auto* p = static_cast<Precomp*>(h);
+    ColMajorMatrix<float> xCm = Wrap(xC, p->H, n);
+    ColMajorMatrix<FullCode> Bm = WrapCodes(B, p->m, n);
+    ColMajorMatrix<float> a;
+    stlq::SolveLeastSquaresAll(*p, xCm, Bm, &a);
+    std::memcpy(a_out, a.data.data(), sizeof(float) * a.data.size());
+}
+
+// ComputeXNorm2 (cost_utils.cpp:88-110).
+void ref_xnorm2(const float* X, int d, int n, float* out) {
+    ColMajorMatrix<float> Xm = Wrap(X, d, n);
+    std::vector<float> v;
+    stlq::ComputeXNorm2(Xm, &v);
+    std::memcpy(out, v.data(), sizeof(float) * v.size());
+}
+
+// ComputeCosts (cost_utils.cpp:139-158).
+void ref_costs(void* h, const float* xC, int n, const std::uint8_t* B, const float* a,
+               const float* xnorm2, float* out) {
+    const auto* p = static_cast<Precomp*>(h);
+    ColMajorMatrix<float> xCm = Wrap(xC, p->H, n);
+    ColMajorMatrix<FullCode> Bm = WrapCodes(B, p->m, n);
+    ColMajorMatrix<float> am = Wrap(a, p->m, n);
+    std::vector<float> xn(xnorm2, xnorm2 + n), c;
+    stlq::ComputeCosts(*p, xCm, Bm, am, xn, &c);
+    std::memcpy(out, c.data(), sizeof(float) * c.size());
+}
+
+// MeanMseFromPrecomp (src/linkage/linkage_tools.cpp:170-219).
+float ref_mean_mse(void* h, const float* X, int n, const float* xC, const std::uint8_t* B, const float* a) {
+    const auto* p = static_cast<Precomp*>(h);
+    ColMajorMatrix<float> Xm = Wrap(X, p->d, n);
+    ColMajorMatrix<float> xCm = Wrap(xC, p->H, n);
+    ColMajorMatrix<FullCode> Bm = WrapCodes(B, p->m, n);
+    ColMajorMatrix<float> am = Wrap(a, p->m, n);
+    return stlq::MeanMseFromPrecomp(Xm, *p, xCm, Bm, am);
+}
+
+// DynamicIcmWithIls{Abs,NoAbs}NoNormal (icm.cpp:872-1003, 1132-1170).  B is in/out; a and cost
+// are outputs (cost may be null).
+void ref_icm(void* h, const float* X, int n, const float* xC, int icm_iters, int ils_iters, int perturb_k,
+             int use_abs, std::uint32_t seed, std::uint64_t sample_id_offset, std::uint8_t* B_io,
+             float* a_out, float* cost_out) {
+    const auto* p = static_cast<Precomp*>(h);
+    ColMajorMatrix<float> Xm = Wrap(X, p->d, n);
+    ColMajorMatrix<float> xCm = Wrap(xC, p->H, n);
+    ColMajorMatrix<FullCode> Bm = WrapCodes(B_io, p->m, n);
+    ColMajorMatrix<float> a;
+    std::vector<float> xn, cost;
+    if (use_abs) {
+        stlq::DynamicIcmWithIlsAbsNoNormal(Xm, *p, xCm, icm_iters, ils_iters, perturb_k, seed, &Bm, &a, &xn,
+                                           &cost, false, sample_id_offset);
+    } else {
+        stlq::DynamicIcmWithIlsNoAbsNoNormal(Xm, *p, xCm, icm_iters, ils_iters, perturb_k, seed, &Bm, &a, &xn,
+                                             &cost, false, sample_id_offset);
+    }
+    std::memcpy(B_io, Bm.data.data(), Bm.data.size());
+    if (a_out) std::memcpy(a_out, a.data.data(), sizeof(float) * a.data.size());
+    if (cost_out) std::memcpy(cost_out, cost.data(), sizeof(float) * cost.size());
+}
+
+// The CPU branch of EncodeBase (encoder_encode_base.inc:1-106), stage by stage.
+// t_stages (optional, 5 doubles): seconds in GEMM, beam, LS + beam MSE, ICM, final MSE.
+int ref_encode_base(void* h, const float* X, int n, int beam, int icm_iters, int ils_iters, int perturb_k,
+                    int use_abs, std::uint32_t seed, std::uint8_t* B_out, float* a_out, float* cost_out,
+                    float* beam_mse, float* final_mse, double* t_stages) {
+    const auto* p = static_cast<Precomp*>(h);
+    if (n <= 0 || p->d <= 0) return 1;
+    double t0 = Now();
+    ColMajorMatrix<float> Xm = Wrap(X, p->d, n);
+    ColMajorMatrix<float> xC(p->H, n);
+    {
+        stlq::ScopedBlasThreads blas_scope(stlq::OmpMaxThreads());
+        stlq::Gemm(true, false, 1.0f, p->C_all, Xm, 0.0f, &xC);
+    }
+    double t1 = Now();
+    stlq::BaseEncoding base;
+    stlq::BeamSearchPrefixLS(Xm, *p, xC, std::max(1, beam), &base.B);
+    double t2 = Now();
+    stlq::SolveLeastSquaresAll(*p, xC, base.B, &base.a);
+    const float bm = stlq::MeanMseFromPrecomp(Xm, *p, xC, base.B, base.a);
+    double t3 = Now();
+    std::vector<float> xn, cost;
+    if (use_abs) {
+        stlq::DynamicIcmWithIlsAbsNoNormal(Xm, *p, xC, icm_iters, ils_iters, perturb_k, seed, &base.B, &base.a,
+                                           &xn, &cost, false, 0);
+    } else {
+        stlq::DynamicIcmWithIlsNoAbsNoNormal(Xm, *p, xC, icm_iters, ils_iters, perturb_k, seed, &base.B,
+                                             &base.a, &xn, &cost, false, 0);
+    }
+    double t4 = Now();
+    const float fm = stlq::MeanMseFromPrecomp(Xm, *p, xC, base.B, base.a);
+    double t5 = Now();
+    std::memcpy(B_out, base.B.data.data(), base.B.data.size());
+    if (a_out) std::memcpy(a_out, base.a.data.data(), sizeof(float) * base.a.data.size());
+    if (cost_out && cost.size() == static_cast<std::size_t>(n)) {
+        std::memcpy(cost_out, cost.data(), sizeof(float) * n);
+    }
+    if (beam_mse) *beam_mse = bm;
+    if (final_mse) *final_mse = fm;
+    if (t_stages) {
+        t_stages[0] = t1 - t0;
+        t_stages[1] = t2 - t1;
+        t_stages[2] = t3 - t2;
+        t_stages[3] = t4 - t3;
+        t_stages[4] = t5 - t4;
+    }
+    return 0;
+}
+
+}  // extern "C"

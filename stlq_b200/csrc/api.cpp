@@ -1,0 +1,609 @@
+// C-ABI of stlq_b200 (include/stlq_b200.h): encoder handles, device scratch, the slice loop of
+// the encode stage, and the pinned double-buffered host path.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/stlq_b200.h"
+#include "launch.h"
+
+using stlq_b200::Dims;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int Fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+#define STLQ_CK(expr)                                                                                \
+    do {                                                                                             \
+        const cudaError_t e_ = (expr);                                                               \
+        if (e_ != cudaSuccess)                                                                       \
+            return Fail(e_ == cudaErrorMemoryAllocation ? STLQ_B200_ENOMEM : STLQ_B200_ECUDA,        \
+                        std::string(#expr) + ": " + cudaGetErrorString(e_));                         \
+    } while (0)
+
+#define STLQ_TRY(expr)              \
+    do {                            \
+        const int rc_ = (expr);     \
+        if (rc_ != 0) return rc_;   \
+    } while (0)
+
+// Makes `device` current for the scope and restores the caller's device afterwards.
+class DeviceScope {
+public:
+    explicit DeviceScope(int device) {
+        if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+        ok_ = cudaSetDevice(device) == cudaSuccess;
+    }
+    ~DeviceScope() {
+        if (prev_ >= 0) cudaSetDevice(prev_);
+    }
+    bool ok() const { return ok_; }
+
+private:
+    int prev_ = -1;
+    bool ok_ = false;
+};
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    int Ensure(size_t need) {
+        if (need <= bytes) return 0;
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+        const cudaError_t e = cudaMalloc(&p, need);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return Fail(STLQ_B200_ENOMEM, "cudaMalloc(" + std::to_string(need) + " bytes) failed: " +
+                                              cudaGetErrorString(e));
+        }
+        bytes = need;
+        return 0;
+    }
+    void Release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <typename T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+struct PinBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    int Ensure(size_t need) {
+        if (need <= bytes) return 0;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+        const cudaError_t e = cudaMallocHost(&p, need);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return Fail(STLQ_B200_ENOMEM, "cudaMallocHost(" + std::to_string(need) + " bytes) failed");
+        }
+        bytes = need;
+        return 0;
+    }
+    void Release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+    }
+};
+
+bool IsPinnedHost(const void* p) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost;
+}
+
+size_t ElemSize(int x_dtype) { return x_dtype == STLQ_B200_U8 ? 1 : 4; }
+
+}  // namespace
+
+struct stlq_b200_encoder {
+    int device = 0;
+    int num_sms = 148;
+    int gemm_mode = STLQ_B200_GEMM_EXACT;
+    Dims dims{};
+    DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
+    // Per-call scratch, grown on demand and kept for the handle's lifetime.
+    DevBuf xC, xn, xnd, partials, orders;
+    std::vector<int> orders_host;
+    int64_t orders_key[4] = {-1, -1, -1, -1};
+    // Host path.
+    cudaStream_t compute = nullptr, copy = nullptr;
+    cudaEvent_t ev_h2d[2] = {}, ev_comp[2] = {}, ev_d2h[2] = {};
+    DevBuf xin[2], Bd[2], ad[2], costd[2], sse_d;
+    PinBuf pin_in[2], pin_B[2], pin_a[2], pin_cost[2], pin_sse;
+};
+
+namespace {
+
+// Vectors per encode slice: bounds the xC scratch (H floats per vector) to ~2 GiB.
+int64_t SliceVectors(const stlq_b200_encoder* enc) {
+    const int64_t by_mem = (int64_t{1} << 31) / (static_cast<int64_t>(enc->dims.H) * 4);
+    return std::max<int64_t>(1024, std::min<int64_t>(by_mem, stlq_b200::MaxGemmSliceVectors()));
+}
+
+int RefineGrid(const stlq_b200_encoder* enc, int64_t n) {
+    const int64_t per_block = stlq_b200::RefineWarpsPerBlock();
+    const int64_t want = (n + per_block - 1) / per_block;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t{enc->num_sms} * 16)));
+}
+
+int CheckEnc(const stlq_b200_encoder* enc) {
+    if (!enc) return Fail(STLQ_B200_EINVAL, "encoder handle is null");
+    return 0;
+}
+
+int CheckEncodeArgs(const stlq_b200_encoder* enc, int x_dtype, int64_t n, int beam, int icm_iters, int ils_iters,
+                    int perturb_k) {
+    STLQ_TRY(CheckEnc(enc));
+    if (x_dtype != STLQ_B200_F32 && x_dtype != STLQ_B200_U8) return Fail(STLQ_B200_EINVAL, "x_dtype must be F32 or U8");
+    if (n < 0) return Fail(STLQ_B200_EINVAL, "n must be >= 0");
+    if (beam < 1 || beam > STLQ_B200_MAX_BEAM)
+        return Fail(STLQ_B200_EINVAL, "beam must be in [1, " + std::to_string(STLQ_B200_MAX_BEAM) + "]");
+    if (icm_iters < 0 || ils_iters < 0 || perturb_k < 0)
+        return Fail(STLQ_B200_EINVAL, "icm_iters, ils_iters and perturb_k must be >= 0");
+    return 0;
+}
+
+// ICM layer orders exactly as the reference draws them: one std::mt19937(seed) for the whole
+// call, `order` reset to iota at each RunIcm call and std::shuffle'd once per ICM iteration
+// (icm.cpp:119-122, 239-243, 890-895, 974-975).  Uploaded only when they change.
+int UploadOrders(stlq_b200_encoder* enc, int icm_iters, int n_ils, uint32_t seed, cudaStream_t stream) {
+    const int m = enc->dims.m;
+    const int64_t key[4] = {m, icm_iters, n_ils, static_cast<int64_t>(seed)};
+    if (std::equal(key, key + 4, enc->orders_key)) return 0;
+    const size_t count = static_cast<size_t>(n_ils + 1) * icm_iters * m;
+    enc->orders_host.assign(std::max<size_t>(count, 1), 0);
+    std::mt19937 rng(static_cast<std::mt19937::result_type>(seed));
+    std::vector<int> order(m);
+    size_t w = 0;
+    for (int call = 0; call <= n_ils; ++call) {
+        std::iota(order.begin(), order.end(), 0);
+        for (int it = 0; it < icm_iters; ++it) {
+            std::shuffle(order.begin(), order.end(), rng);
+            for (int l = 0; l < m; ++l) enc->orders_host[w++] = order[l];
+        }
+    }
+    STLQ_TRY(enc->orders.Ensure(enc->orders_host.size() * sizeof(int)));
+    STLQ_CK(cudaMemcpyAsync(enc->orders.p, enc->orders_host.data(), enc->orders_host.size() * sizeof(int),
+                            cudaMemcpyHostToDevice, stream));
+    STLQ_CK(cudaStreamSynchronize(stream));  // orders_host may change on the next call
+    std::copy(key, key + 4, enc->orders_key);
+    return 0;
+}
+
+int EnsureScratch(stlq_b200_encoder* enc, int64_t slice) {
+    STLQ_TRY(enc->xC.Ensure(static_cast<size_t>(slice) * enc->dims.H * sizeof(float)));
+    STLQ_TRY(enc->xn.Ensure(static_cast<size_t>(slice) * sizeof(float)));
+    STLQ_TRY(enc->xnd.Ensure(static_cast<size_t>(slice) * sizeof(double)));
+    STLQ_TRY(enc->partials.Ensure(static_cast<size_t>(RefineGrid(enc, slice)) * 2 * sizeof(double)));
+    return 0;
+}
+
+// The encode stage on device buffers for n vectors, sliced; sse_dev (2 doubles) accumulates.
+int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters, int ils_iters,
+                 int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset, uint8_t* B, float* a,
+                 float* cost, double* sse_dev, cudaStream_t stream) {
+    const Dims& dims = enc->dims;
+    const int n_ils = (ils_iters <= 0 || perturb_k <= 0 || dims.m <= 1) ? 0 : ils_iters;
+    if (icm_iters > 0) STLQ_TRY(UploadOrders(enc, icm_iters, n_ils, seed, stream));
+    const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), SliceVectors(enc));
+    STLQ_TRY(EnsureScratch(enc, S));
+    const size_t esz = ElemSize(x_dtype);
+    for (int64_t s0 = 0; s0 < n; s0 += S) {
+        const int64_t ns = std::min(S, n - s0);
+        const void* Xs = static_cast<const char*>(X) + static_cast<size_t>(s0) * dims.d * esz;
+        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), dims.H, dims.d, Xs, x_dtype, ns, enc->xC.as<float>(),
+                                             dims.H, enc->xn.as<float>(), enc->xnd.as<double>(), stream));
+        STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
+                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m,
+                                            enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
+        stlq_b200::RefineArgs ra{};
+        ra.dims = dims;
+        ra.Gcol = enc->Gcol.as<float>();
+        ra.invnorm = enc->invnorm.as<float>();
+        ra.xC = enc->xC.as<float>();
+        ra.xnorm2 = enc->xn.as<float>();
+        ra.xnorm2_d = enc->xnd.as<double>();
+        ra.n = ns;
+        ra.mode = 1;
+        ra.icm_iters = icm_iters;
+        ra.n_ils = n_ils;
+        ra.perturb_k = perturb_k;
+        ra.use_abs = use_abs;
+        ra.seed = seed;
+        ra.sample_id_offset = sample_id_offset + static_cast<uint64_t>(s0);
+        ra.orders = icm_iters > 0 ? enc->orders.as<int>() : nullptr;
+        ra.B = B + s0 * dims.m;
+        ra.a = a ? a + s0 * dims.m : nullptr;
+        ra.cost = cost ? cost + s0 : nullptr;
+        ra.partials = sse_dev ? enc->partials.as<double>() : nullptr;
+        const int grid = RefineGrid(enc, ns);
+        STLQ_CK(stlq_b200::LaunchRefine(ra, grid, stream));
+        if (sse_dev) STLQ_CK(stlq_b200::LaunchReducePartials(enc->partials.as<double>(), grid, sse_dev, stream));
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* stlq_b200_last_error(void) { return g_last_error.c_str(); }
+
+const char* stlq_b200_version(void) { return "stlq_b200 0.1.0 sm_100a"; }
+
+int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_all, const float* G,
+                     const float* invnorm, int gemm_mode, stlq_b200_encoder** out) {
+    if (!out) return Fail(STLQ_B200_EINVAL, "out is null");
+    *out = nullptr;
+    if (!h_vec || !C_all) return Fail(STLQ_B200_EINVAL, "h_vec and C_all must be non-null");
+    if (d < 1) return Fail(STLQ_B200_EINVAL, "d must be >= 1");
+    if (m < 1 || m > STLQ_B200_MAX_M) return Fail(STLQ_B200_EINVAL, "m must be in [1, 16]");
+    if (gemm_mode != STLQ_B200_GEMM_EXACT)
+        return Fail(STLQ_B200_EINVAL, "gemm_mode: only STLQ_B200_GEMM_EXACT is available in this build");
+    Dims dims{};
+    dims.d = d;
+    dims.m = m;
+    int H = 0, maxK = 0;
+    for (int l = 0; l < m; ++l) {
+        if (h_vec[l] < 1 || h_vec[l] > STLQ_B200_MAX_K)
+            return Fail(STLQ_B200_EINVAL, "h_vec[" + std::to_string(l) + "] must be in [1, 256] (uint8 codes)");
+        dims.h_vec[l] = h_vec[l];
+        dims.off[l] = H;
+        H += h_vec[l];
+        maxK = std::max(maxK, h_vec[l]);
+    }
+    dims.H = H;
+    dims.maxK = maxK;
+    int ndev = 0;
+    STLQ_CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return Fail(STLQ_B200_EINVAL, "device ordinal out of range");
+    DeviceScope scope(device);
+    if (!scope.ok()) return Fail(STLQ_B200_ECUDA, "cudaSetDevice failed");
+    auto* enc = new stlq_b200_encoder();
+    enc->device = device;
+    enc->dims = dims;
+    enc->gemm_mode = gemm_mode;
+    auto fail = [&](int rc) {
+        stlq_b200_destroy(enc);
+        return rc;
+    };
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) enc->num_sms = prop.multiProcessorCount;
+    const size_t HH = static_cast<size_t>(H) * H;
+    int rc = 0;
+    if ((rc = enc->C.Ensure(sizeof(float) * H * d)) || (rc = enc->Gcol.Ensure(sizeof(float) * HH)) ||
+        (rc = enc->Grow.Ensure(sizeof(float) * HH)) || (rc = enc->Gdiag.Ensure(sizeof(float) * H)) ||
+        (rc = enc->invnorm.Ensure(sizeof(float) * H)) || (rc = enc->err_flag.Ensure(sizeof(unsigned int))))
+        return fail(rc);
+    if (cudaStreamCreateWithFlags(&enc->compute, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&enc->copy, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(Fail(STLQ_B200_ECUDA, "cudaStreamCreate failed"));
+    for (int b = 0; b < 2; ++b) {
+        if (cudaEventCreateWithFlags(&enc->ev_h2d[b], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&enc->ev_comp[b], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&enc->ev_d2h[b], cudaEventDisableTiming) != cudaSuccess)
+            return fail(Fail(STLQ_B200_ECUDA, "cudaEventCreate failed"));
+    }
+    cudaStream_t s = enc->compute;
+    auto ck = [&](cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return 0;
+        return Fail(STLQ_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    if ((rc = ck(cudaMemcpyAsync(enc->C.p, C_all, sizeof(float) * H * d, cudaMemcpyHostToDevice, s), "upload C_all")))
+        return fail(rc);
+    if (G) {
+        rc = ck(cudaMemcpyAsync(enc->Gcol.p, G, sizeof(float) * HH, cudaMemcpyHostToDevice, s), "upload G");
+    } else {
+        // G = C_all^T C_all in the same summation order as xC (BuildPrecomp calls the same Gemm).
+        rc = ck(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), H, d, enc->C.p, STLQ_B200_F32, H, enc->Gcol.as<float>(),
+                                             H, nullptr, nullptr, s),
+                "G gemm");
+    }
+    if (rc) return fail(rc);
+    if (invnorm) {
+        rc = ck(cudaMemcpyAsync(enc->invnorm.p, invnorm, sizeof(float) * H, cudaMemcpyHostToDevice, s), "upload invnorm");
+    } else {
+        rc = ck(stlq_b200::LaunchInvnorm(enc->C.as<float>(), H, d, enc->invnorm.as<float>(), s), "invnorm");
+    }
+    if (rc) return fail(rc);
+    if ((rc = ck(stlq_b200::LaunchTranspose(enc->Gcol.as<float>(), enc->Grow.as<float>(), H, H, s), "transpose G")) ||
+        (rc = ck(stlq_b200::LaunchDiag(enc->Gcol.as<float>(), enc->Gdiag.as<float>(), H, s), "diag G")) ||
+        (rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, sizeof(unsigned int), s), "memset")) ||
+        (rc = ck(cudaStreamSynchronize(s), "create sync")))
+        return fail(rc);
+    *out = enc;
+    return 0;
+}
+
+int stlq_b200_destroy(stlq_b200_encoder* enc) {
+    if (!enc) return 0;
+    DeviceScope scope(enc->device);
+    if (enc->compute) cudaStreamSynchronize(enc->compute);
+    if (enc->copy) cudaStreamSynchronize(enc->copy);
+    for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
+                      &enc->xnd, &enc->partials, &enc->orders, &enc->sse_d})
+        b->Release();
+    for (int i = 0; i < 2; ++i) {
+        enc->xin[i].Release();
+        enc->Bd[i].Release();
+        enc->ad[i].Release();
+        enc->costd[i].Release();
+        enc->pin_in[i].Release();
+        enc->pin_B[i].Release();
+        enc->pin_a[i].Release();
+        enc->pin_cost[i].Release();
+        if (enc->ev_h2d[i]) cudaEventDestroy(enc->ev_h2d[i]);
+        if (enc->ev_comp[i]) cudaEventDestroy(enc->ev_comp[i]);
+        if (enc->ev_d2h[i]) cudaEventDestroy(enc->ev_d2h[i]);
+    }
+    enc->pin_sse.Release();
+    if (enc->compute) cudaStreamDestroy(enc->compute);
+    if (enc->copy) cudaStreamDestroy(enc->copy);
+    delete enc;
+    return 0;
+}
+
+int stlq_b200_dims(const stlq_b200_encoder* enc, int* d, int* m, int* H) {
+    STLQ_TRY(CheckEnc(enc));
+    if (d) *d = enc->dims.d;
+    if (m) *m = enc->dims.m;
+    if (H) *H = enc->dims.H;
+    return 0;
+}
+
+int stlq_b200_sync(stlq_b200_encoder* enc, void* stream) {
+    STLQ_TRY(CheckEnc(enc));
+    DeviceScope scope(enc->device);
+    STLQ_CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    unsigned int flag = 0;
+    STLQ_CK(cudaMemcpy(&flag, enc->err_flag.p, sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag) {
+        cudaMemset(enc->err_flag.p, 0, sizeof(flag));
+        return Fail(STLQ_B200_EDEVICE, "a kernel reported internal error flags 0x" + std::to_string(flag));
+    }
+    return 0;
+}
+
+int stlq_b200_encode_base_device(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, int beam,
+                                 int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                 uint64_t sample_id_offset, uint8_t* B_dev, float* a_dev, float* cost_dev,
+                                 double* sse_out_dev, void* stream) {
+    STLQ_TRY(CheckEncodeArgs(enc, x_dtype, n, beam, icm_iters, ils_iters, perturb_k));
+    if (n > 0 && (!X_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "X_dev and B_dev must be non-null");
+    DeviceScope scope(enc->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (sse_out_dev) STLQ_CK(cudaMemsetAsync(sse_out_dev, 0, 2 * sizeof(double), s));
+    return EncodeDevice(enc, X_dev, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed, sample_id_offset,
+                        B_dev, a_dev, cost_dev, sse_out_dev, s);
+}
+
+// Host buffers: slices of up to `kHostSlice` vectors go through two pinned/device buffer pairs.
+// The copy stream carries H2D of slice s+1 and D2H of slice s-1 while the compute stream encodes
+// slice s; host staging into pinned memory is skipped when the caller's buffers are pinned.
+int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
+                          int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                          uint8_t* B_out, float* a_out, float* cost_out, double* sse_out) {
+    STLQ_TRY(CheckEncodeArgs(enc, x_dtype, n, beam, icm_iters, ils_iters, perturb_k));
+    if (n > 0 && (!X || !B_out)) return Fail(STLQ_B200_EINVAL, "X and B_out must be non-null");
+    DeviceScope scope(enc->device);
+    const Dims& dims = enc->dims;
+    const int64_t kHostSlice = 262144;
+    const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), kHostSlice);
+    const size_t esz = ElemSize(x_dtype);
+    const size_t in_bytes = static_cast<size_t>(S) * dims.d * esz;
+    const bool pin_x = IsPinnedHost(X);
+    const bool pin_B = IsPinnedHost(B_out);
+    const bool pin_a = !a_out || IsPinnedHost(a_out);
+    const bool pin_c = !cost_out || IsPinnedHost(cost_out);
+    for (int b = 0; b < 2; ++b) {
+        STLQ_TRY(enc->xin[b].Ensure(in_bytes));
+        STLQ_TRY(enc->Bd[b].Ensure(static_cast<size_t>(S) * dims.m));
+        STLQ_TRY(enc->ad[b].Ensure(static_cast<size_t>(S) * dims.m * sizeof(float)));
+        STLQ_TRY(enc->costd[b].Ensure(static_cast<size_t>(S) * sizeof(float)));
+        if (!pin_x) STLQ_TRY(enc->pin_in[b].Ensure(in_bytes));
+        if (!pin_B) STLQ_TRY(enc->pin_B[b].Ensure(static_cast<size_t>(S) * dims.m));
+        if (!pin_a) STLQ_TRY(enc->pin_a[b].Ensure(static_cast<size_t>(S) * dims.m * sizeof(float)));
+        if (!pin_c) STLQ_TRY(enc->pin_cost[b].Ensure(static_cast<size_t>(S) * sizeof(float)));
+    }
+    STLQ_TRY(enc->sse_d.Ensure(2 * sizeof(double)));
+    STLQ_TRY(enc->pin_sse.Ensure(2 * sizeof(double)));
+    cudaStream_t cs = enc->compute, ps = enc->copy;
+    STLQ_CK(cudaMemsetAsync(enc->sse_d.p, 0, 2 * sizeof(double), cs));
+    const int64_t nslices = (n + S - 1) / S;
+    std::vector<int64_t> pending;  // slice ids whose outputs still sit in the pinned buffers
+    auto drain = [&](int64_t s) -> int {
+        const int b = static_cast<int>(s % 2);
+        const int64_t s0 = s * S, ns = std::min(S, n - s0);
+        STLQ_CK(cudaEventSynchronize(enc->ev_d2h[b]));
+        if (!pin_B) std::memcpy(B_out + s0 * dims.m, enc->pin_B[b].p, static_cast<size_t>(ns) * dims.m);
+        if (!pin_a) std::memcpy(a_out + s0 * dims.m, enc->pin_a[b].p, static_cast<size_t>(ns) * dims.m * sizeof(float));
+        if (!pin_c) std::memcpy(cost_out + s0, enc->pin_cost[b].p, static_cast<size_t>(ns) * sizeof(float));
+        return 0;
+    };
+    for (int64_t s = 0; s < nslices; ++s) {
+        const int b = static_cast<int>(s % 2);
+        const int64_t s0 = s * S, ns = std::min(S, n - s0);
+        if (s >= 2) STLQ_TRY(drain(s - 2));
+        const char* src = static_cast<const char*>(X) + static_cast<size_t>(s0) * dims.d * esz;
+        const size_t nbytes = static_cast<size_t>(ns) * dims.d * esz;
+        if (!pin_x) {
+            std::memcpy(enc->pin_in[b].p, src, nbytes);
+            src = static_cast<const char*>(enc->pin_in[b].p);
+        }
+        STLQ_CK(cudaMemcpyAsync(enc->xin[b].p, src, nbytes, cudaMemcpyHostToDevice, ps));
+        STLQ_CK(cudaEventRecord(enc->ev_h2d[b], ps));
+        STLQ_CK(cudaStreamWaitEvent(cs, enc->ev_h2d[b], 0));
+        STLQ_TRY(EncodeDevice(enc, enc->xin[b].p, x_dtype, ns, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
+                              sample_id_offset + static_cast<uint64_t>(s0), enc->Bd[b].as<uint8_t>(),
+                              a_out ? enc->ad[b].as<float>() : nullptr, cost_out ? enc->costd[b].as<float>() : nullptr,
+                              sse_out ? enc->sse_d.as<double>() : nullptr, cs));
+        STLQ_CK(cudaEventRecord(enc->ev_comp[b], cs));
+        STLQ_CK(cudaStreamWaitEvent(ps, enc->ev_comp[b], 0));
+        void* dB = pin_B ? static_cast<void*>(B_out + s0 * dims.m) : enc->pin_B[b].p;
+        STLQ_CK(cudaMemcpyAsync(dB, enc->Bd[b].p, static_cast<size_t>(ns) * dims.m, cudaMemcpyDeviceToHost, ps));
+        if (a_out) {
+            void* da = pin_a ? static_cast<void*>(a_out + s0 * dims.m) : enc->pin_a[b].p;
+            STLQ_CK(cudaMemcpyAsync(da, enc->ad[b].p, static_cast<size_t>(ns) * dims.m * sizeof(float),
+                                    cudaMemcpyDeviceToHost, ps));
+        }
+        if (cost_out) {
+            void* dc = pin_c ? static_cast<void*>(cost_out + s0) : enc->pin_cost[b].p;
+            STLQ_CK(cudaMemcpyAsync(dc, enc->costd[b].p, static_cast<size_t>(ns) * sizeof(float), cudaMemcpyDeviceToHost,
+                                    ps));
+        }
+        STLQ_CK(cudaEventRecord(enc->ev_d2h[b], ps));
+    }
+    for (int64_t s = std::max<int64_t>(0, nslices - 2); s < nslices; ++s) STLQ_TRY(drain(s));
+    if (sse_out) {
+        STLQ_CK(cudaMemcpyAsync(enc->pin_sse.p, enc->sse_d.p, 2 * sizeof(double), cudaMemcpyDeviceToHost, cs));
+        STLQ_CK(cudaStreamSynchronize(cs));
+        std::memcpy(sse_out, enc->pin_sse.p, 2 * sizeof(double));
+    }
+    return stlq_b200_sync(enc, cs);
+}
+
+int stlq_b200_xc_gemm(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* xC_dev, void* stream) {
+    STLQ_TRY(CheckEnc(enc));
+    if (n > 0 && (!X_dev || !xC_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    const int64_t S = stlq_b200::MaxGemmSliceVectors();
+    const size_t esz = ElemSize(x_dtype);
+    for (int64_t s0 = 0; s0 < n; s0 += S) {
+        const int64_t ns = std::min(S, n - s0);
+        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), enc->dims.H, enc->dims.d,
+                                             static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
+                                             x_dtype, ns, xC_dev + s0 * enc->dims.H, enc->dims.H, nullptr, nullptr,
+                                             static_cast<cudaStream_t>(stream)));
+    }
+    return 0;
+}
+
+int stlq_b200_xnorm2(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* xnorm2_dev,
+                     void* stream) {
+    STLQ_TRY(CheckEnc(enc));
+    if (n > 0 && (!X_dev || !xnorm2_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    // The norm is fused into the GEMM's first codeword tile: run a one-tile GEMM into scratch.
+    const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), stlq_b200::MaxGemmSliceVectors());
+    const int rows = std::min(enc->dims.H, 1);
+    STLQ_TRY(enc->xC.Ensure(static_cast<size_t>(S) * rows * sizeof(float)));
+    const size_t esz = ElemSize(x_dtype);
+    for (int64_t s0 = 0; s0 < n; s0 += S) {
+        const int64_t ns = std::min(S, n - s0);
+        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), rows, enc->dims.d,
+                                             static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
+                                             x_dtype, ns, enc->xC.as<float>(), rows, xnorm2_dev + s0, nullptr,
+                                             static_cast<cudaStream_t>(stream)));
+    }
+    return 0;
+}
+
+int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const float* xC_dev, int64_t n, int beam,
+                          uint8_t* B_dev, void* stream) {
+    STLQ_TRY(CheckEncodeArgs(enc, STLQ_B200_F32, n, beam, 0, 0, 0));
+    if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), xnorm2_dev, xC_dev, n,
+                                        beam, B_dev, enc->err_flag.as<unsigned int>(), enc->num_sms,
+                                        static_cast<cudaStream_t>(stream)));
+    return 0;
+}
+
+int stlq_b200_solve_ls(stlq_b200_encoder* enc, const float* xC_dev, const uint8_t* B_dev, int64_t n, float* a_dev,
+                       void* stream) {
+    STLQ_TRY(CheckEnc(enc));
+    if (n > 0 && (!xC_dev || !B_dev || !a_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    stlq_b200::RefineArgs ra{};
+    ra.dims = enc->dims;
+    ra.Gcol = enc->Gcol.as<float>();
+    ra.invnorm = enc->invnorm.as<float>();
+    ra.xC = xC_dev;
+    ra.n = n;
+    ra.mode = 0;
+    ra.B = const_cast<uint8_t*>(B_dev);  // read only in mode 0
+    ra.a = a_dev;
+    STLQ_CK(stlq_b200::LaunchRefine(ra, RefineGrid(enc, n), static_cast<cudaStream_t>(stream)));
+    return 0;
+}
+
+int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnorm2_dev, int64_t n, int icm_iters,
+                  int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset, uint8_t* B_dev,
+                  float* a_dev, float* cost_dev, void* stream) {
+    STLQ_TRY(CheckEncodeArgs(enc, STLQ_B200_F32, n, 1, icm_iters, ils_iters, perturb_k));
+    if (n > 0 && (!xC_dev || !xnorm2_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int n_ils = (ils_iters <= 0 || perturb_k <= 0 || enc->dims.m <= 1) ? 0 : ils_iters;
+    if (icm_iters > 0) STLQ_TRY(UploadOrders(enc, icm_iters, n_ils, seed, s));
+    stlq_b200::RefineArgs ra{};
+    ra.dims = enc->dims;
+    ra.Gcol = enc->Gcol.as<float>();
+    ra.invnorm = enc->invnorm.as<float>();
+    ra.xC = xC_dev;
+    ra.xnorm2 = xnorm2_dev;
+    ra.n = n;
+    ra.mode = 1;
+    ra.icm_iters = icm_iters;
+    ra.n_ils = n_ils;
+    ra.perturb_k = perturb_k;
+    ra.use_abs = use_abs;
+    ra.seed = seed;
+    ra.sample_id_offset = sample_id_offset;
+    ra.orders = icm_iters > 0 ? enc->orders.as<int>() : nullptr;
+    ra.B = B_dev;
+    ra.a = a_dev;
+    ra.cost = cost_dev;
+    STLQ_CK(stlq_b200::LaunchRefine(ra, RefineGrid(enc, n), s));
+    return 0;
+}
+
+int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const float* xC_dev, const uint8_t* B_dev,
+                  const float* a_dev, int64_t n, double* sse_dev, void* stream) {
+    STLQ_TRY(CheckEnc(enc));
+    if (n > 0 && (!X_dev || !xC_dev || !B_dev || !a_dev || !sse_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), stlq_b200::MaxGemmSliceVectors());
+    STLQ_TRY(enc->xnd.Ensure(static_cast<size_t>(S) * sizeof(double)));
+    STLQ_TRY(enc->xC.Ensure(static_cast<size_t>(S) * sizeof(float)));
+    const int grid = static_cast<int>(std::min<int64_t>((S + 255) / 256, int64_t{enc->num_sms} * 8));
+    STLQ_TRY(enc->partials.Ensure(static_cast<size_t>(grid) * 2 * sizeof(double)));
+    const size_t esz = ElemSize(x_dtype);
+    for (int64_t s0 = 0; s0 < n; s0 += S) {
+        const int64_t ns = std::min(S, n - s0);
+        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), 1, enc->dims.d,
+                                             static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
+                                             x_dtype, ns, enc->xC.as<float>(), 1, nullptr, enc->xnd.as<double>(), s));
+        const int g = static_cast<int>(std::min<int64_t>((ns + 255) / 256, grid));
+        STLQ_CK(stlq_b200::LaunchSse(enc->dims, enc->Gcol.as<float>(), xC_dev + s0 * enc->dims.H, enc->xnd.as<double>(),
+                                     B_dev + s0 * enc->dims.m, a_dev + s0 * enc->dims.m, ns, enc->partials.as<double>(),
+                                     g, s));
+        STLQ_CK(stlq_b200::LaunchReducePartials(enc->partials.as<double>(), g, sse_dev, s));
+    }
+    return 0;
+}
+
+}  // extern "C"

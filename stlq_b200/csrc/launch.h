@@ -1,0 +1,51 @@
+// Host-side launchers of the stlq_b200 kernels (defined in the .cu files of this directory).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "types.h"
+
+namespace stlq_b200 {
+
+cudaError_t LaunchXcGemmExact(const float* C, int rows, int d, const void* X, int x_dtype, int64_t n, float* out,
+                              int ldo, float* xnorm2, double* xnorm2_d, cudaStream_t stream);
+int MaxGemmSliceVectors();
+
+cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
+                             const float* xC, int64_t n, int beam, uint8_t* Bout, unsigned int* err_flag,
+                             int num_sms, cudaStream_t stream);
+
+struct RefineArgs {
+    Dims dims;
+    const float* Gcol;
+    const float* invnorm;
+    const float* xC;
+    const float* xnorm2;
+    const double* xnorm2_d;
+    int64_t n;
+    int mode;  // 0 = LS only, 1 = full (LS, ICM, ILS, cost)
+    int icm_iters;
+    int n_ils;
+    int perturb_k;
+    int use_abs;
+    uint32_t seed;
+    uint64_t sample_id_offset;
+    const int* orders;  // [(n_ils + 1)][icm_iters][m]
+    uint8_t* B;
+    float* a;
+    float* cost;
+    double* partials;  // [grid][2] (beam SSE, final SSE) or null
+};
+
+cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream);
+cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* out, cudaStream_t stream);
+cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const uint8_t* B,
+                      const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
+int RefineWarpsPerBlock();
+
+cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream);
+cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream);
+cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream);
+
+}  // namespace stlq_b200

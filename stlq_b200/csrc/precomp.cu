@@ -1,0 +1,62 @@
+// Device-side parts of BuildPrecomp (reference src/quantizer/encoder_precomp.inc:1-53) that the
+// encoder derives from C_all and G: the row-major copy of G used by the beam kernel's coalesced
+// cross-term gathers, the diagonal alpha = G(h, h), and 1/||c_h||.
+#include <cstdint>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace stlq_b200 {
+
+namespace {
+
+// out[c * rows + r] = in[r * cols + c] through 32x32 shared-memory tiles.
+__global__ void TransposeKernel(const float* __restrict__ in, float* __restrict__ out, int rows, int cols) {
+    __shared__ float tile[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = by + j, c = bx + threadIdx.x;
+        if (r < rows && c < cols) tile[j][threadIdx.x] = in[static_cast<size_t>(r) * cols + c];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int c = bx + j, r = by + threadIdx.x;
+        if (r < rows && c < cols) out[static_cast<size_t>(c) * rows + r] = tile[threadIdx.x][j];
+    }
+}
+
+__global__ void DiagKernel(const float* __restrict__ Gcol, float* __restrict__ diag, int H) {
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h < H) diag[h] = Gcol[static_cast<size_t>(h) * H + h];
+}
+
+// invnorm_flat[h] = 1/sqrt(sum_r c_r^2) with the reference's sequential float sum
+// (encoder_precomp.inc:31-39); 0 for a zero codeword.
+__global__ void InvnormKernel(const float* __restrict__ C, int H, int d, float* __restrict__ invnorm) {
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= H) return;
+    const float* c = C + static_cast<size_t>(h) * d;
+    float s = 0.0f;
+    for (int r = 0; r < d; ++r) s = __fadd_rn(s, __fmul_rn(c[r], c[r]));
+    invnorm[h] = s > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(s)) : 0.0f;
+}
+
+}  // namespace
+
+cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream) {
+    dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+    TransposeKernel<<<grid, block, 0, stream>>>(in, out, rows, cols);
+    return cudaGetLastError();
+}
+
+cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream) {
+    DiagKernel<<<(H + 255) / 256, 256, 0, stream>>>(Gcol, diag, H);
+    return cudaGetLastError();
+}
+
+cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream) {
+    InvnormKernel<<<(H + 127) / 128, 128, 0, stream>>>(C, H, d, invnorm);
+    return cudaGetLastError();
+}
+
+}  // namespace stlq_b200

@@ -1,0 +1,410 @@
+// Least squares, cost, MSE and ICM/ILS refinement for sm_100a, fused per vector.
+//
+// Reference semantics:
+//   SolveLeastSquaresAll / SolveLeastSquaresSample   src/quantizer/least_squares.cpp:86-129, 252-318, 406-560
+//   SampleCost / ComputeCosts                         src/quantizer/cost_utils.cpp:112-158
+//   MeanMseFromPrecomp (per-vector term, double)      src/linkage/linkage_tools.cpp:170-219
+//   RunIcm<UseAbs>, DynamicIcmWithIlsImpl             src/quantizer/icm.cpp:89-344, 872-1003
+//
+// Every step of ICM and ILS is independent across vectors once the layer orders are known (the
+// reference draws them on the host from one std::mt19937 and the same orders apply to every
+// vector), so one warp carries a vector through LS, cost, all ICM sweeps and all ILS rounds
+// without returning to the host: the reference launches one kernel per layer per sweep and
+// copies state through the host between them (icm_cuda_kernels.inc:2183-2261).
+//
+// Layout: one warp per vector, 4 warps per CTA.  The ICM scores of a layer are spread over the
+// 32 lanes (coalesced reads of G's column segment); the argmax reduces with shuffles; the small
+// SPD solves run on lane 0 from a per-warp shared-memory matrix.
+#include <cstdint>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace stlq_b200 {
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kRefineThreads = 32 * kWarps;
+
+struct WarpState {
+    float A[kMaxM * kMaxM];
+    float b[kMaxM];
+    float x[kMaxM];
+    float y[kMaxM];
+    float a[kMaxM];
+    float backup[kMaxM];
+    int code[kMaxM];
+    int cand[kMaxM];
+    float acand[kMaxM];
+};
+
+__device__ __forceinline__ float GAt(const float* Gcol, int H, int row, int col) {
+    return Gcol[static_cast<size_t>(col) * H + row];
+}
+
+// Fixed-size Cholesky for m in {5, 10} (CholeskyUpperFixed, least_squares.cpp:44-66), row-major.
+__device__ bool CholFixed(float* A, int m) {
+    for (int k = 0; k < m; ++k) {
+        float sum = A[k * m + k];
+        for (int j = 0; j < k; ++j) {
+            const float v = A[j * m + k];
+            sum = sub_rn(sum, mul_rn(v, v));
+        }
+        if (sum <= kIcmEps) return false;
+        const float diag = __fsqrt_rn(sum);
+        A[k * m + k] = diag;
+        for (int i = k + 1; i < m; ++i) {
+            float s = A[k * m + i];
+            for (int j = 0; j < k; ++j) s = sub_rn(s, mul_rn(A[j * m + k], A[j * m + i]));
+            A[k * m + i] = div_rn(s, diag);
+        }
+    }
+    return true;
+}
+
+// Upper Cholesky for the other m (LAPACK spotrf 'U' at least_squares.cpp:289): unblocked column
+// algorithm of xPOTF2, dot products as FMA chains, row scaled by the reciprocal pivot.
+__device__ bool CholLapack(float* A, int m) {  // column-major A[r + c*m]
+    for (int j = 0; j < m; ++j) {
+        float dot = 0.0f;
+        for (int k = 0; k < j; ++k) dot = __fmaf_rn(A[k + j * m], A[k + j * m], dot);
+        float ajj = sub_rn(A[j + j * m], dot);
+        if (!(ajj > 0.0f)) return false;
+        ajj = __fsqrt_rn(ajj);
+        A[j + j * m] = ajj;
+        const float r = div_rn(1.0f, ajj);
+        for (int i = j + 1; i < m; ++i) {
+            float s = 0.0f;
+            for (int k = 0; k < j; ++k) s = __fmaf_rn(A[k + j * m], A[k + i * m], s);
+            A[j + i * m] = mul_rn(sub_rn(A[j + i * m], s), r);
+        }
+    }
+    return true;
+}
+
+// One vector's LS solve with the reference's retry policy (3 diagonal bumps 1e-6 x10^i).
+__device__ bool SolveLs(const Dims& dims, const float* Gcol, const float* xc, const int* code, WarpState& ws,
+                        float* a_out) {
+    const int m = dims.m, H = dims.H;
+    const bool fixed = (m == 5 || m == 10);
+    float lambda = 0.0f;
+    for (int attempt = 0; attempt < 4; ++attempt) {
+        for (int e = 0; e < m * m; ++e) ws.A[e] = 0.0f;
+        for (int j = 0; j < m; ++j) {
+            const int fj = dims.off[j] + code[j];
+            ws.b[j] = xc[fj];
+            for (int k = 0; k <= j; ++k) {
+                const int fk = dims.off[k] + code[k];
+                const float g = GAt(Gcol, H, fk, fj);
+                if (fixed) ws.A[k * m + j] = g;
+                else ws.A[k + j * m] = g;
+            }
+            if (fixed) ws.A[j * m + j] = add_rn(ws.A[j * m + j], lambda);
+            else ws.A[j + j * m] = add_rn(ws.A[j + j * m], lambda);
+        }
+        const bool ok = fixed ? CholFixed(ws.A, m) : CholLapack(ws.A, m);
+        if (ok) {
+            if (fixed) {
+                for (int i = 0; i < m; ++i) {
+                    float s = ws.b[i];
+                    for (int k = 0; k < i; ++k) s = sub_rn(s, mul_rn(ws.A[k * m + i], ws.y[k]));
+                    ws.y[i] = div_rn(s, ws.A[i * m + i]);
+                }
+                for (int i = m - 1; i >= 0; --i) {
+                    float s = ws.y[i];
+                    for (int k = i + 1; k < m; ++k) s = sub_rn(s, mul_rn(ws.A[i * m + k], ws.x[k]));
+                    ws.x[i] = div_rn(s, ws.A[i * m + i]);
+                }
+                for (int i = 0; i < m; ++i) a_out[i] = ws.x[i];
+            } else {
+                for (int i = 0; i < m; ++i) {
+                    float s = 0.0f;
+                    for (int k = 0; k < i; ++k) s = __fmaf_rn(ws.A[k + i * m], ws.b[k], s);
+                    ws.b[i] = div_rn(sub_rn(ws.b[i], s), ws.A[i + i * m]);
+                }
+                for (int i = m - 1; i >= 0; --i) {
+                    float s = 0.0f;
+                    for (int k = i + 1; k < m; ++k) s = __fmaf_rn(ws.A[i + k * m], ws.b[k], s);
+                    ws.b[i] = div_rn(sub_rn(ws.b[i], s), ws.A[i + i * m]);
+                }
+                for (int i = 0; i < m; ++i) a_out[i] = ws.b[i];
+            }
+            return true;
+        }
+        lambda = (attempt == 0) ? kIcmEps : mul_rn(lambda, 10.0f);
+    }
+    return false;
+}
+
+// SampleCost (cost_utils.cpp:112-137).
+__device__ float SampleCost(const Dims& dims, const float* Gcol, const float* xc, const int* code, const float* a,
+                            float xn2) {
+    const int m = dims.m, H = dims.H;
+    float term1 = 0.0f, term2 = 0.0f;
+    for (int l = 0; l < m; ++l) {
+        const int fl = dims.off[l] + code[l];
+        term1 = add_rn(term1, mul_rn(a[l], xc[fl]));
+        for (int k = 0; k < m; ++k) {
+            const int fk = dims.off[k] + code[k];
+            term2 = add_rn(term2, mul_rn(mul_rn(a[l], a[k]), GAt(Gcol, H, fl, fk)));
+        }
+    }
+    return add_rn(sub_rn(xn2, mul_rn(2.0f, term1)), term2);
+}
+
+// Per-vector term of MeanMseFromPrecomp in double, clamped at 0.
+__device__ double VectorSse(const Dims& dims, const float* Gcol, const float* xc, const int* code, const float* a,
+                            double nx) {
+    const int m = dims.m, H = dims.H;
+    double t1 = 0.0, t2 = 0.0;
+    for (int j = 0; j < m; ++j)
+        t1 = __dadd_rn(t1, __dmul_rn(static_cast<double>(a[j]), static_cast<double>(xc[dims.off[j] + code[j]])));
+    for (int j = 0; j < m; ++j)
+        for (int k = 0; k < m; ++k)
+            t2 = __dadd_rn(t2, __dmul_rn(__dmul_rn(static_cast<double>(a[j]), static_cast<double>(a[k])),
+                                         static_cast<double>(GAt(Gcol, H, dims.off[j] + code[j], dims.off[k] + code[k]))));
+    const double e = __dadd_rn(__dsub_rn(nx, __dmul_rn(2.0, t1)), t2);
+    return e < 0.0 ? 0.0 : e;
+}
+
+struct SplitMix64 {  // icm.cpp:55-65
+    uint64_t state;
+    __device__ uint64_t Next() {
+        uint64_t z = (state += 0x9e3779b97f4a7c15ULL);
+        z = (z ^ (z >> 30U)) * 0xbf58476d1ce4e5b9ULL;
+        z = (z ^ (z >> 27U)) * 0x94d049bb133111ebULL;
+        return z ^ (z >> 31U);
+    }
+};
+
+__device__ __forceinline__ uint32_t UniformBelow(SplitMix64& r, uint32_t bound) {  // icm.cpp:76-87
+    return static_cast<uint32_t>(__umul64hi(r.Next(), static_cast<uint64_t>(bound)));
+}
+
+// One RunIcm call (icm.cpp:89-344) on `code` (in/out) for the warp's vector; a and cost out.
+// With do_init false the caller has already solved LS and the cost for `code` (RunIcm's first
+// step, icm.cpp:109-114), so only the sweeps run.
+__device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* invnorm, const float* xc, float xn2,
+                           int icm_iters, const int* orders, bool use_abs, int* code, float* a, float* cost,
+                           WarpState& ws, bool do_init = true) {
+    const int lane = threadIdx.x & 31;
+    const int m = dims.m, H = dims.H;
+    if (do_init && lane == 0) {
+        if (!SolveLs(dims, Gcol, xc, code, ws, a))
+            for (int l = 0; l < m; ++l) a[l] = 0.0f;
+        *cost = SampleCost(dims, Gcol, xc, code, a, xn2);
+    }
+    __syncwarp();
+    bool active = true;
+    for (int it = 0; it < icm_iters && active; ++it) {
+        bool changed = false;
+        for (int oi = 0; oi < m; ++oi) {
+            const int j = orders[it * m + oi];
+            const int hj = dims.h_vec[j];
+            if (j == 0 || hj <= 1) continue;
+            const int startf = dims.off[j];
+            const int old_code = code[j];
+            // score(t) = (xC(t) - sum_{l != j} a_l G(t, flat_l)) * invnorm(t)   (icm.cpp:272-300)
+            float best_s = __int_as_float(0xff800000);  // -inf
+            int best_t = 0x7fffffff;
+            for (int t = lane; t < hj; t += 32) {
+                float v = xc[startf + t];
+                for (int l = 0; l < m; ++l) {
+                    if (l == j) continue;
+                    const int fl = dims.off[l] + code[l];
+                    v = sub_rn(v, mul_rn(a[l], __ldg(Gcol + static_cast<size_t>(fl) * H + startf + t)));
+                }
+                const float val = mul_rn(v, __ldg(invnorm + startf + t));
+                const float s = use_abs ? fabsf(val) : val;
+                if (s > best_s) {  // first strict maximum in t order
+                    best_s = s;
+                    best_t = t;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float s2 = __shfl_xor_sync(0xffffffffu, best_s, o);
+                const int t2 = __shfl_xor_sync(0xffffffffu, best_t, o);
+                if (s2 > best_s || (s2 == best_s && t2 < best_t)) {
+                    best_s = s2;
+                    best_t = t2;
+                }
+            }
+            const int best = (best_s > __int_as_float(0xff800000)) ? best_t : old_code;
+            if (best == old_code) continue;
+            if (lane == 0) {
+                for (int l = 0; l < m; ++l) ws.backup[l] = a[l];
+                code[j] = best;
+                bool keep = SolveLs(dims, Gcol, xc, code, ws, a);
+                if (keep) {
+                    const float nc = SampleCost(dims, Gcol, xc, code, a, xn2);
+                    keep = add_rn(nc, kIcmEps) < *cost;
+                    if (keep) {
+                        *cost = nc;
+                        changed = true;
+                    }
+                }
+                if (!keep) {
+                    code[j] = old_code;
+                    for (int l = 0; l < m; ++l) a[l] = ws.backup[l];
+                }
+            }
+            changed = __shfl_sync(0xffffffffu, changed, 0);
+            __syncwarp();
+        }
+        if (!changed) active = false;
+    }
+}
+
+}  // namespace
+
+
+
+__global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
+    __shared__ WarpState wss[kWarps];
+    __shared__ double sse_w[kWarps][2];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    WarpState& ws = wss[warp];
+    const Dims& dims = p.dims;
+    const int m = dims.m;
+    double sse_beam = 0.0, sse_final = 0.0;
+    for (int64_t vec = static_cast<int64_t>(blockIdx.x) * kWarps + warp; vec < p.n;
+         vec += static_cast<int64_t>(gridDim.x) * kWarps) {
+        const float* xc = p.xC + vec * dims.H;
+        if (lane < m) ws.code[lane] = p.B[vec * m + lane];
+        __syncwarp();
+        if (p.mode == 0) {
+            if (lane == 0) {
+                if (!SolveLs(dims, p.Gcol, xc, ws.code, ws, ws.a))
+                    for (int l = 0; l < m; ++l) ws.a[l] = 0.0f;
+            }
+            __syncwarp();
+            if (lane < m) p.a[vec * m + lane] = ws.a[lane];
+            __syncwarp();
+            continue;
+        }
+        const float xn2 = p.xnorm2[vec];
+        float cost = 0.0f;
+        // RunIcm's first step recomputes LS and cost for the beam codes (icm.cpp:109-114); with
+        // the MSE requested, the LS result is also the beam-stage coefficients.
+        RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, 0, p.orders, p.use_abs, ws.code, ws.a, &cost, ws);
+        if (p.partials && lane == 0) sse_beam += VectorSse(dims, p.Gcol, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+        __syncwarp();
+        if (p.icm_iters > 0)
+            RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
+                       /*do_init=*/false);
+        cost = __shfl_sync(0xffffffffu, cost, 0);
+        const int ksel = min(p.perturb_k, m);
+        for (int outer = 0; outer < p.n_ils; ++outer) {
+            if (lane < m) ws.cand[lane] = ws.code[lane];
+            __syncwarp();
+            if (lane == 0) {  // icm.cpp:953-972
+                const uint64_t ig = p.sample_id_offset + static_cast<uint64_t>(vec);
+                SplitMix64 r{static_cast<uint64_t>(p.seed) ^ (static_cast<uint64_t>(outer + 1) * 0x9e3779b97f4a7c15ULL) ^
+                             ((ig + 1) * 0xbf58476d1ce4e5b9ULL)};
+                for (int s = 0; s < ksel; ++s) {
+                    const int layer = 1 + static_cast<int>(UniformBelow(r, static_cast<uint32_t>(m - 1)));
+                    const int h = dims.h_vec[layer];
+                    if (h <= 1) continue;
+                    const int old_code = ws.cand[layer];
+                    const int raw = static_cast<int>(UniformBelow(r, static_cast<uint32_t>(h - 1)));
+                    ws.cand[layer] = raw >= old_code ? raw + 1 : raw;
+                }
+            }
+            __syncwarp();
+            float ccost = 0.0f;
+            RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, p.icm_iters,
+                       p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, ws.cand, ws.acand,
+                       &ccost, ws);
+            ccost = __shfl_sync(0xffffffffu, ccost, 0);
+            if (add_rn(ccost, kIcmEps) < cost) {  // icm.cpp:979-990
+                if (lane < m) {
+                    ws.code[lane] = ws.cand[lane];
+                    ws.a[lane] = ws.acand[lane];
+                }
+                cost = ccost;
+            }
+            __syncwarp();
+        }
+        if (p.partials && lane == 0) sse_final += VectorSse(dims, p.Gcol, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+        if (lane < m) {
+            p.B[vec * m + lane] = static_cast<uint8_t>(ws.code[lane]);
+            if (p.a) p.a[vec * m + lane] = ws.a[lane];
+        }
+        if (lane == 0 && p.cost) p.cost[vec] = cost;
+        __syncwarp();
+    }
+    if (p.partials) {
+        if (lane == 0) {
+            sse_w[warp][0] = sse_beam;
+            sse_w[warp][1] = sse_final;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double s0 = 0.0, s1 = 0.0;
+            for (int w = 0; w < kWarps; ++w) {
+                s0 += sse_w[w][0];
+                s1 += sse_w[w][1];
+            }
+            p.partials[2 * blockIdx.x] = s0;
+            p.partials[2 * blockIdx.x + 1] = s1;
+        }
+    }
+}
+
+// Sums the per-CTA partials in a fixed order and adds them into out[0..1].
+__global__ void ReducePartialsKernel(const double* partials, int nblocks, double* out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        double s0 = 0.0, s1 = 0.0;
+        for (int b = 0; b < nblocks; ++b) {
+            s0 += partials[2 * b];
+            s1 += partials[2 * b + 1];
+        }
+        out[0] += s0;
+        out[1] += s1;
+    }
+}
+
+// Per-vector MSE term alone (stlq_b200_sse): one thread per vector.
+__global__ void SseKernel(Dims dims, const float* Gcol, const float* xC, const double* xnorm2_d, const uint8_t* B,
+                          const float* a, int64_t n, double* partials) {
+    __shared__ double red[256];
+    double s = 0.0;
+    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n;
+         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int code[kMaxM];
+        for (int l = 0; l < dims.m; ++l) code[l] = B[v * dims.m + l];
+        s += VectorSse(dims, Gcol, xC + v * dims.H, code, a + v * dims.m, xnorm2_d[v]);
+    }
+    red[threadIdx.x] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < blockDim.x; ++i) t += red[i];
+        partials[2 * blockIdx.x] = 0.0;
+        partials[2 * blockIdx.x + 1] = t;
+    }
+}
+
+cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream) {
+    if (args.n <= 0) return cudaSuccess;
+    RefineKernel<<<grid, kRefineThreads, 0, stream>>>(args);
+    return cudaGetLastError();
+}
+
+cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* out, cudaStream_t stream) {
+    ReducePartialsKernel<<<1, 32, 0, stream>>>(partials, nblocks, out);
+    return cudaGetLastError();
+}
+
+cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const uint8_t* B,
+                      const float* a, int64_t n, double* partials, int grid, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    SseKernel<<<grid, 256, 0, stream>>>(dims, Gcol, xC, xnorm2_d, B, a, n, partials);
+    return cudaGetLastError();
+}
+
+int RefineWarpsPerBlock() { return kWarps; }
+
+}  // namespace stlq_b200

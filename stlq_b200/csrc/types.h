@@ -1,0 +1,31 @@
+// Plain types shared by the host launchers and the kernels of stlq_b200.
+#pragma once
+
+#include <cstdint>
+
+namespace stlq_b200 {
+
+constexpr int kMaxM = 16;
+constexpr int kMaxK = 256;
+constexpr int kMaxBeam = 32;
+constexpr float kIcmEps = 1e-6f;  // icm.cpp:29, least_squares.cpp:19
+
+// Device-side error flags (bit set by a kernel that met a state it cannot handle; read by the
+// host after the stream synchronises).  Kernels never trap.
+enum DeviceError : unsigned int {
+    kErrNone = 0,
+    kErrSurvivorOverflow = 1u << 0,
+    kErrBadShape = 1u << 1,
+};
+
+// Encoder constants shared by every kernel, passed by value.
+struct Dims {
+    int d;        // vector dimension
+    int m;        // codebooks
+    int H;        // sum of h_vec
+    int maxK;     // max of h_vec
+    int h_vec[kMaxM];
+    int off[kMaxM];
+};
+
+}  // namespace stlq_b200

@@ -1,0 +1,232 @@
+"""ctypes host layer over libstlq_b200.so with the reference's encoder-stage names.
+
+Array convention (the reference's column-major matrices, include/stlq/common/types.h:37-55): a
+reference ``d x n`` matrix is a C-contiguous array of shape ``(n, d)`` here, so vector j is row j.
+Codes are ``(n, m)`` uint8, coefficients ``(n, m)`` float32, ``xC`` is ``(n, H)`` float32.
+
+Host entry points take numpy arrays; ``*_device`` / stage entry points take CUDA torch tensors and
+run on the tensor's current stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+GEMM_EXACT, GEMM_STRICT, GEMM_FAST = 0, 1, 2
+_MODES = {"exact": GEMM_EXACT, "strict": GEMM_STRICT, "fast": GEMM_FAST}
+F32, U8 = 0, 1
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+
+class StlqB200Error(RuntimeError):
+    pass
+
+
+def library_path() -> str:
+    return os.environ.get("STLQ_B200_LIB", os.path.join(_HERE, "libstlq_b200.so"))
+
+
+def load_library():
+    """Load libstlq_b200.so (built by ``python -m stlq_b200.build``); raises if it is missing."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = library_path()
+    if not os.path.exists(path):
+        raise StlqB200Error(f"{path} is missing: build it with `python -m stlq_b200.build` (no CPU fallback exists)")
+    lib = ctypes.CDLL(path)
+    c_int, c_i64, c_u32, c_u64, vp = ctypes.c_int, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p
+    lib.stlq_b200_last_error.restype = ctypes.c_char_p
+    lib.stlq_b200_version.restype = ctypes.c_char_p
+    lib.stlq_b200_create.argtypes = [c_int, c_int, c_int, vp, vp, vp, vp, c_int, ctypes.POINTER(vp)]
+    lib.stlq_b200_destroy.argtypes = [vp]
+    lib.stlq_b200_encode_base.argtypes = [vp, vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_int, c_u32, c_u64,
+                                          vp, vp, vp, vp]
+    lib.stlq_b200_encode_base_device.argtypes = [vp, vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_int, c_u32,
+                                                 c_u64, vp, vp, vp, vp, vp]
+    lib.stlq_b200_xc_gemm.argtypes = [vp, vp, c_int, c_i64, vp, vp]
+    lib.stlq_b200_xnorm2.argtypes = [vp, vp, c_int, c_i64, vp, vp]
+    lib.stlq_b200_beam_search.argtypes = [vp, vp, vp, c_i64, c_int, vp, vp]
+    lib.stlq_b200_solve_ls.argtypes = [vp, vp, vp, c_i64, vp, vp]
+    lib.stlq_b200_icm.argtypes = [vp, vp, vp, c_i64, c_int, c_int, c_int, c_int, c_u32, c_u64, vp, vp, vp, vp]
+    lib.stlq_b200_sse.argtypes = [vp, vp, c_int, vp, vp, vp, c_i64, vp, vp]
+    lib.stlq_b200_sync.argtypes = [vp, vp]
+    lib.stlq_b200_dims.argtypes = [vp, vp, vp, vp]
+    _LIB = lib
+    return lib
+
+
+def _check(lib, rc: int, what: str) -> None:
+    if rc != 0:
+        raise StlqB200Error(f"{what} failed ({rc}): {lib.stlq_b200_last_error().decode()}")
+
+
+def _np_ptr(a):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else None
+
+
+def _t_ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _dtype_code(x) -> int:
+    name = str(x.dtype)
+    if name.endswith("uint8"):
+        return U8
+    if name.endswith("float32"):
+        return F32
+    raise StlqB200Error(f"X must be float32 or uint8, got {x.dtype}")
+
+
+class Encoder:
+    """One frozen codebook set on one GPU (BuildPrecomp + the device session).
+
+    C_all: (H, d) float32, row h = flat codeword h (the reference's Precomp::C_all column h).
+    h_vec: codewords per codebook.  G / invnorm: optional precomputed Precomp::G (H x H, either
+    orientation of a symmetric matrix is accepted as stored: G_np[col, row]) and invnorm_flat.
+    """
+
+    def __init__(self, C_all, h_vec, G=None, invnorm=None, device: int = 0, gemm_mode="exact"):
+        self.lib = load_library()
+        self.C_all = np.ascontiguousarray(C_all, np.float32)
+        self.h_vec = np.ascontiguousarray(h_vec, np.int32)
+        self.H, self.d = self.C_all.shape
+        self.m = len(self.h_vec)
+        if int(self.h_vec.sum()) != self.H:
+            raise StlqB200Error("sum(h_vec) must equal C_all.shape[0]")
+        self.device = int(device)
+        mode = _MODES[gemm_mode] if isinstance(gemm_mode, str) else int(gemm_mode)
+        Gc = None if G is None else np.ascontiguousarray(G, np.float32)
+        inv = None if invnorm is None else np.ascontiguousarray(invnorm, np.float32)
+        h = ctypes.c_void_p()
+        rc = self.lib.stlq_b200_create(self.device, self.d, self.m, _np_ptr(self.h_vec), _np_ptr(self.C_all),
+                                       _np_ptr(Gc), _np_ptr(inv), mode, ctypes.byref(h))
+        _check(self.lib, rc, "stlq_b200_create")
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.stlq_b200_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- whole stage, host buffers -------------------------------------------------------
+    def encode_base(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,
+                    seed: int = 38251450, sample_id_offset: int = 0, out=None, want_a=True, want_cost=True):
+        """EncodeBase (encoder_encode_base.inc:1-106) on host arrays.
+
+        Returns dict(B, a, cost, beam_mse, final_mse).  ``out`` may supply preallocated (pinned)
+        arrays under the same keys."""
+        X = np.ascontiguousarray(X)
+        n = X.shape[0]
+        out = dict(out or {})
+        B = out.get("B")
+        B = np.empty((n, self.m), np.uint8) if B is None else B
+        a = out.get("a") if want_a else None
+        a = np.empty((n, self.m), np.float32) if (want_a and a is None) else a
+        cost = out.get("cost") if want_cost else None
+        cost = np.empty(n, np.float32) if (want_cost and cost is None) else cost
+        sse = np.zeros(2, np.float64)
+        rc = self.lib.stlq_b200_encode_base(self.handle, _np_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters,
+                                            perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF, sample_id_offset,
+                                            _np_ptr(B), _np_ptr(a), _np_ptr(cost), _np_ptr(sse))
+        _check(self.lib, rc, "stlq_b200_encode_base")
+        nn = max(n, 1)
+        return dict(B=B, a=a, cost=cost, beam_mse=sse[0] / nn, final_mse=sse[1] / nn, sse=sse)
+
+    # ---- whole stage, device tensors -----------------------------------------------------
+    def encode_base_device(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,
+                           seed: int = 38251450, sample_id_offset: int = 0, B=None, a=None, cost=None, sse=None,
+                           stream=None):
+        """Asynchronous on ``stream`` (default: torch's current stream).  Returns (B, a, cost, sse)."""
+        import torch
+
+        n = X.shape[0]
+        dev = X.device
+        B = torch.empty((n, self.m), dtype=torch.uint8, device=dev) if B is None else B
+        sse = torch.zeros(2, dtype=torch.float64, device=dev) if sse is None else sse
+        s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+        rc = self.lib.stlq_b200_encode_base_device(self.handle, _t_ptr(X), _dtype_code(X), n, beam, icm_iters,
+                                                   ils_iters, perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF,
+                                                   sample_id_offset, _t_ptr(B), _t_ptr(a), _t_ptr(cost), _t_ptr(sse),
+                                                   ctypes.c_void_p(s))
+        _check(self.lib, rc, "stlq_b200_encode_base_device")
+        return B, a, cost, sse
+
+    # ---- stage-level entry points (device tensors) ---------------------------------------
+    def _stream(self, t):
+        import torch
+
+        return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+    def xc_gemm(self, X):
+        import torch
+
+        xC = torch.empty((X.shape[0], self.H), dtype=torch.float32, device=X.device)
+        _check(self.lib, self.lib.stlq_b200_xc_gemm(self.handle, _t_ptr(X), _dtype_code(X), X.shape[0], _t_ptr(xC),
+                                                    self._stream(X)), "stlq_b200_xc_gemm")
+        return xC
+
+    def xnorm2(self, X):
+        import torch
+
+        out = torch.empty(X.shape[0], dtype=torch.float32, device=X.device)
+        _check(self.lib, self.lib.stlq_b200_xnorm2(self.handle, _t_ptr(X), _dtype_code(X), X.shape[0], _t_ptr(out),
+                                                   self._stream(X)), "stlq_b200_xnorm2")
+        return out
+
+    def beam_search(self, xnorm2, xC, beam: int):
+        """BeamSearchPrefixLS (beam_search.cpp:196-422)."""
+        import torch
+
+        B = torch.empty((xC.shape[0], self.m), dtype=torch.uint8, device=xC.device)
+        _check(self.lib, self.lib.stlq_b200_beam_search(self.handle, _t_ptr(xnorm2), _t_ptr(xC), xC.shape[0], beam,
+                                                        _t_ptr(B), self._stream(xC)), "stlq_b200_beam_search")
+        return B
+
+    def solve_ls(self, xC, B):
+        """SolveLeastSquaresAll (least_squares.cpp:406-560)."""
+        import torch
+
+        a = torch.empty((xC.shape[0], self.m), dtype=torch.float32, device=xC.device)
+        _check(self.lib, self.lib.stlq_b200_solve_ls(self.handle, _t_ptr(xC), _t_ptr(B), xC.shape[0], _t_ptr(a),
+                                                     self._stream(xC)), "stlq_b200_solve_ls")
+        return a
+
+    def icm(self, xC, xnorm2, B, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,
+            seed: int = 38251450, sample_id_offset: int = 0):
+        """DynamicIcmWithIls{Abs,NoAbs}NoNormal: returns (B, a, cost); B is copied, not modified."""
+        import torch
+
+        n = xC.shape[0]
+        B = B.clone()
+        a = torch.empty((n, self.m), dtype=torch.float32, device=xC.device)
+        cost = torch.empty(n, dtype=torch.float32, device=xC.device)
+        _check(self.lib, self.lib.stlq_b200_icm(self.handle, _t_ptr(xC), _t_ptr(xnorm2), n, icm_iters, ils_iters,
+                                                perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF, sample_id_offset,
+                                                _t_ptr(B), _t_ptr(a), _t_ptr(cost), self._stream(xC)),
+               "stlq_b200_icm")
+        return B, a, cost
+
+    def sse(self, X, xC, B, a):
+        import torch
+
+        out = torch.zeros(2, dtype=torch.float64, device=X.device)
+        _check(self.lib, self.lib.stlq_b200_sse(self.handle, _t_ptr(X), _dtype_code(X), _t_ptr(xC), _t_ptr(B),
+                                                _t_ptr(a), X.shape[0], _t_ptr(out), self._stream(X)), "stlq_b200_sse")
+        return out[1]
+
+    def sync(self, stream=None):
+        import torch
+
+        s = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
+        _check(self.lib, self.lib.stlq_b200_sync(self.handle, ctypes.c_void_p(s)), "stlq_b200_sync")

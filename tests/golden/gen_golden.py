@@ -1,0 +1,111 @@
+"""Generates the golden fixtures in this directory from the REFERENCE's own code.
+
+Run where the reference sources are available (it builds oracle/_ref/libstlq_ref.so from them):
+
+    python tests/golden/gen_golden.py
+
+Each case stores its inputs (base vectors X, flattened codebooks C_all, h_vec, encode settings)
+and what the reference produced through the EncodeBase stage order (encoder_encode_base.inc):
+  - ``xC_sha``   sha256 of xC = C_all^T X from the reference's BLAS (bit-exact check);
+  - ``xC``       xC itself for cases where it is small;
+  - ``G_sha``    sha256 of the reference's Gram matrix (BuildPrecomp);
+  - ``xnorm2``   ComputeXNorm2;
+  - ``B_beam``   BeamSearchPrefixLS codes;  ``a_beam`` SolveLeastSquaresAll on them;
+  - ``B``, ``a``, ``cost``  after DynamicIcmWithIls*NoNormal;
+  - ``beam_mse``, ``final_mse``  MeanMseFromPrecomp before / after ICM.
+
+The codebooks are a seeded residual k-means stand-in for the reference's trainer (which is outside
+the encode path); the base vectors come from the seeded generators in stlq_b200/synth.py.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+import oracle  # noqa: E402
+from stlq_b200 import synth  # noqa: E402
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def make_case(name, X, books, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, store_xc=None):
+    ref = oracle.Reference(threads=os.cpu_count())
+    C = synth.flatten_books(books)
+    h = np.array([b.shape[0] for b in books], np.int32)
+    P = ref.precomp(h, C)
+    G, inv = P.G_invnorm()
+    xC = P.gemm_xc(X)
+    xn = P.xnorm2(X)
+    B_beam = P.beam_search(X, xC, beam)
+    a_beam = P.solve_ls(xC, B_beam)
+    beam_mse = P.mean_mse(X, xC, B_beam, a_beam)
+    B, a, cost = P.icm(X, xC, B_beam, icm, ils, perturb, use_abs, seed)
+    final_mse = P.mean_mse(X, xC, B, a)
+    full = P.encode_base(X, beam, icm, ils, perturb, use_abs, seed)
+    assert np.array_equal(full["B"], B), name
+    small = store_xc if store_xc is not None else xC.size <= 40_000
+    out = dict(X=X, C_all=C, h_vec=h, beam=beam, icm_iters=icm, ils_iters=ils, perturb_k=perturb,
+               use_abs=int(bool(use_abs)), seed=np.uint32(seed), xC_sha=sha(xC), G_sha=sha(G), invnorm=inv,
+               xnorm2=xn, B_beam=B_beam, a_beam=a_beam, beam_mse=beam_mse, B=B, a=a, cost=cost,
+               final_mse=final_mse, blas_core=ref.blas_core())
+    if small:
+        out["xC"] = xC
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    print(f"{name}: n={X.shape[0]} d={X.shape[1]} h={list(h)} beam={beam} icm={icm} ils={ils} "
+          f"beam_mse={beam_mse:.6g} final_mse={final_mse:.6g}")
+
+
+def main():
+    # The reference's own test setup (tests/test_streaming_encode_base.cpp:67-134): m=3, K=16,
+    # d=16, beam 2, ICM 2, ILS 3, perturb 2, seed 1234 -- at n=600.
+    X = synth.sift_like(2600, d=16, seed=11, n_centres=50)
+    make_case("ref_test_shape", X[:600], synth.train_rvq(X[600:], 3, 16, iters=6, seed=1), beam=2, icm=2, ils=3,
+              perturb=2, seed=1234)
+    # Headline shape: d=128, M=8, K=256, beam 16, 1 ICM sweep.
+    X = synth.sift_like(20300, d=128, seed=0)
+    make_case("d128_m8_k256_b16", X[:300], synth.train_rvq(X[300:], 8, 256, iters=6, seed=0), beam=16, icm=1)
+    # Config-1 style (unit-norm, d=96), beam 16 + ICM 2 + ILS 2.
+    X = synth.deep_like(12300, d=96, seed=1, n_comp=64)
+    make_case("d96_m8_k256_b16_ils", X[:300], synth.train_rvq(X[300:], 8, 256, iters=6, seed=1), beam=16, icm=2,
+              ils=2, perturb=3)
+    # m = 5 and m = 10 take the reference's fixed-size Cholesky path; no-abs ICM.
+    X = synth.sift_like(3400, d=40, seed=5, n_centres=100)
+    make_case("m5_k64_noabs", X[:400], synth.train_rvq(X[400:], 5, 64, iters=6, seed=5), beam=8, icm=3, ils=2,
+              perturb=2, use_abs=False, seed=7)
+    X = synth.sift_like(3400, d=24, seed=6, n_centres=100)
+    make_case("m10_k32", X[:400], synth.train_rvq(X[400:], 10, 32, iters=6, seed=6), beam=4, icm=3)
+    # M = 16 (config-2 depth) at small d.
+    X = synth.gist_like(6300, d=64, seed=2, n_centres=200)
+    make_case("m16_k64_b16", X[:300], synth.train_rvq(X[300:], 16, 64, iters=5, seed=2), beam=16, icm=2)
+    # Ragged codebooks: K below the beam width, K not a power of two, K = 256 next to K = 3.
+    X = synth.sift_like(4300, d=32, seed=8, n_centres=80)
+    rag = [synth.train_rvq(X[300:], 1, k, iters=5, seed=10 + i)[0] for i, k in enumerate([256, 3, 100, 17, 1, 256])]
+    make_case("ragged_h", X[:300], rag, beam=8, icm=2, ils=1, perturb=2)
+    # Edge cases: a zero vector, exact copies of codewords (a residual reaches 0: clamped errors
+    # tie at 0), a duplicated vector, and n = 1 handled by its own case.
+    X = synth.sift_like(2300, d=32, seed=9, n_centres=60)
+    books = synth.train_rvq(X[300:], 4, 32, iters=5, seed=9)
+    E = X[:64].copy()
+    E[0] = 0.0
+    E[1] = books[0][3]
+    E[2] = books[0][5] + books[1][7]
+    E[3] = E[4]
+    make_case("edge_vectors", E, books, beam=4, icm=2)
+    make_case("single_vector", X[100:101], books, beam=4, icm=1)
+    # Beam 1 and beam 32 (the sweep's extremes).
+    make_case("beam1", X[:200], books, beam=1, icm=1)
+    make_case("beam32", X[:200], books, beam=32, icm=0)
+
+
+if __name__ == "__main__":
+    oracle.build(reference=True)
+    main()

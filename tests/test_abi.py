@@ -1,0 +1,73 @@
+"""The C-ABI library loads, exports every entry point include/stlq_b200.h declares, and rejects
+bad arguments on the host before touching a GPU."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+import stlq_b200
+from stlq_b200 import encoder as enc_mod
+
+HEADER = os.path.join(ROOT, "include", "stlq_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(stlq_b200_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = stlq_b200.load_library()
+    syms = declared_symbols()
+    assert len(syms) >= 12
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_version_and_empty_error():
+    lib = stlq_b200.load_library()
+    assert b"sm_100a" in lib.stlq_b200_version()
+    assert isinstance(lib.stlq_b200_last_error(), bytes)
+
+
+@pytest.mark.parametrize("m,h,d,mode,msg", [
+    (0, [], 8, 0, b"m must be"),
+    (17, [4] * 17, 8, 0, b"m must be"),
+    (2, [4, 257], 8, 0, b"h_vec[1]"),
+    (2, [4, 0], 8, 0, b"h_vec[1]"),
+    (2, [4, 4], 0, 0, b"d must be"),
+])
+def test_create_rejects_bad_shapes(m, h, d, mode, msg):
+    lib = stlq_b200.load_library()
+    hv = np.array(h or [1], np.int32)
+    C = np.zeros((max(int(hv.sum()), 1), max(d, 1)), np.float32)
+    out = ctypes.c_void_p()
+    rc = lib.stlq_b200_create(0, d, m, ctypes.c_void_p(hv.ctypes.data), ctypes.c_void_p(C.ctypes.data), None, None,
+                              mode, ctypes.byref(out))
+    assert rc == 1
+    assert msg in lib.stlq_b200_last_error()
+    assert not out.value
+
+
+def test_null_arguments_rejected():
+    lib = stlq_b200.load_library()
+    out = ctypes.c_void_p()
+    assert lib.stlq_b200_create(0, 8, 2, None, None, None, None, 0, ctypes.byref(out)) == 1
+    assert lib.stlq_b200_create(0, 8, 2, None, None, None, None, 0, None) == 1
+    assert lib.stlq_b200_encode_base(None, None, 0, 10, 4, 0, 0, 0, 1, 0, 0, None, None, None, None) == 1
+    assert b"null" in lib.stlq_b200_last_error()
+    assert lib.stlq_b200_beam_search(None, None, None, 1, 4, None, None) == 1
+    assert lib.stlq_b200_sync(None, None) == 1
+    assert lib.stlq_b200_destroy(None) == 0
+
+
+def test_python_layer_refuses_without_library(monkeypatch, tmp_path):
+    monkeypatch.setattr(enc_mod, "_LIB", None)
+    monkeypatch.setenv("STLQ_B200_LIB", str(tmp_path / "missing.so"))
+    with pytest.raises(stlq_b200.StlqB200Error, match="no CPU fallback"):
+        stlq_b200.load_library()
