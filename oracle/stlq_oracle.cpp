@@ -308,38 +308,131 @@ bool CholFixed(float* A, int m) {
     return true;
 }
 
-// LAPACK spotrf('U') + spotrs for the other m (least_squares.cpp:278-316).  Restated as the
-// unblocked column Cholesky of LAPACK's xPOTF2 (pivot <= 0 fails; the row is scaled by the
-// reciprocal of the pivot, as xPOTF2 does with xSCAL) and two triangular solves.  The BLAS
-// kernels' inner summation order is not pinned here: coefficients agree to a few ulps.
-bool CholLapack(float* A, int m) {  // column-major A[r + c*m]
+// LAPACK spotrf('U') + spotrs for the other m (least_squares.cpp:278-316), in the arithmetic of
+// the BLAS/LAPACK the reference links in this image (OpenBLAS 0.3.15, SkylakeX kernels), measured
+// element by element against that library (oracle/Makefile links it into oracle/_ref):
+//  * spotrf = xPOTF2 for m <= 32: pivot a_jj - dot(U[0:j,j], U[0:j,j]) with float products summed
+//    in double; the row update is y - U[0:j,c].U[0:j,j] through the SGEMV-T kernel (rows in
+//    blocks of 4: 4-column groups use 4 FMA lanes [+ 8-lane steps] reduced (l0+l1)+(l2+l3), the
+//    remaining columns 4 mul/add lanes; the last j%4 rows added by contracted FMAs); then the row
+//    is scaled by the float reciprocal of the pivot.  A pivot <= 0 fails (NaN does not).
+//  * spotrs = two STRSM calls: triangular blocks of 16/8/4/2/1 rows, each solved by multiplying
+//    with the reciprocal diagonal and FMA updates, blocks joined by FMA-chain GEMM updates.
+float PotfBlockAvx(const float* a, const float* x, int nb) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int r = 0;
+    if (nb & 4) {
+        for (int l = 0; l < 4; ++l) lane[l] = std::fma(a[l], x[l], lane[l]);
+        r = 4;
+    }
+    for (; r < nb; r += 8)
+        for (int l = 0; l < 8; ++l) lane[l] = std::fma(a[r + l], x[r + l], lane[l]);
+    float q[4];
+    for (int l = 0; l < 4; ++l) q[l] = lane[l] + lane[l + 4];
+    return (q[0] + q[1]) + (q[2] + q[3]);
+}
+
+float PotfBlockSse(const float* a, const float* x, int nb) {
+    float lane[4] = {0, 0, 0, 0};
+    for (int r = 0; r < nb; r += 4)
+        for (int l = 0; l < 4; ++l) {
+            const float p = a[r + l] * x[r + l];
+            lane[l] = lane[l] + p;
+        }
+    return (lane[0] + lane[1]) + (lane[2] + lane[3]);
+}
+
+float PotfLeftover(float y, const float* a, const float* x, int m1, int m3) {
+    if (m3 == 0) return y;
+    const float xt0 = -x[m1];
+    if (m3 == 1) return std::fma(a[m1], xt0, y);
+    const float xt1 = -x[m1 + 1];
+    const float p1 = a[m1 + 1] * xt1;
+    float e = std::fma(a[m1], xt0, p1);
+    if (m3 == 3) e = std::fma(a[m1 + 2], -x[m1 + 2], e);
+    return y + e;
+}
+
+bool CholLapack(float* A, int m) {  // column-major A[r + c*m], upper triangle
     for (int j = 0; j < m; ++j) {
-        float dot = 0.0f;
-        for (int k = 0; k < j; ++k) dot = std::fma(A[k + j * m], A[k + j * m], dot);
-        float ajj = A[j + j * m] - dot;
-        if (!(ajj > 0.0f)) return false;
+        const float* xj = A + static_cast<size_t>(j) * m;
+        double acc = 0.0;
+        for (int k = 0; k < j; ++k) {
+            const float p = xj[k] * xj[k];
+            acc += static_cast<double>(p);
+        }
+        float ajj = A[j + j * m] - static_cast<float>(acc);
+        if (ajj <= 0.0f) return false;
         ajj = std::sqrt(ajj);
         A[j + j * m] = ajj;
         const float r = 1.0f / ajj;
-        for (int i = j + 1; i < m; ++i) {
-            float s = 0.0f;
-            for (int k = 0; k < j; ++k) s = std::fma(A[k + j * m], A[k + i * m], s);
-            A[j + i * m] = (A[j + i * m] - s) * r;
+        const int ncol = m - j - 1, m3 = j & 3, m1 = j - m3, n1 = (ncol >> 2) * 4;
+        for (int ci = 0; ci < ncol; ++ci) {
+            const int c = j + 1 + ci;
+            const float* ac = A + static_cast<size_t>(c) * m;
+            float y = A[j + c * m];
+            if (m1 > 0) {
+                const float K = ci < n1 ? PotfBlockAvx(ac, xj, m1) : PotfBlockSse(ac, xj, m1);
+                y = std::fma(K, -1.0f, y);
+            }
+            y = PotfLeftover(y, ac, xj, m1, m3);
+            A[j + c * m] = y * r;
         }
     }
     return true;
 }
 
-void SolveLapack(const float* A, int m, float* b) {  // U^T y = b, U x = y, in place
-    for (int i = 0; i < m; ++i) {
-        float s = 0.0f;
-        for (int k = 0; k < i; ++k) s = std::fma(A[k + i * m], b[k], s);
-        b[i] = (b[i] - s) / A[i + i * m];
+void TrsmRowsUpdate(const float* A, int m, float* c, int r0, int nr, int t0, int t1, bool upper_t) {
+    // c[r] -= sum_{t in [t0,t1)} U(t,r) c[t] (forward, upper_t) or U(r,t) c[t] (backward), as an
+    // FMA chain from zero, subtracted once.
+    for (int r = r0; r < r0 + nr; ++r) {
+        float acc = 0.0f;
+        for (int t = t0; t < t1; ++t) acc = std::fma(upper_t ? A[t + r * m] : A[r + t * m], c[t], acc);
+        c[r] = std::fma(acc, -1.0f, c[r]);
     }
-    for (int i = m - 1; i >= 0; --i) {
-        float s = 0.0f;
-        for (int k = i + 1; k < m; ++k) s = std::fma(A[i + k * m], b[k], s);
-        b[i] = (b[i] - s) / A[i + i * m];
+}
+
+void SolveLapack(const float* A, int m, float* c) {  // U^T y = b, then U x = y, in place
+    const int UM = 16;
+    int kk = 0;
+    auto fwd = [&](int r0, int bs) {
+        for (int i = r0; i < r0 + bs; ++i) {
+            const float bb = c[i] * (1.0f / A[i + i * m]);
+            c[i] = bb;
+            for (int k = i + 1; k < r0 + bs; ++k) c[k] = std::fma(-bb, A[i + k * m], c[k]);
+        }
+    };
+    auto bwd = [&](int r0, int bs) {
+        for (int i = r0 + bs - 1; i >= r0; --i) {
+            const float bb = c[i] * (1.0f / A[i + i * m]);
+            c[i] = bb;
+            for (int k = r0; k < i; ++k) c[k] = std::fma(-bb, A[k + i * m], c[k]);
+        }
+    };
+    for (int b = 0; b < m / UM; ++b) {
+        if (kk > 0) TrsmRowsUpdate(A, m, c, kk, UM, 0, kk, true);
+        fwd(kk, UM);
+        kk += UM;
+    }
+    for (int i = UM / 2; i > 0; i >>= 1) {
+        if (!(m & i)) continue;
+        if (kk > 0) TrsmRowsUpdate(A, m, c, kk, i, 0, kk, true);
+        fwd(kk, i);
+        kk += i;
+    }
+    kk = m;
+    for (int i = 1; i < UM; i *= 2) {
+        if (!(m & i)) continue;
+        const int st = (m & ~(i - 1)) - i;
+        if (m - kk > 0) TrsmRowsUpdate(A, m, c, st, i, kk, m, false);
+        bwd(st, i);
+        kk -= i;
+    }
+    for (int b = m / UM - 1; b >= 0; --b) {
+        const int st = b * UM;
+        if (m - kk > 0) TrsmRowsUpdate(A, m, c, st, UM, kk, m, false);
+        bwd(st, UM);
+        kk -= UM;
     }
 }
 

@@ -63,24 +63,126 @@ __device__ bool CholFixed(float* A, int m) {
     return true;
 }
 
-// Upper Cholesky for the other m (LAPACK spotrf 'U' at least_squares.cpp:289): unblocked column
-// algorithm of xPOTF2, dot products as FMA chains, row scaled by the reciprocal pivot.
-__device__ bool CholLapack(float* A, int m) {  // column-major A[r + c*m]
+// LAPACK spotrf('U') / spotrs for the other m (least_squares.cpp:278-316), in the arithmetic of
+// the BLAS/LAPACK build the reference links (OpenBLAS 0.3.15 SkylakeX kernels, pinned element
+// by element against that library):
+//  * pivot: a_jj - sum of float products accumulated in double; sqrt; fails when <= 0;
+//  * row update through SGEMV-T: rows in blocks of 4 reduced per 4-column group on 4 (+8) FMA
+//    lanes as (l0+l1)+(l2+l3), leftover columns on 4 mul/add lanes, the last j%4 rows by
+//    contracted FMAs; the row is then scaled by the float reciprocal of the pivot;
+//  * spotrs: triangular blocks of 16/8/4/2/1 rows solved with the reciprocal diagonal and FMA
+//    updates, blocks joined by FMA-chain updates.
+__device__ float PotfBlockAvx(const float* a, const float* x, int nb) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int r = 0;
+    if (nb & 4) {
+        for (int l = 0; l < 4; ++l) lane[l] = __fmaf_rn(a[l], x[l], lane[l]);
+        r = 4;
+    }
+    for (; r < nb; r += 8)
+        for (int l = 0; l < 8; ++l) lane[l] = __fmaf_rn(a[r + l], x[r + l], lane[l]);
+    float q[4];
+    for (int l = 0; l < 4; ++l) q[l] = add_rn(lane[l], lane[l + 4]);
+    return add_rn(add_rn(q[0], q[1]), add_rn(q[2], q[3]));
+}
+
+__device__ float PotfBlockSse(const float* a, const float* x, int nb) {
+    float lane[4] = {0, 0, 0, 0};
+    for (int r = 0; r < nb; r += 4)
+        for (int l = 0; l < 4; ++l) lane[l] = add_rn(lane[l], mul_rn(a[r + l], x[r + l]));
+    return add_rn(add_rn(lane[0], lane[1]), add_rn(lane[2], lane[3]));
+}
+
+__device__ float PotfLeftover(float y, const float* a, const float* x, int m1, int m3) {
+    if (m3 == 0) return y;
+    const float xt0 = -x[m1];
+    if (m3 == 1) return __fmaf_rn(a[m1], xt0, y);
+    const float p1 = mul_rn(a[m1 + 1], -x[m1 + 1]);
+    float e = __fmaf_rn(a[m1], xt0, p1);
+    if (m3 == 3) e = __fmaf_rn(a[m1 + 2], -x[m1 + 2], e);
+    return add_rn(y, e);
+}
+
+__device__ bool CholLapack(float* A, int m) {  // column-major A[r + c*m], upper triangle
     for (int j = 0; j < m; ++j) {
-        float dot = 0.0f;
-        for (int k = 0; k < j; ++k) dot = __fmaf_rn(A[k + j * m], A[k + j * m], dot);
-        float ajj = sub_rn(A[j + j * m], dot);
-        if (!(ajj > 0.0f)) return false;
+        const float* xj = A + j * m;
+        double acc = 0.0;
+        for (int k = 0; k < j; ++k) acc = __dadd_rn(acc, static_cast<double>(mul_rn(xj[k], xj[k])));
+        float ajj = sub_rn(A[j + j * m], static_cast<float>(acc));
+        if (ajj <= 0.0f) return false;
         ajj = __fsqrt_rn(ajj);
         A[j + j * m] = ajj;
         const float r = div_rn(1.0f, ajj);
-        for (int i = j + 1; i < m; ++i) {
-            float s = 0.0f;
-            for (int k = 0; k < j; ++k) s = __fmaf_rn(A[k + j * m], A[k + i * m], s);
-            A[j + i * m] = mul_rn(sub_rn(A[j + i * m], s), r);
+        const int ncol = m - j - 1, m3 = j & 3, m1 = j - m3, n1 = (ncol >> 2) * 4;
+        for (int ci = 0; ci < ncol; ++ci) {
+            const int c = j + 1 + ci;
+            const float* ac = A + c * m;
+            float y = A[j + c * m];
+            if (m1 > 0) {
+                const float K = ci < n1 ? PotfBlockAvx(ac, xj, m1) : PotfBlockSse(ac, xj, m1);
+                y = __fmaf_rn(K, -1.0f, y);
+            }
+            y = PotfLeftover(y, ac, xj, m1, m3);
+            A[j + c * m] = mul_rn(y, r);
         }
     }
     return true;
+}
+
+// c[r] -= sum_t U(t,r) c[t] (forward) or U(r,t) c[t] (backward) over t in [t0, t1), as one FMA
+// chain from zero subtracted once (the GEMM update between STRSM blocks).
+__device__ void TrsmUpdate(const float* A, int m, float* c, int r0, int nr, int t0, int t1, bool fwd) {
+    for (int r = r0; r < r0 + nr; ++r) {
+        float acc = 0.0f;
+        for (int t = t0; t < t1; ++t) acc = __fmaf_rn(fwd ? A[t + r * m] : A[r + t * m], c[t], acc);
+        c[r] = __fmaf_rn(acc, -1.0f, c[r]);
+    }
+}
+
+__device__ void TrsmFwdBlock(const float* A, int m, float* c, int r0, int bs) {
+    for (int i = r0; i < r0 + bs; ++i) {
+        const float bb = mul_rn(c[i], div_rn(1.0f, A[i + i * m]));
+        c[i] = bb;
+        for (int k = i + 1; k < r0 + bs; ++k) c[k] = __fmaf_rn(-bb, A[i + k * m], c[k]);
+    }
+}
+
+__device__ void TrsmBwdBlock(const float* A, int m, float* c, int r0, int bs) {
+    for (int i = r0 + bs - 1; i >= r0; --i) {
+        const float bb = mul_rn(c[i], div_rn(1.0f, A[i + i * m]));
+        c[i] = bb;
+        for (int k = r0; k < i; ++k) c[k] = __fmaf_rn(-bb, A[k + i * m], c[k]);
+    }
+}
+
+__device__ void SolveLapack(const float* A, int m, float* c) {  // U^T y = b, U x = y, in place
+    constexpr int UM = 16;
+    int kk = 0;
+    for (int b = 0; b < m / UM; ++b) {
+        if (kk > 0) TrsmUpdate(A, m, c, kk, UM, 0, kk, true);
+        TrsmFwdBlock(A, m, c, kk, UM);
+        kk += UM;
+    }
+    for (int i = UM / 2; i > 0; i >>= 1) {
+        if (!(m & i)) continue;
+        if (kk > 0) TrsmUpdate(A, m, c, kk, i, 0, kk, true);
+        TrsmFwdBlock(A, m, c, kk, i);
+        kk += i;
+    }
+    kk = m;
+    for (int i = 1; i < UM; i *= 2) {
+        if (!(m & i)) continue;
+        const int st = (m & ~(i - 1)) - i;
+        if (m - kk > 0) TrsmUpdate(A, m, c, st, i, kk, m, false);
+        TrsmBwdBlock(A, m, c, st, i);
+        kk -= i;
+    }
+    for (int b = m / UM - 1; b >= 0; --b) {
+        const int st = b * UM;
+        if (m - kk > 0) TrsmUpdate(A, m, c, st, UM, kk, m, false);
+        TrsmBwdBlock(A, m, c, st, UM);
+        kk -= UM;
+    }
 }
 
 // One vector's LS solve with the reference's retry policy (3 diagonal bumps 1e-6 x10^i).
@@ -118,16 +220,7 @@ __device__ bool SolveLs(const Dims& dims, const float* Gcol, const float* xc, co
                 }
                 for (int i = 0; i < m; ++i) a_out[i] = ws.x[i];
             } else {
-                for (int i = 0; i < m; ++i) {
-                    float s = 0.0f;
-                    for (int k = 0; k < i; ++k) s = __fmaf_rn(ws.A[k + i * m], ws.b[k], s);
-                    ws.b[i] = div_rn(sub_rn(ws.b[i], s), ws.A[i + i * m]);
-                }
-                for (int i = m - 1; i >= 0; --i) {
-                    float s = 0.0f;
-                    for (int k = i + 1; k < m; ++k) s = __fmaf_rn(ws.A[i + k * m], ws.b[k], s);
-                    ws.b[i] = div_rn(sub_rn(ws.b[i], s), ws.A[i + i * m]);
-                }
+                SolveLapack(ws.A, m, ws.b);
                 for (int i = 0; i < m; ++i) a_out[i] = ws.b[i];
             }
             return true;

@@ -97,9 +97,11 @@ __global__ void __launch_bounds__(kGemmThreads) XcGemmExactKernel(const float* _
                 for (int kk = 0; kk < kn; ++kk) {
                     const int k = k0 + kk;
                     const float x = Xs[kk][nj];
-                    dsum += static_cast<double>(x) * static_cast<double>(x);
                     const bool mine = (k < body) ? ((k & 3) == lane) : (lane == 0);
-                    if (mine) lane_sum = __fadd_rn(lane_sum, __fmul_rn(x, x));
+                    if (mine) {
+                        lane_sum = __fadd_rn(lane_sum, __fmul_rn(x, x));
+                        dsum = __dadd_rn(dsum, __dmul_rn(static_cast<double>(x), static_cast<double>(x)));
+                    }
                 }
             }
             __syncthreads();

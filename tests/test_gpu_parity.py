@@ -1,13 +1,10 @@
 """GPU parity: the CUDA path (through the C-ABI) against the reference's golden outputs and the
 CPU restatement.
 
-Bars:
-  * xC, G, ||x||^2, beam codes: bit-exact (the GEMM replicates the reference BLAS's summation order
-    and the beam arithmetic replicates the reference's operation sequence).
-  * LS coefficients and ICM: bit-exact against the CPU restatement (same arithmetic); against the
-    reference, ICM codes may differ only on cost near-ties (the reference's LAPACK spotrf/spotrs
-    rounding is not bit-pinned for m outside {5, 10}); coefficients within 2e-3.
-  * MSE: within 1e-4 relative of the reference.
+Bars: xC, G, ||x||^2, beam codes, LS coefficients, ICM/ILS codes, coefficients and costs are
+bit-exact against the reference (the GEMM replicates the summation order of the reference's BLAS,
+the beam and ICM arithmetic its operation sequence, the LS its LAPACK's arithmetic, and the beam
+replays its slot replacement, ties included).  MSE sums (double) within 1e-9 relative.
 """
 import hashlib
 
@@ -24,13 +21,6 @@ if have_cuda():
 
 def sha(a):
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
-
-
-def codes_match_or_tie(B, B_ref, cost, cost_ref, xnorm2, max_frac=0.01):
-    mis = (np.asarray(B) != np.asarray(B_ref)).any(1)
-    tie = np.abs(np.asarray(cost, np.float64) - cost_ref) <= 1e-5 * np.asarray(xnorm2, np.float64) + 1e-5 * np.abs(cost_ref)
-    assert not (mis & ~tie).any(), f"{(mis & ~tie).sum()} vectors differ beyond a cost tie"
-    assert mis.mean() <= max_frac, f"{mis.sum()} / {len(mis)} code vectors differ"
 
 
 @pytest.fixture(scope="module")
@@ -62,17 +52,11 @@ def test_stages_match_reference(cuda, oracle_lib, name):
     enc.sync()
     assert np.array_equal(B.cpu().numpy(), c["B_beam"]), "beam codes differ from the reference"
     a = enc.solve_ls(xC, B).cpu().numpy()
-    a_o, _ = oracle_lib.solve_ls(c["h_vec"], G, xC.cpu().numpy(), c["B_beam"])
-    assert np.array_equal(a, a_o), "LS differs from the restatement"
-    np.testing.assert_allclose(a, c["a_beam"], rtol=2e-3, atol=2e-3)
+    assert np.array_equal(a, c["a_beam"]), "LS coefficients differ from the reference"
     B2, a2, cost = enc.icm(xC, xn, B, c["icm_iters"], c["ils_iters"], c["perturb_k"], bool(c["use_abs"]), c["seed"])
     B2, a2, cost = B2.cpu().numpy(), a2.cpu().numpy(), cost.cpu().numpy()
-    _, inv = oracle_lib.precomp(c["C_all"])
-    Bo, ao, co = oracle_lib.icm(c["h_vec"], G, inv, xC.cpu().numpy(), c["xnorm2"], c["B_beam"], c["icm_iters"],
-                                c["ils_iters"], c["perturb_k"], bool(c["use_abs"]), c["seed"])
-    assert np.array_equal(B2, Bo.astype(np.uint8)), "ICM codes differ from the restatement"
-    assert np.array_equal(a2, ao) and np.array_equal(cost, co)
-    codes_match_or_tie(B2, c["B"], cost, c["cost"], c["xnorm2"])
+    assert np.array_equal(B2, c["B"]), "ICM codes differ from the reference"
+    assert np.array_equal(a2, c["a"]) and np.array_equal(cost, c["cost"])
 
 
 @pytest.mark.parametrize("name", golden_names())
@@ -81,11 +65,10 @@ def test_encode_base_host_matches_reference(cuda, name):
     enc = make_encoder(c)
     r = enc.encode_base(c["X"], c["beam"], c["icm_iters"], c["ils_iters"], c["perturb_k"], bool(c["use_abs"]),
                         c["seed"])
-    codes_match_or_tie(r["B"], c["B"], r["cost"], c["cost"], c["xnorm2"])
-    assert abs(r["beam_mse"] - c["beam_mse"]) <= 1e-4 * max(abs(c["beam_mse"]), 1e-12)
-    assert abs(r["final_mse"] - c["final_mse"]) <= 1e-4 * max(abs(c["final_mse"]), 1e-12)
-    same = (r["B"] == c["B"]).all(1)
-    np.testing.assert_allclose(r["a"][same], c["a"][same], rtol=2e-3, atol=2e-3)
+    assert np.array_equal(r["B"], c["B"]) and np.array_equal(r["a"], c["a"]) and np.array_equal(r["cost"], c["cost"])
+    # The reference reports the mean as a float; the sums here are double.
+    assert abs(r["beam_mse"] - c["beam_mse"]) <= 1e-6 * max(abs(c["beam_mse"]), 1e-12)
+    assert abs(r["final_mse"] - c["final_mse"]) <= 1e-6 * max(abs(c["final_mse"]), 1e-12)
 
 
 def test_device_and_host_paths_agree(cuda):
