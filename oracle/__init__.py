@@ -38,6 +38,8 @@ def build(reference: bool = True) -> None:
     targets = ["oracle"]
     if reference and os.path.isdir(os.environ.get("STLQ_REF_DIR", "/root/reference")):
         targets.append("ref")
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "stlq_b200", "libstlq_b200.so")):
+            targets.append("adapter")
     env = dict(os.environ)
     if "STLQ_REF_DIR" in env:
         env["REF"] = env["STLQ_REF_DIR"]
@@ -267,3 +269,64 @@ class RefPrecomp:
         if rc != 0:
             raise RuntimeError(f"ref_encode_base failed: {rc}")
         return dict(B=B, a=a, cost=cost, beam_mse=bm.value, final_mse=fm.value, t_stages=t)
+
+
+ADAPTER_SO = os.path.join(HERE, "_ref", "libstlq_adapter_test.so")
+
+
+class AdapterHarness:
+    """The drop-in C++ adapter (stlq_b200/adapter) driven with the reference's own types: the
+    library holds the reference objects too, so a Precomp built here feeds both sides."""
+
+    def __init__(self, path: str = ADAPTER_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: build it with `make -C oracle adapter`")
+        self.lib = ctypes.CDLL(path)
+        L = self.lib
+        L.ref_precomp_create.restype = ctypes.c_void_p
+        L.ref_precomp_destroy.argtypes = [ctypes.c_void_p]
+        L.ref_set_threads(os.cpu_count() or 1)
+
+    def precomp(self, h_vec, C_all):
+        h = np.asarray(h_vec, np.int32)
+        C = _f32(C_all)
+        H, d = C.shape
+        return ctypes.c_void_p(self.lib.ref_precomp_create(d, len(h), _p(h, _i32p), _p(C, _f32p))), len(h), H
+
+    def gemm_xc(self, pre, H, X):
+        X = _f32(X)
+        out = np.empty((X.shape[0], H), np.float32)
+        self.lib.ref_gemm_xc(pre, _p(X, _f32p), X.shape[0], _p(out, _f32p))
+        return out
+
+    def encode_base(self, pre, m, X, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, device=0):
+        X = _f32(X)
+        n = X.shape[0]
+        B = np.empty((n, m), np.uint8)
+        a = np.empty((n, m), np.float32)
+        mse = np.zeros(2, np.float32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.adapter_encode_base(pre, _p(X, _f32p), n, beam, icm, ils, perturb, int(bool(use_abs)), seed,
+                                          device, _p(B, _u8p), _p(a, _f32p), _p(mse, _f32p), err, 512)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return B, a, mse
+
+    def stages(self, pre, m, H, X, xC, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, device=0):
+        X = _f32(X)
+        n = X.shape[0]
+        Bb = np.empty((n, m), np.uint8)
+        ab = np.empty((n, m), np.float32)
+        Bi = np.empty((n, m), np.uint8)
+        ai = np.empty((n, m), np.float32)
+        cost = np.empty(n, np.float32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.adapter_stages(pre, _p(X, _f32p), n, _p(_f32(xC), _f32p), beam, icm, ils, perturb,
+                                     int(bool(use_abs)), ctypes.c_uint(seed), device, _p(Bb, _u8p), _p(ab, _f32p),
+                                     _p(Bi, _u8p), _p(ai, _f32p), _p(cost, _f32p), err, 512)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return Bb, ab, Bi, ai, cost
+
+    def release(self):
+        self.lib.adapter_release()

@@ -1,0 +1,58 @@
+// Drop-in C++ adapter: the reference's encode-stage signatures on top of the stlq_b200 C-ABI.
+//
+// Compiled inside the reference tree (it includes the reference's headers), it gives a maintainer
+// B200 replacements with the exact signatures EncodeBase calls:
+//   stlq::b200::EncodeBase                     <- stlq::EncodeBase            (include/stlq/quantizer/encoder.h:66-74)
+//   stlq::b200::BeamSearchPrefixLS             <- stlq::BeamSearchPrefixLS    (include/stlq/quantizer/beam_search.h:18-22)
+//   stlq::b200::SolveLeastSquaresAll           <- stlq::SolveLeastSquaresAll  (include/stlq/quantizer/least_squares.h)
+//   stlq::b200::DynamicIcmWithIls{Abs,NoAbs}NoNormalCuda
+//                                              <- stlq::DynamicIcmWithIls*NoNormalCuda (include/stlq/quantizer/icm_cuda.h:31-68)
+// Semantics: the same inputs, outputs and ownership as the reference (callers own the matrices;
+// outputs are resized here).  Errors: EncodeBase returns false and fills *error; the others throw
+// std::runtime_error, like the reference's CUDA helpers (icm_cuda_kernels.inc:10-15).
+//
+// One encoder handle per (host thread, device, Precomp::build_tag) is cached thread-locally, the
+// way the reference caches its CUDA sessions by build_tag (icm_cuda_kernels.inc:2110-2118).
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "stlq/common/config.h"
+#include "stlq/common/types.h"
+
+namespace stlq {
+
+class KernelProvider;
+
+namespace b200 {
+
+bool EncodeBase(const Config& config, const Dataset& dataset, const CodebookPack& codebooks, const Precomp& precomp,
+                KernelProvider* kernels, BaseEncoding* base, float* out_beam_mse, float* out_final_mse,
+                std::string* error);
+
+void BeamSearchPrefixLS(const ColMajorMatrix<float>& X, const Precomp& precomp, const ColMajorMatrix<float>& xC,
+                        int H_beam, ColMajorMatrix<FullCode>* B, int device = 0);
+
+void SolveLeastSquaresAll(const Precomp& precomp, const ColMajorMatrix<float>& xC, const ColMajorMatrix<FullCode>& B,
+                          ColMajorMatrix<float>* a, int device = 0);
+
+void DynamicIcmWithIlsAbsNoNormalCuda(const ColMajorMatrix<float>& X, const Precomp& precomp,
+                                      const ColMajorMatrix<float>& xC, int icm_iters, int ils_iters, int perturb_k,
+                                      std::uint32_t seed, ColMajorMatrix<FullCode>* B, ColMajorMatrix<float>* a,
+                                      std::vector<float>* X_norm2, std::vector<float>* cost,
+                                      bool print_progress = true, std::uint64_t sample_id_offset = 0, int device = 0);
+
+void DynamicIcmWithIlsNoAbsNoNormalCuda(const ColMajorMatrix<float>& X, const Precomp& precomp,
+                                        const ColMajorMatrix<float>& xC, int icm_iters, int ils_iters, int perturb_k,
+                                        std::uint32_t seed, ColMajorMatrix<FullCode>* B, ColMajorMatrix<float>* a,
+                                        std::vector<float>* X_norm2, std::vector<float>* cost,
+                                        bool print_progress = true, std::uint64_t sample_id_offset = 0,
+                                        int device = 0);
+
+// Drops this thread's cached encoder handles (e.g. before the device is reset).
+void ReleaseThreadEncoders();
+
+}  // namespace b200
+}  // namespace stlq

@@ -2,6 +2,7 @@
 // the encode stage, and the pinned double-buffered host path.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <random>
@@ -121,6 +122,9 @@ struct stlq_b200_encoder {
     int device = 0;
     int num_sms = 148;
     int gemm_mode = STLQ_B200_GEMM_EXACT;
+    // Self-check of the beam pre-filter (environment STLQ_B200_CHECK_FILTER=1 at create time):
+    // every candidate is also evaluated exactly and a wrongly dropped one raises EDEVICE.
+    int check_filter = 0;
     Dims dims{};
     DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
     // Per-call scratch, grown on demand and kept for the handle's lifetime.
@@ -216,7 +220,7 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), dims.H, dims.d, Xs, x_dtype, ns, enc->xC.as<float>(),
                                              dims.H, enc->xn.as<float>(), enc->xnd.as<double>(), stream));
         STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
-                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m,
+                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
         stlq_b200::RefineArgs ra{};
         ra.dims = dims;
@@ -285,6 +289,7 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     enc->device = device;
     enc->dims = dims;
     enc->gemm_mode = gemm_mode;
+    if (const char* cf = std::getenv("STLQ_B200_CHECK_FILTER")) enc->check_filter = std::atoi(cf) != 0;
     auto fail = [&](int rc) {
         stlq_b200_destroy(enc);
         return rc;
@@ -526,7 +531,7 @@ int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const
     if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
     STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), xnorm2_dev, xC_dev, n,
-                                        beam, B_dev, enc->err_flag.as<unsigned int>(), enc->num_sms,
+                                        beam, B_dev, enc->check_filter, enc->err_flag.as<unsigned int>(), enc->num_sms,
                                         static_cast<cudaStream_t>(stream)));
     return 0;
 }

@@ -16,6 +16,7 @@ enum DeviceError : unsigned int {
     kErrNone = 0,
     kErrSurvivorOverflow = 1u << 0,
     kErrBadShape = 1u << 1,
+    kErrFilterMiss = 1u << 2,  // self-check: a candidate the beam pre-filter dropped would have entered
 };
 
 // Encoder constants shared by every kernel, passed by value.
