@@ -167,7 +167,7 @@ def cpu_reference_sample(C, h_vec, X, args, seconds, gpu_codes=None):
     if gpu_codes is not None:
         same = (gpu_codes[:ns] == r["B"]).all(1)
         match = {"frac": float(same.mean()), "vectors": ns, "mismatched": int((~same).sum()),
-                 "reference_final_mse": float(r["final_mse"])}
+                 "reference_final_mse": float(r["final_mse"]), "reference_blas_core": ref.blas_core()}
     return ns / dt, ref.threads, ns, match, r
 
 
@@ -354,7 +354,8 @@ def run_ours(args):
                                                                gpu_codes=B.cpu().numpy())
             cpu = {"value": v, "unit": "vectors/s", "cores": cores, "kind": "reference",
                    "sample": f"first {ns} vectors of rank 0's shard, same codebooks and settings, "
-                             f"reference CPU encoder (oracle/_ref) with {cores} threads"}
+                             f"reference CPU encoder (oracle/_ref) with {cores} threads, "
+                             f"OpenBLAS core {(code_match or {}).get('reference_blas_core')}"}
         except Exception as exc:  # the reference library did not travel or does not load
             cpu = {"value": None, "unit": "vectors/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {exc}"}

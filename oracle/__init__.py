@@ -26,6 +26,24 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libstlq_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libstlq_ref.so")
 
+def _pin_blas_kernels() -> None:
+    """The golden fixtures and the bit-exact pins were made with OpenBLAS's SkylakeX kernels (the
+    ones it selects on this container's CPU).  OpenBLAS picks its kernels per CPU at load time, so
+    on another host the reference's BLAS/LAPACK arithmetic could differ; select the same kernels
+    there too when the CPU can run them (AVX-512F) and the caller has not chosen one."""
+    if "OPENBLAS_CORETYPE" in os.environ:
+        return
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = f.read()
+    except OSError:
+        return
+    if " avx512f" in flags:
+        os.environ["OPENBLAS_CORETYPE"] = "SKYLAKEX"
+
+
+_pin_blas_kernels()
+
 _f32p = ctypes.POINTER(ctypes.c_float)
 _f64p = ctypes.POINTER(ctypes.c_double)
 _i32p = ctypes.POINTER(ctypes.c_int)

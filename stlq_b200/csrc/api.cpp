@@ -128,7 +128,7 @@ struct stlq_b200_encoder {
     Dims dims{};
     DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
     // Per-call scratch, grown on demand and kept for the handle's lifetime.
-    DevBuf xC, xn, xnd, partials, orders;
+    DevBuf xC, xn, xnd, partials, orders, redo;
     std::vector<int> orders_host;
     int64_t orders_key[4] = {-1, -1, -1, -1};
     // Host path.
@@ -201,6 +201,7 @@ int EnsureScratch(stlq_b200_encoder* enc, int64_t slice) {
     STLQ_TRY(enc->xn.Ensure(static_cast<size_t>(slice) * sizeof(float)));
     STLQ_TRY(enc->xnd.Ensure(static_cast<size_t>(slice) * sizeof(double)));
     STLQ_TRY(enc->partials.Ensure(static_cast<size_t>(RefineGrid(enc, slice)) * 2 * sizeof(double)));
+    STLQ_TRY(enc->redo.Ensure(static_cast<size_t>(slice + 1) * sizeof(int)));
     return 0;
 }
 
@@ -220,7 +221,8 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), dims.H, dims.d, Xs, x_dtype, ns, enc->xC.as<float>(),
                                              dims.H, enc->xn.as<float>(), enc->xnd.as<double>(), stream));
         STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
-                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->check_filter,
+                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->redo.as<int>(),
+                                            enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
         stlq_b200::RefineArgs ra{};
         ra.dims = dims;
@@ -348,7 +350,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
     for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
-                      &enc->xnd, &enc->partials, &enc->orders, &enc->sse_d})
+                      &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
         enc->xin[i].Release();
@@ -530,8 +532,9 @@ int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const
     STLQ_TRY(CheckEncodeArgs(enc, STLQ_B200_F32, n, beam, 0, 0, 0));
     if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
+    STLQ_TRY(enc->redo.Ensure(static_cast<size_t>(n + 1) * sizeof(int)));
     STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), xnorm2_dev, xC_dev, n,
-                                        beam, B_dev, enc->check_filter, enc->err_flag.as<unsigned int>(), enc->num_sms,
+                                        beam, B_dev, enc->redo.as<int>(), enc->check_filter, enc->err_flag.as<unsigned int>(), enc->num_sms,
                                         static_cast<cudaStream_t>(stream)));
     return 0;
 }

@@ -1,185 +1,154 @@
 // Beam search with prefix least squares (BeamSearchPrefixLS, reference
-// src/quantizer/beam_search.cpp:196-422) for sm_100a.
+// src/quantizer/beam_search.cpp:196-422) for sm_100a: two kernels with identical results.
 //
-// One CTA of 128 threads encodes one vector at a time (persistent grid-stride loop).  Thread t
-// owns codewords k = t, t+128 of the layer being expanded, for every live beam slot, so the
-// per-code values (alpha = G(k,k), gamma = xC(k)) stay in registers and the per-slot values (the
-// Cholesky factor R, coefficients, error) are warp-uniform shared-memory broadcasts.
+// Both: one CTA of 128 threads encodes one vector at a time.  Thread t owns codewords t, t+128 of
+// the layer being expanded, for every live beam slot; per-code values (alpha = G(k,k),
+// gamma = xC(k)) stay in registers, per-slot values (Cholesky factor R, coefficients, error) are
+// warp-uniform shared-memory broadcasts.  Every error that decides anything is computed in the
+// reference's float operation sequence (beam::EvalExact), so it is bit-identical to the
+// reference's given the same xC, G and ||x||^2.
 //
-// Exactness.  Every candidate error that can influence the result is computed with the
-// reference's float operation sequence (forward and back substitution of SolveCholUpperRawFixed,
-// delta = A.v, eta = A.a_old, IEEE division and square root, no fused multiply-add), so it is
-// bit-identical to the reference's given the same xC, G and ||x||^2.
+// The reference's beam keeps B slots; a candidate (scanned slot-major, code-minor) enters when its
+// error is strictly below the current worst slot error and replaces the first slot holding it
+// (beam_search.cpp:101-113, 252-260, 320-333); the final pick is the first slot with the
+// smallest error (:409-416).  What ends in the slots is the B smallest errors; the slot ORDER (its
+// replacement history, which is also the next layer's scan order) and the final pick can only
+// matter when two candidates have bit-equal errors at the selection boundary or at the minimum.
 //
-// Selection reproduces the reference's beam, slot order included.  The reference scans
-// candidates slot-major, code-minor; a candidate enters when its error is strictly below the
-// current worst slot error and replaces the first slot holding that worst error
-// (beam_search.cpp:101-113, 252-260, 320-333).  Warp 0 replays that scan (slots one per lane;
-// the first worst slot is a max-reduce plus a ballot).
+// BeamFastKernel uses that: per layer it bounds every candidate's exact error from a cheap
+// evaluation (beam::CheapBounds), takes tau = a value below which B candidates provably lie,
+// evaluates exactly only the candidates whose lower bound is <= tau, and selects the B smallest
+// exact errors.  When an exact tie sits at the boundary (or at the final minimum), or the survivor
+// list would overflow, the vector is handed to BeamReplayKernel.
 //
-// Work saving without changing any decision.  A layer runs in four phases:
-//   A. slot 0's candidates are evaluated exactly and replayed; tau = the worst slot error after
-//      them.  The worst error never increases during the scan, so no later candidate with an
-//      exact error >= tau can enter the beam;
-//   B. every other candidate is evaluated with a cheap FMA/reciprocal formula (forward
-//      substitution only, delta = |y|^2) together with a bound on its rounding error relative to
-//      the exact sequence; a candidate is kept when its cheap error minus the bound is below tau
-//      (and always when the slot or the candidate is ill-conditioned or the value is not finite);
-//   C. the kept candidates are compacted in scan order and evaluated exactly by all threads;
-//   D. warp 0 continues the replay over the kept candidates only.
-// Dropped candidates provably cannot enter the beam, so the replay sees the same sequence of
-// entering candidates as the reference.  With STLQ_B200_CHECK_FILTER set, the kernel evaluates
-// every candidate exactly as well and raises an error flag if a dropped one would have entered.
+// BeamReplayKernel evaluates every candidate exactly and replays the reference's replacement
+// scan itself (warp 0, slots one per lane), so ties resolve exactly as in the reference.
 #include <cstdint>
 
-#include "common.cuh"
+#include "beam_common.cuh"
 #include "launch.h"
 
 namespace stlq_b200 {
 
+using namespace beam;
+
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
-constexpr int kCpt = kMaxK / kThreads;  // codewords per thread
-constexpr unsigned kFull = 0xffffffffu;
-// A slot whose last pivot satisfies R_LL^2 < kIllCond * G(c,c) (its codeword nearly in the span of
-// the earlier ones) evaluates all its candidates exactly; so does a candidate whose cheap denom
-// falls below kDenomGuard * alpha.
-constexpr float kIllCond = 1e-4f;
-constexpr float kDenomGuard = 1e-3f;
+constexpr int kSurvCap = 512;  // exactly evaluated survivors per layer in the fast kernel
 
-// Beam slots in dynamic shared memory, sized by the runtime beam width.
-template <int MAXM>
-struct SlotView {
-    float* R;     // [beam][MAXM*MAXM] upper Cholesky factor, row-major R[r*MAXM + c], r <= c
-    float* rinv;  // [beam][MAXM] 1/R_ii (cheap path only)
-    float* a;     // [beam][MAXM]
-    float* E;     // [beam]
-    int* code;    // [beam][MAXM]
-    int* ill;     // [beam] 1 when any pivot was ill-conditioned
-    __device__ float* Rh(int h) const { return R + h * MAXM * MAXM; }
-    __device__ float* rinvh(int h) const { return rinv + h * MAXM; }
-    __device__ float* ah(int h) const { return a + h * MAXM; }
-    __device__ int* codeh(int h) const { return code + h * MAXM; }
-    __host__ __device__ static constexpr size_t Bytes(int beam) {
-        return sizeof(float) * static_cast<size_t>(beam) * (MAXM * MAXM + 2 * MAXM + 1) +
-               sizeof(int) * static_cast<size_t>(beam) * (MAXM + 1);
-    }
-    __device__ static SlotView At(unsigned char* p, int beam) {
-        SlotView v;
-        v.R = reinterpret_cast<float*>(p);
-        v.rinv = v.R + beam * MAXM * MAXM;
-        v.a = v.rinv + beam * MAXM;
-        v.E = v.a + beam * MAXM;
-        v.code = reinterpret_cast<int*>(v.E + beam);
-        v.ill = v.code + beam * MAXM;
-        return v;
-    }
+struct LayerTable {
+    int cand[kMaxBeam];  // candidate (scan index) held by each slot, slot order
+    int n_slots;         // slots filled
+    int redo;            // fast kernel: hand the vector to the replay kernel
+    uint32_t tau_key[kWarps];
+    int n_surv;
+    uint32_t key_b;
 };
 
-// Shared state of the layer loop.
-struct LayerShared {
-    int cand[kMaxBeam];     // scan index of the candidate held by each slot
-    int n_finite;           // slots with a finite error (a prefix)
-    float tau;              // worst slot error after slot 0's candidates
-    int n_kept;             // compacted candidates of phase C
-    int chunk_off[kMaxBeam * kCpt * kWarps + 1];
-    unsigned chunk_mask[kMaxBeam * kCpt * kWarps];
-};
-
-__device__ __forceinline__ float PosInf() { return __int_as_float(0x7f800000); }
-
-// Exact candidate evaluation for slot h at layer L (compile-time L so the substitutions unroll).
-// Returns the error; +inf for a candidate the reference skips (denom == 0, :309-311) or that can
-// never enter the beam (e >= +inf or NaN, :320).  Optionally returns y, v, denom and a_last.
+// Copies the winners' state into the next slot buffer (beam_search.cpp:337-383): parent prefix of
+// R, then each winner's own R column (y, sqrt(denom)), coefficients a_t - v_t a_last, a_last, code.
 template <int MAXM, int L>
-__device__ __forceinline__ float EvalExact(const SlotView<MAXM>& cur, int h, const int (&flat)[MAXM],
-                                           const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
-                                           float* y_out, float* v_out, float* denom_out, float* alast_out) {
-    const float* Rh = cur.Rh(h);
-    const float* ah = cur.ah(h);
-    float A[L], y[L], v[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) A[t] = __ldg(Grow + static_cast<size_t>(flat[t]) * H + col);
-    // Forward solve R^T y = A (beam_search.cpp:138-147).
-#pragma unroll
-    for (int i = 0; i < L; ++i) {
-        float s = A[i];
-#pragma unroll
-        for (int k = 0; k < i; ++k) s = sub_rn(s, mul_rn(Rh[k * MAXM + i], y[k]));
-        y[i] = div_rn(s, Rh[i * MAXM + i]);
+__device__ void Materialize(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt,
+                            const LayerTable& lt, int newH, const float* __restrict__ Grow,
+                            const float* __restrict__ Gdiag, const float* __restrict__ xc) {
+    const int tid = threadIdx.x;
+    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    for (int e = tid; e < newH * L * L; e += kThreads) {
+        const int o = e / (L * L), rc = e % (L * L), r = rc / L, c = rc % L;
+        if (r <= c) nxt.Rh(o)[r * MAXM + c] = cur.Rh(lt.cand[o] / K)[r * MAXM + c];
     }
-    // Back solve R v = y (beam_search.cpp:152-161).
-#pragma unroll
-    for (int i = L - 1; i >= 0; --i) {
-        float s = y[i];
-#pragma unroll
-        for (int k = i + 1; k < L; ++k) s = sub_rn(s, mul_rn(Rh[i * MAXM + k], v[k]));
-        v[i] = div_rn(s, Rh[i * MAXM + i]);
-    }
-    float delta = 0.0f, eta = 0.0f;
-#pragma unroll
-    for (int t = 0; t < L; ++t) {
-        delta = add_rn(delta, mul_rn(A[t], v[t]));
-        eta = add_rn(eta, mul_rn(A[t], ah[t]));
-    }
-    const float denom = sub_rn(alpha, delta);
-    const float diff = sub_rn(gamma, eta);
-    const float a_last = div_rn(diff, denom);
-    float e = sub_rn(cur.E[h], mul_rn(diff, a_last));
-    if (e < 0.0f) e = 0.0f;
-    if (y_out) {
+    if (tid < newH) {
+        const int o = tid;
+        const int idx = lt.cand[o];
+        const int h = idx / K, k = idx - h * K;
+        const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
+        float y[L], v[L], denom, a_last;
+        const float ak = __ldg(Gdiag + offL + k);
+        const float e =
+            EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, ak, __ldg(xc + offL + k), y, v, &denom, &a_last);
 #pragma unroll
         for (int t = 0; t < L; ++t) {
-            y_out[t] = y[t];
-            v_out[t] = v[t];
+            nxt.codeh(o)[t] = cur.codeh(h)[t];
+            nxt.ah(o)[t] = sub_rn(cur.ah(h)[t], mul_rn(v[t], a_last));
+            nxt.Rh(o)[t * MAXM + L] = y[t];
+            nxt.rinvh(o)[t] = cur.rinvh(h)[t];
         }
-        *denom_out = denom;
-        *alast_out = a_last;
+        const float rll = __fsqrt_rn(denom);
+        nxt.codeh(o)[L] = k;
+        nxt.ah(o)[L] = a_last;
+        nxt.Rh(o)[L * MAXM + L] = rll;
+        nxt.rinvh(o)[L] = __frcp_rn(rll);
+        nxt.E[o] = e;
+        nxt.ill[o] = cur.ill[h] | !(denom >= kIllCond * ak);
     }
-    return (denom != 0.0f && e < PosInf()) ? e : PosInf();
 }
 
-// Cheap evaluation: true when the candidate may have an exact error below tau.
-// e' = E_old - diff^2/denom with y from FMA forward substitution, delta = |y|^2, eta = A.a.  The
-// bound de covers the rounding of both this and the exact sequence: relative errors of order
-// L ulp in diff (scale |gamma| + sum|A_t a_t|) and in denom (scale alpha + delta), propagated
-// through r = diff^2/denom, plus the final subtraction; kept with a factor 16.
+// No finite candidate in a layer (beam_search.cpp:385-400): the previous slots are kept.  The code
+// of this layer is written as 0; the reference copies a stale buffer value there.
 template <int MAXM, int L>
-__device__ __forceinline__ bool MayEnter(const SlotView<MAXM>& cur, int h, const int (&flat)[MAXM],
-                                         const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
-                                         float tau) {
-    const float* Rh = cur.Rh(h);
-    const float* rinv = cur.rinvh(h);
-    const float* ah = cur.ah(h);
-    float A[L], y[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) A[t] = __ldg(Grow + static_cast<size_t>(flat[t]) * H + col);
-    float delta = 0.0f, eta = 0.0f, seta = fabsf(gamma);
-#pragma unroll
-    for (int i = 0; i < L; ++i) {
-        float s = A[i];
-#pragma unroll
-        for (int k = 0; k < i; ++k) s = fmaf(-Rh[k * MAXM + i], y[k], s);
-        y[i] = s * rinv[i];
-        delta = fmaf(y[i], y[i], delta);
-        const float p = A[i] * ah[i];
-        eta += p;
-        seta += fabsf(p);
+__device__ int KeepPrevious(const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH, int beam) {
+    const int tid = threadIdx.x;
+    const int keep = min(curH, beam);
+    for (int e = tid; e < keep * MAXM * MAXM; e += kThreads) nxt.R[e] = cur.R[e];
+    for (int e = tid; e < keep * MAXM; e += kThreads) {
+        const int t = e % MAXM;
+        nxt.code[e] = t < L ? cur.code[e] : 0;
+        nxt.a[e] = t < L ? cur.a[e] : 0.0f;
+        nxt.rinv[e] = cur.rinv[e];
     }
-    const float denom = alpha - delta;
-    const float diff = gamma - eta;
-    const float r = __fdividef(diff * diff, denom);
-    const float ep = cur.E[h] - r;
-    constexpr float u = 1.2e-7f * (L + 2);
-    const float de = 2.0f * fabsf(diff) * (u * seta) / denom + fabsf(r) * (u * (alpha + delta)) / denom +
-                     1.2e-7f * (cur.E[h] + fabsf(r));
-    const bool force = cur.ill[h] || !(denom > kDenomGuard * alpha);
-    return force || !(ep - 16.0f * de >= tau);
+    for (int h = tid; h < keep; h += kThreads) {
+        nxt.E[h] = cur.E[h];
+        nxt.ill[h] = cur.ill[h];
+    }
+    return max(1, keep);
 }
 
-// Warp-0 state of the replay of the reference's replace-worst scan: lane s < beam holds slot s.
+// Layer 0 state of slot o holding codeword k (beam_search.cpp:248-258).
+template <int MAXM>
+__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, const float* Gdiag, const float* xc, float nx2) {
+    const float alpha = __ldg(Gdiag + k);
+    const float gamma = __ldg(xc + k);
+    const float a1 = div_rn(gamma, alpha);
+    const float r00 = __fsqrt_rn(alpha);
+    s.codeh(o)[0] = k;
+    s.ah(o)[0] = a1;
+    s.E[o] = sub_rn(nx2, mul_rn(gamma, a1));
+    s.Rh(o)[0] = r00;
+    s.rinvh(o)[0] = __frcp_rn(r00);
+    s.ill[o] = 0;
+}
+
+// Every layer-0 codeword is zero: the reference carries one slot with error +inf through every
+// layer (each later candidate is then non-finite and the fallback keeps the slot), ending with
+// code 0 in every layer.
+template <int MAXM>
+__device__ void DeadSlot0(const SlotView<MAXM>& s) {
+    const int tid = threadIdx.x;
+    if (tid < MAXM) {
+        s.codeh(0)[tid] = 0;
+        s.ah(0)[tid] = 0.0f;
+        s.rinvh(0)[tid] = 0.0f;
+    }
+    for (int e = tid; e < MAXM * MAXM; e += kThreads) s.Rh(0)[e] = 0.0f;
+    if (tid == 0) {
+        s.E[0] = PosInf();
+        s.ill[0] = 1;
+    }
+}
+
+// Layer-0 error of codeword k: a1 = gamma/alpha, e1 = ||x||^2 - gamma*a1, not clamped; a zero
+// codeword (alpha == 0) is skipped (beam_search.cpp:240-252).
+__device__ __forceinline__ float Layer0Error(const float* Gdiag, const float* xc, float nx2, int k) {
+    const float alpha = __ldg(Gdiag + k);
+    const float gamma = __ldg(xc + k);
+    const float e1 = sub_rn(nx2, mul_rn(gamma, div_rn(gamma, alpha)));
+    return (alpha != 0.0f && e1 < PosInf()) ? e1 : PosInf();
+}
+
+// ---------------------------------------------------------------------------------------------
+// Replay kernel: exact errors for every candidate and the reference's replacement scan.
+
+// Warp-0 replay state: lane s < beam holds slot s.
 struct Replay {
     float es;
     int cs;
@@ -197,47 +166,40 @@ struct Replay {
         widx = __ffs(__ballot_sync(kFull, key == wkey)) - 1;
         worst = KeyToFloat(wkey);
     }
-    // Offers 32 candidates (lane l holds candidate id ids and error e; invalid lanes +inf).
-    __device__ void Offer(float e, int id) {
+    // Scans errs[0..n) in order: one ballot per 32 candidates, entering ones replayed in order.
+    __device__ void Scan(const float* errs, int n) {
         const int lane = threadIdx.x & 31;
-        unsigned mask = __ballot_sync(kFull, e < worst);
-        while (mask) {
-            const int l = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const float el = __shfl_sync(kFull, e, l);
-            const int il = __shfl_sync(kFull, id, l);
-            if (el < worst) {  // the worst only decreases: re-test against the current one
-                if (lane == widx) {
-                    es = el;
-                    cs = il;
+        for (int base = 0; base < n; base += 32) {
+            const float e = base + lane < n ? errs[base + lane] : PosInf();
+            unsigned mask = __ballot_sync(kFull, e < worst);
+            while (mask) {
+                const int l = __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float el = __shfl_sync(kFull, e, l);
+                if (el < worst) {  // the worst only decreases: re-test against the current one
+                    if (lane == widx) {
+                        es = el;
+                        cs = base + l;
+                    }
+                    Refresh();
                 }
-                Refresh();
             }
         }
     }
-    __device__ void Publish(int beam, LayerShared& ls) {
+    __device__ void Publish(int beam, LayerTable& lt) {
         const int lane = threadIdx.x & 31;
-        if (lane < beam) ls.cand[lane] = cs;
+        if (lane < beam) lt.cand[lane] = cs;
         const unsigned fin = __ballot_sync(kFull, lane < beam && es < PosInf());
-        if (lane == 0) ls.n_finite = __popc(fin);
+        if (lane == 0) lt.n_slots = __popc(fin);
     }
 };
 
 template <int MAXM, int L>
-__device__ __forceinline__ void FlatOf(const Dims& dims, const SlotView<MAXM>& cur, int h, int (&flat)[MAXM]) {
-#pragma unroll
-    for (int t = 0; t < MAXM; ++t) flat[t] = t < L ? dims.off[t] + cur.codeh(h)[t] : 0;
-}
-
-template <int MAXM, int L>
-__device__ void ExpandLayer(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
+__device__ void ReplayLayer(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
-                            const float* __restrict__ xc, int beam, float* errs, uint16_t* list, LayerShared& ls,
-                            int check, unsigned int* err_flag) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int H = dims.H;
-    const int K = dims.h_vec[L];
-    const int offL = dims.off[L];
+                            const float* __restrict__ xc, int beam, float* errs, LayerTable& lt) {
+    const int tid = threadIdx.x;
+    const int K = dims.h_vec[L], offL = dims.off[L];
     float alpha[kCpt], gamma[kCpt];
 #pragma unroll
     for (int c = 0; c < kCpt; ++c) {
@@ -245,275 +207,95 @@ __device__ void ExpandLayer(const Dims& dims, const SlotView<MAXM>& cur, const S
         alpha[c] = k < K ? __ldg(Gdiag + offL + k) : 0.0f;
         gamma[c] = k < K ? __ldg(xc + offL + k) : 0.0f;
     }
-    // Phase A: slot 0 exactly, then its replay; tau bounds every later entering error.
-    {
-        int flat[MAXM];
-        FlatOf<MAXM, L>(dims, cur, 0, flat);
+    for (int h = 0; h < curH; ++h) {
+        const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) {
             const int k = tid + c * kThreads;
             if (k < K)
-                errs[k] = EvalExact<MAXM, L>(cur, 0, flat, Grow, H, offL + k, alpha[c], gamma[c], nullptr, nullptr,
-                                             nullptr, nullptr);
+                errs[h * K + k] = EvalExact<MAXM, L>(cur, h, flat, Grow, dims.H, offL + k, alpha[c], gamma[c],
+                                                     nullptr, nullptr, nullptr, nullptr);
         }
     }
     __syncthreads();
-    Replay rp;
-    if (warp == 0) {
+    if (tid < 32) {
+        Replay rp;
         rp.Init(beam);
-        for (int base = 0; base < K; base += 32) {
-            const int j = base + lane;
-            rp.Offer(j < K ? errs[j] : PosInf(), j);
-        }
-        if (lane == 0) ls.tau = rp.worst;
+        rp.Scan(errs, curH * K);
+        rp.Publish(beam, lt);
     }
     __syncthreads();
-    const float tau = ls.tau;
-    // Phase B: cheap evaluation of the other slots -> one keep-mask per 32 candidates.
-    for (int h = 1; h < curH; ++h) {
-        int flat[MAXM];
-        FlatOf<MAXM, L>(dims, cur, h, flat);
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            const int k = tid + c * kThreads;
-            bool keep = false;
-            if (k < K) {
-                keep = MayEnter<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], tau);
-                if (check && !keep) {
-                    const float e = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], nullptr,
-                                                       nullptr, nullptr, nullptr);
-                    if (e < tau) atomicOr(err_flag, kErrFilterMiss);
-                }
-            }
-            const unsigned mask = __ballot_sync(kFull, keep);
-            if (lane == 0) ls.chunk_mask[((h - 1) * kCpt + c) * kWarps + warp] = mask;
-        }
-    }
-    __syncthreads();
-    // Phase C: compact the kept candidates in scan order, then evaluate them exactly.
-    const int nq = (curH - 1) * kCpt * kWarps;
-    if (warp == 0) {
-        const int per = (nq + 31) / 32;
-        const int q0 = lane * per;
-        int s = 0;
-        for (int q = q0; q < min(q0 + per, nq); ++q) s += __popc(ls.chunk_mask[q]);
-        int incl = s;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(kFull, incl, o);
-            if (lane >= o) incl += v;
-        }
-        int run = incl - s;
-        for (int q = q0; q < min(q0 + per, nq); ++q) {
-            ls.chunk_off[q] = run;
-            run += __popc(ls.chunk_mask[q]);
-        }
-        if (lane == 31) ls.n_kept = incl;
-    }
-    __syncthreads();
-    for (int h = 1; h < curH; ++h) {
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            const int q = ((h - 1) * kCpt + c) * kWarps + warp;
-            const unsigned mask = ls.chunk_mask[q];
-            if ((mask >> lane) & 1u)
-                list[ls.chunk_off[q] + __popc(mask & ((1u << lane) - 1u))] =
-                    static_cast<uint16_t>(h * K + tid + c * kThreads);
-        }
-    }
-    __syncthreads();
-    const int n_kept = ls.n_kept;
-    for (int p = tid; p < n_kept; p += kThreads) {
-        const int idx = list[p];
-        const int h = idx / K, k = idx - h * K;
-        int flat[MAXM];
-        FlatOf<MAXM, L>(dims, cur, h, flat);
-        errs[idx] = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, __ldg(Gdiag + offL + k), __ldg(xc + offL + k),
-                                       nullptr, nullptr, nullptr, nullptr);
-    }
-    __syncthreads();
-    // Phase D: the replay continues over the kept candidates only.
-    if (warp == 0) {
-        for (int base = 0; base < n_kept; base += 32) {
-            const int p = base + lane;
-            const int id = p < n_kept ? list[p] : -1;
-            rp.Offer(p < n_kept ? errs[id] : PosInf(), id);
-        }
-        rp.Publish(beam, ls);
-    }
-    __syncthreads();
-    const int newH = ls.n_finite;
+    const int newH = lt.n_slots;
     if (newH == 0) {
-        // No finite candidate (beam_search.cpp:385-400): keep the previous slots.  The code of
-        // this layer is written as 0; the reference copies a stale buffer value there.
-        const int keep = min(curH, beam);
-        for (int e = tid; e < keep * MAXM * MAXM; e += kThreads) nxt.R[e] = cur.R[e];
-        for (int e = tid; e < keep * MAXM; e += kThreads) {
-            const int t = e % MAXM;
-            nxt.code[e] = t < L ? cur.code[e] : 0;
-            nxt.a[e] = t < L ? cur.a[e] : 0.0f;
-            nxt.rinv[e] = cur.rinv[e];
-        }
-        for (int h = tid; h < keep; h += kThreads) {
-            nxt.E[h] = cur.E[h];
-            nxt.ill[h] = cur.ill[h];
-        }
-        __syncthreads();
-        curH = max(1, keep);
-        return;
-    }
-    // Materialise the winners (beam_search.cpp:337-383): copy the parent's prefix, then the
-    // winner's own column of R, coefficients and code.
-    for (int e = tid; e < newH * L * L; e += kThreads) {
-        const int o = e / (L * L), rc = e % (L * L), r = rc / L, c = rc % L;
-        if (r <= c) nxt.Rh(o)[r * MAXM + c] = cur.Rh(ls.cand[o] / K)[r * MAXM + c];
-    }
-    if (tid < newH) {
-        const int o = tid;
-        const int idx = ls.cand[o];
-        const int h = idx / K, k = idx - h * K;
-        int flat[MAXM];
-        FlatOf<MAXM, L>(dims, cur, h, flat);
-        float y[L], v[L], denom, a_last;
-        const float ak = __ldg(Gdiag + offL + k);
-        const float e = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, ak, __ldg(xc + offL + k), y, v, &denom,
-                                           &a_last);
-#pragma unroll
-        for (int t = 0; t < L; ++t) {
-            nxt.codeh(o)[t] = cur.codeh(h)[t];
-            nxt.ah(o)[t] = sub_rn(cur.ah(h)[t], mul_rn(v[t], a_last));
-            nxt.Rh(o)[t * MAXM + L] = y[t];
-            nxt.rinvh(o)[t] = cur.rinvh(h)[t];
-        }
-        const float rll = __fsqrt_rn(denom);
-        nxt.codeh(o)[L] = k;
-        nxt.ah(o)[L] = a_last;
-        nxt.Rh(o)[L * MAXM + L] = rll;
-        nxt.rinvh(o)[L] = __frcp_rn(rll);
-        nxt.E[o] = e;
-        nxt.ill[o] = cur.ill[h] | !(denom >= kIllCond * ak);
+        curH = KeepPrevious<MAXM, L>(cur, nxt, curH, beam);
+    } else {
+        Materialize<MAXM, L>(dims, cur, nxt, lt, newH, Grow, Gdiag, xc);
+        curH = newH;
     }
     __syncthreads();
-    curH = newH;
 }
 
 template <int MAXM>
-__device__ void ExpandLayerDispatch(int L, const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt,
-                                    int& curH, const float* Grow, const float* Gdiag, const float* xc, int beam,
-                                    float* errs, uint16_t* list, LayerShared& ls, int check, unsigned int* err) {
-#define STLQ_B200_EXPAND(LL)                                                                                   \
-    case LL:                                                                                                   \
-        if constexpr (LL < MAXM)                                                                               \
-            ExpandLayer<MAXM, LL>(dims, cur, nxt, curH, Grow, Gdiag, xc, beam, errs, list, ls, check, err);   \
+__device__ void ReplayDispatch(int L, const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
+                               const float* Grow, const float* Gdiag, const float* xc, int beam, float* errs,
+                               LayerTable& lt) {
+#define STLQ_B200_REPLAY(LL)                                                                    \
+    case LL:                                                                                    \
+        if constexpr (LL < MAXM) ReplayLayer<MAXM, LL>(dims, cur, nxt, curH, Grow, Gdiag, xc, beam, errs, lt); \
         break;
     switch (L) {
-        STLQ_B200_EXPAND(1) STLQ_B200_EXPAND(2) STLQ_B200_EXPAND(3) STLQ_B200_EXPAND(4) STLQ_B200_EXPAND(5)
-        STLQ_B200_EXPAND(6) STLQ_B200_EXPAND(7) STLQ_B200_EXPAND(8) STLQ_B200_EXPAND(9) STLQ_B200_EXPAND(10)
-        STLQ_B200_EXPAND(11) STLQ_B200_EXPAND(12) STLQ_B200_EXPAND(13) STLQ_B200_EXPAND(14) STLQ_B200_EXPAND(15)
+        STLQ_B200_REPLAY(1) STLQ_B200_REPLAY(2) STLQ_B200_REPLAY(3) STLQ_B200_REPLAY(4) STLQ_B200_REPLAY(5)
+        STLQ_B200_REPLAY(6) STLQ_B200_REPLAY(7) STLQ_B200_REPLAY(8) STLQ_B200_REPLAY(9) STLQ_B200_REPLAY(10)
+        STLQ_B200_REPLAY(11) STLQ_B200_REPLAY(12) STLQ_B200_REPLAY(13) STLQ_B200_REPLAY(14) STLQ_B200_REPLAY(15)
         default: break;
     }
-#undef STLQ_B200_EXPAND
+#undef STLQ_B200_REPLAY
 }
 
+// Encodes the vectors listed in vec_list[0 .. *count) (or 0 .. n when vec_list is null).
 template <int MAXM>
-struct BeamSmem {
-    static size_t Bytes(int beam, int maxK) {
-        size_t b = 2 * SlotView<MAXM>::Bytes(beam);
-        b = (b + 15) & ~size_t(15);
-        b += sizeof(LayerShared);
-        b = (b + 15) & ~size_t(15);
-        b += sizeof(float) * beam * maxK;      // errs
-        b += sizeof(uint16_t) * beam * maxK;   // list
-        return b + 16;
-    }
-};
-
-template <int MAXM>
-__global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamSearchKernel(Dims dims, const float* __restrict__ Grow,
+__global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const float* __restrict__ Grow,
                                                              const float* __restrict__ Gdiag,
                                                              const float* __restrict__ xnorm2,
                                                              const float* __restrict__ xC, int64_t n, int beam,
-                                                             uint8_t* __restrict__ Bout, int check,
-                                                             unsigned int* err_flag) {
+                                                             uint8_t* __restrict__ Bout, const int* vec_list,
+                                                             const int* count) {
     extern __shared__ __align__(16) unsigned char smem[];
     const size_t sv = SlotView<MAXM>::Bytes(beam);
     size_t off = (2 * sv + 15) & ~size_t(15);
-    LayerShared& ls = *reinterpret_cast<LayerShared*>(smem + off);
-    off = (off + sizeof(LayerShared) + 15) & ~size_t(15);
-    float* errs = reinterpret_cast<float*>(smem + off);
-    uint16_t* list = reinterpret_cast<uint16_t*>(errs + beam * dims.maxK);
+    LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
+    float* errs = reinterpret_cast<float*>(smem + ((off + sizeof(LayerTable) + 15) & ~size_t(15)));
     const int tid = threadIdx.x;
-    const int m = dims.m;
-    const int K0 = dims.h_vec[0];
-
-    for (int64_t vec = blockIdx.x; vec < n; vec += gridDim.x) {
+    const int m = dims.m, K0 = dims.h_vec[0];
+    const int64_t total = vec_list ? static_cast<int64_t>(*count) : n;
+    for (int64_t i = blockIdx.x; i < total; i += gridDim.x) {
+        const int64_t vec = vec_list ? vec_list[i] : i;
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
-        int ci = 0;  // index of the current slot buffer
-        // Layer 0 (beam_search.cpp:238-263): a1 = gamma/alpha, e1 = ||x||^2 - gamma*a1 (no
-        // clamp); a zero codeword (alpha == 0) is skipped.
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            const int k = tid + c * kThreads;
-            if (k < K0) {
-                const float alpha = __ldg(Gdiag + k);
-                const float gamma = __ldg(xc + k);
-                const float a1 = div_rn(gamma, alpha);
-                const float e1 = sub_rn(nx2, mul_rn(gamma, a1));
-                errs[k] = (alpha != 0.0f && e1 < PosInf()) ? e1 : PosInf();
-            }
-        }
+        for (int k = tid; k < K0; k += kThreads) errs[k] = Layer0Error(Gdiag, xc, nx2, k);
         __syncthreads();
         if (tid < 32) {
             Replay rp;
             rp.Init(beam);
-            for (int base = 0; base < K0; base += 32) {
-                const int j = base + tid;
-                rp.Offer(j < K0 ? errs[j] : PosInf(), j);
-            }
-            rp.Publish(beam, ls);
+            rp.Scan(errs, K0);
+            rp.Publish(beam, lt);
         }
         __syncthreads();
-        int curH = ls.n_finite;
+        int curH = lt.n_slots;
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (tid < curH) {
-            const int k = ls.cand[tid];
-            const float alpha = __ldg(Gdiag + k);
-            const float gamma = __ldg(xc + k);
-            const float a1 = div_rn(gamma, alpha);
-            const float r00 = __fsqrt_rn(alpha);
-            s0.codeh(tid)[0] = k;
-            s0.ah(tid)[0] = a1;
-            s0.E[tid] = sub_rn(nx2, mul_rn(gamma, a1));
-            s0.Rh(tid)[0] = r00;
-            s0.rinvh(tid)[0] = __frcp_rn(r00);
-            s0.ill[tid] = 0;
-        }
+        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
         if (curH == 0) {
-            // No finite layer-0 candidate (every codeword zero): the reference carries one slot
-            // with error +inf through every layer (every later candidate is then non-finite and
-            // the fallback keeps the slot), ending with code 0 in every layer.
-            if (tid < MAXM) {
-                s0.codeh(0)[tid] = 0;
-                s0.ah(0)[tid] = 0.0f;
-                s0.rinvh(0)[tid] = 0.0f;
-            }
-            for (int e = tid; e < MAXM * MAXM; e += kThreads) s0.Rh(0)[e] = 0.0f;
-            if (tid == 0) {
-                s0.E[0] = PosInf();
-                s0.ill[0] = 1;
-            }
+            DeadSlot0<MAXM>(s0);
             curH = 1;
         }
         __syncthreads();
+        int ci = 0;
         for (int L = 1; L < m; ++L) {
-            ExpandLayerDispatch<MAXM>(L, dims, SlotView<MAXM>::At(smem + ci * sv, beam),
-                                      SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs,
-                                      list, ls, check, err_flag);
+            ReplayDispatch<MAXM>(L, dims, SlotView<MAXM>::At(smem + ci * sv, beam),
+                                 SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, lt);
             ci ^= 1;
         }
-        // Final pick: the first slot holding the smallest error (beam_search.cpp:409-416).
-        if (tid < 32) {
+        if (tid < 32) {  // first slot with the smallest error (beam_search.cpp:409-416)
             const SlotView<MAXM> cur = SlotView<MAXM>::At(smem + ci * sv, beam);
             const uint32_t key = tid < curH ? OrderKey(cur.E[tid]) : 0xffffffffu;
             const uint32_t kmin = __reduce_min_sync(kFull, key);
@@ -524,32 +306,272 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamSearchKernel(
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Fast kernel: exact B smallest errors of each layer; ties handed to the replay kernel.
+
+// Ascending bitonic sort of one key per lane across the warp; returns this lane's sorted key.
+__device__ __forceinline__ uint32_t WarpSortAsc(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint32_t o = __shfl_xor_sync(kFull, v, j);
+            const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+            v = (lower == up) ? min(v, o) : max(v, o);
+        }
+    }
+    return v;
+}
+
+// Selection shared by every layer of the fast kernel.  Inputs: lo[idx] (a lower bound of each
+// candidate's exact error; the exact error itself in layer 0) for idx < n_cand, and this thread's
+// smallest upper bound `hmin`.  Each warp's 32 per-thread minima belong to distinct candidates, so
+// the B-th smallest of them bounds the B-th smallest exact error from above: tau = the least such
+// bound over the warps.  Candidates with lo <= tau survive (everything else is provably larger
+// than the B-th smallest exact error), are evaluated exactly by `exact(idx)` and ranked by
+// (error, scan index).  Fills lt.cand with the B smallest and returns the slot count, or -1 when
+// the vector must go to the replay kernel (an exact tie at the boundary, or too many survivors).
+template <typename ExactFn>
+__device__ int FastSelect(const float* lo, int n_cand, uint32_t hmin, int beam, LayerTable& lt, uint16_t* surv,
+                          float* ex, int* rank, ExactFn exact) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t sorted = WarpSortAsc(hmin);
+    const uint32_t tw = __shfl_sync(kFull, sorted, beam - 1);
+    if (lane == 0) lt.tau_key[warp] = tw;
+    if (tid == 0) {
+        lt.n_surv = 0;
+        lt.n_slots = 0;
+        lt.key_b = 0u;
+    }
+    __syncthreads();
+    uint32_t tk = lt.tau_key[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) tk = min(tk, lt.tau_key[w]);
+    // Fewer than B finite upper bounds in every warp: no pruning.
+    const float tau = tk >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tk);
+    for (int idx = tid; idx < n_cand; idx += kThreads) {
+        if (lo[idx] <= tau) {
+            const int p = atomicAdd(&lt.n_surv, 1);
+            if (p < kSurvCap) surv[p] = static_cast<uint16_t>(idx);
+        }
+    }
+    __syncthreads();
+    const int S = lt.n_surv;
+    if (S > kSurvCap) return -1;  // uniform: every thread read the same count
+    for (int p = tid; p < S; p += kThreads) ex[p] = exact(static_cast<int>(surv[p]));
+    __syncthreads();
+    int my_valid = 0;
+    for (int p = tid; p < S; p += kThreads) {
+        const uint32_t kp = OrderKey(ex[p]);
+        const uint64_t cp = (static_cast<uint64_t>(kp) << 32) | surv[p];
+        int r = 0;
+        for (int q = 0; q < S; ++q) r += ((static_cast<uint64_t>(OrderKey(ex[q])) << 32) | surv[q]) < cp;
+        rank[p] = r;
+        const bool valid = ex[p] < PosInf();
+        my_valid += valid;
+        if (valid && r < beam) lt.cand[r] = surv[p];
+        if (valid && r == beam - 1) lt.key_b = kp;
+    }
+    if (my_valid) atomicAdd(&lt.n_slots, my_valid);
+    __syncthreads();
+    const int n_valid = lt.n_slots;
+    if (n_valid > beam) {
+        // Tie at the boundary: another survivor with the B-th smallest error's exact value.
+        const uint32_t kb = lt.key_b;
+        int tie = 0;
+        for (int p = tid; p < S; p += kThreads) tie |= (rank[p] >= beam && OrderKey(ex[p]) == kb);
+        if (__syncthreads_or(tie)) return -1;
+    }
+    return min(n_valid, beam);
+}
+
+template <int MAXM, int L>
+__device__ int FastLayer(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
+                         const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
+                         int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, int* rank, int check,
+                         unsigned int* err_flag) {
+    const int tid = threadIdx.x;
+    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    float alpha[kCpt], gamma[kCpt];
+#pragma unroll
+    for (int c = 0; c < kCpt; ++c) {
+        const int k = tid + c * kThreads;
+        alpha[c] = k < K ? __ldg(Gdiag + offL + k) : 0.0f;
+        gamma[c] = k < K ? __ldg(xc + offL + k) : 0.0f;
+    }
+    uint32_t hmin = 0xffffffffu;
+    for (int h = 0; h < curH; ++h) {
+        const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
+#pragma unroll
+        for (int c = 0; c < kCpt; ++c) {
+            const int k = tid + c * kThreads;
+            if (k < K) {
+                float l, hi;
+                CheapBounds<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], &l, &hi);
+                lo[h * K + k] = l;
+                hmin = min(hmin, OrderKey(hi));
+                if (check) {  // self-check: the exact error must lie inside the bounds
+                    const float e = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], nullptr,
+                                                       nullptr, nullptr, nullptr);
+                    if (e < PosInf() && !(e >= l && e <= hi)) atomicOr(err_flag, kErrFilterMiss);
+                }
+            }
+        }
+    }
+    auto exact = [&](int idx) {
+        const int h = idx / K, k = idx - h * K;
+        return EvalExact<MAXM, L>(cur, h, FlatOf<MAXM, L>(dims, cur, h), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+                                  __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
+    };
+    const int newH = FastSelect(lo, curH * K, hmin, beam, lt, surv, ex, rank, exact);
+    if (newH < 0) return -1;
+    if (newH == 0) {
+        const int keep = KeepPrevious<MAXM, L>(cur, nxt, curH, beam);
+        __syncthreads();
+        return keep;
+    }
+    Materialize<MAXM, L>(dims, cur, nxt, lt, newH, Grow, Gdiag, xc);
+    __syncthreads();
+    return newH;
+}
+
 template <int MAXM>
-cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2, const float* xC,
-                        int64_t n, int beam, uint8_t* Bout, int check, unsigned int* err_flag, int num_sms,
-                        cudaStream_t stream) {
-    const size_t smem = BeamSmem<MAXM>::Bytes(beam, dims.maxK);
-    cudaError_t e = cudaFuncSetAttribute(BeamSearchKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+__device__ int FastDispatch(int L, const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
+                            const float* Grow, const float* Gdiag, const float* xc, int beam, float* lo,
+                            LayerTable& lt, uint16_t* surv, float* ex, int* rank, int check, unsigned int* err) {
+#define STLQ_B200_FAST(LL)                                                                                   \
+    case LL:                                                                                                 \
+        if constexpr (LL < MAXM)                                                                             \
+            return FastLayer<MAXM, LL>(dims, cur, nxt, curH, Grow, Gdiag, xc, beam, lo, lt, surv, ex, rank,    \
+                                       check, err);                                                          \
+        break;
+    switch (L) {
+        STLQ_B200_FAST(1) STLQ_B200_FAST(2) STLQ_B200_FAST(3) STLQ_B200_FAST(4) STLQ_B200_FAST(5)
+        STLQ_B200_FAST(6) STLQ_B200_FAST(7) STLQ_B200_FAST(8) STLQ_B200_FAST(9) STLQ_B200_FAST(10)
+        STLQ_B200_FAST(11) STLQ_B200_FAST(12) STLQ_B200_FAST(13) STLQ_B200_FAST(14) STLQ_B200_FAST(15)
+        default: break;
+    }
+#undef STLQ_B200_FAST
+    return -1;
+}
+
+template <int MAXM>
+__global__ void __launch_bounds__(kThreads) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
+                                                           const float* __restrict__ Gdiag,
+                                                           const float* __restrict__ xnorm2,
+                                                           const float* __restrict__ xC, int64_t n, int beam,
+                                                           uint8_t* __restrict__ Bout, int* redo_list, int* redo_count,
+                                                           int check, unsigned int* err_flag) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const size_t sv = SlotView<MAXM>::Bytes(beam);
+    size_t off = (2 * sv + 15) & ~size_t(15);
+    LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
+    off = (off + sizeof(LayerTable) + 15) & ~size_t(15);
+    float* lo = reinterpret_cast<float*>(smem + off);
+    float* ex = lo + beam * dims.maxK;
+    int* rank = reinterpret_cast<int*>(ex + kSurvCap);
+    uint16_t* surv = reinterpret_cast<uint16_t*>(rank + kSurvCap);
+    const int tid = threadIdx.x;
+    const int m = dims.m, K0 = dims.h_vec[0];
+    for (int64_t vec = blockIdx.x; vec < n; vec += gridDim.x) {
+        const float* xc = xC + vec * dims.H;
+        const float nx2 = __ldg(xnorm2 + vec);
+        // Layer 0: exact errors are cheap; they serve as their own bounds.
+        uint32_t hmin = 0xffffffffu;
+#pragma unroll
+        for (int c = 0; c < kCpt; ++c) {
+            const int k = tid + c * kThreads;
+            if (k < K0) {
+                const float e1 = Layer0Error(Gdiag, xc, nx2, k);
+                lo[k] = e1;
+                hmin = min(hmin, OrderKey(e1));
+            }
+        }
+        int curH = FastSelect(lo, K0, hmin, beam, lt, surv, ex, rank, [&](int idx) { return lo[idx]; });
+        const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
+        if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
+        if (curH == 0) {
+            DeadSlot0<MAXM>(s0);
+            curH = 1;
+        }
+        __syncthreads();
+        int ci = 0;
+        for (int L = 1; L < m && curH > 0; ++L) {
+            curH = FastDispatch<MAXM>(L, dims, SlotView<MAXM>::At(smem + ci * sv, beam),
+                                      SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo,
+                                      lt, surv, ex, rank, check, err_flag);
+            ci ^= 1;
+        }
+        const SlotView<MAXM> cur = SlotView<MAXM>::At(smem + ci * sv, beam);
+        // Slots are sorted by (error, scan index): slot 0 is the pick unless the minimum is tied.
+        const bool redo = curH < 0 || (curH >= 2 && OrderKey(cur.E[0]) == OrderKey(cur.E[1]));
+        if (redo) {
+            if (tid == 0) redo_list[atomicAdd(redo_count, 1)] = static_cast<int>(vec);
+        } else if (tid < m) {
+            Bout[vec * m + tid] = static_cast<uint8_t>(cur.codeh(0)[tid]);
+        }
+        __syncthreads();
+    }
+}
+
+template <int MAXM>
+size_t FastSmemBytes(int beam, int maxK) {
+    size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
+    b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
+    return b + sizeof(float) * beam * maxK + (sizeof(float) + sizeof(int) + sizeof(uint16_t)) * kSurvCap + 16;
+}
+
+template <int MAXM>
+size_t ReplaySmemBytes(int beam, int maxK) {
+    size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
+    b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
+    return b + sizeof(float) * beam * maxK + 16;
+}
+
+template <typename KernelT>
+cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* grid) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, BeamSearchKernel<MAXM>, kThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess) return e;
-    const int64_t grid = std::min<int64_t>(n, static_cast<int64_t>(num_sms) * std::max(per_sm, 1));
-    BeamSearchKernel<MAXM><<<static_cast<int>(grid), kThreads, smem, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam,
-                                                                               Bout, check, err_flag);
+    *grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n, static_cast<int64_t>(num_sms) * std::max(per_sm, 1))));
+    return cudaSuccess;
+}
+
+template <int MAXM>
+cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2, const float* xC,
+                        int64_t n, int beam, uint8_t* Bout, int* redo, int check, unsigned int* err_flag, int num_sms,
+                        cudaStream_t stream) {
+    int grid = 0;
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
+    cudaError_t e = Prepare(BeamFastKernel<MAXM>, fsm, num_sms, n, &grid);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+    BeamFastKernel<MAXM><<<grid, kThreads, fsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
+                                                          check, err_flag);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK);
+    e = Prepare(BeamReplayKernel<MAXM>, rsm, num_sms, n, &grid);
+    if (e != cudaSuccess) return e;
+    BeamReplayKernel<MAXM><<<grid, kThreads, rsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
+                                                            redo);
     return cudaGetLastError();
 }
 
 }  // namespace
 
+// redo: n + 1 ints of scratch (a count, then vector ids handed from the fast to the replay kernel).
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
-                             const float* xC, int64_t n, int beam, uint8_t* Bout, int check, unsigned int* err_flag,
-                             int num_sms, cudaStream_t stream) {
+                             const float* xC, int64_t n, int beam, uint8_t* Bout, int* redo, int check,
+                             unsigned int* err_flag, int num_sms, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     if (dims.m <= 8)
-        return LaunchBeamT<8>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, check, err_flag, num_sms, stream);
-    return LaunchBeamT<16>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, check, err_flag, num_sms, stream);
+        return LaunchBeamT<8>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, num_sms, stream);
+    return LaunchBeamT<16>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, num_sms, stream);
 }
 
 }  // namespace stlq_b200

@@ -13,7 +13,7 @@ cudaError_t LaunchXcGemmExact(const float* C, int rows, int d, const void* X, in
 int MaxGemmSliceVectors();
 
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
-                             const float* xC, int64_t n, int beam, uint8_t* Bout, int check,
+                             const float* xC, int64_t n, int beam, uint8_t* Bout, int* redo, int check,
                              unsigned int* err_flag, int num_sms, cudaStream_t stream);
 
 struct RefineArgs {
