@@ -126,6 +126,27 @@ int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnor
 int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const float* xC_dev,
                   const uint8_t* B_dev, const float* a_dev, int64_t n, double* sse_dev, void* stream);
 
+/* Beam search like stlq_b200_beam_search, but the call allocates no device memory: no cudaMalloc,
+ * cudaFree or allocating library routine.  It exists for callers that cannot allocate while they
+ * encode, for example a service or framework whose caching allocator or memory pool owns all
+ * free device memory (an allocation would fail, or fragment and stall that pool), or a
+ * latency-critical path where an allocation's implicit device synchronisation is unacceptable.
+ * It has no counterpart in the reference.
+ *
+ * The beam search hands vectors whose exact errors tie at a selection boundary between its two
+ * kernels through a scratch list; here that list is a static device array sized for
+ * STLQ_B200_NOALLOC_MAX_VECTORS vectors (4 MiB, held by every GPU that loads the library until
+ * the process exits).  n above that limit is rejected with STLQ_B200_EINVAL; split such calls.
+ * The encoder handle (which allocates its codebook tables) and the inputs and outputs are the
+ * caller's, created beforehand.
+ * The first call on each device sets up that device (it looks up the array's device address and
+ * loads the beam kernels); make that first call before any stream capture.  All calls share the
+ * one array: each clears it before use, and calls whose work overlaps on the GPU (concurrent
+ * streams, several host threads) race and must not be issued. */
+#define STLQ_B200_NOALLOC_MAX_VECTORS (1 << 20)
+int stlq_b200_beam_search_noalloc(stlq_b200_encoder* enc, const float* xnorm2_dev, const float* xC_dev, int64_t n,
+                                  int beam, uint8_t* B_dev, void* stream);
+
 /* Block until all work this encoder enqueued on `stream` has finished; returns
  * STLQ_B200_EDEVICE if a kernel flagged an internal error since the last check. */
 int stlq_b200_sync(stlq_b200_encoder* enc, void* stream);

@@ -253,6 +253,25 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
 
 }  // namespace
 
+namespace stlq_b200 {
+
+// Internal accessors for entry points defined in other translation units.
+int GetBeamInputs(const stlq_b200_encoder* enc, BeamInputs* out) {
+    if (!enc) return Fail(STLQ_B200_EINVAL, "encoder handle is null");
+    out->dims = enc->dims;
+    out->Grow = enc->Grow.as<float>();
+    out->Gdiag = enc->Gdiag.as<float>();
+    out->err_flag = enc->err_flag.as<unsigned int>();
+    out->check_filter = enc->check_filter;
+    out->num_sms = enc->num_sms;
+    out->device = enc->device;
+    return 0;
+}
+
+int SetError(int code, const char* msg) { return Fail(code, msg); }
+
+}  // namespace stlq_b200
+
 extern "C" {
 
 const char* stlq_b200_last_error(void) { return g_last_error.c_str(); }

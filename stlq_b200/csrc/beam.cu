@@ -562,7 +562,22 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
     return cudaGetLastError();
 }
 
+template <int MAXM>
+cudaError_t PrepareT(const Dims& dims, int beam) {
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK);
+    cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(fsm));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(BeamReplayKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(rsm));
+}
+
 }  // namespace
+
+cudaError_t PrepareBeamKernels(const Dims& dims, int beam) {
+    return dims.m <= 8 ? PrepareT<8>(dims, beam) : PrepareT<16>(dims, beam);
+}
 
 // redo: n + 1 ints of scratch (a count, then vector ids handed from the fast to the replay kernel).
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,

@@ -44,6 +44,20 @@ cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, cons
                       const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
 int RefineWarpsPerBlock();
 
+// Loads both beam kernels and sets their shared-memory attributes (no launch).
+cudaError_t PrepareBeamKernels(const Dims& dims, int beam);
+
+// What the beam-search launch needs from an encoder handle (api.cpp).
+struct BeamInputs {
+    Dims dims;
+    const float* Grow;
+    const float* Gdiag;
+    unsigned int* err_flag;
+    int check_filter;
+    int num_sms;
+    int device;
+};
+
 cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream);
 cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream);
 cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream);

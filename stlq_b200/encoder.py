@@ -51,6 +51,7 @@ def load_library():
     lib.stlq_b200_xc_gemm.argtypes = [vp, vp, c_int, c_i64, vp, vp]
     lib.stlq_b200_xnorm2.argtypes = [vp, vp, c_int, c_i64, vp, vp]
     lib.stlq_b200_beam_search.argtypes = [vp, vp, vp, c_i64, c_int, vp, vp]
+    lib.stlq_b200_beam_search_noalloc.argtypes = [vp, vp, vp, c_i64, c_int, vp, vp]
     lib.stlq_b200_solve_ls.argtypes = [vp, vp, vp, c_i64, vp, vp]
     lib.stlq_b200_icm.argtypes = [vp, vp, vp, c_i64, c_int, c_int, c_int, c_int, c_u32, c_u64, vp, vp, vp, vp]
     lib.stlq_b200_sse.argtypes = [vp, vp, c_int, vp, vp, vp, c_i64, vp, vp]
@@ -191,6 +192,17 @@ class Encoder:
         B = torch.empty((xC.shape[0], self.m), dtype=torch.uint8, device=xC.device)
         _check(self.lib, self.lib.stlq_b200_beam_search(self.handle, _t_ptr(xnorm2), _t_ptr(xC), xC.shape[0], beam,
                                                         _t_ptr(B), self._stream(xC)), "stlq_b200_beam_search")
+        return B
+
+    def beam_search_noalloc(self, xnorm2, xC, beam: int, out=None):
+        """The same beam search through the entry point that allocates no device memory; ``out``
+        (uint8, n x m) may be supplied by callers that cannot let torch allocate either."""
+        import torch
+
+        B = torch.empty((xC.shape[0], self.m), dtype=torch.uint8, device=xC.device) if out is None else out
+        _check(self.lib, self.lib.stlq_b200_beam_search_noalloc(self.handle, _t_ptr(xnorm2), _t_ptr(xC), xC.shape[0],
+                                                                beam, _t_ptr(B), self._stream(xC)),
+               "stlq_b200_beam_search_noalloc")
         return B
 
     def solve_ls(self, xC, B):
