@@ -41,6 +41,7 @@ struct LayerTable {
     int n_slots;         // slots filled
     int redo;            // fast kernel: hand the vector to the replay kernel
     uint32_t tau_key[kWarps];
+    uint32_t mins[kWarps * kMaxBeam];  // each warp's B smallest per-thread upper bounds, sorted
     int n_surv;
     uint32_t key_b;
 };
@@ -336,19 +337,43 @@ template <typename ExactFn>
 __device__ int FastSelect(const float* lo, int n_cand, uint32_t hmin, int beam, LayerTable& lt, uint16_t* surv,
                           float* ex, int* rank, ExactFn exact) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Each warp sorts its 32 minima; only a warp's B smallest can be among the B smallest of all
+    // 128, so warp 0 ranks those 4B values and takes the B-th.
     const uint32_t sorted = WarpSortAsc(hmin);
-    const uint32_t tw = __shfl_sync(kFull, sorted, beam - 1);
-    if (lane == 0) lt.tau_key[warp] = tw;
+    if (lane < beam) lt.mins[warp * kMaxBeam + lane] = sorted;
     if (tid == 0) {
         lt.n_surv = 0;
         lt.n_slots = 0;
         lt.key_b = 0u;
     }
     __syncthreads();
-    uint32_t tk = lt.tau_key[0];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) tk = min(tk, lt.tau_key[w]);
-    // Fewer than B finite upper bounds in every warp: no pruning.
+    if (warp == 0) {
+        uint32_t tb = 0xffffffffu;
+        for (int i = lane; i < kWarps * beam; i += 32) {
+            const int w = i / beam, j = i % beam;
+            const uint32_t v = lt.mins[w * kMaxBeam + j];
+            // Rank of (v, list w) in the union ordered by (value, list): j in its own list plus,
+            // in every other sorted list, the entries before it (binary search).
+            int r = j;
+            for (int w2 = 0; w2 < kWarps; ++w2) {
+                if (w2 == w) continue;
+                int a = 0, b = beam;
+                while (a < b) {
+                    const int mid = (a + b) >> 1;
+                    const uint32_t u = lt.mins[w2 * kMaxBeam + mid];
+                    if (u < v || (u == v && w2 < w)) a = mid + 1;
+                    else b = mid;
+                }
+                r += a;
+            }
+            if (r == beam - 1) tb = v;
+        }
+        tb = __reduce_min_sync(kFull, tb);
+        if (lane == 0) lt.tau_key[0] = tb;
+    }
+    __syncthreads();
+    const uint32_t tk = lt.tau_key[0];
+    // Fewer than B finite upper bounds: no pruning.
     const float tau = tk >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tk);
     for (int idx = tid; idx < n_cand; idx += kThreads) {
         if (lo[idx] <= tau) {
@@ -403,19 +428,31 @@ __device__ int FastLayer(const Dims& dims, const SlotView<MAXM>& cur, const Slot
     uint32_t hmin = 0xffffffffu;
     for (int h = 0; h < curH; ++h) {
         const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
+        float l[kCpt], hi[kCpt];
+        // Both codewords' bounds first, stores after: the slot state they read stays in registers.
+#pragma unroll
+        for (int c = 0; c < kCpt; ++c) {
+            l[c] = PosInf();
+            hi[c] = PosInf();
+            if (tid + c * kThreads < K)
+                CheapBounds<MAXM, L>(cur, h, flat, Grow, H, offL + tid + c * kThreads, alpha[c], gamma[c], &l[c],
+                                     &hi[c]);
+        }
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) {
             const int k = tid + c * kThreads;
             if (k < K) {
-                float l, hi;
-                CheapBounds<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], &l, &hi);
-                lo[h * K + k] = l;
-                hmin = min(hmin, OrderKey(hi));
-                if (check) {  // self-check: the exact error must lie inside the bounds
-                    const float e = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], nullptr,
-                                                       nullptr, nullptr, nullptr);
-                    if (e < PosInf() && !(e >= l && e <= hi)) atomicOr(err_flag, kErrFilterMiss);
-                }
+                lo[h * K + k] = l[c];
+                hmin = min(hmin, OrderKey(hi[c]));
+            }
+        }
+        if (check) {  // self-check: the exact error must lie inside the bounds
+            for (int c = 0; c < kCpt; ++c) {
+                const int k = tid + c * kThreads;
+                if (k >= K) continue;
+                const float e = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], nullptr,
+                                                   nullptr, nullptr, nullptr);
+                if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
             }
         }
     }
@@ -457,7 +494,7 @@ __device__ int FastDispatch(int L, const Dims& dims, const SlotView<MAXM>& cur, 
 }
 
 template <int MAXM>
-__global__ void __launch_bounds__(kThreads) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
+__global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
                                                            const float* __restrict__ Gdiag,
                                                            const float* __restrict__ xnorm2,
                                                            const float* __restrict__ xC, int64_t n, int beam,
@@ -532,6 +569,9 @@ size_t ReplaySmemBytes(int beam, int maxK) {
 template <typename KernelT>
 cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* grid) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             static_cast<int>(cudaSharedmemCarveoutMaxShared));
     if (e != cudaSuccess) return e;
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
