@@ -327,6 +327,9 @@ def run_ours(args):
     xn = enc.xnorm2(X[:S])
     for _ in range(2):
         enc.beam_search(xn, xC, args.beam)
+    enc.beam_stats(reset=True)
+    enc.beam_search(xn, xC, args.beam)
+    beam_stats = enc.beam_stats(reset=True)
     reps = 3
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -392,6 +395,8 @@ def run_ours(args):
                          "frac": F_cand * S / beam_s / 1e12 / fp32_peak, "flops_per_vector": F_cand,
                          "peak_source": "cuBLAS SGEMM (TF32 off) measured in this run"},
                 "beam_ms_per_262144": beam_s * 1e3, "gemm_ms_per_262144": gemm_s * 1e3,
+                "beam_exact_per_layer": beam_stats["exact_per_layer"],
+                "beam_replayed_fraction": beam_stats["replayed_fraction"],
                 "gemm_tflops": F_gemm * S / gemm_s / 1e12,
                 "whole_job_fraction_of_2term_bound": value / world * max(t_gemm, t_hbm),
                 "whole_job_fraction_of_3term_bound": value / world * max(t_gemm, t_hbm, t_cand),

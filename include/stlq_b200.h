@@ -151,6 +151,12 @@ int stlq_b200_beam_search_noalloc(stlq_b200_encoder* enc, const float* xnorm2_de
  * STLQ_B200_EDEVICE if a kernel flagged an internal error since the last check. */
 int stlq_b200_sync(stlq_b200_encoder* enc, void* stream);
 
+/* Beam-search counters accumulated since the last reset (diagnostics, no counterpart in the
+ * reference): out[0] candidates evaluated exactly by the fast kernel, out[1] layers expanded,
+ * out[2] vectors, out[3] vectors handed to the slot-replay kernel (exact ties).  Synchronises the
+ * device; reset != 0 clears the counters. */
+int stlq_b200_beam_stats(stlq_b200_encoder* enc, uint64_t out[4], int reset);
+
 /* Shape queries. */
 int stlq_b200_dims(const stlq_b200_encoder* enc, int* d, int* m, int* H);
 

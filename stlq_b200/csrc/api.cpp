@@ -116,6 +116,10 @@ bool IsPinnedHost(const void* p) {
 
 size_t ElemSize(int x_dtype) { return x_dtype == STLQ_B200_U8 ? 1 : 4; }
 
+// Device flag word (kernels OR error bits into it) followed, at byte 16, by four 64-bit beam
+// counters: survivors evaluated exactly, layers, vectors, vectors handed to the replay kernel.
+constexpr size_t kFlagBytes = 64;
+
 }  // namespace
 
 struct stlq_b200_encoder {
@@ -321,7 +325,7 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     int rc = 0;
     if ((rc = enc->C.Ensure(sizeof(float) * H * d)) || (rc = enc->Gcol.Ensure(sizeof(float) * HH)) ||
         (rc = enc->Grow.Ensure(sizeof(float) * HH)) || (rc = enc->Gdiag.Ensure(sizeof(float) * H)) ||
-        (rc = enc->invnorm.Ensure(sizeof(float) * H)) || (rc = enc->err_flag.Ensure(sizeof(unsigned int))))
+        (rc = enc->invnorm.Ensure(sizeof(float) * H)) || (rc = enc->err_flag.Ensure(kFlagBytes)))
         return fail(rc);
     if (cudaStreamCreateWithFlags(&enc->compute, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&enc->copy, cudaStreamNonBlocking) != cudaSuccess)
@@ -356,7 +360,7 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     if (rc) return fail(rc);
     if ((rc = ck(stlq_b200::LaunchTranspose(enc->Gcol.as<float>(), enc->Grow.as<float>(), H, H, s), "transpose G")) ||
         (rc = ck(stlq_b200::LaunchDiag(enc->Gcol.as<float>(), enc->Gdiag.as<float>(), H, s), "diag G")) ||
-        (rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, sizeof(unsigned int), s), "memset")) ||
+        (rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, kFlagBytes, s), "memset")) ||
         (rc = ck(cudaStreamSynchronize(s), "create sync")))
         return fail(rc);
     *out = enc;
@@ -388,6 +392,16 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamDestroy(enc->compute);
     if (enc->copy) cudaStreamDestroy(enc->copy);
     delete enc;
+    return 0;
+}
+
+int stlq_b200_beam_stats(stlq_b200_encoder* enc, uint64_t out[4], int reset) {
+    STLQ_TRY(CheckEnc(enc));
+    if (!out) return Fail(STLQ_B200_EINVAL, "out is null");
+    DeviceScope scope(enc->device);
+    STLQ_CK(cudaDeviceSynchronize());
+    STLQ_CK(cudaMemcpy(out, static_cast<char*>(enc->err_flag.p) + 16, 4 * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    if (reset) STLQ_CK(cudaMemset(static_cast<char*>(enc->err_flag.p) + 16, 0, 4 * sizeof(uint64_t)));
     return 0;
 }
 

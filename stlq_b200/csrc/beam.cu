@@ -499,7 +499,8 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
                                                            const float* __restrict__ xnorm2,
                                                            const float* __restrict__ xC, int64_t n, int beam,
                                                            uint8_t* __restrict__ Bout, int* redo_list, int* redo_count,
-                                                           int check, unsigned int* err_flag) {
+                                                           int check, unsigned int* err_flag,
+                                                           unsigned long long* stats) {
     extern __shared__ __align__(16) unsigned char smem[];
     const size_t sv = SlotView<MAXM>::Bytes(beam);
     size_t off = (2 * sv + 15) & ~size_t(15);
@@ -511,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
     uint16_t* surv = reinterpret_cast<uint16_t*>(rank + kSurvCap);
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
+    unsigned long long n_surv = 0, n_layers = 0, n_vec = 0, n_redo = 0;  // thread 0's tallies
     for (int64_t vec = blockIdx.x; vec < n; vec += gridDim.x) {
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
@@ -539,16 +541,26 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
                                       SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo,
                                       lt, surv, ex, rank, check, err_flag);
             ci ^= 1;
+            n_surv += lt.n_surv;
+            ++n_layers;
         }
         const SlotView<MAXM> cur = SlotView<MAXM>::At(smem + ci * sv, beam);
         // Slots are sorted by (error, scan index): slot 0 is the pick unless the minimum is tied.
         const bool redo = curH < 0 || (curH >= 2 && OrderKey(cur.E[0]) == OrderKey(cur.E[1]));
+        ++n_vec;
+        n_redo += redo;
         if (redo) {
             if (tid == 0) redo_list[atomicAdd(redo_count, 1)] = static_cast<int>(vec);
         } else if (tid < m) {
             Bout[vec * m + tid] = static_cast<uint8_t>(cur.codeh(0)[tid]);
         }
         __syncthreads();
+    }
+    if (stats && tid == 0) {  // survivors evaluated exactly, layers, vectors, vectors handed to replay
+        atomicAdd(stats + 0, n_surv);
+        atomicAdd(stats + 1, n_layers);
+        atomicAdd(stats + 2, n_vec);
+        atomicAdd(stats + 3, n_redo);
     }
 }
 
@@ -582,8 +594,8 @@ cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* gr
 
 template <int MAXM>
 cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2, const float* xC,
-                        int64_t n, int beam, uint8_t* Bout, int* redo, int check, unsigned int* err_flag, int num_sms,
-                        cudaStream_t stream) {
+                        int64_t n, int beam, uint8_t* Bout, int* redo, int check, unsigned int* err_flag,
+                        unsigned long long* stats, int num_sms, cudaStream_t stream) {
     int grid = 0;
     const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
     cudaError_t e = Prepare(BeamFastKernel<MAXM>, fsm, num_sms, n, &grid);
@@ -591,7 +603,7 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
     e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
     BeamFastKernel<MAXM><<<grid, kThreads, fsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
-                                                          check, err_flag);
+                                                          check, err_flag, stats);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK);
@@ -624,9 +636,13 @@ cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* G
                              const float* xC, int64_t n, int beam, uint8_t* Bout, int* redo, int check,
                              unsigned int* err_flag, int num_sms, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
+    // The encoder's flag word is followed by four 64-bit counters (BeamStats).
+    unsigned long long* stats = err_flag ? reinterpret_cast<unsigned long long*>(err_flag + 4) : nullptr;
     if (dims.m <= 8)
-        return LaunchBeamT<8>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, num_sms, stream);
-    return LaunchBeamT<16>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, num_sms, stream);
+        return LaunchBeamT<8>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms,
+                              stream);
+    return LaunchBeamT<16>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms,
+                           stream);
 }
 
 }  // namespace stlq_b200

@@ -57,6 +57,7 @@ def load_library():
     lib.stlq_b200_sse.argtypes = [vp, vp, c_int, vp, vp, vp, c_i64, vp, vp]
     lib.stlq_b200_sync.argtypes = [vp, vp]
     lib.stlq_b200_dims.argtypes = [vp, vp, vp, vp]
+    lib.stlq_b200_beam_stats.argtypes = [vp, vp, c_int]
     _LIB = lib
     return lib
 
@@ -236,6 +237,15 @@ class Encoder:
         _check(self.lib, self.lib.stlq_b200_sse(self.handle, _t_ptr(X), _dtype_code(X), _t_ptr(xC), _t_ptr(B),
                                                 _t_ptr(a), X.shape[0], _t_ptr(out), self._stream(X)), "stlq_b200_sse")
         return out[1]
+
+    def beam_stats(self, reset: bool = True) -> dict:
+        """Beam counters since the last reset: exactly evaluated candidates, layers, vectors and
+        vectors resolved by the slot-replay kernel (exact ties)."""
+        out = np.zeros(4, np.uint64)
+        _check(self.lib, self.lib.stlq_b200_beam_stats(self.handle, _np_ptr(out), int(reset)), "stlq_b200_beam_stats")
+        s, layers, vecs, redo = (int(v) for v in out)
+        return {"exact_candidates": s, "layers": layers, "vectors": vecs, "replayed_vectors": redo,
+                "exact_per_layer": s / max(layers, 1), "replayed_fraction": redo / max(vecs, 1)}
 
     def sync(self, stream=None):
         import torch
