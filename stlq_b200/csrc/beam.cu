@@ -325,20 +325,17 @@ __device__ __forceinline__ uint32_t WarpSortAsc(uint32_t v) {
     return v;
 }
 
-// Selection shared by every layer of the fast kernel.  Inputs: lo[idx] (a lower bound of each
-// candidate's exact error; the exact error itself in layer 0) for idx < n_cand, and this thread's
-// smallest upper bound `hmin`.  Each warp's 32 per-thread minima belong to distinct candidates, so
-// the B-th smallest of them bounds the B-th smallest exact error from above: tau = the least such
-// bound over the warps.  Candidates with lo <= tau survive (everything else is provably larger
-// than the B-th smallest exact error), are evaluated exactly by `exact(idx)` and ranked by
-// (error, scan index).  Fills lt.cand with the B smallest and returns the slot count, or -1 when
-// the vector must go to the replay kernel (an exact tie at the boundary, or too many survivors).
-template <typename ExactFn>
-__device__ int FastSelect(const float* lo, int n_cand, uint32_t hmin, int beam, LayerTable& lt, uint16_t* surv,
-                          float* ex, int* rank, ExactFn exact) {
+// Selection shared by every layer of the fast kernel, out of line so that one copy serves every
+// layer.  Inputs: lo[idx] (a lower bound of each candidate's exact error; the exact error itself
+// in layer 0) and this thread's smallest upper bound `hmin`.  The 128 per-thread minima belong to
+// distinct candidates, so their B-th smallest, tau, bounds the B-th smallest exact error from
+// above; every candidate with lo <= tau is a survivor (all others are provably larger than the
+// B-th smallest exact error).  Returns the survivor count, or -1 when the list overflows.
+__device__ __noinline__ int SelectSurvivors(const float* lo, int n_cand, uint32_t hmin, int beam, LayerTable& lt,
+                                            uint16_t* surv) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Each warp sorts its 32 minima; only a warp's B smallest can be among the B smallest of all
-    // 128, so warp 0 ranks those 4B values and takes the B-th.
+    // 128, so warp 0 ranks those 4B values (binary search into the other sorted lists).
     const uint32_t sorted = WarpSortAsc(hmin);
     if (lane < beam) lt.mins[warp * kMaxBeam + lane] = sorted;
     if (tid == 0) {
@@ -352,8 +349,6 @@ __device__ int FastSelect(const float* lo, int n_cand, uint32_t hmin, int beam, 
         for (int i = lane; i < kWarps * beam; i += 32) {
             const int w = i / beam, j = i % beam;
             const uint32_t v = lt.mins[w * kMaxBeam + j];
-            // Rank of (v, list w) in the union ordered by (value, list): j in its own list plus,
-            // in every other sorted list, the entries before it (binary search).
             int r = j;
             for (int w2 = 0; w2 < kWarps; ++w2) {
                 if (w2 == w) continue;
@@ -373,8 +368,7 @@ __device__ int FastSelect(const float* lo, int n_cand, uint32_t hmin, int beam, 
     }
     __syncthreads();
     const uint32_t tk = lt.tau_key[0];
-    // Fewer than B finite upper bounds: no pruning.
-    const float tau = tk >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tk);
+    const float tau = tk >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tk);  // < B finite bounds: keep all
     for (int idx = tid; idx < n_cand; idx += kThreads) {
         if (lo[idx] <= tau) {
             const int p = atomicAdd(&lt.n_surv, 1);
@@ -383,9 +377,14 @@ __device__ int FastSelect(const float* lo, int n_cand, uint32_t hmin, int beam, 
     }
     __syncthreads();
     const int S = lt.n_surv;
-    if (S > kSurvCap) return -1;  // uniform: every thread read the same count
-    for (int p = tid; p < S; p += kThreads) ex[p] = exact(static_cast<int>(surv[p]));
-    __syncthreads();
+    return S > kSurvCap ? -1 : S;
+}
+
+// Ranks the S survivors by (exact error, scan index), fills lt.cand with the B smallest and returns
+// the slot count, or -1 when an exact tie sits at the selection boundary.
+__device__ __noinline__ int RankSurvivors(const float* ex, const uint16_t* surv, int S, int beam, LayerTable& lt,
+                                          int* rank) {
+    const int tid = threadIdx.x;
     int my_valid = 0;
     for (int p = tid; p < S; p += kThreads) {
         const uint32_t kp = OrderKey(ex[p]);
@@ -456,12 +455,16 @@ __device__ int FastLayer(const Dims& dims, const SlotView<MAXM>& cur, const Slot
             }
         }
     }
-    auto exact = [&](int idx) {
+    const int S = SelectSurvivors(lo, curH * K, hmin, beam, lt, surv);
+    if (S < 0) return -1;
+    for (int p = tid; p < S; p += kThreads) {
+        const int idx = surv[p];
         const int h = idx / K, k = idx - h * K;
-        return EvalExact<MAXM, L>(cur, h, FlatOf<MAXM, L>(dims, cur, h), Grow, H, offL + k, __ldg(Gdiag + offL + k),
-                                  __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
-    };
-    const int newH = FastSelect(lo, curH * K, hmin, beam, lt, surv, ex, rank, exact);
+        ex[p] = EvalExact<MAXM, L>(cur, h, FlatOf<MAXM, L>(dims, cur, h), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+                                   __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
+    }
+    __syncthreads();
+    const int newH = RankSurvivors(ex, surv, S, beam, lt, rank);
     if (newH < 0) return -1;
     if (newH == 0) {
         const int keep = KeepPrevious<MAXM, L>(cur, nxt, curH, beam);
@@ -527,7 +530,12 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
                 hmin = min(hmin, OrderKey(e1));
             }
         }
-        int curH = FastSelect(lo, K0, hmin, beam, lt, surv, ex, rank, [&](int idx) { return lo[idx]; });
+        int curH = SelectSurvivors(lo, K0, hmin, beam, lt, surv);
+        if (curH >= 0) {
+            for (int p = tid; p < curH; p += kThreads) ex[p] = lo[surv[p]];
+            __syncthreads();
+            curH = RankSurvivors(ex, surv, curH, beam, lt, rank);
+        }
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
         if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
         if (curH == 0) {

@@ -148,11 +148,12 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     }
     const float denom = alpha - delta;
     const float diff = gamma - eta;
-    const float r = __fdividef(diff * diff, denom);
+    const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
+    const float r = diff * diff * rden;
     const float Eo = cur.E[h];
     const float ep = fmaxf(Eo - r, 0.0f);
     constexpr float u = 1.2e-7f * (L + 2);
-    const float de = 2.0f * fabsf(diff) * (u * seta) / denom + fabsf(r) * (u * (alpha + delta)) / denom +
+    const float de = (2.0f * fabsf(diff) * (u * seta) + fabsf(r) * (u * (alpha + delta))) * fabsf(rden) +
                      1.2e-7f * (Eo + fabsf(r));
     const float w = 16.0f * de;
     const bool force = cur.ill[h] || !(denom > kDenomGuard * alpha) || !(w < PosInf()) || !(ep < PosInf());
