@@ -131,8 +131,10 @@ struct stlq_b200_encoder {
     int check_filter = 0;
     Dims dims{};
     DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
+    // Tensor-core modes: C_all split into TF32 hi / lo parts once at create.
+    DevBuf Chi, Clo;
     // Per-call scratch, grown on demand and kept for the handle's lifetime.
-    DevBuf xC, xn, xnd, partials, orders, redo;
+    DevBuf xC, xn, xnd, partials, orders, redo, Xhi, Xlo;
     std::vector<int> orders_host;
     int64_t orders_key[4] = {-1, -1, -1, -1};
     // Host path.
@@ -200,6 +202,31 @@ int UploadOrders(stlq_b200_encoder* enc, int icm_iters, int n_ils, uint32_t seed
     return 0;
 }
 
+bool TensorCoreMode(const stlq_b200_encoder* enc) { return enc->gemm_mode != STLQ_B200_GEMM_EXACT; }
+
+// xC (rows x n, ldo-strided per vector) and optional norms for n <= MaxGemmSliceVectors() vectors
+// in the encoder's GEMM mode.
+int LaunchXc(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int rows, float* out, int ldo, float* xn,
+             double* xnd, cudaStream_t stream) {
+    const int d = enc->dims.d;
+    if (!TensorCoreMode(enc)) {
+        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), rows, d, X, x_dtype, n, out, ldo, xn, xnd, stream));
+        return 0;
+    }
+    if (n <= 0) return 0;
+    const bool strict = enc->gemm_mode == STLQ_B200_GEMM_STRICT;
+    const size_t count = static_cast<size_t>(n) * d;
+    STLQ_TRY(enc->Xhi.Ensure(count * sizeof(float)));
+    if (strict) STLQ_TRY(enc->Xlo.Ensure(count * sizeof(float)));
+    float* xlo = strict ? enc->Xlo.as<float>() : nullptr;
+    STLQ_CK(stlq_b200::LaunchSplitTf32(X, x_dtype, static_cast<int64_t>(count), enc->Xhi.as<float>(), xlo, stream));
+    STLQ_CK(stlq_b200::LaunchXcGemmTc(enc->Chi.as<float>(), strict ? enc->Clo.as<float>() : nullptr, rows,
+                                      enc->Xhi.as<float>(), xlo, n, d, out, ldo, strict, enc->err_flag.as<unsigned int>(),
+                                      stream));
+    if (xn || xnd) STLQ_CK(stlq_b200::LaunchNorms(X, x_dtype, n, d, xn, xnd, stream));
+    return 0;
+}
+
 int EnsureScratch(stlq_b200_encoder* enc, int64_t slice) {
     STLQ_TRY(enc->xC.Ensure(static_cast<size_t>(slice) * enc->dims.H * sizeof(float)));
     STLQ_TRY(enc->xn.Ensure(static_cast<size_t>(slice) * sizeof(float)));
@@ -222,8 +249,8 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
     for (int64_t s0 = 0; s0 < n; s0 += S) {
         const int64_t ns = std::min(S, n - s0);
         const void* Xs = static_cast<const char*>(X) + static_cast<size_t>(s0) * dims.d * esz;
-        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), dims.H, dims.d, Xs, x_dtype, ns, enc->xC.as<float>(),
-                                             dims.H, enc->xn.as<float>(), enc->xnd.as<double>(), stream));
+        STLQ_TRY(LaunchXc(enc, Xs, x_dtype, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
+                          enc->xnd.as<double>(), stream));
         STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
                                             enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->redo.as<int>(),
                                             enc->check_filter,
@@ -289,8 +316,10 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     if (!h_vec || !C_all) return Fail(STLQ_B200_EINVAL, "h_vec and C_all must be non-null");
     if (d < 1) return Fail(STLQ_B200_EINVAL, "d must be >= 1");
     if (m < 1 || m > STLQ_B200_MAX_M) return Fail(STLQ_B200_EINVAL, "m must be in [1, 16]");
-    if (gemm_mode != STLQ_B200_GEMM_EXACT)
-        return Fail(STLQ_B200_EINVAL, "gemm_mode: only STLQ_B200_GEMM_EXACT is available in this build");
+    if (gemm_mode != STLQ_B200_GEMM_EXACT && gemm_mode != STLQ_B200_GEMM_STRICT && gemm_mode != STLQ_B200_GEMM_FAST)
+        return Fail(STLQ_B200_EINVAL, "gemm_mode must be STLQ_B200_GEMM_EXACT, _STRICT or _FAST");
+    if (gemm_mode != STLQ_B200_GEMM_EXACT && d % 4 != 0)
+        return Fail(STLQ_B200_EINVAL, "gemm_mode STRICT/FAST needs d to be a multiple of 4 (16-byte TMA rows)");
     Dims dims{};
     dims.d = d;
     dims.m = m;
@@ -352,6 +381,15 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
                 "G gemm");
     }
     if (rc) return fail(rc);
+    if (gemm_mode != STLQ_B200_GEMM_EXACT) {
+        const bool strict = gemm_mode == STLQ_B200_GEMM_STRICT;
+        if ((rc = enc->Chi.Ensure(sizeof(float) * H * d)) || (strict && (rc = enc->Clo.Ensure(sizeof(float) * H * d))))
+            return fail(rc);
+        rc = ck(stlq_b200::LaunchSplitTf32(enc->C.p, STLQ_B200_F32, static_cast<int64_t>(H) * d, enc->Chi.as<float>(),
+                                           strict ? enc->Clo.as<float>() : nullptr, s),
+                "split C_all");
+        if (rc) return fail(rc);
+    }
     if (invnorm) {
         rc = ck(cudaMemcpyAsync(enc->invnorm.p, invnorm, sizeof(float) * H, cudaMemcpyHostToDevice, s), "upload invnorm");
     } else {
@@ -373,7 +411,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
     for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
-                      &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
+                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
         enc->xin[i].Release();
@@ -421,7 +459,12 @@ int stlq_b200_sync(stlq_b200_encoder* enc, void* stream) {
     STLQ_CK(cudaMemcpy(&flag, enc->err_flag.p, sizeof(flag), cudaMemcpyDeviceToHost));
     if (flag) {
         cudaMemset(enc->err_flag.p, 0, sizeof(flag));
-        return Fail(STLQ_B200_EDEVICE, "a kernel reported internal error flags 0x" + std::to_string(flag));
+        std::string what;
+        if (flag & stlq_b200::kErrSurvivorOverflow) what += " beam-survivor-overflow";
+        if (flag & stlq_b200::kErrBadShape) what += " bad-shape";
+        if (flag & stlq_b200::kErrFilterMiss) what += " beam-filter-miss";
+        if (flag & stlq_b200::kErrWaitTimeout) what += " tensor-core-gemm-wait-timeout";
+        return Fail(STLQ_B200_EDEVICE, "a kernel reported internal errors:" + what);
     }
     return 0;
 }
@@ -532,10 +575,9 @@ int stlq_b200_xc_gemm(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, in
     const size_t esz = ElemSize(x_dtype);
     for (int64_t s0 = 0; s0 < n; s0 += S) {
         const int64_t ns = std::min(S, n - s0);
-        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), enc->dims.H, enc->dims.d,
-                                             static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
-                                             x_dtype, ns, xC_dev + s0 * enc->dims.H, enc->dims.H, nullptr, nullptr,
-                                             static_cast<cudaStream_t>(stream)));
+        STLQ_TRY(LaunchXc(enc, static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz, x_dtype,
+                          ns, enc->dims.H, xC_dev + s0 * enc->dims.H, enc->dims.H, nullptr, nullptr,
+                          static_cast<cudaStream_t>(stream)));
     }
     return 0;
 }

@@ -12,6 +12,16 @@ cudaError_t LaunchXcGemmExact(const float* C, int rows, int d, const void* X, in
                               int ldo, float* xnorm2, double* xnorm2_d, cudaStream_t stream);
 int MaxGemmSliceVectors();
 
+// Tensor-core (tcgen05) GEMM of the STRICT (split = true, 3xTF32) and FAST (1xTF32) modes.
+// A = rows x d and B = n x d row-major fp32 (hi parts; lo parts used when split); d % 4 == 0 and
+// 16-byte aligned bases (TMA); n <= 65535 * 128.  Bounded waits raise kErrWaitTimeout in *err.
+cudaError_t LaunchXcGemmTc(const float* a_hi, const float* a_lo, int rows, const float* b_hi, const float* b_lo,
+                           int64_t n, int d, float* out, int ldo, bool split, unsigned int* err, cudaStream_t stream);
+// hi = x rounded to TF32, lo = (x - hi) rounded to TF32 (lo may be null); x is F32 or U8.
+cudaError_t LaunchSplitTf32(const void* x, int x_dtype, int64_t count, float* hi, float* lo, cudaStream_t stream);
+// ||x||^2 per vector in float (the reference's 4-lane SIMD order) and in double; either may be null.
+cudaError_t LaunchNorms(const void* X, int x_dtype, int64_t n, int d, float* xn, double* xnd, cudaStream_t stream);
+
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
                              const float* xC, int64_t n, int beam, uint8_t* Bout, int* redo, int check,
                              unsigned int* err_flag, int num_sms, cudaStream_t stream);

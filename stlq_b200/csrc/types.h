@@ -17,6 +17,7 @@ enum DeviceError : unsigned int {
     kErrSurvivorOverflow = 1u << 0,
     kErrBadShape = 1u << 1,
     kErrFilterMiss = 1u << 2,  // self-check: a candidate the beam pre-filter dropped would have entered
+    kErrWaitTimeout = 1u << 3,  // a bounded barrier wait of the tensor-core GEMM ran out
 };
 
 // Encoder constants shared by every kernel, passed by value.

@@ -41,6 +41,9 @@ def test_version_and_empty_error():
     (2, [4, 257], 8, 0, b"h_vec[1]"),
     (2, [4, 0], 8, 0, b"h_vec[1]"),
     (2, [4, 4], 0, 0, b"d must be"),
+    (2, [4, 4], 8, 3, b"gemm_mode must be"),
+    (2, [4, 4], 6, 1, b"multiple of 4"),
+    (2, [4, 4], 10, 2, b"multiple of 4"),
 ])
 def test_create_rejects_bad_shapes(m, h, d, mode, msg):
     lib = stlq_b200.load_library()

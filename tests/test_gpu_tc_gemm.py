@@ -1,0 +1,103 @@
+"""GPU: the tensor-core GEMM modes (tcgen05, TMEM, TMA) against a float64 product.
+
+STLQ_B200_GEMM_STRICT (3xTF32) and STLQ_B200_GEMM_FAST (1xTF32) are accuracy modes, not
+bit-parity modes (STLQ_B200_GEMM_EXACT is the bit-identical one, covered by test_gpu_parity.py).
+Their bar is an error bound relative to sum_k |c_k x_k| per output element:
+  STRICT: 2e-5   (each product carries ~2^-21 relative error; FP32 accumulation over d <= 960)
+  FAST:   2e-3   (TF32 rounding of both operands, 2 * 2^-11 per product)
+The whole encode stage in STRICT mode must reproduce the exact mode's beam/final MSE to 1e-4
+relative on the reference's d=128 fixture.
+"""
+import numpy as np
+import pytest
+
+from conftest import have_cuda, load_case
+
+pytestmark = pytest.mark.gpu
+
+if have_cuda():
+    import torch
+
+TOL = {"strict": 2e-5, "fast": 2e-3}
+
+# (d, h_vec, n, input dtype): full tiles, ragged codeword/vector/K edges, long K, uint8 input.
+SHAPES = [
+    (128, [256] * 8, 1000, np.float32),
+    (100, [37, 256, 7], 333, np.float32),
+    (960, [256] * 4, 257, np.float32),
+    (4, [3], 5, np.float32),
+    (128, [256] * 2, 700, np.uint8),
+]
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not have_cuda():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def case(d, h_vec, n, dtype, seed):
+    rng = np.random.default_rng(seed)
+    H = int(sum(h_vec))
+    C = rng.standard_normal((H, d)).astype(np.float32)
+    if dtype == np.uint8:
+        X = rng.integers(0, 256, size=(n, d), dtype=np.uint8)
+    else:
+        X = (rng.standard_normal((n, d)) * 3.0).astype(np.float32)
+    return C, X
+
+
+@pytest.mark.parametrize("mode", ["strict", "fast"])
+@pytest.mark.parametrize("shape", range(len(SHAPES)))
+def test_tc_gemm_error_bound(cuda, mode, shape):
+    import stlq_b200
+
+    d, h_vec, n, dtype = SHAPES[shape]
+    C, X = case(d, h_vec, n, dtype, 1000 + shape)
+    enc = stlq_b200.Encoder(C, np.array(h_vec, np.int32), device=0, gemm_mode=mode)
+    ref_enc = stlq_b200.Encoder(C, np.array(h_vec, np.int32), device=0, gemm_mode="exact")
+    Xt = torch.from_numpy(X).to(cuda)
+    xc = enc.xc_gemm(Xt)
+    xc_exact = ref_enc.xc_gemm(Xt)
+    enc.sync()
+    ref_enc.sync()
+    X64 = X.astype(np.float64)
+    ref = X64 @ C.astype(np.float64).T
+    scale = np.abs(X64) @ np.abs(C.astype(np.float64)).T
+    scale = np.maximum(scale, 1e-30)
+    err = np.abs(xc.cpu().numpy().astype(np.float64) - ref) / scale
+    err_exact = np.abs(xc_exact.cpu().numpy().astype(np.float64) - ref) / scale
+    print(f"mode={mode} d={d} H={sum(h_vec)} n={n}: max rel err {err.max():.3e} (exact GEMM {err_exact.max():.3e})")
+    assert np.isfinite(err).all()
+    assert err.max() <= TOL[mode], f"{mode} GEMM error {err.max():.3e} above {TOL[mode]:.0e}"
+    # The norms of the tensor-core modes come from their own kernel, in the reference's order.
+    assert np.array_equal(enc.xnorm2(Xt).cpu().numpy(), ref_enc.xnorm2(Xt).cpu().numpy())
+
+
+def test_tc_gemm_two_calls_in_a_row_identical(cuda):
+    import stlq_b200
+
+    C, X = case(128, [256] * 8, 4096, np.float32, 7)
+    enc = stlq_b200.Encoder(C, np.array([256] * 8, np.int32), device=0, gemm_mode="strict")
+    Xt = torch.from_numpy(X).to(cuda)
+    a = enc.xc_gemm(Xt).cpu().numpy()
+    b = enc.xc_gemm(Xt).cpu().numpy()
+    enc.sync()
+    assert np.array_equal(a, b), "tensor-core GEMM is not deterministic"
+
+
+@pytest.mark.parametrize("mode,tol", [("strict", 1e-4), ("fast", 2e-2)])
+def test_tc_encode_matches_exact_mode(cuda, mode, tol):
+    import stlq_b200
+
+    c = load_case("d128_m8_k256_b16")
+    args = (c["beam"], c["icm_iters"], c["ils_iters"], c["perturb_k"], bool(c["use_abs"]), c["seed"])
+    ex = stlq_b200.Encoder(c["C_all"], c["h_vec"], device=0, gemm_mode="exact").encode_base(c["X"], *args)
+    tc = stlq_b200.Encoder(c["C_all"], c["h_vec"], device=0, gemm_mode=mode).encode_base(c["X"], *args)
+    same = float((tc["B"] == ex["B"]).all(axis=1).mean())
+    print(f"{mode}: codes identical for {same:.3%} of vectors; beam mse {tc['beam_mse']:.6g} vs {ex['beam_mse']:.6g}; "
+          f"final {tc['final_mse']:.6g} vs {ex['final_mse']:.6g}")
+    assert np.array_equal(ex["B"], c["B"])
+    assert abs(tc["beam_mse"] - ex["beam_mse"]) <= tol * ex["beam_mse"]
+    assert abs(tc["final_mse"] - ex["final_mse"]) <= tol * ex["final_mse"]
