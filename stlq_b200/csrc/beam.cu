@@ -18,11 +18,14 @@
 // BeamFastKernel uses that: per layer it bounds every candidate's exact error from a cheap
 // evaluation (beam::CheapBounds), takes tau = a value below which B candidates provably lie,
 // evaluates exactly only the candidates whose lower bound is <= tau, and selects the B smallest
-// exact errors.  When an exact tie sits at the boundary (or at the final minimum), or the survivor
-// list would overflow, the vector is handed to BeamReplayKernel.
+// exact errors (its slots hold them in ascending (error, scan index) order).  When an exact tie
+// sits at the boundary (or at the final minimum), or the survivor list would overflow, the vector
+// is handed to BeamReplayKernel.
 //
 // BeamReplayKernel evaluates every candidate exactly and replays the reference's replacement
 // scan itself (warp 0, slots one per lane), so ties resolve exactly as in the reference.
+//
+// The layer index is a run-time argument of every routine (see beam_common.cuh).
 #include <cstdint>
 
 #include "beam_common.cuh"
@@ -35,47 +38,73 @@ using namespace beam;
 namespace {
 
 constexpr int kSurvCap = 512;  // exactly evaluated survivors per layer in the fast kernel
+constexpr int kKeep = 64;      // survivors whose exact-evaluation results are kept for Materialize
+
+// Per kept survivor: y[MAXM], v[MAXM], denom, a_last.
+template <int MAXM>
+__host__ __device__ constexpr int KeepStride() { return 2 * MAXM + 2; }
 
 struct LayerTable {
-    int cand[kMaxBeam];  // candidate (scan index) held by each slot, slot order
-    int n_slots;         // slots filled
-    int redo;            // fast kernel: hand the vector to the replay kernel
-    uint32_t tau_key[kWarps];
-    uint32_t mins[kWarps * kMaxBeam];  // each warp's B smallest per-thread upper bounds, sorted
+    int cand[kMaxBeam];   // candidate (scan index) held by each slot, slot order
+    int candp[kMaxBeam];  // fast kernel: the winner's position in the survivor list
+    int n_slots;          // slots filled
     int n_surv;
-    uint32_t key_b;
+    uint32_t key_b;       // fast kernel: error keys ranked B-1 and B (boundary tie test)
+    uint32_t key_n;
+    int wsum[kWarps];     // survivors found by each warp
+    uint32_t mins[kWarps * kMaxBeam];  // each warp's B smallest per-thread upper bounds, sorted
 };
 
 // Copies the winners' state into the next slot buffer (beam_search.cpp:337-383): parent prefix of
 // R, then each winner's own R column (y, sqrt(denom)), coefficients a_t - v_t a_last, a_last, code.
-template <int MAXM, int L>
-__device__ void Materialize(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt,
+// With `keep` (fast kernel) a winner whose survivor position is below kKeep takes y, v, denom,
+// a_last and its error from the exact evaluation already made; otherwise they are recomputed.
+template <int MAXM>
+__device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt,
                             const LayerTable& lt, int newH, const float* __restrict__ Grow,
-                            const float* __restrict__ Gdiag, const float* __restrict__ xc) {
+                            const float* __restrict__ Gdiag, const float* __restrict__ xc,
+                            const float* keep = nullptr, const float* ex = nullptr) {
+    constexpr int NL = MAXM - 1;
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
-    for (int e = tid; e < newH * L * L; e += kThreads) {
-        const int o = e / (L * L), rc = e % (L * L), r = rc / L, c = rc % L;
-        if (r <= c) nxt.Rh(o)[r * MAXM + c] = cur.Rh(lt.cand[o] / K)[r * MAXM + c];
+    // R prefix of each winner's parent: rows r <= c < L, one (winner, column) pair per thread.
+    for (int e = tid; e < newH * L; e += kThreads) {
+        const int o = e / L, c = e - o * L;
+        const float* src = cur.Rh(lt.cand[o] / K) + c * MAXM;
+        float* dst = nxt.Rh(o) + c * MAXM;
+        for (int r = 0; r <= c; ++r) dst[r] = src[r];
     }
     if (tid < newH) {
         const int o = tid;
         const int idx = lt.cand[o];
         const int h = idx / K, k = idx - h * K;
-        const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
-        float y[L], v[L], denom, a_last;
+        float y[NL], v[NL], denom, a_last, e;
         const float ak = __ldg(Gdiag + offL + k);
-        const float e =
-            EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, ak, __ldg(xc + offL + k), y, v, &denom, &a_last);
+        const int p = keep ? lt.candp[o] : kKeep;
+        if (p < kKeep) {
+            const float* st = keep + p * KeepStride<MAXM>();
 #pragma unroll
-        for (int t = 0; t < L; ++t) {
-            nxt.codeh(o)[t] = cur.codeh(h)[t];
+            for (int t = 0; t < NL; ++t) {
+                y[t] = st[t];
+                v[t] = st[MAXM + t];
+            }
+            denom = st[2 * MAXM];
+            a_last = st[2 * MAXM + 1];
+            e = ex[p];
+        } else {
+            e = EvalExactL<MAXM>(cur, h, L, FlatOf<MAXM>(cur, h, L), Grow, H, offL + k, ak,
+                                 __ldg(xc + offL + k), y, v, &denom, &a_last);
+        }
+#pragma unroll
+        for (int t = 0; t < NL; ++t) {
+            if (t >= L) break;
+            nxt.flath(o)[t] = cur.flath(h)[t];
             nxt.ah(o)[t] = sub_rn(cur.ah(h)[t], mul_rn(v[t], a_last));
-            nxt.Rh(o)[t * MAXM + L] = y[t];
+            nxt.Rh(o)[L * MAXM + t] = y[t];
             nxt.rinvh(o)[t] = cur.rinvh(h)[t];
         }
         const float rll = __fsqrt_rn(denom);
-        nxt.codeh(o)[L] = k;
+        nxt.flath(o)[L] = offL + k;
         nxt.ah(o)[L] = a_last;
         nxt.Rh(o)[L * MAXM + L] = rll;
         nxt.rinvh(o)[L] = __frcp_rn(rll);
@@ -85,15 +114,16 @@ __device__ void Materialize(const Dims& dims, const SlotView<MAXM>& cur, const S
 }
 
 // No finite candidate in a layer (beam_search.cpp:385-400): the previous slots are kept.  The code
-// of this layer is written as 0; the reference copies a stale buffer value there.
-template <int MAXM, int L>
-__device__ int KeepPrevious(const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH, int beam) {
+// of this layer is written as 0 (flat index offL); the reference copies a stale buffer value there.
+template <int MAXM>
+__device__ int KeepPrevious(int L, int offL, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
+                            int beam) {
     const int tid = threadIdx.x;
     const int keep = min(curH, beam);
     for (int e = tid; e < keep * MAXM * MAXM; e += kThreads) nxt.R[e] = cur.R[e];
     for (int e = tid; e < keep * MAXM; e += kThreads) {
         const int t = e % MAXM;
-        nxt.code[e] = t < L ? cur.code[e] : 0;
+        nxt.flat[e] = t < L ? cur.flat[e] : offL;
         nxt.a[e] = t < L ? cur.a[e] : 0.0f;
         nxt.rinv[e] = cur.rinv[e];
     }
@@ -111,7 +141,7 @@ __device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, const float* Gd
     const float gamma = __ldg(xc + k);
     const float a1 = div_rn(gamma, alpha);
     const float r00 = __fsqrt_rn(alpha);
-    s.codeh(o)[0] = k;
+    s.flath(o)[0] = k;  // layer 0 starts at flat index 0
     s.ah(o)[0] = a1;
     s.E[o] = sub_rn(nx2, mul_rn(gamma, a1));
     s.Rh(o)[0] = r00;
@@ -123,10 +153,10 @@ __device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, const float* Gd
 // layer (each later candidate is then non-finite and the fallback keeps the slot), ending with
 // code 0 in every layer.
 template <int MAXM>
-__device__ void DeadSlot0(const SlotView<MAXM>& s) {
+__device__ void DeadSlot0(const Dims& dims, const SlotView<MAXM>& s) {
     const int tid = threadIdx.x;
     if (tid < MAXM) {
-        s.codeh(0)[tid] = 0;
+        s.flath(0)[tid] = tid < dims.m ? dims.off[tid] : 0;
         s.ah(0)[tid] = 0.0f;
         s.rinvh(0)[tid] = 0.0f;
     }
@@ -195,8 +225,8 @@ struct Replay {
     }
 };
 
-template <int MAXM, int L>
-__device__ void ReplayLayer(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
+template <int MAXM>
+__device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                             const float* __restrict__ xc, int beam, float* errs, LayerTable& lt) {
     const int tid = threadIdx.x;
@@ -209,13 +239,13 @@ __device__ void ReplayLayer(const Dims& dims, const SlotView<MAXM>& cur, const S
         gamma[c] = k < K ? __ldg(xc + offL + k) : 0.0f;
     }
     for (int h = 0; h < curH; ++h) {
-        const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
+        const FlatArr<MAXM> flat = FlatOf<MAXM>(cur, h, L);
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) {
             const int k = tid + c * kThreads;
             if (k < K)
-                errs[h * K + k] = EvalExact<MAXM, L>(cur, h, flat, Grow, dims.H, offL + k, alpha[c], gamma[c],
-                                                     nullptr, nullptr, nullptr, nullptr);
+                errs[h * K + k] = EvalExactL<MAXM>(cur, h, L, flat, Grow, dims.H, offL + k, alpha[c], gamma[c],
+                                                   nullptr, nullptr, nullptr, nullptr);
         }
     }
     __syncthreads();
@@ -228,29 +258,12 @@ __device__ void ReplayLayer(const Dims& dims, const SlotView<MAXM>& cur, const S
     __syncthreads();
     const int newH = lt.n_slots;
     if (newH == 0) {
-        curH = KeepPrevious<MAXM, L>(cur, nxt, curH, beam);
+        curH = KeepPrevious<MAXM>(L, offL, cur, nxt, curH, beam);
     } else {
-        Materialize<MAXM, L>(dims, cur, nxt, lt, newH, Grow, Gdiag, xc);
+        Materialize<MAXM>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc);
         curH = newH;
     }
     __syncthreads();
-}
-
-template <int MAXM>
-__device__ void ReplayDispatch(int L, const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
-                               const float* Grow, const float* Gdiag, const float* xc, int beam, float* errs,
-                               LayerTable& lt) {
-#define STLQ_B200_REPLAY(LL)                                                                    \
-    case LL:                                                                                    \
-        if constexpr (LL < MAXM) ReplayLayer<MAXM, LL>(dims, cur, nxt, curH, Grow, Gdiag, xc, beam, errs, lt); \
-        break;
-    switch (L) {
-        STLQ_B200_REPLAY(1) STLQ_B200_REPLAY(2) STLQ_B200_REPLAY(3) STLQ_B200_REPLAY(4) STLQ_B200_REPLAY(5)
-        STLQ_B200_REPLAY(6) STLQ_B200_REPLAY(7) STLQ_B200_REPLAY(8) STLQ_B200_REPLAY(9) STLQ_B200_REPLAY(10)
-        STLQ_B200_REPLAY(11) STLQ_B200_REPLAY(12) STLQ_B200_REPLAY(13) STLQ_B200_REPLAY(14) STLQ_B200_REPLAY(15)
-        default: break;
-    }
-#undef STLQ_B200_REPLAY
 }
 
 // Encodes the vectors listed in vec_list[0 .. *count) (or 0 .. n when vec_list is null).
@@ -286,14 +299,14 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
         if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
         if (curH == 0) {
-            DeadSlot0<MAXM>(s0);
+            DeadSlot0<MAXM>(dims, s0);
             curH = 1;
         }
         __syncthreads();
         int ci = 0;
         for (int L = 1; L < m; ++L) {
-            ReplayDispatch<MAXM>(L, dims, SlotView<MAXM>::At(smem + ci * sv, beam),
-                                 SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, lt);
+            ReplayLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
+                              SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, lt);
             ci ^= 1;
         }
         if (tid < 32) {  // first slot with the smallest error (beam_search.cpp:409-416)
@@ -301,7 +314,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
             const uint32_t key = tid < curH ? OrderKey(cur.E[tid]) : 0xffffffffu;
             const uint32_t kmin = __reduce_min_sync(kFull, key);
             const int best = __ffs(__ballot_sync(kFull, key == kmin)) - 1;
-            if (tid < m) Bout[vec * m + tid] = static_cast<uint8_t>(cur.codeh(best)[tid]);
+            if (tid < m) Bout[vec * m + tid] = static_cast<uint8_t>(cur.flath(best)[tid] - dims.off[tid]);
         }
         __syncthreads();
     }
@@ -327,177 +340,229 @@ __device__ __forceinline__ uint32_t WarpSortAsc(uint32_t v) {
 
 // Selection shared by every layer of the fast kernel, out of line so that one copy serves every
 // layer.  Inputs: lo[idx] (a lower bound of each candidate's exact error; the exact error itself
-// in layer 0) and this thread's smallest upper bound `hmin`.  The 128 per-thread minima belong to
-// distinct candidates, so their B-th smallest, tau, bounds the B-th smallest exact error from
-// above; every candidate with lo <= tau is a survivor (all others are provably larger than the
-// B-th smallest exact error).  Returns the survivor count, or -1 when the list overflows.
+// in layer 0; 16-byte aligned) and this thread's smallest upper bound `hmin`.  The 128 per-thread
+// minima belong to distinct candidates, so their B-th smallest, tau, bounds the B-th smallest
+// exact error from above; every candidate with lo <= tau is a survivor (all others are provably
+// larger than the B-th smallest exact error).  Returns the survivor count, or -1 when the list
+// overflows.
 __device__ __noinline__ int SelectSurvivors(const float* lo, int n_cand, uint32_t hmin, int beam, LayerTable& lt,
                                             uint16_t* surv) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Each warp sorts its 32 minima; only a warp's B smallest can be among the B smallest of all
-    // 128, so warp 0 ranks those 4B values (binary search into the other sorted lists).
+    // 128, so ranking those 4B values (binary search into the other sorted lists) finds tau.  Every
+    // warp does it, so tau needs no second barrier.
     const uint32_t sorted = WarpSortAsc(hmin);
     if (lane < beam) lt.mins[warp * kMaxBeam + lane] = sorted;
-    if (tid == 0) {
-        lt.n_surv = 0;
-        lt.n_slots = 0;
-        lt.key_b = 0u;
-    }
     __syncthreads();
-    if (warp == 0) {
-        uint32_t tb = 0xffffffffu;
-        for (int i = lane; i < kWarps * beam; i += 32) {
-            const int w = i / beam, j = i % beam;
-            const uint32_t v = lt.mins[w * kMaxBeam + j];
-            int r = j;
-            for (int w2 = 0; w2 < kWarps; ++w2) {
-                if (w2 == w) continue;
-                int a = 0, b = beam;
-                while (a < b) {
-                    const int mid = (a + b) >> 1;
-                    const uint32_t u = lt.mins[w2 * kMaxBeam + mid];
-                    if (u < v || (u == v && w2 < w)) a = mid + 1;
-                    else b = mid;
-                }
-                r += a;
+    uint32_t tb = 0xffffffffu;
+    for (int i = lane; i < kWarps * beam; i += 32) {
+        const int w = i / beam, j = i - w * beam;
+        const uint32_t v = lt.mins[w * kMaxBeam + j];
+        int r = j;
+        for (int w2 = 0; w2 < kWarps; ++w2) {
+            if (w2 == w) continue;
+            int a = 0, b = beam;
+            while (a < b) {
+                const int mid = (a + b) >> 1;
+                const uint32_t u = lt.mins[w2 * kMaxBeam + mid];
+                if (u < v || (u == v && w2 < w)) a = mid + 1;
+                else b = mid;
             }
-            if (r == beam - 1) tb = v;
+            r += a;
         }
-        tb = __reduce_min_sync(kFull, tb);
-        if (lane == 0) lt.tau_key[0] = tb;
+        if (r == beam - 1) tb = v;
+    }
+    tb = __reduce_min_sync(kFull, tb);
+    const float tau = tb >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tb);  // < B finite bounds: keep all
+    // Count this thread's survivors (four candidates per 128-bit load), scan the counts across the
+    // block, then write the survivors at their offsets.
+    const float4* lo4 = reinterpret_cast<const float4*>(lo);
+    const int n4 = n_cand >> 2;
+    int cnt = 0;
+    for (int c = tid; c < n4; c += kThreads) {
+        const float4 v = lo4[c];
+        cnt += (v.x <= tau) + (v.y <= tau) + (v.z <= tau) + (v.w <= tau);
+    }
+    for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads) cnt += lo[idx] <= tau;
+    int incl = cnt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(kFull, incl, d);
+        if (lane >= d) incl += o;
+    }
+    if (lane == 31) lt.wsum[warp] = incl;
+    __syncthreads();
+    int base = 0, S = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        const int ws = lt.wsum[w];
+        base += w < warp ? ws : 0;
+        S += ws;
+    }
+    if (S <= kSurvCap && cnt > 0) {
+        int p = base + incl - cnt;
+        for (int c = tid; c < n4; c += kThreads) {
+            const float4 v = lo4[c];
+            if (v.x <= tau) surv[p++] = static_cast<uint16_t>(4 * c);
+            if (v.y <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 1);
+            if (v.z <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 2);
+            if (v.w <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 3);
+        }
+        for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads)
+            if (lo[idx] <= tau) surv[p++] = static_cast<uint16_t>(idx);
     }
     __syncthreads();
-    const uint32_t tk = lt.tau_key[0];
-    const float tau = tk >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tk);  // < B finite bounds: keep all
-    for (int idx = tid; idx < n_cand; idx += kThreads) {
-        if (lo[idx] <= tau) {
-            const int p = atomicAdd(&lt.n_surv, 1);
-            if (p < kSurvCap) surv[p] = static_cast<uint16_t>(idx);
-        }
-    }
-    __syncthreads();
-    const int S = lt.n_surv;
+    if (tid == 0) lt.n_surv = S;
     return S > kSurvCap ? -1 : S;
 }
 
-// Ranks the S survivors by (exact error, scan index), fills lt.cand with the B smallest and returns
-// the slot count, or -1 when an exact tie sits at the selection boundary.
+// Survivor sort key: (error, scan index, survivor position); the scan index makes it unique.
+__device__ __forceinline__ uint64_t SurvKey(float e, int idx, int p) {
+    return (static_cast<uint64_t>(OrderKey(e)) << 32) | (static_cast<uint32_t>(idx) << 9) | static_cast<uint32_t>(p);
+}
+
+// Ranks the S survivors by (exact error, scan index) and fills lt.cand / lt.candp with the B
+// smallest in that order.  Returns the slot count, or -1 when an exact tie sits at the selection
+// boundary.  keys: kSurvCap 64-bit words of scratch.
 __device__ __noinline__ int RankSurvivors(const float* ex, const uint16_t* surv, int S, int beam, LayerTable& lt,
-                                          int* rank) {
+                                          uint64_t* keys) {
     const int tid = threadIdx.x;
+    constexpr uint64_t kInvalid = static_cast<uint64_t>(0xff800000u) << 32;  // OrderKey(+inf)
+    for (int p = tid; p < S; p += kThreads) keys[p] = SurvKey(ex[p], surv[p], p);
+    if (tid == 0) {
+        lt.n_slots = 0;
+        lt.key_b = 0u;
+        lt.key_n = 1u;
+    }
+    __syncthreads();
     int my_valid = 0;
     for (int p = tid; p < S; p += kThreads) {
-        const uint32_t kp = OrderKey(ex[p]);
-        const uint64_t cp = (static_cast<uint64_t>(kp) << 32) | surv[p];
+        const uint64_t kp = keys[p];
         int r = 0;
-        for (int q = 0; q < S; ++q) r += ((static_cast<uint64_t>(OrderKey(ex[q])) << 32) | surv[q]) < cp;
-        rank[p] = r;
-        const bool valid = ex[p] < PosInf();
+        for (int q = 0; q < S; ++q) r += keys[q] < kp;
+        const bool valid = kp < kInvalid;
         my_valid += valid;
-        if (valid && r < beam) lt.cand[r] = surv[p];
-        if (valid && r == beam - 1) lt.key_b = kp;
+        if (valid && r < beam) {
+            lt.cand[r] = static_cast<int>(static_cast<uint32_t>(kp) >> 9);
+            lt.candp[r] = p;
+        }
+        if (r == beam - 1) lt.key_b = static_cast<uint32_t>(kp >> 32);
+        if (r == beam) lt.key_n = static_cast<uint32_t>(kp >> 32);
     }
     if (my_valid) atomicAdd(&lt.n_slots, my_valid);
     __syncthreads();
     const int n_valid = lt.n_slots;
-    if (n_valid > beam) {
-        // Tie at the boundary: another survivor with the B-th smallest error's exact value.
-        const uint32_t kb = lt.key_b;
-        int tie = 0;
-        for (int p = tid; p < S; p += kThreads) tie |= (rank[p] >= beam && OrderKey(ex[p]) == kb);
-        if (__syncthreads_or(tie)) return -1;
-    }
+    // Tie at the boundary: the survivor ranked B has the B-th smallest error's exact value.
+    if (n_valid > beam && lt.key_b == lt.key_n) return -1;
     return min(n_valid, beam);
 }
 
+// Self-check of the cheap bounds (STLQ_B200_CHECK_FILTER): the exact error of each candidate must
+// lie inside them; a miss raises kErrFilterMiss.  Inlined: a call site inside the hot loop, even
+// one never taken, costs the loop registers.
+template <int MAXM>
+__device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int H,
+                                         const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
+                                         const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
+                                         unsigned int* err_flag) {
+    const FlatArr<MAXM> flat = FlatOf<MAXM>(cur, h, L);
+    for (int c = 0; c < kCpt; ++c) {
+        if (!ok[c]) continue;
+        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, H, col[c], alpha[c], gamma[c], nullptr, nullptr,
+                                         nullptr, nullptr);
+        if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
+    }
+}
+
+// The cheap pass of layer L over every live slot: lower bounds into lo[h * K + k], and the
+// thread's smallest upper bound as the return value.  One copy per layer, inlined (with L a
+// compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
+// call boundary costs more than the copies save).
 template <int MAXM, int L>
-__device__ int FastLayer(const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
-                         const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
-                         int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, int* rank, int check,
-                         unsigned int* err_flag) {
+__device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int H,
+                                           const float* __restrict__ Grow, const float* __restrict__ Gdiag,
+                                           const float* __restrict__ xc, float* lo, int check,
+                                           unsigned int* err_flag) {
     const int tid = threadIdx.x;
-    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
     float alpha[kCpt], gamma[kCpt];
+    int col[kCpt];
+    bool ok[kCpt];
 #pragma unroll
     for (int c = 0; c < kCpt; ++c) {
         const int k = tid + c * kThreads;
-        alpha[c] = k < K ? __ldg(Gdiag + offL + k) : 0.0f;
-        gamma[c] = k < K ? __ldg(xc + offL + k) : 0.0f;
+        ok[c] = k < K;
+        col[c] = offL + k;
+        alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
+        gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
     }
     uint32_t hmin = 0xffffffffu;
     for (int h = 0; h < curH; ++h) {
-        const FlatArr<MAXM> flat = FlatOf<MAXM, L>(dims, cur, h);
         float l[kCpt], hi[kCpt];
-        // Both codewords' bounds first, stores after: the slot state they read stays in registers.
+        CheapBounds<MAXM, L>(cur, h, Grow, H, col, ok, alpha, gamma, l, hi);
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) {
-            l[c] = PosInf();
-            hi[c] = PosInf();
-            if (tid + c * kThreads < K)
-                CheapBounds<MAXM, L>(cur, h, flat, Grow, H, offL + tid + c * kThreads, alpha[c], gamma[c], &l[c],
-                                     &hi[c]);
-        }
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            const int k = tid + c * kThreads;
-            if (k < K) {
-                lo[h * K + k] = l[c];
+            if (ok[c]) {
+                lo[h * K + tid + c * kThreads] = l[c];
                 hmin = min(hmin, OrderKey(hi[c]));
             }
         }
-        if (check) {  // self-check: the exact error must lie inside the bounds
-            for (int c = 0; c < kCpt; ++c) {
-                const int k = tid + c * kThreads;
-                if (k >= K) continue;
-                const float e = EvalExact<MAXM, L>(cur, h, flat, Grow, H, offL + k, alpha[c], gamma[c], nullptr,
-                                                   nullptr, nullptr, nullptr);
-                if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
-            }
-        }
+        if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag);
     }
+    return hmin;
+}
+
+template <int MAXM>
+__device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int H,
+                                  const float* Grow, const float* Gdiag, const float* xc, float* lo, int check,
+                                  unsigned int* err) {
+#define STLQ_B200_CHEAP(LL)                                                                                   \
+    case LL:                                                                                                  \
+        if constexpr (LL < MAXM) return CheapPass<MAXM, LL>(cur, curH, K, offL, H, Grow, Gdiag, xc, lo, check, err); \
+        break;
+    switch (L) {
+        STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
+        STLQ_B200_CHEAP(6) STLQ_B200_CHEAP(7) STLQ_B200_CHEAP(8) STLQ_B200_CHEAP(9) STLQ_B200_CHEAP(10)
+        STLQ_B200_CHEAP(11) STLQ_B200_CHEAP(12) STLQ_B200_CHEAP(13) STLQ_B200_CHEAP(14) STLQ_B200_CHEAP(15)
+        default: break;
+    }
+#undef STLQ_B200_CHEAP
+    return 0u;  // unreachable: 1 <= L < m <= MAXM
+}
+
+template <int MAXM>
+__device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
+                         const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
+                         int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, uint64_t* keys, float* keep,
+                         int check, unsigned int* err_flag) {
+    const int tid = threadIdx.x;
+    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    const uint32_t hmin = CheapDispatch<MAXM>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, lo, check, err_flag);
     const int S = SelectSurvivors(lo, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     for (int p = tid; p < S; p += kThreads) {
         const int idx = surv[p];
         const int h = idx / K, k = idx - h * K;
-        ex[p] = EvalExact<MAXM, L>(cur, h, FlatOf<MAXM, L>(dims, cur, h), Grow, H, offL + k, __ldg(Gdiag + offL + k),
-                                   __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
+        float* st = keep + p * KeepStride<MAXM>();
+        const bool kp = p < kKeep;
+        ex[p] = EvalExactL<MAXM>(cur, h, L, FlatOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+                                 __ldg(xc + offL + k), kp ? st : nullptr, kp ? st + MAXM : nullptr,
+                                 kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr);
     }
     __syncthreads();
-    const int newH = RankSurvivors(ex, surv, S, beam, lt, rank);
+    const int newH = RankSurvivors(ex, surv, S, beam, lt, keys);
     if (newH < 0) return -1;
     if (newH == 0) {
-        const int keep = KeepPrevious<MAXM, L>(cur, nxt, curH, beam);
+        const int kept = KeepPrevious<MAXM>(L, offL, cur, nxt, curH, beam);
         __syncthreads();
-        return keep;
+        return kept;
     }
-    Materialize<MAXM, L>(dims, cur, nxt, lt, newH, Grow, Gdiag, xc);
+    Materialize<MAXM>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc, keep, ex);
     __syncthreads();
     return newH;
 }
 
 template <int MAXM>
-__device__ int FastDispatch(int L, const Dims& dims, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
-                            const float* Grow, const float* Gdiag, const float* xc, int beam, float* lo,
-                            LayerTable& lt, uint16_t* surv, float* ex, int* rank, int check, unsigned int* err) {
-#define STLQ_B200_FAST(LL)                                                                                   \
-    case LL:                                                                                                 \
-        if constexpr (LL < MAXM)                                                                             \
-            return FastLayer<MAXM, LL>(dims, cur, nxt, curH, Grow, Gdiag, xc, beam, lo, lt, surv, ex, rank,    \
-                                       check, err);                                                          \
-        break;
-    switch (L) {
-        STLQ_B200_FAST(1) STLQ_B200_FAST(2) STLQ_B200_FAST(3) STLQ_B200_FAST(4) STLQ_B200_FAST(5)
-        STLQ_B200_FAST(6) STLQ_B200_FAST(7) STLQ_B200_FAST(8) STLQ_B200_FAST(9) STLQ_B200_FAST(10)
-        STLQ_B200_FAST(11) STLQ_B200_FAST(12) STLQ_B200_FAST(13) STLQ_B200_FAST(14) STLQ_B200_FAST(15)
-        default: break;
-    }
-#undef STLQ_B200_FAST
-    return -1;
-}
-
-template <int MAXM>
-__global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
+__global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
                                                            const float* __restrict__ Gdiag,
                                                            const float* __restrict__ xnorm2,
                                                            const float* __restrict__ xC, int64_t n, int beam,
@@ -509,10 +574,11 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
     size_t off = (2 * sv + 15) & ~size_t(15);
     LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
     off = (off + sizeof(LayerTable) + 15) & ~size_t(15);
-    float* lo = reinterpret_cast<float*>(smem + off);
+    uint64_t* keys = reinterpret_cast<uint64_t*>(smem + off);
+    float* lo = reinterpret_cast<float*>(keys + kSurvCap);
     float* ex = lo + beam * dims.maxK;
-    int* rank = reinterpret_cast<int*>(ex + kSurvCap);
-    uint16_t* surv = reinterpret_cast<uint16_t*>(rank + kSurvCap);
+    float* keep = ex + kSurvCap;
+    uint16_t* surv = reinterpret_cast<uint16_t*>(keep + kKeep * KeepStride<MAXM>());
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     unsigned long long n_surv = 0, n_layers = 0, n_vec = 0, n_redo = 0;  // thread 0's tallies
@@ -534,20 +600,20 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
         if (curH >= 0) {
             for (int p = tid; p < curH; p += kThreads) ex[p] = lo[surv[p]];
             __syncthreads();
-            curH = RankSurvivors(ex, surv, curH, beam, lt, rank);
+            curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
         }
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
         if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
         if (curH == 0) {
-            DeadSlot0<MAXM>(s0);
+            DeadSlot0<MAXM>(dims, s0);
             curH = 1;
         }
         __syncthreads();
         int ci = 0;
         for (int L = 1; L < m && curH > 0; ++L) {
-            curH = FastDispatch<MAXM>(L, dims, SlotView<MAXM>::At(smem + ci * sv, beam),
-                                      SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo,
-                                      lt, surv, ex, rank, check, err_flag);
+            curH = FastLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
+                                   SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo, lt,
+                                   surv, ex, keys, keep, check, err_flag);
             ci ^= 1;
             n_surv += lt.n_surv;
             ++n_layers;
@@ -560,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 5 : 1) BeamFastKernel(Di
         if (redo) {
             if (tid == 0) redo_list[atomicAdd(redo_count, 1)] = static_cast<int>(vec);
         } else if (tid < m) {
-            Bout[vec * m + tid] = static_cast<uint8_t>(cur.codeh(0)[tid]);
+            Bout[vec * m + tid] = static_cast<uint8_t>(cur.flath(0)[tid] - dims.off[tid]);
         }
         __syncthreads();
     }
@@ -576,7 +642,8 @@ template <int MAXM>
 size_t FastSmemBytes(int beam, int maxK) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
-    return b + sizeof(float) * beam * maxK + (sizeof(float) + sizeof(int) + sizeof(uint16_t)) * kSurvCap + 16;
+    return b + sizeof(uint64_t) * kSurvCap + sizeof(float) * beam * maxK + (sizeof(float) + sizeof(uint16_t)) * kSurvCap +
+           sizeof(float) * kKeep * KeepStride<MAXM>() + 16;
 }
 
 template <int MAXM>
@@ -586,6 +653,9 @@ size_t ReplaySmemBytes(int beam, int maxK) {
     return b + sizeof(float) * beam * maxK + 16;
 }
 
+// Sets the kernel's shared-memory size, finds how many CTAs fit on an SM, then asks for the
+// smallest shared-memory carve-out that still holds them: the rest of the SM's unified 256 KB
+// stays L1 cache for the gathers of Gram-matrix entries.  Grid: one CTA per resident slot.
 template <typename KernelT>
 cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* grid) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -596,6 +666,23 @@ cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* gr
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess) return e;
+    int dev = 0, sm_smem = 0, reserved = 0;
+    if (per_sm > 0 && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess && sm_smem > 0) {
+        const int64_t need = static_cast<int64_t>(per_sm) * (static_cast<int64_t>(smem) + reserved);
+        const int pct = static_cast<int>(std::min<int64_t>(100, (100 * need + sm_smem - 1) / sm_smem));
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, pct);
+        if (e != cudaSuccess) return e;
+        int check = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&check, kernel, kThreads, smem);
+        if (e != cudaSuccess) return e;
+        if (check < per_sm) {  // the hint cost occupancy: keep the maximum carve-out
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     static_cast<int>(cudaSharedmemCarveoutMaxShared));
+            if (e != cudaSuccess) return e;
+        }
+    }
     *grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n, static_cast<int64_t>(num_sms) * std::max(per_sm, 1))));
     return cudaSuccess;
 }

@@ -25,31 +25,38 @@ __device__ __forceinline__ float PosInf() { return __int_as_float(0x7f800000); }
 // Beam slots in dynamic shared memory, sized by the runtime beam width.
 template <int MAXM>
 struct SlotView {
-    float* R;     // [beam][MAXM*MAXM] upper Cholesky factor, row-major R[r*MAXM + c], r <= c
+    float* R;     // [beam][MAXM*MAXM] upper Cholesky factor by columns: R(r, c) at [c*MAXM + r], r <= c
     float* rinv;  // [beam][MAXM] 1/R_ii (cheap bound only)
     float* a;     // [beam][MAXM]
     float* E;     // [beam]
-    int* code;    // [beam][MAXM]
+    int* flat;    // [beam][MAXM] flat codeword index of each prefix code (layer offset + code)
     int* ill;     // [beam] 1 when any pivot was ill-conditioned
     __device__ float* Rh(int h) const { return R + h * MAXM * MAXM; }
     __device__ float* rinvh(int h) const { return rinv + h * MAXM; }
     __device__ float* ah(int h) const { return a + h * MAXM; }
-    __device__ int* codeh(int h) const { return code + h * MAXM; }
+    __device__ int* flath(int h) const { return flat + h * MAXM; }
+    // Rounded to 16 bytes: a second buffer placed after the first stays 16-byte aligned.
     __host__ __device__ static constexpr size_t Bytes(int beam) {
-        return sizeof(float) * static_cast<size_t>(beam) * (MAXM * MAXM + 2 * MAXM + 1) +
-               sizeof(int) * static_cast<size_t>(beam) * (MAXM + 1);
+        return (sizeof(float) * static_cast<size_t>(beam) * (MAXM * MAXM + 2 * MAXM + 1) +
+                sizeof(int) * static_cast<size_t>(beam) * (MAXM + 1) + 15) &
+               ~static_cast<size_t>(15);
     }
     __device__ static SlotView At(unsigned char* p, int beam) {
         SlotView v;
         v.R = reinterpret_cast<float*>(p);
         v.rinv = v.R + beam * MAXM * MAXM;
         v.a = v.rinv + beam * MAXM;
-        v.E = v.a + beam * MAXM;
-        v.code = reinterpret_cast<int*>(v.E + beam);
-        v.ill = v.code + beam * MAXM;
+        v.flat = reinterpret_cast<int*>(v.a + beam * MAXM);  // 16-byte aligned rows (int4 loads)
+        v.E = reinterpret_cast<float*>(v.flat + beam * MAXM);
+        v.ill = reinterpret_cast<int*>(v.E + beam);
         return v;
     }
 };
+
+// The kernels take the layer index L (1 <= L < m <= MAXM) at run time: one copy of each routine
+// serves every layer.  Per-layer copies (L as a template parameter) made the kernels several times
+// larger than the instruction cache, and instruction fetch became their main stall.  Loops run to
+// the compile-time bound NL = MAXM - 1 with warp-uniform guards on L.
 
 // Flat codeword indices of slot h's prefix (passed by value so they stay in registers).
 template <int MAXM>
@@ -57,11 +64,14 @@ struct FlatArr {
     int v[MAXM];
 };
 
-template <int MAXM, int L>
-__device__ __forceinline__ FlatArr<MAXM> FlatOf(const Dims& dims, const SlotView<MAXM>& cur, int h) {
+template <int MAXM>
+__device__ __forceinline__ FlatArr<MAXM> FlatOf(const SlotView<MAXM>& cur, int h, int L) {
     FlatArr<MAXM> f;
 #pragma unroll
-    for (int t = 0; t < MAXM; ++t) f.v[t] = t < L ? dims.off[t] + cur.codeh(h)[t] : 0;
+    for (int t = 0; t < MAXM; ++t) {
+        if (t >= L) break;
+        f.v[t] = cur.flath(h)[t];
+    }
     return f;
 }
 
@@ -70,33 +80,43 @@ __device__ __forceinline__ FlatArr<MAXM> FlatOf(const Dims& dims, const SlotView
 // eta = A.a_old, :299-305; denom, a_last, e with the clamp at 0, :307-318).  Returns the error,
 // +inf for a candidate the reference skips (denom == 0) or that can never enter the beam
 // (e >= +inf or NaN, :320).  Optionally returns y, v, denom and a_last for materialisation.
-// Kept out of line: several call sites share one copy, which keeps the kernels' code small.
-template <int MAXM, int L>
-__device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, const FlatArr<MAXM> flat,
+// NL bounds L; with kFixed the layer is NL itself (a per-layer copy).
+template <int MAXM, int NL, bool kFixed>
+__device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt, const FlatArr<MAXM> flat,
                                         const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
                                         float* y_out, float* v_out, float* denom_out, float* alast_out) {
+    const int L = kFixed ? NL : Lrt;
     const float* Rh = cur.Rh(h);
     const float* ah = cur.ah(h);
-    float A[L], y[L], v[L];
+    float A[NL], y[NL], v[NL];
 #pragma unroll
-    for (int t = 0; t < L; ++t) A[t] = __ldg(Grow + static_cast<size_t>(flat.v[t]) * H + col);
+    for (int t = 0; t < NL; ++t) {
+        if (t >= L) break;
+        A[t] = __ldg(Grow + static_cast<size_t>(flat.v[t]) * H + col);
+    }
 #pragma unroll
-    for (int i = 0; i < L; ++i) {
+    for (int i = 0; i < NL; ++i) {
+        if (i >= L) break;
         float s = A[i];
 #pragma unroll
-        for (int k = 0; k < i; ++k) s = sub_rn(s, mul_rn(Rh[k * MAXM + i], y[k]));
+        for (int k = 0; k < i; ++k) s = sub_rn(s, mul_rn(Rh[i * MAXM + k], y[k]));
         y[i] = div_rn(s, Rh[i * MAXM + i]);
     }
 #pragma unroll
-    for (int i = L - 1; i >= 0; --i) {
+    for (int i = NL - 1; i >= 0; --i) {
+        if (i >= L) continue;
         float s = y[i];
 #pragma unroll
-        for (int k = i + 1; k < L; ++k) s = sub_rn(s, mul_rn(Rh[i * MAXM + k], v[k]));
+        for (int k = i + 1; k < NL; ++k) {
+            if (k >= L) break;
+            s = sub_rn(s, mul_rn(Rh[k * MAXM + i], v[k]));
+        }
         v[i] = div_rn(s, Rh[i * MAXM + i]);
     }
     float delta = 0.0f, eta = 0.0f;
 #pragma unroll
-    for (int t = 0; t < L; ++t) {
+    for (int t = 0; t < NL; ++t) {
+        if (t >= L) break;
         delta = add_rn(delta, mul_rn(A[t], v[t]));
         eta = add_rn(eta, mul_rn(A[t], ah[t]));
     }
@@ -107,7 +127,8 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, const F
     if (e < 0.0f) e = 0.0f;
     if (y_out) {
 #pragma unroll
-        for (int t = 0; t < L; ++t) {
+        for (int t = 0; t < NL; ++t) {
+            if (t >= L) break;
             y_out[t] = y[t];
             v_out[t] = v[t];
         }
@@ -117,7 +138,35 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, const F
     return (denom != 0.0f && e < PosInf()) ? e : PosInf();
 }
 
-// Cheap bounds [lo, hi] on a candidate's exact error.
+// EvalExact for layer L: one copy per layer in the 8-layer kernel (small copies, the fastest
+// code); in the 16-layer kernel, whose per-layer copies would not fit the instruction cache, one
+// copy for L <= 7 and one for the rest.
+template <int MAXM>
+__device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, int L, const FlatArr<MAXM>& flat,
+                                            const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
+                                            float* y_out, float* v_out, float* denom_out, float* alast_out) {
+#define STLQ_B200_EXACT(NL, FIX) \
+    EvalExact<MAXM, NL, FIX>(cur, h, L, flat, Grow, H, col, alpha, gamma, y_out, v_out, denom_out, alast_out)
+    if constexpr (MAXM <= 8) {
+        switch (L) {
+            case 1: return STLQ_B200_EXACT(1, true);
+            case 2: return STLQ_B200_EXACT(2, true);
+            case 3: return STLQ_B200_EXACT(3, true);
+            case 4: return STLQ_B200_EXACT(4, true);
+            case 5: return STLQ_B200_EXACT(5, true);
+            case 6: return STLQ_B200_EXACT(6, true);
+            default: return STLQ_B200_EXACT(MAXM - 1, true);
+        }
+    } else {
+        if (L <= 7) return STLQ_B200_EXACT(7, false);
+        return STLQ_B200_EXACT(MAXM - 1, false);
+    }
+#undef STLQ_B200_EXACT
+}
+
+// Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
+// kCpt codewords (col[q], valid when ok[q]).  L is a compile-time constant here: this is the hot
+// loop, and each layer's copy is small (see CheapPass in beam.cu).
 // e' = E_old - diff^2/denom with y from FMA forward substitution, delta = |y|^2, eta = A.a.  The
 // half-width covers the rounding of both this and the exact sequence: relative errors of order
 // L ulp in diff (scale |gamma| + sum|A_t a_t|) and in denom (scale alpha + delta), propagated
@@ -125,40 +174,62 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, const F
 // whose cheap value is unreliable (ill-conditioned slot, denom <= kDenomGuard * alpha, NaN)
 // gets [-inf, +inf].
 template <int MAXM, int L>
-__device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const FlatArr<MAXM>& flat,
-                                            const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
-                                            float* lo, float* hi) {
+__device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* __restrict__ Grow, int H,
+                                            const int (&col)[kCpt], const bool (&ok)[kCpt],
+                                            const float (&alpha)[kCpt], const float (&gamma)[kCpt],
+                                            float (&lo)[kCpt], float (&hi)[kCpt]) {
     const float* Rh = cur.Rh(h);
     const float* rinv = cur.rinvh(h);
     const float* ah = cur.ah(h);
-    float A[L], y[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) A[t] = __ldg(Grow + static_cast<size_t>(flat.v[t]) * H + col);
-    float delta = 0.0f, eta = 0.0f, seta = fabsf(gamma);
+    const int* fl = cur.flath(h);
+    // Slot values are warp-uniform shared-memory broadcasts, loaded where they are used (loading
+    // them ahead into registers costs more in spills than it saves in load instructions).
+    float A[kCpt][L], y[kCpt][L];
 #pragma unroll
     for (int i = 0; i < L; ++i) {
-        float s = A[i];
+        const size_t row = static_cast<size_t>(fl[i]) * H;
 #pragma unroll
-        for (int k = 0; k < i; ++k) s = fmaf(-Rh[k * MAXM + i], y[k], s);
-        y[i] = s * rinv[i];
-        delta = fmaf(y[i], y[i], delta);
-        const float p = A[i] * ah[i];
-        eta += p;
-        seta += fabsf(p);
+        for (int q = 0; q < kCpt; ++q) A[q][i] = ok[q] ? __ldg(Grow + row + col[q]) : 0.0f;
     }
-    const float denom = alpha - delta;
-    const float diff = gamma - eta;
-    const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
-    const float r = diff * diff * rden;
+    float delta[kCpt], eta[kCpt], seta[kCpt];
+#pragma unroll
+    for (int q = 0; q < kCpt; ++q) {
+        delta[q] = 0.0f;
+        eta[q] = 0.0f;
+        seta[q] = fabsf(gamma[q]);
+    }
+#pragma unroll
+    for (int i = 0; i < L; ++i) {
+        const float ri = rinv[i], ai = ah[i];
+#pragma unroll
+        for (int q = 0; q < kCpt; ++q) {
+            float s = A[q][i];
+#pragma unroll
+            for (int k = 0; k < i; ++k) s = fmaf(-Rh[i * MAXM + k], y[q][k], s);
+            y[q][i] = s * ri;
+            delta[q] = fmaf(y[q][i], y[q][i], delta[q]);
+            const float p = A[q][i] * ai;
+            eta[q] += p;
+            seta[q] += fabsf(p);
+        }
+    }
     const float Eo = cur.E[h];
-    const float ep = fmaxf(Eo - r, 0.0f);
+    const int ill = cur.ill[h];
     constexpr float u = 1.2e-7f * (L + 2);
-    const float de = (2.0f * fabsf(diff) * (u * seta) + fabsf(r) * (u * (alpha + delta))) * fabsf(rden) +
-                     1.2e-7f * (Eo + fabsf(r));
-    const float w = 16.0f * de;
-    const bool force = cur.ill[h] || !(denom > kDenomGuard * alpha) || !(w < PosInf()) || !(ep < PosInf());
-    *lo = force ? -PosInf() : ep - w;
-    *hi = force ? PosInf() : ep + w;
+#pragma unroll
+    for (int q = 0; q < kCpt; ++q) {
+        const float denom = alpha[q] - delta[q];
+        const float diff = gamma[q] - eta[q];
+        const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
+        const float r = diff * diff * rden;
+        const float ep = fmaxf(Eo - r, 0.0f);
+        const float de = (2.0f * fabsf(diff) * (u * seta[q]) + fabsf(r) * (u * (alpha[q] + delta[q]))) * fabsf(rden) +
+                         1.2e-7f * (Eo + fabsf(r));
+        const float w = 16.0f * de;
+        const bool force = ill || !(denom > kDenomGuard * alpha[q]) || !(w < PosInf()) || !(ep < PosInf());
+        lo[q] = !ok[q] ? PosInf() : force ? -PosInf() : ep - w;
+        hi[q] = !ok[q] ? PosInf() : force ? PosInf() : ep + w;
+    }
 }
 
 }  // namespace beam
