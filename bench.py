@@ -43,6 +43,9 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-fp32-peak", action="store_true", help="skip the SGEMM FP32 peak measurement")
+    p.add_argument("--no-strict", action="store_true", help="skip the STRICT (tensor-core GEMM) mode leg")
+    p.add_argument("--gemm-only", choices=["exact", "strict", "fast"], default=None,
+                   help="profiling aid: run only the xC GEMM of this mode on one 262,144-vector slice")
     return p.parse_args()
 
 
@@ -218,6 +221,76 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def recon_sse(X, C, h_vec, B, a):
+    """Per-vector ||x - sum_t a_t c_{B_t}||^2 in float64 (X n x d, C H x d, B/a n x m)."""
+    off = np.concatenate([[0], np.cumsum(h_vec)[:-1]]).astype(np.int64)
+    rec = np.einsum("nm,nmd->nd", a.astype(np.float64), C[B.astype(np.int64) + off].astype(np.float64))
+    return ((X.astype(np.float64) - rec) ** 2).sum(1)
+
+
+def strict_leg(torch, C_np, h_vec, X, X_np, args, S, offset, ref_sample, peaks, reps=3):
+    """STLQ_B200_GEMM_STRICT (tcgen05 3xTF32 xC GEMM): the GEMM alone on an S-vector slice, one
+    encode of the whole shard, and agreement with the reference's CPU codes on the CPU sample."""
+    import stlq_b200
+
+    enc = stlq_b200.Encoder(C_np, h_vec, device=X.device.index or 0, gemm_mode="strict")
+    H, n = int(sum(h_vec)), X.shape[0]
+    for _ in range(2):
+        xc = enc.xc_gemm(X[:S])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        xc = enc.xc_gemm(X[:S])
+    e1.record()
+    torch.cuda.synchronize()
+    gemm_s = e0.elapsed_time(e1) / 1e3 / reps
+    del xc
+    B = torch.empty((n, args.m), dtype=torch.uint8, device=X.device)
+    a = torch.empty((n, args.m), dtype=torch.float32, device=X.device)
+    cost = torch.empty(n, dtype=torch.float32, device=X.device)
+    sse = torch.zeros(2, dtype=torch.float64, device=X.device)
+    enc.encode_base_device(X, args.beam, args.icm, 0, 0, True, 38251450, offset, B=B, a=a, cost=cost, sse=sse)
+    torch.cuda.synchronize()
+    sse.zero_()
+    e0.record()
+    enc.encode_base_device(X, args.beam, args.icm, 0, 0, True, 38251450, offset, B=B, a=a, cost=cost, sse=sse)
+    e1.record()
+    torch.cuda.synchronize()
+    enc.sync()
+    step_s = e0.elapsed_time(e1) / 1e3
+    flops_1x = 2.0 * args.d * H * S
+    tf32_peak = peaks["bf16_tflops"] / 2  # dense TF32 tensor rate is half the BF16 rate on B200
+    out = {
+        "gemm_mode": "strict (tcgen05.mma kind::tf32, 3xTF32 split, TMEM accumulator, TMA operands)",
+        "value": n / step_s, "unit": "vectors/s", "ms_per_step": 1e3 * step_s,
+        "final_mse": float(sse[1].item()) / n,
+        "gemm_ms_per_262144": gemm_s * 1e3 * 262144 / S,
+        "gemm_fp32_equiv_tflops": flops_1x / gemm_s / 1e12,
+        "tensor": {"achieved": 3 * flops_1x / gemm_s / 1e12, "peak": tf32_peak, "unit": "TFLOP/s",
+                   "frac": 3 * flops_1x / gemm_s / 1e12 / tf32_peak,
+                   "note": "3 TF32 MMAs per product; peak = measured cuBLAS BF16 / 2 (dense TF32 rate)"},
+    }
+    if ref_sample is not None:
+        ns = len(ref_sample["B"])
+        Bs, As = B[:ns].cpu().numpy(), a[:ns].cpu().numpy()
+        same = (Bs == ref_sample["B"]).all(1)
+        Xs = X_np[:ns]
+        ours = recon_sse(Xs, C_np, h_vec, Bs, As)
+        refs = recon_sse(Xs, C_np, h_vec, ref_sample["B"], ref_sample["a"])
+        bad = ~same
+        rel = np.abs(ours[bad] - refs[bad]) / np.maximum(refs[bad], 1e-30)
+        out["code_match"] = {
+            "frac": float(same.mean()), "vectors": ns, "mismatched": int(bad.sum()),
+            "mismatched_cost_rel_max": float(rel.max()) if rel.size else 0.0,
+            "mismatched_within_1e-5": float((rel <= 1e-5).mean()) if rel.size else 1.0,
+            "mse_rel_diff": float(abs(ours.mean() - refs.mean()) / refs.mean()),
+            "cost": "per-vector reconstruction error ||x - sum a_t c_t||^2 in float64, ours vs reference",
+        }
+    enc.close()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -351,9 +424,10 @@ def run_ours(args):
 
     cpu = None
     code_match = None
+    ref_sample = None
     if rank == 0 and not args.no_cpu:
         try:
-            v, cores, ns, code_match, _ = cpu_reference_sample(C_np, h_vec, X_np, args, args.cpu_seconds,
+            v, cores, ns, code_match, ref_sample = cpu_reference_sample(C_np, h_vec, X_np, args, args.cpu_seconds,
                                                                gpu_codes=B.cpu().numpy())
             cpu = {"value": v, "unit": "vectors/s", "cores": cores, "kind": "reference",
                    "sample": f"first {ns} vectors of rank 0's shard, same codebooks and settings, "
@@ -362,6 +436,9 @@ def run_ours(args):
         except Exception as exc:  # the reference library did not travel or does not load
             cpu = {"value": None, "unit": "vectors/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {exc}"}
+    strict = None
+    if rank == 0 and not args.no_strict:
+        strict = strict_leg(torch, C_np, h_vec, X, X_np, args, S, offset, ref_sample, load_measured_peaks()[0])
     if rank == 0:
         peaks, peaks_src = load_measured_peaks()
         fp32_peak = float("nan") if args.no_fp32_peak else measure_fp32_peak(torch, device)
@@ -386,7 +463,7 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "mse": total_mse,
             "roofline": {
-                "bound": "hbm", "kernel": "BeamSearchKernel<8>", "achieved": achieved_gbs,
+                "bound": "hbm", "kernel": "BeamFastKernel<8>", "achieved": achieved_gbs,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"],
                 "traffic": None, "peak_source": peaks_src,
                 "note": "algorithmic bytes per vector = xC row (4H) + ||x||^2 (4) + codes (M); the kernel is "
@@ -404,6 +481,7 @@ def run_ours(args):
             "clocks": clock_info,
             "cpu_baseline": cpu,
             "code_match": code_match,
+            "strict_mode": strict,
         }
         if e2e:
             line["e2e"] = e2e
@@ -414,8 +492,29 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_gemm_only(args):
+    """Profiling aid (not a bench line): the xC GEMM of one mode on a slice, three launches."""
+    import torch
+
+    import stlq_b200
+    from stlq_b200 import synth
+
+    device = torch.device("cuda", 0)
+    C = make_codebooks(args, device)
+    enc = stlq_b200.Encoder(C, [args.k] * args.m, device=0, gemm_mode=args.gemm_only)
+    X = torch.from_numpy(synth.sift_like(min(args.n, 262_144), d=args.d, seed=4)).to(device)
+    for _ in range(3):
+        xc = enc.xc_gemm(X)
+    torch.cuda.synchronize()
+    enc.sync()
+    print(json.dumps({"gemm_only": args.gemm_only, "vectors": X.shape[0], "checksum": float(xc.double().sum())}))
+
+
 def main():
     args = parse_args()
+    if args.gemm_only:
+        run_gemm_only(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
