@@ -354,22 +354,30 @@ __device__ __noinline__ int SelectSurvivors(const float* lo, int n_cand, uint32_
     const uint32_t sorted = WarpSortAsc(hmin);
     if (lane < beam) lt.mins[warp * kMaxBeam + lane] = sorted;
     __syncthreads();
+    // Rank of value v (list w, position j) among all 4B values: j plus, in each other list, the
+    // number of entries ordered before it (ties broken by list index).  The searches over the
+    // other lists are independent: fixed-step binary searches, interleaved.
     uint32_t tb = 0xffffffffu;
     for (int i = lane; i < kWarps * beam; i += 32) {
         const int w = i / beam, j = i - w * beam;
         const uint32_t v = lt.mins[w * kMaxBeam + j];
-        int r = j;
-        for (int w2 = 0; w2 < kWarps; ++w2) {
-            if (w2 == w) continue;
-            int a = 0, b = beam;
-            while (a < b) {
-                const int mid = (a + b) >> 1;
-                const uint32_t u = lt.mins[w2 * kMaxBeam + mid];
-                if (u < v || (u == v && w2 < w)) a = mid + 1;
-                else b = mid;
+        int pos[kWarps];
+#pragma unroll
+        for (int w2 = 0; w2 < kWarps; ++w2) pos[w2] = 0;
+#pragma unroll
+        for (int step = kMaxBeam; step > 0; step >>= 1) {  // counts up to 2 * kMaxBeam - 1 >= beam
+#pragma unroll
+            for (int w2 = 0; w2 < kWarps; ++w2) {
+                const int t = pos[w2] + step;  // entries [0, pos) are known to come before v
+                if (t <= beam) {
+                    const uint32_t u = lt.mins[w2 * kMaxBeam + t - 1];
+                    if (u < v || (u == v && w2 < w)) pos[w2] = t;
+                }
             }
-            r += a;
         }
+        int r = j;
+#pragma unroll
+        for (int w2 = 0; w2 < kWarps; ++w2) r += w2 == w ? 0 : pos[w2];
         if (r == beam - 1) tb = v;
     }
     tb = __reduce_min_sync(kFull, tb);
@@ -495,7 +503,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
         alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
         gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
     }
-    uint32_t hmin = 0xffffffffu;
+    float hmin = PosInf();  // never NaN: a bound is finite or +-inf
     for (int h = 0; h < curH; ++h) {
         float l[kCpt], hi[kCpt];
         CheapBounds<MAXM, L>(cur, h, Grow, H, col, ok, alpha, gamma, l, hi);
@@ -503,12 +511,12 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
         for (int c = 0; c < kCpt; ++c) {
             if (ok[c]) {
                 lo[h * K + tid + c * kThreads] = l[c];
-                hmin = min(hmin, OrderKey(hi[c]));
+                hmin = fminf(hmin, hi[c]);
             }
         }
         if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag);
     }
-    return hmin;
+    return OrderKey(hmin);
 }
 
 template <int MAXM>

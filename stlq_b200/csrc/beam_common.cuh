@@ -165,7 +165,7 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 }
 
 // Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
-// kCpt codewords (col[q], valid when ok[q]).  L is a compile-time constant here: this is the hot
+// kCpt codewords (col[q]; the values of a codeword with !ok[q] are meaningless and unused).  L is a compile-time constant here: this is the hot
 // loop, and each layer's copy is small (see CheapPass in beam.cu).
 // e' = E_old - diff^2/denom with y from FMA forward substitution, delta = |y|^2, eta = A.a.  The
 // half-width covers the rounding of both this and the exact sequence: relative errors of order
@@ -208,14 +208,15 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
             for (int k = 0; k < i; ++k) s = fmaf(-Rh[i * MAXM + k], y[q][k], s);
             y[q][i] = s * ri;
             delta[q] = fmaf(y[q][i], y[q][i], delta[q]);
-            const float p = A[q][i] * ai;
-            eta[q] += p;
-            seta[q] += fabsf(p);
+            eta[q] = fmaf(A[q][i], ai, eta[q]);
+            seta[q] = fmaf(fabsf(A[q][i]), fabsf(ai), seta[q]);
         }
     }
     const float Eo = cur.E[h];
-    const int ill = cur.ill[h];
-    constexpr float u = 1.2e-7f * (L + 2);
+    const bool ill = cur.ill[h] != 0;
+    // Half-width w = 16 * de with de as documented above; the factor 16 is folded into the constants.
+    constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
+    constexpr float e16 = 16.0f * 1.2e-7f;
 #pragma unroll
     for (int q = 0; q < kCpt; ++q) {
         const float denom = alpha[q] - delta[q];
@@ -223,12 +224,11 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
         const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
         const float r = diff * diff * rden;
         const float ep = fmaxf(Eo - r, 0.0f);
-        const float de = (2.0f * fabsf(diff) * (u * seta[q]) + fabsf(r) * (u * (alpha[q] + delta[q]))) * fabsf(rden) +
-                         1.2e-7f * (Eo + fabsf(r));
-        const float w = 16.0f * de;
+        const float w = fmaf(2.0f * fabsf(diff) * seta[q] + fabsf(r) * (alpha[q] + delta[q]), u16 * fabsf(rden),
+                             e16 * (Eo + fabsf(r)));
         const bool force = ill || !(denom > kDenomGuard * alpha[q]) || !(w < PosInf()) || !(ep < PosInf());
-        lo[q] = !ok[q] ? PosInf() : force ? -PosInf() : ep - w;
-        hi[q] = !ok[q] ? PosInf() : force ? PosInf() : ep + w;
+        lo[q] = force ? -PosInf() : ep - w;
+        hi[q] = force ? PosInf() : ep + w;
     }
 }
 
