@@ -22,8 +22,9 @@
 // sits at the boundary (or at the final minimum), or the survivor list would overflow, the vector
 // is handed to BeamReplayKernel.
 //
-// BeamReplayKernel evaluates every candidate exactly and replays the reference's replacement
-// scan itself (warp 0, slots one per lane), so ties resolve exactly as in the reference.
+// BeamReplayKernel replays the reference's replacement scan itself (warp 0, slots one per lane), so
+// ties resolve exactly as in the reference; it evaluates exactly every candidate that the cheap
+// bounds cannot exclude from entering the scan (ReplayLayer).
 //
 // The layer index is a run-time argument of every routine (see beam_common.cuh).
 #include <cstdint>
@@ -177,6 +178,83 @@ __device__ __forceinline__ float Layer0Error(const float* Gdiag, const float* xc
 }
 
 // ---------------------------------------------------------------------------------------------
+// Cheap pass shared by both kernels.
+
+// Self-check of the cheap bounds (STLQ_B200_CHECK_FILTER): the exact error of each candidate must
+// lie inside them; a miss raises kErrFilterMiss.  Inlined: a call site inside the hot loop, even
+// one never taken, costs the loop registers.
+template <int MAXM>
+__device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int H,
+                                         const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
+                                         const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
+                                         unsigned int* err_flag) {
+    const FlatArr<MAXM> flat = FlatOf<MAXM>(cur, h, L);
+    for (int c = 0; c < kCpt; ++c) {
+        if (!ok[c]) continue;
+        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, H, col[c], alpha[c], gamma[c], nullptr, nullptr,
+                                         nullptr, nullptr);
+        if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
+    }
+}
+
+// The cheap pass of layer L over every live slot: lower bounds into lo[h * K + k] (with kHi also
+// the upper bounds into hi_out), and the thread's smallest upper bound as the return value.  One copy per layer, inlined (with L a
+// compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
+// call boundary costs more than the copies save).
+template <int MAXM, int L, bool kHi>
+__device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int H,
+                                           const float* __restrict__ Grow, const float* __restrict__ Gdiag,
+                                           const float* __restrict__ xc, float* lo, float* hi_out, int check,
+                                           unsigned int* err_flag) {
+    const int tid = threadIdx.x;
+    float alpha[kCpt], gamma[kCpt];
+    int col[kCpt];
+    bool ok[kCpt];
+#pragma unroll
+    for (int c = 0; c < kCpt; ++c) {
+        const int k = tid + c * kThreads;
+        ok[c] = k < K;
+        col[c] = offL + k;
+        alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
+        gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
+    }
+    float hmin = PosInf();  // never NaN: a bound is finite or +-inf
+    for (int h = 0; h < curH; ++h) {
+        float l[kCpt], hi[kCpt];
+        CheapBounds<MAXM, L>(cur, h, Grow, H, col, ok, alpha, gamma, l, hi);
+#pragma unroll
+        for (int c = 0; c < kCpt; ++c) {
+            if (ok[c]) {
+                lo[h * K + tid + c * kThreads] = l[c];
+                if (kHi) hi_out[h * K + tid + c * kThreads] = hi[c];
+                hmin = fminf(hmin, hi[c]);
+            }
+        }
+        if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag);
+    }
+    return OrderKey(hmin);
+}
+
+template <int MAXM, bool kHi>
+__device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int H,
+                                  const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
+                                  int check, unsigned int* err) {
+#define STLQ_B200_CHEAP(LL)                                                                          \
+    case LL:                                                                                         \
+        if constexpr (LL < MAXM)                                                                     \
+            return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, H, Grow, Gdiag, xc, lo, hi_out, check, err); \
+        break;
+    switch (L) {
+        STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
+        STLQ_B200_CHEAP(6) STLQ_B200_CHEAP(7) STLQ_B200_CHEAP(8) STLQ_B200_CHEAP(9) STLQ_B200_CHEAP(10)
+        STLQ_B200_CHEAP(11) STLQ_B200_CHEAP(12) STLQ_B200_CHEAP(13) STLQ_B200_CHEAP(14) STLQ_B200_CHEAP(15)
+        default: break;
+    }
+#undef STLQ_B200_CHEAP
+    return 0u;  // unreachable: 1 <= L < m <= MAXM
+}
+
+// ---------------------------------------------------------------------------------------------
 // Replay kernel: exact errors for every candidate and the reference's replacement scan.
 
 // Warp-0 replay state: lane s < beam holds slot s.
@@ -217,6 +295,38 @@ struct Replay {
             }
         }
     }
+    // Pre-scan on the cheap bounds.  Scanning hi[] with the same rule makes `worst` the B-th
+    // smallest upper bound of the prefix, an upper bound of the exact scan's worst at the same
+    // position (each exact error is <= its hi).  A candidate whose lo is not below that bound at the
+    // start of its 32-candidate batch can never enter the exact scan: its error is set to +inf in
+    // lo[] and it needs no exact evaluation.  The others keep their lo and their indices are
+    // appended to list[] (which may overwrite hi[] entries already consumed).  Returns their count.
+    __device__ int PreScan(float* lo, float* hi, int n, int* list) {
+        const int lane = threadIdx.x & 31;
+        int count = 0;
+        for (int base = 0; base < n; base += 32) {
+            const bool in = base + lane < n;
+            const float h = in ? hi[base + lane] : PosInf();
+            const float l = in ? lo[base + lane] : PosInf();
+            const bool need = in && l < worst;
+            __syncwarp();  // every lane has read its batch entries before list[] overwrites them
+            const unsigned nm = __ballot_sync(kFull, need);
+            if (need) list[count + __popc(nm & ((1u << lane) - 1u))] = base + lane;
+            else if (in) lo[base + lane] = PosInf();
+            count += __popc(nm);
+            unsigned mask = __ballot_sync(kFull, h < worst);
+            while (mask) {
+                const int b = __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float hb = __shfl_sync(kFull, h, b);
+                if (hb < worst) {
+                    if (lane == widx) es = hb;
+                    Refresh();
+                }
+            }
+        }
+        return count;
+    }
     __device__ void Publish(int beam, LayerTable& lt) {
         const int lane = threadIdx.x & 31;
         if (lane < beam) lt.cand[lane] = cs;
@@ -225,34 +335,38 @@ struct Replay {
     }
 };
 
+// One layer of the replay: cheap bounds for every candidate, the pre-scan that finds the
+// candidates able to enter, exact errors for those only (all others are +inf, which enters no
+// slot), then the reference's replacement scan over the exact errors.
 template <int MAXM>
 __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
-                            const float* __restrict__ xc, int beam, float* errs, LayerTable& lt) {
+                            const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt) {
     const int tid = threadIdx.x;
-    const int K = dims.h_vec[L], offL = dims.off[L];
-    float alpha[kCpt], gamma[kCpt];
-#pragma unroll
-    for (int c = 0; c < kCpt; ++c) {
-        const int k = tid + c * kThreads;
-        alpha[c] = k < K ? __ldg(Gdiag + offL + k) : 0.0f;
-        gamma[c] = k < K ? __ldg(xc + offL + k) : 0.0f;
+    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    const int n_cand = curH * K;
+    CheapDispatch<MAXM, true>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, errs, his, 0, nullptr);
+    __syncthreads();
+    int* list = reinterpret_cast<int*>(his);
+    if (tid < 32) {
+        Replay rp;
+        rp.Init(beam);
+        const int need = rp.PreScan(errs, his, n_cand, list);
+        if (tid == 0) lt.n_surv = need;
     }
-    for (int h = 0; h < curH; ++h) {
-        const FlatArr<MAXM> flat = FlatOf<MAXM>(cur, h, L);
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            const int k = tid + c * kThreads;
-            if (k < K)
-                errs[h * K + k] = EvalExactL<MAXM>(cur, h, L, flat, Grow, dims.H, offL + k, alpha[c], gamma[c],
-                                                   nullptr, nullptr, nullptr, nullptr);
-        }
+    __syncthreads();
+    const int need = lt.n_surv;
+    for (int p = tid; p < need; p += kThreads) {
+        const int idx = list[p];
+        const int h = idx / K, k = idx - h * K;
+        errs[idx] = EvalExactL<MAXM>(cur, h, L, FlatOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+                                     __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
     }
     __syncthreads();
     if (tid < 32) {
         Replay rp;
         rp.Init(beam);
-        rp.Scan(errs, curH * K);
+        rp.Scan(errs, n_cand);
         rp.Publish(beam, lt);
     }
     __syncthreads();
@@ -279,6 +393,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
     size_t off = (2 * sv + 15) & ~size_t(15);
     LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
     float* errs = reinterpret_cast<float*>(smem + ((off + sizeof(LayerTable) + 15) & ~size_t(15)));
+    float* his = errs + beam * dims.maxK;
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     const int64_t total = vec_list ? static_cast<int64_t>(*count) : n;
@@ -306,7 +421,8 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         int ci = 0;
         for (int L = 1; L < m; ++L) {
             ReplayLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
-                              SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, lt);
+                              SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, his,
+                              lt);
             ci ^= 1;
         }
         if (tid < 32) {  // first slot with the smallest error (beam_search.cpp:409-416)
@@ -465,78 +581,6 @@ __device__ __noinline__ int RankSurvivors(const float* ex, const uint16_t* surv,
     return min(n_valid, beam);
 }
 
-// Self-check of the cheap bounds (STLQ_B200_CHECK_FILTER): the exact error of each candidate must
-// lie inside them; a miss raises kErrFilterMiss.  Inlined: a call site inside the hot loop, even
-// one never taken, costs the loop registers.
-template <int MAXM>
-__device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int H,
-                                         const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
-                                         const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
-                                         unsigned int* err_flag) {
-    const FlatArr<MAXM> flat = FlatOf<MAXM>(cur, h, L);
-    for (int c = 0; c < kCpt; ++c) {
-        if (!ok[c]) continue;
-        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, H, col[c], alpha[c], gamma[c], nullptr, nullptr,
-                                         nullptr, nullptr);
-        if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
-    }
-}
-
-// The cheap pass of layer L over every live slot: lower bounds into lo[h * K + k], and the
-// thread's smallest upper bound as the return value.  One copy per layer, inlined (with L a
-// compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
-// call boundary costs more than the copies save).
-template <int MAXM, int L>
-__device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int H,
-                                           const float* __restrict__ Grow, const float* __restrict__ Gdiag,
-                                           const float* __restrict__ xc, float* lo, int check,
-                                           unsigned int* err_flag) {
-    const int tid = threadIdx.x;
-    float alpha[kCpt], gamma[kCpt];
-    int col[kCpt];
-    bool ok[kCpt];
-#pragma unroll
-    for (int c = 0; c < kCpt; ++c) {
-        const int k = tid + c * kThreads;
-        ok[c] = k < K;
-        col[c] = offL + k;
-        alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
-        gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
-    }
-    float hmin = PosInf();  // never NaN: a bound is finite or +-inf
-    for (int h = 0; h < curH; ++h) {
-        float l[kCpt], hi[kCpt];
-        CheapBounds<MAXM, L>(cur, h, Grow, H, col, ok, alpha, gamma, l, hi);
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            if (ok[c]) {
-                lo[h * K + tid + c * kThreads] = l[c];
-                hmin = fminf(hmin, hi[c]);
-            }
-        }
-        if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag);
-    }
-    return OrderKey(hmin);
-}
-
-template <int MAXM>
-__device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int H,
-                                  const float* Grow, const float* Gdiag, const float* xc, float* lo, int check,
-                                  unsigned int* err) {
-#define STLQ_B200_CHEAP(LL)                                                                                   \
-    case LL:                                                                                                  \
-        if constexpr (LL < MAXM) return CheapPass<MAXM, LL>(cur, curH, K, offL, H, Grow, Gdiag, xc, lo, check, err); \
-        break;
-    switch (L) {
-        STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
-        STLQ_B200_CHEAP(6) STLQ_B200_CHEAP(7) STLQ_B200_CHEAP(8) STLQ_B200_CHEAP(9) STLQ_B200_CHEAP(10)
-        STLQ_B200_CHEAP(11) STLQ_B200_CHEAP(12) STLQ_B200_CHEAP(13) STLQ_B200_CHEAP(14) STLQ_B200_CHEAP(15)
-        default: break;
-    }
-#undef STLQ_B200_CHEAP
-    return 0u;  // unreachable: 1 <= L < m <= MAXM
-}
-
 template <int MAXM>
 __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
                          const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
@@ -544,7 +588,8 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
                          int check, unsigned int* err_flag) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
-    const uint32_t hmin = CheapDispatch<MAXM>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, lo, check, err_flag);
+    const uint32_t hmin =
+        CheapDispatch<MAXM, false>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, lo, nullptr, check, err_flag);
     const int S = SelectSurvivors(lo, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     for (int p = tid; p < S; p += kThreads) {
@@ -658,7 +703,7 @@ template <int MAXM>
 size_t ReplaySmemBytes(int beam, int maxK) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
-    return b + sizeof(float) * beam * maxK + 16;
+    return b + 2 * sizeof(float) * beam * maxK + 16;  // errors (lower bounds first) and upper bounds
 }
 
 // Sets the kernel's shared-memory size, finds how many CTAs fit on an SM, then asks for the
