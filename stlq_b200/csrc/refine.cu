@@ -14,7 +14,9 @@
 //
 // Layout: one warp per vector, 4 warps per CTA.  The ICM scores of a layer are spread over the
 // 32 lanes (coalesced reads of G's column segment); the argmax reduces with shuffles; the small
-// SPD solves run on lane 0 from a per-warp shared-memory matrix.
+// SPD solves run on lane 0 from a per-warp shared-memory matrix.  The m x m Gram submatrix of the
+// current codes is cached per warp in shared memory (loaded by all lanes, two rows/columns per
+// trial code change), so lane 0's solves, costs and MSE terms read no global memory.
 #include <cstdint>
 
 #include "common.cuh"
@@ -37,10 +39,65 @@ struct WarpState {
     int code[kMaxM];
     int cand[kMaxM];
     float acand[kMaxM];
+    float Gs[kMaxM * kMaxM];  // Gs[r*m + c] = G(flat_r, flat_c) for the codes being refined
+    float Gbak[2 * kMaxM];    // row and column of a trial code change, for the rollback
 };
 
 __device__ __forceinline__ float GAt(const float* Gcol, int H, int row, int col) {
     return Gcol[static_cast<size_t>(col) * H + row];
+}
+
+// Gram entry G(flat_r, flat_c) of layers r and c, from the global matrix or the warp's cache.
+struct GramGlobal {
+    const float* Gcol;
+    int H;
+    const int* off;
+    const int* code;
+    __device__ float operator()(int r, int c) const { return GAt(Gcol, H, off[r] + code[r], off[c] + code[c]); }
+};
+struct GramShared {
+    const float* Gs;
+    int m;
+    __device__ float operator()(int r, int c) const { return Gs[r * m + c]; }
+};
+
+// All lanes: ws.Gs for `code`.
+__device__ void LoadGram(const Dims& dims, const float* Gcol, const int* code, float* Gs) {
+    const int lane = threadIdx.x & 31, m = dims.m;
+    __syncwarp();
+    for (int e = lane; e < m * m; e += 32) {
+        const int r = e / m, c = e - r * m;
+        Gs[e] = GAt(Gcol, dims.H, dims.off[r] + code[r], dims.off[c] + code[c]);
+    }
+    __syncwarp();
+}
+
+// All lanes: row and column j of Gs for code[j]'s new value, the old ones saved in bak.
+__device__ void UpdateGram(const Dims& dims, const float* Gcol, const int* code, int j, float* Gs, float* bak) {
+    const int lane = threadIdx.x & 31, m = dims.m;
+    __syncwarp();
+    if (lane < m) {
+        const int fj = dims.off[j] + code[j], fk = dims.off[lane] + code[lane];
+        bak[lane] = Gs[j * m + lane];
+        bak[m + lane] = Gs[lane * m + j];
+        const float row = GAt(Gcol, dims.H, fj, fk), col = GAt(Gcol, dims.H, fk, fj);
+        __syncwarp(0xffffffffu >> (32 - m));
+        Gs[j * m + lane] = row;
+        Gs[lane * m + j] = col;
+    }
+    __syncwarp();
+}
+
+// All lanes: undoes UpdateGram.
+__device__ void RestoreGram(int m, int j, float* Gs, const float* bak) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+    if (lane < m) {
+        Gs[j * m + lane] = bak[lane];
+        __syncwarp(0xffffffffu >> (32 - m));
+        Gs[lane * m + j] = bak[m + lane];
+    }
+    __syncwarp();
 }
 
 // Fixed-size Cholesky for m in {5, 10} (CholeskyUpperFixed, least_squares.cpp:44-66), row-major.
@@ -186,9 +243,10 @@ __device__ void SolveLapack(const float* A, int m, float* c) {  // U^T y = b, U 
 }
 
 // One vector's LS solve with the reference's retry policy (3 diagonal bumps 1e-6 x10^i).
-__device__ bool SolveLs(const Dims& dims, const float* Gcol, const float* xc, const int* code, WarpState& ws,
+template <class Gram>
+__device__ bool SolveLs(const Dims& dims, const Gram& G, const float* xc, const int* code, WarpState& ws,
                         float* a_out) {
-    const int m = dims.m, H = dims.H;
+    const int m = dims.m;
     const bool fixed = (m == 5 || m == 10);
     float lambda = 0.0f;
     for (int attempt = 0; attempt < 4; ++attempt) {
@@ -197,8 +255,7 @@ __device__ bool SolveLs(const Dims& dims, const float* Gcol, const float* xc, co
             const int fj = dims.off[j] + code[j];
             ws.b[j] = xc[fj];
             for (int k = 0; k <= j; ++k) {
-                const int fk = dims.off[k] + code[k];
-                const float g = GAt(Gcol, H, fk, fj);
+                const float g = G(k, j);
                 if (fixed) ws.A[k * m + j] = g;
                 else ws.A[k + j * m] = g;
             }
@@ -231,32 +288,31 @@ __device__ bool SolveLs(const Dims& dims, const float* Gcol, const float* xc, co
 }
 
 // SampleCost (cost_utils.cpp:112-137).
-__device__ float SampleCost(const Dims& dims, const float* Gcol, const float* xc, const int* code, const float* a,
+template <class Gram>
+__device__ float SampleCost(const Dims& dims, const Gram& G, const float* xc, const int* code, const float* a,
                             float xn2) {
-    const int m = dims.m, H = dims.H;
+    const int m = dims.m;
     float term1 = 0.0f, term2 = 0.0f;
     for (int l = 0; l < m; ++l) {
         const int fl = dims.off[l] + code[l];
         term1 = add_rn(term1, mul_rn(a[l], xc[fl]));
-        for (int k = 0; k < m; ++k) {
-            const int fk = dims.off[k] + code[k];
-            term2 = add_rn(term2, mul_rn(mul_rn(a[l], a[k]), GAt(Gcol, H, fl, fk)));
-        }
+        for (int k = 0; k < m; ++k) term2 = add_rn(term2, mul_rn(mul_rn(a[l], a[k]), G(l, k)));
     }
     return add_rn(sub_rn(xn2, mul_rn(2.0f, term1)), term2);
 }
 
 // Per-vector term of MeanMseFromPrecomp in double, clamped at 0.
-__device__ double VectorSse(const Dims& dims, const float* Gcol, const float* xc, const int* code, const float* a,
+template <class Gram>
+__device__ double VectorSse(const Dims& dims, const Gram& G, const float* xc, const int* code, const float* a,
                             double nx) {
-    const int m = dims.m, H = dims.H;
+    const int m = dims.m;
     double t1 = 0.0, t2 = 0.0;
     for (int j = 0; j < m; ++j)
         t1 = __dadd_rn(t1, __dmul_rn(static_cast<double>(a[j]), static_cast<double>(xc[dims.off[j] + code[j]])));
     for (int j = 0; j < m; ++j)
         for (int k = 0; k < m; ++k)
             t2 = __dadd_rn(t2, __dmul_rn(__dmul_rn(static_cast<double>(a[j]), static_cast<double>(a[k])),
-                                         static_cast<double>(GAt(Gcol, H, dims.off[j] + code[j], dims.off[k] + code[k]))));
+                                         static_cast<double>(G(j, k))));
     const double e = __dadd_rn(__dsub_rn(nx, __dmul_rn(2.0, t1)), t2);
     return e < 0.0 ? 0.0 : e;
 }
@@ -283,10 +339,14 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
                            WarpState& ws, bool do_init = true) {
     const int lane = threadIdx.x & 31;
     const int m = dims.m, H = dims.H;
-    if (do_init && lane == 0) {
-        if (!SolveLs(dims, Gcol, xc, code, ws, a))
-            for (int l = 0; l < m; ++l) a[l] = 0.0f;
-        *cost = SampleCost(dims, Gcol, xc, code, a, xn2);
+    const GramShared G{ws.Gs, m};
+    if (do_init) {
+        LoadGram(dims, Gcol, code, ws.Gs);
+        if (lane == 0) {
+            if (!SolveLs(dims, G, xc, code, ws, a))
+                for (int l = 0; l < m; ++l) a[l] = 0.0f;
+            *cost = SampleCost(dims, G, xc, code, a, xn2);
+        }
     }
     __syncwarp();
     bool active = true;
@@ -326,12 +386,15 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
             }
             const int best = (best_s > __int_as_float(0xff800000)) ? best_t : old_code;
             if (best == old_code) continue;
+            __syncwarp();
+            if (lane == 0) code[j] = best;
+            UpdateGram(dims, Gcol, code, j, ws.Gs, ws.Gbak);
+            bool keep = false;
             if (lane == 0) {
                 for (int l = 0; l < m; ++l) ws.backup[l] = a[l];
-                code[j] = best;
-                bool keep = SolveLs(dims, Gcol, xc, code, ws, a);
+                keep = SolveLs(dims, G, xc, code, ws, a);
                 if (keep) {
-                    const float nc = SampleCost(dims, Gcol, xc, code, a, xn2);
+                    const float nc = SampleCost(dims, G, xc, code, a, xn2);
                     keep = add_rn(nc, kIcmEps) < *cost;
                     if (keep) {
                         *cost = nc;
@@ -344,6 +407,8 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
                 }
             }
             changed = __shfl_sync(0xffffffffu, changed, 0);
+            keep = __shfl_sync(0xffffffffu, keep, 0);
+            if (!keep) RestoreGram(m, j, ws.Gs, ws.Gbak);
             __syncwarp();
         }
         if (!changed) active = false;
@@ -368,8 +433,9 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
         if (lane < m) ws.code[lane] = p.B[vec * m + lane];
         __syncwarp();
         if (p.mode == 0) {
+            LoadGram(dims, p.Gcol, ws.code, ws.Gs);
             if (lane == 0) {
-                if (!SolveLs(dims, p.Gcol, xc, ws.code, ws, ws.a))
+                if (!SolveLs(dims, GramShared{ws.Gs, m}, xc, ws.code, ws, ws.a))
                     for (int l = 0; l < m; ++l) ws.a[l] = 0.0f;
             }
             __syncwarp();
@@ -382,7 +448,8 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
         // RunIcm's first step recomputes LS and cost for the beam codes (icm.cpp:109-114); with
         // the MSE requested, the LS result is also the beam-stage coefficients.
         RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, 0, p.orders, p.use_abs, ws.code, ws.a, &cost, ws);
-        if (p.partials && lane == 0) sse_beam += VectorSse(dims, p.Gcol, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+        if (p.partials && lane == 0)
+            sse_beam += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
         __syncwarp();
         if (p.icm_iters > 0)
             RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
@@ -420,7 +487,10 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
             }
             __syncwarp();
         }
-        if (p.partials && lane == 0) sse_final += VectorSse(dims, p.Gcol, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+        if (p.partials) {
+            if (p.n_ils > 0) LoadGram(dims, p.Gcol, ws.code, ws.Gs);  // the cache holds the last ILS candidate
+            if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+        }
         if (lane < m) {
             p.B[vec * m + lane] = static_cast<uint8_t>(ws.code[lane]);
             if (p.a) p.a[vec * m + lane] = ws.a[lane];
@@ -468,7 +538,8 @@ __global__ void SseKernel(Dims dims, const float* Gcol, const float* xC, const d
          v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         int code[kMaxM];
         for (int l = 0; l < dims.m; ++l) code[l] = B[v * dims.m + l];
-        s += VectorSse(dims, Gcol, xC + v * dims.H, code, a + v * dims.m, xnorm2_d[v]);
+        s += VectorSse(dims, GramGlobal{Gcol, dims.H, dims.off, code}, xC + v * dims.H, code, a + v * dims.m,
+                       xnorm2_d[v]);
     }
     red[threadIdx.x] = s;
     __syncthreads();
