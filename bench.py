@@ -365,7 +365,8 @@ def run_ours(args):
     total_mse = float(sse[1].item()) / (world * n)
     launches_per_step = 0
     slice_v = min((1 << 31) // (H * 4), 65535 * 64)
-    launches_per_step = ((n + slice_v - 1) // slice_v) * 4
+    # Per slice: xC GEMM, norms, beam fast + replay kernels, refine, partial-sum reduction.
+    launches_per_step = ((n + slice_v - 1) // slice_v) * 6
 
     # e2e: the same stage through the host-buffer C-ABI call (pinned host input and outputs;
     # H2D + encode + D2H inside the timed region, synchronous call, wall clock).

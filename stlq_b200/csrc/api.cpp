@@ -587,18 +587,8 @@ int stlq_b200_xnorm2(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int
     STLQ_TRY(CheckEnc(enc));
     if (n > 0 && (!X_dev || !xnorm2_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
-    // The norm is fused into the GEMM's first codeword tile: run a one-tile GEMM into scratch.
-    const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), stlq_b200::MaxGemmSliceVectors());
-    const int rows = std::min(enc->dims.H, 1);
-    STLQ_TRY(enc->xC.Ensure(static_cast<size_t>(S) * rows * sizeof(float)));
-    const size_t esz = ElemSize(x_dtype);
-    for (int64_t s0 = 0; s0 < n; s0 += S) {
-        const int64_t ns = std::min(S, n - s0);
-        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), rows, enc->dims.d,
-                                             static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
-                                             x_dtype, ns, enc->xC.as<float>(), rows, xnorm2_dev + s0, nullptr,
-                                             static_cast<cudaStream_t>(stream)));
-    }
+    STLQ_CK(stlq_b200::LaunchNorms(X_dev, x_dtype, n, enc->dims.d, xnorm2_dev, nullptr,
+                                   static_cast<cudaStream_t>(stream)));
     return 0;
 }
 
@@ -671,15 +661,13 @@ int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), stlq_b200::MaxGemmSliceVectors());
     STLQ_TRY(enc->xnd.Ensure(static_cast<size_t>(S) * sizeof(double)));
-    STLQ_TRY(enc->xC.Ensure(static_cast<size_t>(S) * sizeof(float)));
     const int grid = static_cast<int>(std::min<int64_t>((S + 255) / 256, int64_t{enc->num_sms} * 8));
     STLQ_TRY(enc->partials.Ensure(static_cast<size_t>(grid) * 2 * sizeof(double)));
     const size_t esz = ElemSize(x_dtype);
     for (int64_t s0 = 0; s0 < n; s0 += S) {
         const int64_t ns = std::min(S, n - s0);
-        STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), 1, enc->dims.d,
-                                             static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
-                                             x_dtype, ns, enc->xC.as<float>(), 1, nullptr, enc->xnd.as<double>(), s));
+        STLQ_CK(stlq_b200::LaunchNorms(static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
+                                       x_dtype, ns, enc->dims.d, nullptr, enc->xnd.as<double>(), s));
         const int g = static_cast<int>(std::min<int64_t>((ns + 255) / 256, grid));
         STLQ_CK(stlq_b200::LaunchSse(enc->dims, enc->Gcol.as<float>(), xC_dev + s0 * enc->dims.H, enc->xnd.as<double>(),
                                      B_dev + s0 * enc->dims.m, a_dev + s0 * enc->dims.m, ns, enc->partials.as<double>(),

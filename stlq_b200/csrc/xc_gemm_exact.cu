@@ -7,13 +7,14 @@
 // summed in order.  Reproducing that order makes xC, and therefore every later decision of the
 // encoder, bit-identical to the reference's.
 //
-// The same kernel fuses ||x||^2 per vector in the order GCC gives the reference's
-// `#pragma omp simd reduction` (4 lanes, tail into lane 0, lanes summed in order;
-// cost_utils.cpp:99-109, beam_search.cpp:218-223) plus the double-precision norm used by the MSE
-// (linkage_tools.cpp:187-191): the CTAs of the first codeword tile write them.
-//
-// Tiling: a CTA computes 128 codewords x 64 vectors; 256 threads, each an 8 x 4 register tile;
-// K advances 16 at a time through shared memory.  Output layout: xC[vec * H + codeword].
+// Tiling: a CTA computes 128 codewords x 128 vectors with 256 threads, each an 8 x 8 register tile
+// (rows tx*4..+3 and 64+tx*4..+3, vectors ty*4..+3 and 64+ty*4..+3, so that every shared-memory
+// read is a 128-bit broadcast or a conflict-free row).  K advances 16 at a time through two
+// shared-memory buffers: the next step's global loads are in flight while the current one is
+// multiplied, with one barrier per step.  Every K block boundary (a multiple of 16) falls between
+// steps; a partial last step runs only its kn terms, so no output gets an extra (+0) term.
+// Output layout: xC[vec * ldo + codeword].  ||x||^2 comes from LaunchNorms (same order as the
+// reference's SIMD loop).
 #include <cstdint>
 
 #include "common.cuh"
@@ -23,7 +24,7 @@ namespace stlq_b200 {
 
 namespace {
 
-constexpr int kBR = 128, kBJ = 64, kBK = 16, kTR = 8, kTJ = 4, kGemmThreads = 256;
+constexpr int kTM = 128, kTN = 128, kBK = 16, kGemmThreads = 256;
 
 __host__ __device__ __forceinline__ int NextKBlock(int rem) {
     const int Q = 448, U = 16;
@@ -32,149 +33,171 @@ __host__ __device__ __forceinline__ int NextKBlock(int rem) {
     return rem;
 }
 
+// Loads rows [row0, row0 + 128) x k [k0, k0 + 16) of a row-major matrix with `d` columns into
+// registers: thread t holds rows t/4 and t/4 + 64, columns 4*(t%4)..+3 (zero outside).
 template <typename T>
-__device__ __forceinline__ float ToF(T v) { return static_cast<float>(v); }
-
-template <typename T, bool kNorms>
-__global__ void __launch_bounds__(kGemmThreads) XcGemmExactKernel(const float* __restrict__ C, int rows, int d,
-                                                                  const T* __restrict__ X, int64_t n,
-                                                                  float* __restrict__ out, int ldo,
-                                                                  float* __restrict__ xnorm2,
-                                                                  double* __restrict__ xnorm2_d) {
-    __shared__ __align__(16) float Cs[kBK][kBR + 4];
-    __shared__ __align__(16) float Xs[kBK][kBJ + 4];
-    const int tid = threadIdx.x;
-    const int tr = tid % 16, tj = tid / 16;
-    const int r0 = blockIdx.x * kBR;
-    const int64_t j0 = static_cast<int64_t>(blockIdx.y) * kBJ;
-
-    float tot[kTR][kTJ], part[kTR][kTJ];
+struct TileLoader {
+    float v[2][4];
+    __device__ __forceinline__ void Load(const T* __restrict__ M, int64_t nrows, int d, int64_t row0, int k0,
+                                         bool vec4) {  // vec4: 4-element loads are aligned
+        const int tid = threadIdx.x;
+        const int kq = 4 * (tid & 3);
 #pragma unroll
-    for (int i = 0; i < kTR; ++i)
-#pragma unroll
-        for (int j = 0; j < kTJ; ++j) tot[i][j] = 0.0f;
-
-    // Norm lanes: thread (nj = tid / 4, lane = tid % 4) owns vector j0+nj, lane `lane`.
-    const bool do_norm = kNorms && blockIdx.x == 0;
-    float lane_sum = 0.0f;
-    double dsum = 0.0;
-    const int body = (d / 4) * 4;
-
-    bool first_block = true;
-    for (int kb0 = 0; kb0 < d;) {
-        const int kblk = NextKBlock(d - kb0);
-#pragma unroll
-        for (int i = 0; i < kTR; ++i)
-#pragma unroll
-            for (int j = 0; j < kTJ; ++j) part[i][j] = 0.0f;
-        for (int k0 = kb0; k0 < kb0 + kblk; k0 += kBK) {
-            const int kn = min(kBK, kb0 + kblk - k0);
-            // Stage C (128 x kn) and X (64 x kn), transposed to [k][row].
-            for (int e = tid; e < kBR * kBK; e += kGemmThreads) {
-                const int r = e / kBK, kk = e % kBK;
-                const int gr = r0 + r;
-                Cs[kk][r] = (kk < kn && gr < rows) ? __ldg(C + static_cast<size_t>(gr) * d + k0 + kk) : 0.0f;
-            }
-            for (int e = tid; e < kBJ * kBK; e += kGemmThreads) {
-                const int j = e / kBK, kk = e % kBK;
-                const int64_t gj = j0 + j;
-                Xs[kk][j] = (kk < kn && gj < n) ? ToF(X[gj * d + k0 + kk]) : 0.0f;
-            }
-            __syncthreads();
-            for (int kk = 0; kk < kn; ++kk) {
-                float a[kTR], b[kTJ];
-#pragma unroll
-                for (int i = 0; i < kTR; ++i) a[i] = Cs[kk][tr * kTR + i];
-#pragma unroll
-                for (int j = 0; j < kTJ; ++j) b[j] = Xs[kk][tj * kTJ + j];
-#pragma unroll
-                for (int i = 0; i < kTR; ++i)
-#pragma unroll
-                    for (int j = 0; j < kTJ; ++j) part[i][j] = __fmaf_rn(a[i], b[j], part[i][j]);
-            }
-            if (do_norm) {
-                const int nj = tid / 4, lane = tid % 4;
-                for (int kk = 0; kk < kn; ++kk) {
-                    const int k = k0 + kk;
-                    const float x = Xs[kk][nj];
-                    const bool mine = (k < body) ? ((k & 3) == lane) : (lane == 0);
-                    if (mine) {
-                        lane_sum = __fadd_rn(lane_sum, __fmul_rn(x, x));
-                        dsum = __dadd_rn(dsum, __dmul_rn(static_cast<double>(x), static_cast<double>(x)));
-                    }
+        for (int h = 0; h < 2; ++h) {
+            const int64_t r = row0 + (tid >> 2) + 64 * h;
+            const int k = k0 + kq;
+            if (r < nrows && vec4 && k + 3 < d) {
+                const T* p = M + r * d + k;
+                if constexpr (sizeof(T) == 4) {
+                    const float4 q = __ldg(reinterpret_cast<const float4*>(p));
+                    v[h][0] = q.x, v[h][1] = q.y, v[h][2] = q.z, v[h][3] = q.w;
+                } else {
+                    const uchar4 q = *reinterpret_cast<const uchar4*>(p);
+                    v[h][0] = q.x, v[h][1] = q.y, v[h][2] = q.z, v[h][3] = q.w;
                 }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    v[h][c] = (r < nrows && k + c < d) ? static_cast<float>(M[r * d + k + c]) : 0.0f;
             }
-            __syncthreads();
         }
-#pragma unroll
-        for (int i = 0; i < kTR; ++i)
-#pragma unroll
-            for (int j = 0; j < kTJ; ++j) tot[i][j] = first_block ? part[i][j] : __fadd_rn(tot[i][j], part[i][j]);
-        first_block = false;
-        kb0 += kblk;
     }
-
+    // Transposed into S[k][row].
+    __device__ __forceinline__ void Store(float (*S)[kTM]) const {
+        const int tid = threadIdx.x;
+        const int kq = 4 * (tid & 3);
 #pragma unroll
-    for (int j = 0; j < kTJ; ++j) {
-        const int64_t gj = j0 + tj * kTJ + j;
-        if (gj >= n) continue;
-        float* o = out + gj * ldo + r0 + tr * kTR;
-        if (r0 + tr * kTR + kTR <= rows && (ldo % 4) == 0) {
-            reinterpret_cast<float4*>(o)[0] = make_float4(tot[0][j], tot[1][j], tot[2][j], tot[3][j]);
-            reinterpret_cast<float4*>(o)[1] = make_float4(tot[4][j], tot[5][j], tot[6][j], tot[7][j]);
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) S[kq + c][(tid >> 2) + 64 * h] = v[h][c];
+    }
+};
+
+template <typename T, bool kMulti>
+__global__ void __launch_bounds__(kGemmThreads, kMulti ? 1 : 2)
+    XcGemmExactKernel(const float* __restrict__ C, int rows, int d, const T* __restrict__ X, int64_t n,
+                      float* __restrict__ out, int ldo, bool cvec, bool xvec, bool ovec) {
+    __shared__ __align__(16) float Cs[2][kBK][kTM];
+    __shared__ __align__(16) float Xs[2][kBK][kTN];
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int r0 = blockIdx.x * kTM;
+    const int64_t j0 = static_cast<int64_t>(blockIdx.y) * kTN;
+
+    float part[8][8];
+    float tot[kMulti ? 8 : 1][kMulti ? 8 : 1];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) part[i][j] = 0.0f;
+    bool first = true;
+    int kb_end = NextKBlock(d);  // end of the current K block
+
+    TileLoader<float> lc;
+    TileLoader<T> lx;
+    lc.Load(C, rows, d, r0, 0, cvec);
+    lx.Load(X, n, d, j0, 0, xvec);
+    lc.Store(Cs[0]);
+    lx.Store(Xs[0]);
+    __syncthreads();
+    const int steps = (d + kBK - 1) / kBK;
+    for (int s = 0; s < steps; ++s) {
+        const int k0 = s * kBK, buf = s & 1;
+        if (s + 1 < steps) {
+            lc.Load(C, rows, d, r0, k0 + kBK, cvec);
+            lx.Load(X, n, d, j0, k0 + kBK, xvec);
+        }
+        if (kMulti && k0 == kb_end) {  // a new K block: fold the finished block's chains
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if constexpr (kMulti) tot[i][j] = first ? part[i][j] : __fadd_rn(tot[i][j], part[i][j]);
+                    part[i][j] = 0.0f;
+                }
+            first = false;
+            kb_end += NextKBlock(d - k0);
+        }
+        const int kn = min(kBK, d - k0);
+        auto step = [&](int kk) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&Cs[buf][kk][tx * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&Cs[buf][kk][64 + tx * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Xs[buf][kk][ty * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Xs[buf][kk][64 + ty * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) part[i][j] = __fmaf_rn(a[i], b[j], part[i][j]);
+        };
+        if (kn == kBK) {
+#pragma unroll
+            for (int kk = 0; kk < kBK; ++kk) step(kk);
         } else {
-#pragma unroll
-            for (int i = 0; i < kTR; ++i)
-                if (r0 + tr * kTR + i < rows) o[i] = tot[i][j];
+            for (int kk = 0; kk < kn; ++kk) step(kk);
         }
+        if (s + 1 < steps) {
+            lc.Store(Cs[buf ^ 1]);
+            lx.Store(Xs[buf ^ 1]);
+        }
+        __syncthreads();
     }
 
-    if (do_norm) {
-        // Combine the 4 lanes of each vector in order: ((l0 + l1) + l2) + l3.
-        __shared__ float lanes[kBJ][4];
-        __shared__ double dl[kBJ][4];
-        const int nj = tid / 4, lane = tid % 4;
-        lanes[nj][lane] = lane_sum;
-        dl[nj][lane] = dsum;
-        __syncthreads();
-        if (tid < kBJ && j0 + tid < n) {
-            float s = __fadd_rn(lanes[tid][0], lanes[tid][1]);
-            s = __fadd_rn(s, lanes[tid][2]);
-            s = __fadd_rn(s, lanes[tid][3]);
-            if (xnorm2) xnorm2[j0 + tid] = s;
-            if (xnorm2_d) xnorm2_d[j0 + tid] = (dl[tid][0] + dl[tid][1]) + (dl[tid][2] + dl[tid][3]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int64_t gj = j0 + (j < 4 ? ty * 4 + j : 64 + ty * 4 + (j - 4));
+        if (gj >= n) continue;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if constexpr (kMulti) v[i] = first ? part[i][j] : __fadd_rn(tot[i][j], part[i][j]);
+            else v[i] = part[i][j];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = r0 + 64 * h + tx * 4;
+            float* o = out + gj * ldo + r;
+            if (r + 4 <= rows && ovec) {
+                *reinterpret_cast<float4*>(o) = make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (r + i < rows) o[i] = v[4 * h + i];
+            }
         }
     }
+}
+
+template <typename T>
+cudaError_t LaunchT(const float* C, int rows, int d, const T* X, int64_t n, float* out, int ldo, cudaStream_t stream) {
+    const int64_t gy = (n + kTN - 1) / kTN;
+    if (gy > 65535) return cudaErrorInvalidValue;  // callers slice n
+    dim3 grid((rows + kTM - 1) / kTM, static_cast<unsigned>(gy));
+    // Vector loads need every row to start aligned: d % 4 == 0 and an aligned base.
+    const bool cvec = d % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0;
+    const bool xvec = d % 4 == 0 && reinterpret_cast<uintptr_t>(X) % (4 * sizeof(T)) == 0;
+    const bool ovec = ldo % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    if (d > 448)
+        XcGemmExactKernel<T, true><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, X, n, out, ldo, cvec, xvec, ovec);
+    else
+        XcGemmExactKernel<T, false><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, X, n, out, ldo, cvec, xvec, ovec);
+    return cudaGetLastError();
 }
 
 }  // namespace
 
-// out (ldo-strided per vector) = C^T X for `rows` codewords; optional norms.
+// out (ldo-strided per vector) = C^T X for `rows` codewords; optional norms (LaunchNorms).
 cudaError_t LaunchXcGemmExact(const float* C, int rows, int d, const void* X, int x_dtype, int64_t n, float* out,
                               int ldo, float* xnorm2, double* xnorm2_d, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    const int64_t gy = (n + kBJ - 1) / kBJ;
-    if (gy > 65535) return cudaErrorInvalidValue;  // callers slice n
-    dim3 grid((rows + kBR - 1) / kBR, static_cast<unsigned>(gy));
-    const bool norms = xnorm2 || xnorm2_d;
-    if (x_dtype == 0) {
-        if (norms)
-            XcGemmExactKernel<float, true><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, static_cast<const float*>(X),
-                                                                             n, out, ldo, xnorm2, xnorm2_d);
-        else
-            XcGemmExactKernel<float, false><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, static_cast<const float*>(X),
-                                                                              n, out, ldo, nullptr, nullptr);
-    } else {
-        if (norms)
-            XcGemmExactKernel<uint8_t, true><<<grid, kGemmThreads, 0, stream>>>(
-                C, rows, d, static_cast<const uint8_t*>(X), n, out, ldo, xnorm2, xnorm2_d);
-        else
-            XcGemmExactKernel<uint8_t, false><<<grid, kGemmThreads, 0, stream>>>(
-                C, rows, d, static_cast<const uint8_t*>(X), n, out, ldo, nullptr, nullptr);
-    }
-    return cudaGetLastError();
+    cudaError_t e = x_dtype == 0 ? LaunchT(C, rows, d, static_cast<const float*>(X), n, out, ldo, stream)
+                                 : LaunchT(C, rows, d, static_cast<const uint8_t*>(X), n, out, ldo, stream);
+    if (e != cudaSuccess) return e;
+    if (xnorm2 || xnorm2_d) return LaunchNorms(X, x_dtype, n, d, xnorm2, xnorm2_d, stream);
+    return cudaSuccess;
 }
 
-int MaxGemmSliceVectors() { return 65535 * kBJ; }
+int MaxGemmSliceVectors() { return 65535 * 64; }
 
 }  // namespace stlq_b200

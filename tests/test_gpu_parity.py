@@ -133,3 +133,39 @@ def test_empty_and_single(cuda):
     assert r["B"].shape == (0, len(c["h_vec"]))
     r = enc.encode_base(c["X"], 4, 1)
     assert np.array_equal(r["B"], c["B"])
+
+
+@pytest.mark.parametrize("d,H,n", [(128, 2048, 1000), (4, 3, 5), (17, 300, 129), (100, 257, 333), (448, 130, 70),
+                                   (449, 128, 64), (960, 512, 257), (1000, 200, 131), (1345, 64, 40)])
+def test_exact_gemm_k_blocks_and_edges(cuda, oracle_lib, d, H, n):
+    """xC and ||x||^2 of the exact GEMM against the pinned restatement (bit-exact): K-block
+    boundaries, ragged codeword/vector tiles, d not a multiple of 4 (scalar loads)."""
+    import stlq_b200
+
+    rng = np.random.default_rng(d * 7 + H)
+    C = rng.standard_normal((H, d)).astype(np.float32)
+    X = (rng.standard_normal((n, d)) * 5).astype(np.float32)
+    enc = stlq_b200.Encoder(C, np.array([H], np.int32) if H <= 256 else np.array([256] * (H // 256) + ([H % 256] if H % 256 else []), np.int32))
+    Xt = torch.from_numpy(X).to(cuda)
+    assert np.array_equal(enc.xc_gemm(Xt).cpu().numpy(), oracle_lib.gemm_xc(C, X))
+    assert np.array_equal(enc.xnorm2(Xt).cpu().numpy(), oracle_lib.xnorm2(X))
+    enc.sync()
+
+
+def test_exact_gemm_u8_and_unaligned_input(cuda, oracle_lib):
+    """uint8 input equals its float copy; an input starting off a 16-byte boundary takes the
+    scalar-load path and gives the same bits."""
+    import stlq_b200
+
+    rng = np.random.default_rng(5)
+    d, H, n = 128, 512, 300
+    C = rng.standard_normal((H, d)).astype(np.float32)
+    Xu = rng.integers(0, 256, size=(n + 1, d), dtype=np.uint8)
+    enc = stlq_b200.Encoder(C, np.array([256, 256], np.int32))
+    ref = oracle_lib.gemm_xc(C, Xu[:n].astype(np.float32))
+    assert np.array_equal(enc.xc_gemm(torch.from_numpy(Xu[:n]).to(cuda)).cpu().numpy(), ref)
+    flat = torch.from_numpy(Xu.astype(np.float32).reshape(-1)).to(cuda)
+    shifted = flat[1:1 + n * d].view(n, d)  # 4-byte aligned, not 16-byte aligned
+    want = oracle_lib.gemm_xc(C, Xu.astype(np.float32).reshape(-1)[1:1 + n * d].reshape(n, d))
+    assert np.array_equal(enc.xc_gemm(shifted).cpu().numpy(), want)
+    enc.sync()

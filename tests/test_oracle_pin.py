@@ -94,3 +94,16 @@ def test_oracle_matches_reference_library(oracle_lib, shape):
     B2o, _, c2o = oracle_lib.icm(h, G, inv, xC, xn, Bo, icm, ils, 2, True, 99)
     assert np.array_equal(B2r.astype(np.uint16), B2o)
     assert np.array_equal(c2o, c2r)
+
+
+@pytest.mark.skipif(not ref_available, reason="oracle/_ref not built here")
+@pytest.mark.parametrize("d", [447, 448, 449, 500, 895, 896, 960, 1000, 1345])
+def test_oracle_gemm_k_blocks_match_reference(oracle_lib, d):
+    """The restated SGEMM K-block order (448-deep blocks, a remainder in (448, 896) halved and
+    rounded up to 16) against the reference's BLAS, for d on both sides of each boundary."""
+    rng = np.random.default_rng(d)
+    C = rng.standard_normal((37, d)).astype(np.float32)
+    X = (rng.standard_normal((19, d)) * 8).astype(np.float32)
+    P = oracle.Reference(threads=1).precomp([37], C)
+    assert np.array_equal(P.gemm_xc(X), oracle_lib.gemm_xc(C, X))
+    assert np.array_equal(P.xnorm2(X), oracle_lib.xnorm2(X))
