@@ -93,19 +93,19 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
             a_last = st[2 * MAXM + 1];
             e = ex[p];
         } else {
-            e = EvalExactL<MAXM>(cur, h, L, FlatOf<MAXM>(cur, h, L), Grow, H, offL + k, ak,
+            e = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, ak,
                                  __ldg(xc + offL + k), y, v, &denom, &a_last);
         }
 #pragma unroll
         for (int t = 0; t < NL; ++t) {
             if (t >= L) break;
-            nxt.flath(o)[t] = cur.flath(h)[t];
+            nxt.rowh(o)[t] = cur.rowh(h)[t];
             nxt.ah(o)[t] = sub_rn(cur.ah(h)[t], mul_rn(v[t], a_last));
             nxt.Rh(o)[L * MAXM + t] = y[t];
             nxt.rinvh(o)[t] = cur.rinvh(h)[t];
         }
         const float rll = __fsqrt_rn(denom);
-        nxt.flath(o)[L] = offL + k;
+        nxt.rowh(o)[L] = (offL + k) * H;
         nxt.ah(o)[L] = a_last;
         nxt.Rh(o)[L * MAXM + L] = rll;
         nxt.rinvh(o)[L] = __frcp_rn(rll);
@@ -115,16 +115,17 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
 }
 
 // No finite candidate in a layer (beam_search.cpp:385-400): the previous slots are kept.  The code
-// of this layer is written as 0 (flat index offL); the reference copies a stale buffer value there.
+// of this layer is written as 0 (Grow row row0 = offL * H); the reference copies a stale buffer
+// value there.
 template <int MAXM>
-__device__ int KeepPrevious(int L, int offL, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
+__device__ int KeepPrevious(int L, int row0, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
                             int beam) {
     const int tid = threadIdx.x;
     const int keep = min(curH, beam);
     for (int e = tid; e < keep * MAXM * MAXM; e += kThreads) nxt.R[e] = cur.R[e];
     for (int e = tid; e < keep * MAXM; e += kThreads) {
         const int t = e % MAXM;
-        nxt.flat[e] = t < L ? cur.flat[e] : offL;
+        nxt.row[e] = t < L ? cur.row[e] : row0;
         nxt.a[e] = t < L ? cur.a[e] : 0.0f;
         nxt.rinv[e] = cur.rinv[e];
     }
@@ -137,12 +138,13 @@ __device__ int KeepPrevious(int L, int offL, const SlotView<MAXM>& cur, const Sl
 
 // Layer 0 state of slot o holding codeword k (beam_search.cpp:248-258).
 template <int MAXM>
-__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, const float* Gdiag, const float* xc, float nx2) {
+__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, int H, const float* Gdiag, const float* xc,
+                          float nx2) {
     const float alpha = __ldg(Gdiag + k);
     const float gamma = __ldg(xc + k);
     const float a1 = div_rn(gamma, alpha);
     const float r00 = __fsqrt_rn(alpha);
-    s.flath(o)[0] = k;  // layer 0 starts at flat index 0
+    s.rowh(o)[0] = k * H;  // layer 0 starts at flat index 0
     s.ah(o)[0] = a1;
     s.E[o] = sub_rn(nx2, mul_rn(gamma, a1));
     s.Rh(o)[0] = r00;
@@ -157,7 +159,7 @@ template <int MAXM>
 __device__ void DeadSlot0(const Dims& dims, const SlotView<MAXM>& s) {
     const int tid = threadIdx.x;
     if (tid < MAXM) {
-        s.flath(0)[tid] = tid < dims.m ? dims.off[tid] : 0;
+        s.rowh(0)[tid] = tid < dims.m ? dims.off[tid] * dims.H : 0;
         s.ah(0)[tid] = 0.0f;
         s.rinvh(0)[tid] = 0.0f;
     }
@@ -188,7 +190,7 @@ __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int
                                          const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
                                          const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
                                          unsigned int* err_flag) {
-    const FlatArr<MAXM> flat = FlatOf<MAXM>(cur, h, L);
+    const RowArr<MAXM> flat = RowsOf<MAXM>(cur, h, L);
     for (int c = 0; c < kCpt; ++c) {
         if (!ok[c]) continue;
         const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, H, col[c], alpha[c], gamma[c], nullptr, nullptr,
@@ -218,10 +220,13 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
         alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
         gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
     }
+    const float* gq[kCpt];
+#pragma unroll
+    for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
     float hmin = PosInf();  // never NaN: a bound is finite or +-inf
     for (int h = 0; h < curH; ++h) {
         float l[kCpt], hi[kCpt];
-        CheapBounds<MAXM, L>(cur, h, Grow, H, col, ok, alpha, gamma, l, hi);
+        CheapBounds<MAXM, L>(cur, h, gq, ok, alpha, gamma, l, hi);
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) {
             if (ok[c]) {
@@ -359,7 +364,7 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     for (int p = tid; p < need; p += kThreads) {
         const int idx = list[p];
         const int h = idx / K, k = idx - h * K;
-        errs[idx] = EvalExactL<MAXM>(cur, h, L, FlatOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+        errs[idx] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
                                      __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
     }
     __syncthreads();
@@ -372,7 +377,7 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     __syncthreads();
     const int newH = lt.n_slots;
     if (newH == 0) {
-        curH = KeepPrevious<MAXM>(L, offL, cur, nxt, curH, beam);
+        curH = KeepPrevious<MAXM>(L, offL * H, cur, nxt, curH, beam);
     } else {
         Materialize<MAXM>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc);
         curH = newH;
@@ -412,7 +417,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         __syncthreads();
         int curH = lt.n_slots;
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
+        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.H, Gdiag, xc, nx2);
         if (curH == 0) {
             DeadSlot0<MAXM>(dims, s0);
             curH = 1;
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
             const uint32_t key = tid < curH ? OrderKey(cur.E[tid]) : 0xffffffffu;
             const uint32_t kmin = __reduce_min_sync(kFull, key);
             const int best = __ffs(__ballot_sync(kFull, key == kmin)) - 1;
-            if (tid < m) Bout[vec * m + tid] = static_cast<uint8_t>(cur.flath(best)[tid] - dims.off[tid]);
+            if (tid < m) Bout[vec * m + tid] = static_cast<uint8_t>(cur.rowh(best)[tid] / dims.H - dims.off[tid]);
         }
         __syncthreads();
     }
@@ -597,7 +602,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
         const int h = idx / K, k = idx - h * K;
         float* st = keep + p * KeepStride<MAXM>();
         const bool kp = p < kKeep;
-        ex[p] = EvalExactL<MAXM>(cur, h, L, FlatOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+        ex[p] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
                                  __ldg(xc + offL + k), kp ? st : nullptr, kp ? st + MAXM : nullptr,
                                  kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr);
     }
@@ -605,7 +610,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
     const int newH = RankSurvivors(ex, surv, S, beam, lt, keys);
     if (newH < 0) return -1;
     if (newH == 0) {
-        const int kept = KeepPrevious<MAXM>(L, offL, cur, nxt, curH, beam);
+        const int kept = KeepPrevious<MAXM>(L, offL * H, cur, nxt, curH, beam);
         __syncthreads();
         return kept;
     }
@@ -656,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
             curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
         }
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], Gdiag, xc, nx2);
+        if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.H, Gdiag, xc, nx2);
         if (curH == 0) {
             DeadSlot0<MAXM>(dims, s0);
             curH = 1;
@@ -679,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         if (redo) {
             if (tid == 0) redo_list[atomicAdd(redo_count, 1)] = static_cast<int>(vec);
         } else if (tid < m) {
-            Bout[vec * m + tid] = static_cast<uint8_t>(cur.flath(0)[tid] - dims.off[tid]);
+            Bout[vec * m + tid] = static_cast<uint8_t>(cur.rowh(0)[tid] / dims.H - dims.off[tid]);
         }
         __syncthreads();
     }

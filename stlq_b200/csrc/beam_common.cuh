@@ -29,12 +29,12 @@ struct SlotView {
     float* rinv;  // [beam][MAXM] 1/R_ii (cheap bound only)
     float* a;     // [beam][MAXM]
     float* E;     // [beam]
-    int* flat;    // [beam][MAXM] flat codeword index of each prefix code (layer offset + code)
+    int* row;     // [beam][MAXM] row of each prefix codeword in Grow: (layer offset + code) * H
     int* ill;     // [beam] 1 when any pivot was ill-conditioned
     __device__ float* Rh(int h) const { return R + h * MAXM * MAXM; }
     __device__ float* rinvh(int h) const { return rinv + h * MAXM; }
     __device__ float* ah(int h) const { return a + h * MAXM; }
-    __device__ int* flath(int h) const { return flat + h * MAXM; }
+    __device__ int* rowh(int h) const { return row + h * MAXM; }
     // Rounded to 16 bytes: a second buffer placed after the first stays 16-byte aligned.
     __host__ __device__ static constexpr size_t Bytes(int beam) {
         return (sizeof(float) * static_cast<size_t>(beam) * (MAXM * MAXM + 2 * MAXM + 1) +
@@ -46,8 +46,8 @@ struct SlotView {
         v.R = reinterpret_cast<float*>(p);
         v.rinv = v.R + beam * MAXM * MAXM;
         v.a = v.rinv + beam * MAXM;
-        v.flat = reinterpret_cast<int*>(v.a + beam * MAXM);  // 16-byte aligned rows (int4 loads)
-        v.E = reinterpret_cast<float*>(v.flat + beam * MAXM);
+        v.row = reinterpret_cast<int*>(v.a + beam * MAXM);  // 16-byte aligned per slot (int4 loads)
+        v.E = reinterpret_cast<float*>(v.row + beam * MAXM);
         v.ill = reinterpret_cast<int*>(v.E + beam);
         return v;
     }
@@ -58,19 +58,19 @@ struct SlotView {
 // larger than the instruction cache, and instruction fetch became their main stall.  Loops run to
 // the compile-time bound NL = MAXM - 1 with warp-uniform guards on L.
 
-// Flat codeword indices of slot h's prefix (passed by value so they stay in registers).
+// Grow row offsets of slot h's prefix codewords (passed by value so they stay in registers).
 template <int MAXM>
-struct FlatArr {
+struct RowArr {
     int v[MAXM];
 };
 
 template <int MAXM>
-__device__ __forceinline__ FlatArr<MAXM> FlatOf(const SlotView<MAXM>& cur, int h, int L) {
-    FlatArr<MAXM> f;
+__device__ __forceinline__ RowArr<MAXM> RowsOf(const SlotView<MAXM>& cur, int h, int L) {
+    RowArr<MAXM> f;
 #pragma unroll
     for (int t = 0; t < MAXM; ++t) {
         if (t >= L) break;
-        f.v[t] = cur.flath(h)[t];
+        f.v[t] = cur.rowh(h)[t];
     }
     return f;
 }
@@ -82,7 +82,7 @@ __device__ __forceinline__ FlatArr<MAXM> FlatOf(const SlotView<MAXM>& cur, int h
 // (e >= +inf or NaN, :320).  Optionally returns y, v, denom and a_last for materialisation.
 // NL bounds L; with kFixed the layer is NL itself (a per-layer copy).
 template <int MAXM, int NL, bool kFixed>
-__device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt, const FlatArr<MAXM> flat,
+__device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt, const RowArr<MAXM> flat,
                                         const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
                                         float* y_out, float* v_out, float* denom_out, float* alast_out) {
     const int L = kFixed ? NL : Lrt;
@@ -92,7 +92,7 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt
 #pragma unroll
     for (int t = 0; t < NL; ++t) {
         if (t >= L) break;
-        A[t] = __ldg(Grow + static_cast<size_t>(flat.v[t]) * H + col);
+        A[t] = __ldg(Grow + flat.v[t] + col);
     }
 #pragma unroll
     for (int i = 0; i < NL; ++i) {
@@ -142,7 +142,7 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt
 // code); in the 16-layer kernel, whose per-layer copies would not fit the instruction cache, one
 // copy for L <= 7 and one for the rest.
 template <int MAXM>
-__device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, int L, const FlatArr<MAXM>& flat,
+__device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, int L, const RowArr<MAXM>& flat,
                                             const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
                                             float* y_out, float* v_out, float* denom_out, float* alast_out) {
 #define STLQ_B200_EXACT(NL, FIX) \
@@ -165,7 +165,8 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 }
 
 // Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
-// kCpt codewords (col[q]; the values of a codeword with !ok[q] are meaningless and unused).  L is a compile-time constant here: this is the hot
+// kCpt codewords (Gram column pointers gq[q] = Grow + col[q]; the values of a codeword with !ok[q]
+// are meaningless and unused).  L is a compile-time constant here: this is the hot
 // loop, and each layer's copy is small (see CheapPass in beam.cu).
 // e' = E_old - diff^2/denom with y from FMA forward substitution, delta = |y|^2, eta = A.a.  The
 // half-width covers the rounding of both this and the exact sequence: relative errors of order
@@ -174,22 +175,22 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 // whose cheap value is unreliable (ill-conditioned slot, denom <= kDenomGuard * alpha, NaN)
 // gets [-inf, +inf].
 template <int MAXM, int L>
-__device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* __restrict__ Grow, int H,
-                                            const int (&col)[kCpt], const bool (&ok)[kCpt],
+__device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* const (&gq)[kCpt],
+                                            const bool (&ok)[kCpt],
                                             const float (&alpha)[kCpt], const float (&gamma)[kCpt],
                                             float (&lo)[kCpt], float (&hi)[kCpt]) {
     const float* Rh = cur.Rh(h);
     const float* rinv = cur.rinvh(h);
     const float* ah = cur.ah(h);
-    const int* fl = cur.flath(h);
+    const int* rw = cur.rowh(h);
     // Slot values are warp-uniform shared-memory broadcasts, loaded where they are used (loading
     // them ahead into registers costs more in spills than it saves in load instructions).
     float A[kCpt][L], y[kCpt][L];
 #pragma unroll
     for (int i = 0; i < L; ++i) {
-        const size_t row = static_cast<size_t>(fl[i]) * H;
+        const int r = rw[i];
 #pragma unroll
-        for (int q = 0; q < kCpt; ++q) A[q][i] = ok[q] ? __ldg(Grow + row + col[q]) : 0.0f;
+        for (int q = 0; q < kCpt; ++q) A[q][i] = ok[q] ? __ldg(gq[q] + r) : 0.0f;
     }
     float delta[kCpt], eta[kCpt], seta[kCpt];
 #pragma unroll
