@@ -434,6 +434,20 @@ def run_ours(args):
                    "sample": f"first {ns} vectors of rank 0's shard, same codebooks and settings, "
                              f"reference CPU encoder (oracle/_ref) with {cores} threads, "
                              f"OpenBLAS core {(code_match or {}).get('reference_blas_core')}"}
+            if code_match is not None:  # the remaining parity metrics: coefficients, costs, MSE
+                a_gpu = a[:ns].cpu().numpy()
+                cost_gpu = cost[:ns].cpu().numpy()
+                same = (B[:ns].cpu().numpy() == ref_sample["B"]).all(1)
+                rel = np.abs(cost_gpu[~same].astype(np.float64) - ref_sample["cost"][~same]) / \
+                    np.maximum(np.abs(ref_sample["cost"][~same].astype(np.float64)), 1e-30)
+                ours_mse = float(recon_sse(X_np[:ns], C_np, h_vec, B[:ns].cpu().numpy(), a_gpu).mean())
+                ref_mse = float(recon_sse(X_np[:ns], C_np, h_vec, ref_sample["B"], ref_sample["a"]).mean())
+                code_match.update({
+                    "coeff_max_abs_diff": float(np.abs(a_gpu - ref_sample["a"]).max()),
+                    "cost_bit_identical": bool(np.array_equal(cost_gpu, ref_sample["cost"])),
+                    "mismatched_cost_rel_max": float(rel.max()) if rel.size else 0.0,
+                    "mse_rel_diff": abs(ours_mse - ref_mse) / ref_mse,
+                })
         except Exception as exc:  # the reference library did not travel or does not load
             cpu = {"value": None, "unit": "vectors/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {exc}"}
