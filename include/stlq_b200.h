@@ -147,6 +147,37 @@ int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const 
 int stlq_b200_beam_search_noalloc(stlq_b200_encoder* enc, const float* xnorm2_dev, const float* xC_dev, int64_t n,
                                   int beam, uint8_t* B_dev, void* stream);
 
+/* ---- Large-root encoder (the large pipeline's basic encode) ----
+ * Replaces BuildPrecompLargeRoot (src/quantizer/precomp_large_root.cpp:27-160),
+ * BeamSearchPrefixLSLargeRoot (src/quantizer/beam_search.cpp:579-992, declared in
+ * include/stlq/quantizer/beam_search.h:26-32), SolveLeastSquaresAllLargeRoot
+ * (least_squares.cpp:567-745), ComputeCostsLargeRoot (cost_utils.cpp:160-235) and
+ * DynamicIcmWithIls{Abs,NoAbs}NoNormalLargeRoot (icm.cpp:347-870, 1005-1210), as the large
+ * pipeline runs them per block (src/quantizer/encode_base_streaming.cpp:1040-1300).
+ * Codebook 0 of C_all is the root (cluster ids); this build supports h_vec[0] <= 256.  The
+ * large-root arithmetic differs from the regular encoder's in the root codewords' norms and the
+ * root dot products (the reference's SIMD-order loops), the beam's triangular solves (multiplied
+ * by 1/R_ii) and the cost's summation order; the codes equal the reference's large-root codes.
+ * The stage entry points above also accept such a handle (codes as m x n, root first). */
+int stlq_b200_create_large_root(int device, int d, int m, const int* h_vec, const float* C_all, int gemm_mode,
+                                stlq_b200_encoder** out);
+
+/* Host buffers.  cluster_out: n root codes; B_small_out: (m-1) x n codes of layers 1..m-1;
+ * a_out: m x n coefficients; cost_out: n final costs (may be NULL); cost_sums_out: 2 doubles
+ * (may be NULL): the sums over vectors of the beam-stage and the final SampleCostLargeRoot, whose
+ * means the large pipeline reports as beam and final MSE. */
+int stlq_b200_encode_base_large_root(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam,
+                                     int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                     uint64_t sample_id_offset, uint32_t* cluster_out, uint8_t* B_small_out,
+                                     float* a_out, float* cost_out, double* cost_sums_out);
+
+/* Device buffers, asynchronous on `stream` (cost_sums_dev: 2 doubles on the device or NULL). */
+int stlq_b200_encode_base_large_root_device(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n,
+                                            int beam, int icm_iters, int ils_iters, int perturb_k, int use_abs,
+                                            uint32_t seed, uint64_t sample_id_offset, uint32_t* cluster_dev,
+                                            uint8_t* B_small_dev, float* a_dev, float* cost_dev,
+                                            double* cost_sums_dev, void* stream);
+
 /* Block until all work this encoder enqueued on `stream` has finished; returns
  * STLQ_B200_EDEVICE if a kernel flagged an internal error since the last check. */
 int stlq_b200_sync(stlq_b200_encoder* enc, void* stream);

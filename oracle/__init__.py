@@ -205,6 +205,29 @@ class Reference:
     def precomp(self, h_vec, C_all):
         return RefPrecomp(self, h_vec, C_all)
 
+    def large_root_encode(self, h_vec, C_all, X, beam, icm_iters, ils_iters=0, perturb_k=0, use_abs=True,
+                          seed=38251450, sample_id_offset=0):
+        """The large pipeline's basic encode (BuildPrecompLargeRoot + BeamSearchPrefixLSLargeRoot +
+        SolveLeastSquaresAllLargeRoot + ComputeCostsLargeRoot + DynamicIcmWithIls*LargeRoot).
+        C_all: (H, d) with the root codewords first; X: (n, d)."""
+        h = np.asarray(h_vec, np.int32)
+        C, Xf = _f32(C_all), _f32(X)
+        m, n, d = len(h), Xf.shape[0], Xf.shape[1]
+        cluster = np.empty(n, np.uint32)
+        B_small = np.empty((n, max(m - 1, 0)), np.uint8)
+        a = np.empty((n, m), np.float32)
+        cost_beam = np.empty(n, np.float32)
+        cost = np.empty(n, np.float32)
+        rc = self.lib.ref_large_root_encode(
+            ctypes.c_int(d), ctypes.c_int(m), _p(h, _i32p), _p(C, _f32p), _p(Xf, _f32p), ctypes.c_int(n),
+            ctypes.c_int(beam), ctypes.c_int(icm_iters), ctypes.c_int(ils_iters), ctypes.c_int(perturb_k),
+            ctypes.c_int(int(bool(use_abs))), ctypes.c_uint32(seed & 0xFFFFFFFF), ctypes.c_uint64(sample_id_offset),
+            cluster.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), B_small.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+            _p(a, _f32p), _p(cost_beam, _f32p), _p(cost, _f32p))
+        if rc != 0:
+            raise RuntimeError(f"ref_large_root_encode failed ({rc})")
+        return dict(cluster=cluster, B_small=B_small, a=a, cost_beam=cost_beam, cost=cost)
+
 
 class RefPrecomp:
     def __init__(self, ref: Reference, h_vec, C_all):

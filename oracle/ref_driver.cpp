@@ -10,11 +10,14 @@
 //     and calls the reference's stlq::Gemm for G, exactly as BuildPrecomp does.
 //   - ref_encode_base restates the stage order of EncodeBase
 //     (src/quantizer/encoder_encode_base.inc:1-106), CPU branch.
+//   - ref_large_root_encode restates the stage order of the large pipeline's basic encode
+//     (src/quantizer/encode_base_streaming.cpp:1040-1300, CPU branch).
 #include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include <omp.h>
@@ -27,6 +30,7 @@
 #include "stlq/quantizer/cost_utils.h"
 #include "stlq/quantizer/icm.h"
 #include "stlq/quantizer/least_squares.h"
+#include "stlq/quantizer/precomp_large_root.h"
 
 extern "C" char* openblas_get_corename(void);
 
@@ -243,6 +247,54 @@ int ref_encode_base(void* h, const float* X, int n, int beam, int icm_iters, int
         t_stages[3] = t4 - t3;
         t_stages[4] = t5 - t4;
     }
+    return 0;
+}
+
+// Large-root basic encode: BuildPrecompLargeRoot (codebook 0 is the root), ComputeXcSmall,
+// BeamSearchPrefixLSLargeRoot, SolveLeastSquaresAllLargeRoot + ComputeCostsLargeRoot (the beam
+// costs), DynamicIcmWithIls{Abs,NoAbs}NoNormalLargeRoot (final codes, coefficients and costs).
+// C_all: d x H column-major, root codewords first.  Outputs: cluster (n), B_small ((m-1) x n),
+// a (m x n), cost_beam and cost (n each; may be null).  Returns 0 on success.
+int ref_large_root_encode(int d, int m, const int* h_vec, const float* C_all, const float* X, int n, int beam,
+                          int icm_iters, int ils_iters, int perturb_k, int use_abs, std::uint32_t seed,
+                          std::uint64_t sample_id_offset, std::uint32_t* cluster_out, std::uint8_t* B_small_out,
+                          float* a_out, float* cost_beam_out, float* cost_out) {
+    if (n <= 0 || d <= 0 || m <= 0) return 1;
+    stlq::CodebookPack pack;
+    pack.d = d;
+    int off = 0;
+    for (int l = 0; l < m; ++l) {
+        pack.h_vec.push_back(h_vec[l]);
+        pack.books.push_back(Wrap(C_all + static_cast<std::size_t>(off) * d, d, h_vec[l]));
+        off += h_vec[l];
+    }
+    stlq::PrecompLargeRoot pre;
+    stlq::PrecompLargeRootBuildOptions opts;
+    std::string err;
+    if (!stlq::BuildPrecompLargeRoot(pack, nullptr, opts, &pre, &err)) return 2;
+    ColMajorMatrix<float> Xm = Wrap(X, d, n);
+    ColMajorMatrix<float> xC_small;
+    stlq::ComputeXcSmall(pre, Xm, nullptr, &xC_small);
+    std::vector<std::uint32_t> cluster;
+    ColMajorMatrix<stlq::Code> B_small;
+    stlq::BeamSearchPrefixLSLargeRoot(Xm, pre, xC_small, std::max(1, beam), &cluster, &B_small, nullptr);
+    ColMajorMatrix<float> a;
+    stlq::SolveLeastSquaresAllLargeRoot(pre, Xm, xC_small, cluster, B_small, &a);
+    std::vector<float> xn, cost_beam, cost;
+    stlq::ComputeXNorm2(Xm, &xn);
+    stlq::ComputeCostsLargeRoot(pre, Xm, xC_small, cluster, B_small, a, xn, &cost_beam);
+    if (use_abs) {
+        stlq::DynamicIcmWithIlsAbsNoNormalLargeRoot(Xm, pre, xC_small, icm_iters, ils_iters, perturb_k, seed, cluster,
+                                                    &B_small, &a, &xn, &cost, false, sample_id_offset);
+    } else {
+        stlq::DynamicIcmWithIlsNoAbsNoNormalLargeRoot(Xm, pre, xC_small, icm_iters, ils_iters, perturb_k, seed,
+                                                      cluster, &B_small, &a, &xn, &cost, false, sample_id_offset);
+    }
+    std::memcpy(cluster_out, cluster.data(), sizeof(std::uint32_t) * n);
+    if (m > 1) std::memcpy(B_small_out, B_small.data.data(), B_small.data.size());
+    if (a_out) std::memcpy(a_out, a.data.data(), sizeof(float) * a.data.size());
+    if (cost_beam_out) std::memcpy(cost_beam_out, cost_beam.data(), sizeof(float) * n);
+    if (cost_out && cost.size() == static_cast<std::size_t>(n)) std::memcpy(cost_out, cost.data(), sizeof(float) * n);
     return 0;
 }
 

@@ -134,7 +134,7 @@ struct stlq_b200_encoder {
     // Tensor-core modes: C_all split into TF32 hi / lo parts once at create.
     DevBuf Chi, Clo;
     // Per-call scratch, grown on demand and kept for the handle's lifetime.
-    DevBuf xC, xn, xnd, partials, orders, redo, Xhi, Xlo;
+    DevBuf xC, xn, xnd, partials, orders, redo, Xhi, Xlo, Bfull;
     std::vector<int> orders_host;
     int64_t orders_key[4] = {-1, -1, -1, -1};
     // Host path.
@@ -255,6 +255,9 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
                                             enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->redo.as<int>(),
                                             enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
+        if (dims.large_root)  // LS, cost and ICM take the root term from the SIMD-order dot
+            STLQ_CK(stlq_b200::LaunchRootDot(dims, enc->C.as<float>(), Xs, x_dtype, B + s0 * dims.m, ns,
+                                             enc->xC.as<float>(), stream));
         stlq_b200::RefineArgs ra{};
         ra.dims = dims;
         ra.Gcol = enc->Gcol.as<float>();
@@ -411,7 +414,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
     for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
-                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
+                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
         enc->xin[i].Release();
@@ -565,6 +568,76 @@ int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, in
         std::memcpy(sse_out, enc->pin_sse.p, 2 * sizeof(double));
     }
     return stlq_b200_sync(enc, cs);
+}
+
+int stlq_b200_create_large_root(int device, int d, int m, const int* h_vec, const float* C_all, int gemm_mode,
+                                stlq_b200_encoder** out) {
+    if (!out) return Fail(STLQ_B200_EINVAL, "out is null");
+    *out = nullptr;
+    if (m < 2) return Fail(STLQ_B200_EINVAL, "a large-root encoder needs m >= 2 (a root and at least one small codebook)");
+    STLQ_TRY(stlq_b200_create(device, d, m, h_vec, C_all, nullptr, nullptr, gemm_mode, out));
+    stlq_b200_encoder* enc = *out;
+    DeviceScope scope(enc->device);
+    enc->dims.large_root = 1;
+    DevBuf norms;
+    int rc = norms.Ensure(sizeof(float) * enc->dims.H);
+    cudaStream_t s = enc->compute;
+    auto ck = [&](cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return 0;
+        return Fail(STLQ_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    if (!rc) rc = ck(stlq_b200::LaunchNorms(enc->C.p, STLQ_B200_F32, enc->dims.H, d, norms.as<float>(), nullptr, s),
+                     "codeword norms");
+    if (!rc) rc = ck(stlq_b200::LaunchLargeRootPrecomp(norms.as<float>(), enc->dims.h_vec[0], enc->dims.H,
+                                                       enc->Gcol.as<float>(), enc->Grow.as<float>(),
+                                                       enc->Gdiag.as<float>(), enc->invnorm.as<float>(), s),
+                     "large-root precompute");
+    if (!rc) rc = ck(cudaStreamSynchronize(s), "create sync");
+    norms.Release();
+    if (rc) {
+        stlq_b200_destroy(enc);
+        *out = nullptr;
+    }
+    return rc;
+}
+
+int stlq_b200_encode_base_large_root(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam,
+                                     int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                     uint64_t sample_id_offset, uint32_t* cluster_out, uint8_t* B_small_out,
+                                     float* a_out, float* cost_out, double* cost_sums_out) {
+    STLQ_TRY(CheckEnc(enc));
+    if (!enc->dims.large_root) return Fail(STLQ_B200_EINVAL, "encoder was not created by stlq_b200_create_large_root");
+    if (n > 0 && (!cluster_out || !B_small_out)) return Fail(STLQ_B200_EINVAL, "cluster_out and B_small_out must be non-null");
+    const int m = enc->dims.m;
+    std::vector<uint8_t> B(static_cast<size_t>(std::max<int64_t>(n, 0)) * m);
+    STLQ_TRY(stlq_b200_encode_base(enc, X, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
+                                   sample_id_offset, B.data(), a_out, cost_out, cost_sums_out));
+    for (int64_t v = 0; v < n; ++v) {
+        const uint8_t* b = B.data() + v * m;
+        cluster_out[v] = b[0];
+        std::memcpy(B_small_out + v * (m - 1), b + 1, m - 1);
+    }
+    return 0;
+}
+
+int stlq_b200_encode_base_large_root_device(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n,
+                                            int beam, int icm_iters, int ils_iters, int perturb_k, int use_abs,
+                                            uint32_t seed, uint64_t sample_id_offset, uint32_t* cluster_dev,
+                                            uint8_t* B_small_dev, float* a_dev, float* cost_dev,
+                                            double* cost_sums_dev, void* stream) {
+    STLQ_TRY(CheckEncodeArgs(enc, x_dtype, n, beam, icm_iters, ils_iters, perturb_k));
+    if (!enc->dims.large_root) return Fail(STLQ_B200_EINVAL, "encoder was not created by stlq_b200_create_large_root");
+    if (n > 0 && (!X_dev || !cluster_dev || !B_small_dev))
+        return Fail(STLQ_B200_EINVAL, "X_dev, cluster_dev and B_small_dev must be non-null");
+    DeviceScope scope(enc->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (n <= 0) return 0;
+    STLQ_TRY(enc->Bfull.Ensure(static_cast<size_t>(n) * enc->dims.m));
+    if (cost_sums_dev) STLQ_CK(cudaMemsetAsync(cost_sums_dev, 0, 2 * sizeof(double), s));
+    STLQ_TRY(EncodeDevice(enc, X_dev, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
+                          sample_id_offset, enc->Bfull.as<uint8_t>(), a_dev, cost_dev, cost_sums_dev, s));
+    STLQ_CK(stlq_b200::LaunchSplitRootCodes(enc->dims.m, enc->Bfull.as<uint8_t>(), n, cluster_dev, B_small_dev, s));
+    return 0;
 }
 
 int stlq_b200_xc_gemm(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* xC_dev, void* stream) {

@@ -94,7 +94,7 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
             e = ex[p];
         } else {
             e = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, ak,
-                                 __ldg(xc + offL + k), y, v, &denom, &a_last);
+                                 __ldg(xc + offL + k), y, v, &denom, &a_last, dims.large_root != 0);
         }
 #pragma unroll
         for (int t = 0; t < NL; ++t) {
@@ -189,12 +189,12 @@ template <int MAXM>
 __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int H,
                                          const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
                                          const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
-                                         unsigned int* err_flag) {
+                                         unsigned int* err_flag, bool recip) {
     const RowArr<MAXM> flat = RowsOf<MAXM>(cur, h, L);
     for (int c = 0; c < kCpt; ++c) {
         if (!ok[c]) continue;
         const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, H, col[c], alpha[c], gamma[c], nullptr, nullptr,
-                                         nullptr, nullptr);
+                                         nullptr, nullptr, recip);
         if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
     }
 }
@@ -207,7 +207,7 @@ template <int MAXM, int L, bool kHi>
 __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int H,
                                            const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                                            const float* __restrict__ xc, float* lo, float* hi_out, int check,
-                                           unsigned int* err_flag) {
+                                           unsigned int* err_flag, bool recip) {
     const int tid = threadIdx.x;
     float alpha[kCpt], gamma[kCpt];
     int col[kCpt];
@@ -235,7 +235,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
                 hmin = fminf(hmin, hi[c]);
             }
         }
-        if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag);
+        if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag, recip);
     }
     return OrderKey(hmin);
 }
@@ -243,11 +243,11 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
 template <int MAXM, bool kHi>
 __device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int H,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
-                                  int check, unsigned int* err) {
+                                  int check, unsigned int* err, bool recip) {
 #define STLQ_B200_CHEAP(LL)                                                                          \
     case LL:                                                                                         \
         if constexpr (LL < MAXM)                                                                     \
-            return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, H, Grow, Gdiag, xc, lo, hi_out, check, err); \
+            return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, H, Grow, Gdiag, xc, lo, hi_out, check, err, recip); \
         break;
     switch (L) {
         STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
@@ -350,7 +350,7 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
     const int n_cand = curH * K;
-    CheapDispatch<MAXM, true>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, errs, his, 0, nullptr);
+    CheapDispatch<MAXM, true>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, errs, his, 0, nullptr, dims.large_root != 0);
     __syncthreads();
     int* list = reinterpret_cast<int*>(his);
     if (tid < 32) {
@@ -365,7 +365,7 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
         const int idx = list[p];
         const int h = idx / K, k = idx - h * K;
         errs[idx] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
-                                     __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr);
+                                     __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr, dims.large_root != 0);
     }
     __syncthreads();
     if (tid < 32) {
@@ -594,7 +594,8 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
     const uint32_t hmin =
-        CheapDispatch<MAXM, false>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, lo, nullptr, check, err_flag);
+        CheapDispatch<MAXM, false>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
+                                   dims.large_root != 0);
     const int S = SelectSurvivors(lo, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     for (int p = tid; p < S; p += kThreads) {
@@ -604,7 +605,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
         const bool kp = p < kKeep;
         ex[p] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
                                  __ldg(xc + offL + k), kp ? st : nullptr, kp ? st + MAXM : nullptr,
-                                 kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr);
+                                 kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr, dims.large_root != 0);
     }
     __syncthreads();
     const int newH = RankSurvivors(ex, surv, S, beam, lt, keys);

@@ -80,13 +80,16 @@ __device__ __forceinline__ RowArr<MAXM> RowsOf(const SlotView<MAXM>& cur, int h,
 // eta = A.a_old, :299-305; denom, a_last, e with the clamp at 0, :307-318).  Returns the error,
 // +inf for a candidate the reference skips (denom == 0) or that can never enter the beam
 // (e >= +inf or NaN, :320).  Optionally returns y, v, denom and a_last for materialisation.
-// NL bounds L; with kFixed the layer is NL itself (a per-layer copy).
+// NL bounds L; with kFixed the layer is NL itself (a per-layer copy).  With `recip` (large-root
+// encoders) both substitutions multiply by the float reciprocal 1/R_ii, held in the slot as rinv,
+// as BeamSearchPrefixLSLargeRoot's SolveCholUpperRawBatched does (beam_search.cpp:517-575).
 template <int MAXM, int NL, bool kFixed>
 __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt, const RowArr<MAXM> flat,
                                         const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
-                                        float* y_out, float* v_out, float* denom_out, float* alast_out) {
+                                        float* y_out, float* v_out, float* denom_out, float* alast_out, bool recip) {
     const int L = kFixed ? NL : Lrt;
     const float* Rh = cur.Rh(h);
+    const float* rinv = cur.rinvh(h);
     const float* ah = cur.ah(h);
     float A[NL], y[NL], v[NL];
 #pragma unroll
@@ -100,7 +103,7 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt
         float s = A[i];
 #pragma unroll
         for (int k = 0; k < i; ++k) s = sub_rn(s, mul_rn(Rh[i * MAXM + k], y[k]));
-        y[i] = div_rn(s, Rh[i * MAXM + i]);
+        y[i] = recip ? mul_rn(s, rinv[i]) : div_rn(s, Rh[i * MAXM + i]);
     }
 #pragma unroll
     for (int i = NL - 1; i >= 0; --i) {
@@ -111,7 +114,7 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt
             if (k >= L) break;
             s = sub_rn(s, mul_rn(Rh[k * MAXM + i], v[k]));
         }
-        v[i] = div_rn(s, Rh[i * MAXM + i]);
+        v[i] = recip ? mul_rn(s, rinv[i]) : div_rn(s, Rh[i * MAXM + i]);
     }
     float delta = 0.0f, eta = 0.0f;
 #pragma unroll
@@ -144,9 +147,10 @@ __device__ __noinline__ float EvalExact(const SlotView<MAXM> cur, int h, int Lrt
 template <int MAXM>
 __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, int L, const RowArr<MAXM>& flat,
                                             const float* __restrict__ Grow, int H, int col, float alpha, float gamma,
-                                            float* y_out, float* v_out, float* denom_out, float* alast_out) {
+                                            float* y_out, float* v_out, float* denom_out, float* alast_out,
+                                            bool recip) {
 #define STLQ_B200_EXACT(NL, FIX) \
-    EvalExact<MAXM, NL, FIX>(cur, h, L, flat, Grow, H, col, alpha, gamma, y_out, v_out, denom_out, alast_out)
+    EvalExact<MAXM, NL, FIX>(cur, h, L, flat, Grow, H, col, alpha, gamma, y_out, v_out, denom_out, alast_out, recip)
     if constexpr (MAXM <= 8) {
         switch (L) {
             case 1: return STLQ_B200_EXACT(1, true);

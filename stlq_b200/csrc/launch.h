@@ -71,5 +71,13 @@ struct BeamInputs {
 cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream);
 cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream);
 cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream);
+cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gcol, float* Grow, float* Gdiag,
+                                   float* invnorm, cudaStream_t stream);
+// Large-root mode: xC[vec][root] = the reference's SIMD-order dot of the chosen root codeword with
+// x (Dot, least_squares.cpp:35-42), which its LS, cost and ICM use for the root term.
+cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const uint8_t* B, int64_t n,
+                          float* xC, cudaStream_t stream);
+cudaError_t LaunchSplitRootCodes(int m, const uint8_t* B, int64_t n, uint32_t* cluster, uint8_t* B_small,
+                                 cudaStream_t stream);
 
 }  // namespace stlq_b200

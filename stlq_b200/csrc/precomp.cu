@@ -41,7 +41,29 @@ __global__ void InvnormKernel(const float* __restrict__ C, int H, int d, float* 
     invnorm[h] = s > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(s)) : 0.0f;
 }
 
+// Large-root precompute from the codewords' norms in the reference's SIMD order (Norm2,
+// precomp_large_root.cpp:15-23): invnorm = 1/sqrt(norm) (0 for a zero codeword), and for the h0 root
+// codewords the Gram diagonal is norm0 (BuildPrecompLargeRoot :85-91) instead of the GEMM value.
+__global__ void LargeRootPrecompKernel(const float* __restrict__ norms, int h0, int H, float* Gcol, float* Grow,
+                                       float* Gdiag, float* invnorm) {
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= H) return;
+    const float n2 = norms[h];
+    invnorm[h] = n2 > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(n2)) : 0.0f;
+    if (h < h0) {
+        Gdiag[h] = n2;
+        Gcol[static_cast<size_t>(h) * H + h] = n2;
+        Grow[static_cast<size_t>(h) * H + h] = n2;
+    }
+}
+
 }  // namespace
+
+cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gcol, float* Grow, float* Gdiag,
+                                   float* invnorm, cudaStream_t stream) {
+    LargeRootPrecompKernel<<<(H + 255) / 256, 256, 0, stream>>>(norms, h0, H, Gcol, Grow, Gdiag, invnorm);
+    return cudaGetLastError();
+}
 
 cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream) {
     dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);

@@ -17,6 +17,7 @@
 // SPD solves run on lane 0 from a per-warp shared-memory matrix.  The m x m Gram submatrix of the
 // current codes is cached per warp in shared memory (loaded by all lanes, two rows/columns per
 // trial code change), so lane 0's solves, costs and MSE terms read no global memory.
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -301,6 +302,30 @@ __device__ float SampleCost(const Dims& dims, const Gram& G, const float* xc, co
     return add_rn(sub_rn(xn2, mul_rn(2.0f, term1)), term2);
 }
 
+// SampleCostLargeRoot (cost_utils.cpp:160-209): the same quantity in the large-root encoder's
+// order — root term first, then root-small cross terms 2 a_0 a_j G(0, j), then small-small terms.
+// xc[flat_0] holds the reference's SIMD-order dot of the root codeword with x (LaunchRootDot) and
+// G(0, 0) the root codeword's norm0.
+template <class Gram>
+__device__ float SampleCostLargeRoot(const Dims& dims, const Gram& G, const float* xc, const int* code,
+                                     const float* a, float xn2) {
+    const int m = dims.m;
+    float term1 = mul_rn(a[0], xc[dims.off[0] + code[0]]);
+    for (int l = 1; l < m; ++l) term1 = add_rn(term1, mul_rn(a[l], xc[dims.off[l] + code[l]]));
+    float term2 = mul_rn(mul_rn(a[0], a[0]), G(0, 0));
+    for (int j = 1; j < m; ++j) {
+        term2 = add_rn(term2, mul_rn(mul_rn(mul_rn(2.0f, a[0]), a[j]), G(0, j)));
+        for (int k = 1; k < m; ++k) term2 = add_rn(term2, mul_rn(mul_rn(a[j], a[k]), G(j, k)));
+    }
+    return add_rn(sub_rn(xn2, mul_rn(2.0f, term1)), term2);
+}
+
+template <class Gram>
+__device__ __forceinline__ float Cost(const Dims& dims, const Gram& G, const float* xc, const int* code,
+                                      const float* a, float xn2) {
+    return dims.large_root ? SampleCostLargeRoot(dims, G, xc, code, a, xn2) : SampleCost(dims, G, xc, code, a, xn2);
+}
+
 // Per-vector term of MeanMseFromPrecomp in double, clamped at 0.
 template <class Gram>
 __device__ double VectorSse(const Dims& dims, const Gram& G, const float* xc, const int* code, const float* a,
@@ -345,7 +370,7 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
         if (lane == 0) {
             if (!SolveLs(dims, G, xc, code, ws, a))
                 for (int l = 0; l < m; ++l) a[l] = 0.0f;
-            *cost = SampleCost(dims, G, xc, code, a, xn2);
+            *cost = Cost(dims, G, xc, code, a, xn2);
         }
     }
     __syncwarp();
@@ -394,7 +419,7 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
                 for (int l = 0; l < m; ++l) ws.backup[l] = a[l];
                 keep = SolveLs(dims, G, xc, code, ws, a);
                 if (keep) {
-                    const float nc = SampleCost(dims, G, xc, code, a, xn2);
+                    const float nc = Cost(dims, G, xc, code, a, xn2);
                     keep = add_rn(nc, kIcmEps) < *cost;
                     if (keep) {
                         *cost = nc;
@@ -448,8 +473,11 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
         // RunIcm's first step recomputes LS and cost for the beam codes (icm.cpp:109-114); with
         // the MSE requested, the LS result is also the beam-stage coefficients.
         RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, 0, p.orders, p.use_abs, ws.code, ws.a, &cost, ws);
+        // Beam-stage error: MeanMseFromPrecomp's term, or for a large-root encoder the float cost
+        // itself (the large pipeline averages ComputeCostsLargeRoot, encode_base_streaming.cpp:301-311).
         if (p.partials && lane == 0)
-            sse_beam += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+            sse_beam += dims.large_root ? static_cast<double>(cost)
+                                        : VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
         __syncwarp();
         if (p.icm_iters > 0)
             RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
@@ -487,7 +515,9 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
             }
             __syncwarp();
         }
-        if (p.partials) {
+        if (p.partials && dims.large_root) {
+            if (lane == 0) sse_final += static_cast<double>(cost);
+        } else if (p.partials) {
             if (p.n_ils > 0) LoadGram(dims, p.Gcol, ws.code, ws.Gs);  // the cache holds the last ILS candidate
             if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
         }
@@ -514,6 +544,35 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
             p.partials[2 * blockIdx.x + 1] = s1;
         }
     }
+}
+
+// xC[vec][root] = Dot(C[root], x) in the reference's SIMD order: 4 lanes over the first 4*(d/4)
+// elements (lane = index mod 4), the tail into lane 0, lanes summed in order; each product rounded,
+// then added (no contraction).  4 threads per vector.
+template <typename T>
+__global__ void RootDotKernel(Dims dims, const float* __restrict__ C, const T* __restrict__ X,
+                              const uint8_t* __restrict__ B, int64_t n, float* __restrict__ xC) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t vec = t >> 2;
+    const int l = static_cast<int>(t & 3);
+    const bool ok = vec < n;
+    const int d = dims.d;
+    int root = 0;
+    float s = 0.0f;
+    if (ok) {
+        root = B[vec * dims.m];
+        const float* c = C + static_cast<size_t>(root) * d;
+        const T* x = X + vec * d;
+        const int body = (d / 4) * 4;
+        for (int k = l; k < body; k += 4) s = __fadd_rn(s, __fmul_rn(c[k], static_cast<float>(x[k])));
+        if (l == 0)
+            for (int k = body; k < d; ++k) s = __fadd_rn(s, __fmul_rn(c[k], static_cast<float>(x[k])));
+    }
+    const int base = (threadIdx.x & 31) & ~3;
+    const float s1 = __shfl_sync(0xffffffffu, s, base + 1);
+    const float s2 = __shfl_sync(0xffffffffu, s, base + 2);
+    const float s3 = __shfl_sync(0xffffffffu, s, base + 3);
+    if (ok && l == 0) xC[vec * dims.H + root] = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);
 }
 
 // Sums the per-CTA partials in a fixed order and adds them into out[0..1].
@@ -570,5 +629,33 @@ cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, cons
 }
 
 int RefineWarpsPerBlock() { return kWarps; }
+
+// Large-root outputs from the internal m x n codes: cluster id (the root code) and the (m-1) small
+// codes of each vector (BeamSearchPrefixLSLargeRoot's cluster_id / B_small, beam_search.h:26-32).
+__global__ void SplitRootCodesKernel(int m, const uint8_t* __restrict__ B, int64_t n, uint32_t* __restrict__ cluster,
+                                     uint8_t* __restrict__ B_small) {
+    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n;
+         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        cluster[v] = B[v * m];
+        for (int l = 1; l < m; ++l) B_small[v * (m - 1) + l - 1] = B[v * m + l];
+    }
+}
+
+cudaError_t LaunchSplitRootCodes(int m, const uint8_t* B, int64_t n, uint32_t* cluster, uint8_t* B_small,
+                                 cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 32));
+    SplitRootCodesKernel<<<grid, 256, 0, stream>>>(m, B, n, cluster, B_small);
+    return cudaGetLastError();
+}
+
+cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const uint8_t* B, int64_t n,
+                          float* xC, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const int grid = static_cast<int>((n * 4 + 255) / 256);
+    if (x_dtype == 0) RootDotKernel<float><<<grid, 256, 0, stream>>>(dims, C, static_cast<const float*>(X), B, n, xC);
+    else RootDotKernel<uint8_t><<<grid, 256, 0, stream>>>(dims, C, static_cast<const uint8_t*>(X), B, n, xC);
+    return cudaGetLastError();
+}
 
 }  // namespace stlq_b200

@@ -28,6 +28,10 @@ struct Dims {
     int maxK;     // max of h_vec
     int h_vec[kMaxM];
     int off[kMaxM];
+    // Large-root encoder (PrecompLargeRoot, reference include/stlq/quantizer/precomp_large_root.h):
+    // codebook 0 is the root; the beam's triangular solves multiply by 1/R_ii
+    // (beam_search.cpp:517-575) and costs follow SampleCostLargeRoot (cost_utils.cpp:160-209).
+    int large_root;
 };
 
 }  // namespace stlq_b200

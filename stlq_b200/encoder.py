@@ -58,6 +58,11 @@ def load_library():
     lib.stlq_b200_sync.argtypes = [vp, vp]
     lib.stlq_b200_dims.argtypes = [vp, vp, vp, vp]
     lib.stlq_b200_beam_stats.argtypes = [vp, vp, c_int]
+    lib.stlq_b200_create_large_root.argtypes = [c_int, c_int, c_int, vp, vp, c_int, ctypes.POINTER(vp)]
+    lib.stlq_b200_encode_base_large_root.argtypes = [vp, vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_int, c_u32,
+                                                     c_u64, vp, vp, vp, vp, vp]
+    lib.stlq_b200_encode_base_large_root_device.argtypes = [vp, vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_int,
+                                                            c_u32, c_u64, vp, vp, vp, vp, vp, vp]
     _LIB = lib
     return lib
 
@@ -92,7 +97,10 @@ class Encoder:
     orientation of a symmetric matrix is accepted as stored: G_np[col, row]) and invnorm_flat.
     """
 
-    def __init__(self, C_all, h_vec, G=None, invnorm=None, device: int = 0, gemm_mode="exact"):
+    def __init__(self, C_all, h_vec, G=None, invnorm=None, device: int = 0, gemm_mode="exact",
+                 large_root: bool = False):
+        """large_root: the large pipeline's encoder (stlq_b200_create_large_root): codebook 0 is the
+        root, G and invnorm are always computed on the device."""
         self.lib = load_library()
         self.C_all = np.ascontiguousarray(C_all, np.float32)
         self.h_vec = np.ascontiguousarray(h_vec, np.int32)
@@ -105,9 +113,17 @@ class Encoder:
         Gc = None if G is None else np.ascontiguousarray(G, np.float32)
         inv = None if invnorm is None else np.ascontiguousarray(invnorm, np.float32)
         h = ctypes.c_void_p()
-        rc = self.lib.stlq_b200_create(self.device, self.d, self.m, _np_ptr(self.h_vec), _np_ptr(self.C_all),
-                                       _np_ptr(Gc), _np_ptr(inv), mode, ctypes.byref(h))
-        _check(self.lib, rc, "stlq_b200_create")
+        self.large_root = bool(large_root)
+        if self.large_root:
+            if G is not None or invnorm is not None:
+                raise StlqB200Error("a large-root encoder computes G and invnorm itself")
+            rc = self.lib.stlq_b200_create_large_root(self.device, self.d, self.m, _np_ptr(self.h_vec),
+                                                      _np_ptr(self.C_all), mode, ctypes.byref(h))
+            _check(self.lib, rc, "stlq_b200_create_large_root")
+        else:
+            rc = self.lib.stlq_b200_create(self.device, self.d, self.m, _np_ptr(self.h_vec), _np_ptr(self.C_all),
+                                           _np_ptr(Gc), _np_ptr(inv), mode, ctypes.byref(h))
+            _check(self.lib, rc, "stlq_b200_create")
         self.handle = h
 
     def close(self):
@@ -144,6 +160,46 @@ class Encoder:
         _check(self.lib, rc, "stlq_b200_encode_base")
         nn = max(n, 1)
         return dict(B=B, a=a, cost=cost, beam_mse=sse[0] / nn, final_mse=sse[1] / nn, sse=sse)
+
+    def encode_base_large_root(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0,
+                               use_abs=True, seed: int = 38251450, sample_id_offset: int = 0):
+        """The large pipeline's basic encode on host arrays.  Returns dict(cluster, B_small, a, cost,
+        beam_mse, final_mse) (the MSEs are the means of the beam-stage and final costs)."""
+        X = np.ascontiguousarray(X)
+        n = X.shape[0]
+        cluster = np.empty(n, np.uint32)
+        B_small = np.empty((n, self.m - 1), np.uint8)
+        a = np.empty((n, self.m), np.float32)
+        cost = np.empty(n, np.float32)
+        sums = np.zeros(2, np.float64)
+        rc = self.lib.stlq_b200_encode_base_large_root(
+            self.handle, _np_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters, perturb_k, int(bool(use_abs)),
+            seed & 0xFFFFFFFF, sample_id_offset, _np_ptr(cluster), _np_ptr(B_small), _np_ptr(a), _np_ptr(cost),
+            _np_ptr(sums))
+        _check(self.lib, rc, "stlq_b200_encode_base_large_root")
+        nn = max(n, 1)
+        return dict(cluster=cluster, B_small=B_small, a=a, cost=cost, beam_mse=sums[0] / nn,
+                    final_mse=sums[1] / nn, sums=sums)
+
+    def encode_base_large_root_device(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0,
+                                      use_abs=True, seed: int = 38251450, sample_id_offset: int = 0, stream=None):
+        """Device tensors, asynchronous.  Returns (cluster int32-viewed uint32, B_small, a, cost, sums)."""
+        import torch
+
+        n = X.shape[0]
+        dev = X.device
+        cluster = torch.empty(n, dtype=torch.int32, device=dev)
+        B_small = torch.empty((n, self.m - 1), dtype=torch.uint8, device=dev)
+        a = torch.empty((n, self.m), dtype=torch.float32, device=dev)
+        cost = torch.empty(n, dtype=torch.float32, device=dev)
+        sums = torch.zeros(2, dtype=torch.float64, device=dev)
+        s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+        rc = self.lib.stlq_b200_encode_base_large_root_device(
+            self.handle, _t_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters, perturb_k, int(bool(use_abs)),
+            seed & 0xFFFFFFFF, sample_id_offset, _t_ptr(cluster), _t_ptr(B_small), _t_ptr(a), _t_ptr(cost),
+            _t_ptr(sums), ctypes.c_void_p(s))
+        _check(self.lib, rc, "stlq_b200_encode_base_large_root_device")
+        return cluster, B_small, a, cost, sums
 
     # ---- whole stage, device tensors -----------------------------------------------------
     def encode_base_device(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,

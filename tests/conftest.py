@@ -16,7 +16,23 @@ def pytest_configure(config):
 
 
 def golden_names():
-    return sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN, "*.npz")))
+    """Fixtures of the regular encode stage (EncodeBase)."""
+    names = (os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN, "*.npz")))
+    return sorted(n for n in names if not n.startswith("lr_"))
+
+
+def large_root_names():
+    """Fixtures of the large pipeline's basic encode (large-root encoder)."""
+    return sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN, "lr_*.npz")))
+
+
+def load_lr_case(name):
+    with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
+        c = {k: z[k] for k in z.files}
+    for k in ("beam", "icm_iters", "ils_iters", "perturb_k", "use_abs", "seed"):
+        c[k] = int(c[k])
+    c["name"] = name
+    return c
 
 
 def load_case(name):

@@ -14,6 +14,11 @@ and what the reference produced through the EncodeBase stage order (encoder_enco
   - ``B``, ``a``, ``cost``  after DynamicIcmWithIls*NoNormal;
   - ``beam_mse``, ``final_mse``  MeanMseFromPrecomp before / after ICM.
 
+Cases named ``lr_*`` run the large pipeline's basic encode instead (codebook 0 is the root;
+BuildPrecompLargeRoot, BeamSearchPrefixLSLargeRoot, SolveLeastSquaresAllLargeRoot,
+ComputeCostsLargeRoot, DynamicIcmWithIls*LargeRoot) and store ``cluster``, ``B_small``, ``a``,
+``cost_beam`` and ``cost``.
+
 The codebooks are a seeded residual k-means stand-in for the reference's trainer (which is outside
 the encode path); the base vectors come from the seeded generators in stlq_b200/synth.py.
 """
@@ -64,6 +69,46 @@ def make_case(name, X, books, beam, icm, ils=0, perturb=0, use_abs=True, seed=38
           f"beam_mse={beam_mse:.6g} final_mse={final_mse:.6g}")
 
 
+def make_lr_case(name, X, books, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450):
+    ref = oracle.Reference(threads=os.cpu_count())
+    C = synth.flatten_books(books)
+    h = np.array([b.shape[0] for b in books], np.int32)
+    r = ref.large_root_encode(h, C, X, beam, icm, ils, perturb, use_abs, seed)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), X=X, C_all=C, h_vec=h, beam=beam, icm_iters=icm,
+                        ils_iters=ils, perturb_k=perturb, use_abs=int(bool(use_abs)), seed=np.uint32(seed),
+                        cluster=r["cluster"], B_small=r["B_small"], a=r["a"], cost_beam=r["cost_beam"],
+                        cost=r["cost"], blas_core=ref.blas_core())
+    print(f"{name}: n={X.shape[0]} d={X.shape[1]} h={list(h)} beam={beam} icm={icm} ils={ils} "
+          f"mean cost beam={r['cost_beam'].mean():.6g} final={r['cost'].mean():.6g}")
+
+
+def large_root_cases():
+    # Config-3 shape (large pipeline, M=8, K=256), beam 16, with and without an ICM sweep.
+    X = synth.sift_like(20300, d=128, seed=3)
+    books = synth.train_rvq(X[300:], 8, 256, iters=6, seed=3)
+    make_lr_case("lr_d128_m8_k256_b16", X[:300], books, beam=16, icm=1)
+    make_lr_case("lr_d128_m8_k256_b16_noicm", X[:300], books, beam=16, icm=0)
+    # m = 5 and m = 10 (fixed-size LS) with ILS and no-abs ICM.
+    X = synth.sift_like(3400, d=40, seed=15, n_centres=100)
+    make_lr_case("lr_m5_k64_ils_noabs", X[:400], synth.train_rvq(X[400:], 5, 64, iters=6, seed=15), beam=8, icm=3,
+                 ils=2, perturb=2, use_abs=False, seed=11)
+    X = synth.sift_like(3400, d=24, seed=16, n_centres=100)
+    make_lr_case("lr_m10_k32", X[:400], synth.train_rvq(X[400:], 10, 32, iters=6, seed=16), beam=4, icm=2)
+    # Ragged codebooks with a 200-code root, d not a multiple of 4 (the dot products' tail lanes).
+    X = synth.sift_like(4300, d=30, seed=18, n_centres=80)
+    rag = [synth.train_rvq(X[300:], 1, k, iters=5, seed=20 + i)[0] for i, k in enumerate([200, 3, 100, 17, 256])]
+    make_lr_case("lr_ragged_d30", X[:300], rag, beam=8, icm=2, ils=1, perturb=2)
+    # Edge vectors: zero vector, copies of root codewords, root + small codeword sums.
+    X = synth.sift_like(2300, d=32, seed=19, n_centres=60)
+    books = synth.train_rvq(X[300:], 4, 32, iters=5, seed=19)
+    E = X[:64].copy()
+    E[0] = 0.0
+    E[1] = books[0][3]
+    E[2] = books[0][5] + books[1][7]
+    E[3] = E[4]
+    make_lr_case("lr_edge_vectors", E, books, beam=4, icm=2)
+
+
 def main():
     # The reference's own test setup (tests/test_streaming_encode_base.cpp:67-134): m=3, K=16,
     # d=16, beam 2, ICM 2, ILS 3, perturb 2, seed 1234 -- at n=600.
@@ -108,4 +153,6 @@ def main():
 
 if __name__ == "__main__":
     oracle.build(reference=True)
-    main()
+    if "--large-root-only" not in sys.argv:
+        main()
+    large_root_cases()

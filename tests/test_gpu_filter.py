@@ -56,3 +56,38 @@ def test_filter_self_check(kind, d, m, k, beam, n, oracle_lib):
     B = oracle_lib.beam_search(h, G, xn, xC, beam)
     Bo, ao, _ = oracle_lib.icm(h, G, inv, xC, xn, B, 1)
     assert np.array_equal(Bo.astype(np.uint8), r2["B"][s]) and np.array_equal(ao, r2["a"][s])
+
+
+@pytest.mark.parametrize("d,m,k,beam,n", [(128, 8, 256, 16, 40_000), (40, 5, 64, 8, 20_000)])
+def test_filter_self_check_large_root(d, m, k, beam, n):
+    """The same self-check for the large-root encoder (reciprocal triangular solves); a slice of
+    the codes against the reference's own large-root encode where its library is available."""
+    if not have_cuda():
+        pytest.skip("no CUDA device")
+    import stlq_b200
+    from stlq_b200 import synth
+
+    X = synth.sift_like(n + 20_000, d=d, seed=13)
+    books = synth.train_rvq(X[n:], m, k, iters=5, seed=13, device="cuda")
+    X = X[:n]
+    C = synth.flatten_books(books)
+    h = [k] * m
+    os.environ["STLQ_B200_CHECK_FILTER"] = "1"
+    try:
+        checked = stlq_b200.Encoder(C, h, large_root=True)
+    finally:
+        del os.environ["STLQ_B200_CHECK_FILTER"]
+    plain = stlq_b200.Encoder(C, h, large_root=True)
+    r1 = checked.encode_base_large_root(X, beam, 1)
+    r2 = plain.encode_base_large_root(X, beam, 1)
+    assert np.array_equal(r1["cluster"], r2["cluster"]) and np.array_equal(r1["B_small"], r2["B_small"])
+    try:
+        import oracle
+
+        ref = oracle.Reference(threads=os.cpu_count())
+    except FileNotFoundError:
+        return
+    s = slice(0, 1000)
+    rr = ref.large_root_encode(h, C, X[s], beam, 1)
+    assert np.array_equal(rr["cluster"], r2["cluster"][s]) and np.array_equal(rr["B_small"], r2["B_small"][s])
+    assert np.array_equal(rr["cost"], r2["cost"][s])

@@ -107,3 +107,16 @@ def test_oracle_gemm_k_blocks_match_reference(oracle_lib, d):
     P = oracle.Reference(threads=1).precomp([37], C)
     assert np.array_equal(P.gemm_xc(X), oracle_lib.gemm_xc(C, X))
     assert np.array_equal(P.xnorm2(X), oracle_lib.xnorm2(X))
+
+
+@pytest.mark.skipif(not ref_available, reason="oracle/_ref not built here")
+@pytest.mark.parametrize("name", __import__("conftest").large_root_names())
+def test_large_root_fixtures_reproduce(name):
+    """The large-root fixtures are what the reference's large-root stack produces (rerun here)."""
+    from conftest import load_lr_case
+
+    c = load_lr_case(name)
+    r = oracle.Reference(threads=4).large_root_encode(c["h_vec"], c["C_all"], c["X"], c["beam"], c["icm_iters"],
+                                                      c["ils_iters"], c["perturb_k"], bool(c["use_abs"]), c["seed"])
+    for k in ("cluster", "B_small", "a", "cost_beam", "cost"):
+        assert np.array_equal(r[k], c[k]), k
