@@ -340,6 +340,29 @@ class AdapterHarness:
         self.lib.ref_gemm_xc(pre, _p(X, _f32p), X.shape[0], _p(out, _f32p))
         return out
 
+    def large_root_encode(self, h_vec, C_all, X, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450,
+                          device=0):
+        """stlq::b200::EncodeBaseLargeRoot on a PrecompLargeRoot built by the reference."""
+        h = np.asarray(h_vec, np.int32)
+        C, X = _f32(C_all), _f32(X)
+        m, (n, d) = len(h), X.shape
+        cluster = np.empty(n, np.uint32)
+        B_small = np.empty((n, m - 1), np.uint8)
+        a = np.empty((n, m), np.float32)
+        cost = np.empty(n, np.float32)
+        mse = np.zeros(2, np.float32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.adapter_large_root_encode(
+            ctypes.c_int(d), ctypes.c_int(m), _p(h, _i32p), _p(C, _f32p), _p(X, _f32p), ctypes.c_int(n),
+            ctypes.c_int(beam), ctypes.c_int(icm), ctypes.c_int(ils), ctypes.c_int(perturb),
+            ctypes.c_int(int(bool(use_abs))), ctypes.c_uint(seed & 0xFFFFFFFF), ctypes.c_int(device),
+            cluster.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), _p(B_small, _u8p), _p(a, _f32p),
+            _p(cost, _f32p), _p(mse, _f32p), err, ctypes.c_int(512))
+        if rc != 0:
+            raise RuntimeError(err.value.decode())
+        return dict(cluster=cluster, B_small=B_small, a=a, cost=cost, beam_mse=float(mse[0]),
+                    final_mse=float(mse[1]))
+
     def encode_base(self, pre, m, X, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, device=0):
         X = _f32(X)
         n = X.shape[0]

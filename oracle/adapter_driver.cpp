@@ -3,7 +3,9 @@
 // on the same Precomp object (created by ref_precomp_create in ref_driver.cpp).
 #include <cstdint>
 #include <cstring>
+#include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "stlq/common/config.h"
 #include "stlq/common/types.h"
@@ -78,3 +80,44 @@ extern "C" int adapter_stages(void* pre_h, const float* X, int n, const float* x
 }
 
 extern "C" void adapter_release(void) { stlq::b200::ReleaseThreadEncoders(); }
+
+// The large-root drop-in (stlq::b200::EncodeBaseLargeRoot) on a PrecompLargeRoot built by the
+// reference's BuildPrecompLargeRoot from C_all (d x H, root codewords first).
+extern "C" int adapter_large_root_encode(int d, int m, const int* h_vec, const float* C_all, const float* X, int n,
+                                         int beam, int icm, int ils, int perturb, int use_abs, unsigned seed,
+                                         int device, std::uint32_t* cluster_out, std::uint8_t* B_small_out,
+                                         float* a_out, float* cost_out, float* mse_out, char* err, int errlen) {
+    try {
+        stlq::CodebookPack pack;
+        pack.d = d;
+        int off = 0;
+        for (int l = 0; l < m; ++l) {
+            stlq::ColMajorMatrix<float> book(d, h_vec[l]);
+            std::memcpy(book.data.data(), C_all + static_cast<size_t>(off) * d, sizeof(float) * book.data.size());
+            pack.h_vec.push_back(h_vec[l]);
+            pack.books.push_back(std::move(book));
+            off += h_vec[l];
+        }
+        stlq::PrecompLargeRoot pre;
+        stlq::PrecompLargeRootBuildOptions opts;
+        std::string e;
+        if (!stlq::BuildPrecompLargeRoot(pack, nullptr, opts, &pre, &e)) throw std::runtime_error(e);
+        stlq::ColMajorMatrix<float> Xm(d, n);
+        std::memcpy(Xm.data.data(), X, sizeof(float) * static_cast<size_t>(d) * n);
+        std::vector<std::uint32_t> cluster;
+        stlq::ColMajorMatrix<stlq::Code> B_small;
+        stlq::ColMajorMatrix<float> a;
+        std::vector<float> cost;
+        stlq::b200::EncodeBaseLargeRoot(pre, Xm, beam, icm, ils, perturb, use_abs != 0, seed, 0, &cluster, &B_small,
+                                        &a, &cost, &mse_out[0], &mse_out[1], device);
+        std::memcpy(cluster_out, cluster.data(), sizeof(std::uint32_t) * n);
+        std::memcpy(B_small_out, B_small.data.data(), B_small.data.size());
+        std::memcpy(a_out, a.data.data(), sizeof(float) * a.data.size());
+        std::memcpy(cost_out, cost.data(), sizeof(float) * n);
+    } catch (const std::exception& ex) {
+        std::strncpy(err, ex.what(), static_cast<size_t>(errlen) - 1);
+        err[errlen - 1] = 0;
+        return 1;
+    }
+    return 0;
+}

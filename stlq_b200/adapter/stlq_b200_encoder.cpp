@@ -66,6 +66,26 @@ stlq_b200_encoder* EncoderFor(const Precomp& pre, int device) {
     return h;
 }
 
+// The large-root encoder for this PrecompLargeRoot: C_all = [C0 | C_small] (root codewords first);
+// G, norm0 and invnorm are derived on the device in the reference's orders.
+stlq_b200_encoder* LargeRootEncoderFor(const PrecompLargeRoot& pre, int device) {
+    auto& items = Cache().items;
+    const int H = pre.h_vec.empty() ? 0 : pre.h_vec[0] + pre.H_small;
+    for (auto& e : items) {
+        if (e.device == device && e.build_tag == pre.build_tag && e.c_all == pre.C0.data.data() && e.H == H &&
+            e.d == pre.d)
+            return e.handle;
+    }
+    std::vector<float> c_all(static_cast<size_t>(pre.d) * H);
+    std::memcpy(c_all.data(), pre.C0.data.data(), sizeof(float) * pre.C0.data.size());
+    std::memcpy(c_all.data() + pre.C0.data.size(), pre.C_small.data.data(), sizeof(float) * pre.C_small.data.size());
+    stlq_b200_encoder* h = nullptr;
+    Check(stlq_b200_create_large_root(device, pre.d, pre.m, pre.h_vec.data(), c_all.data(), STLQ_B200_GEMM_EXACT, &h),
+          "stlq_b200_create_large_root");
+    items.push_back({device, pre.build_tag, pre.C0.data.data(), H, pre.d, h});
+    return h;
+}
+
 // Device scratch for the host-buffer stage adapters.
 struct DeviceBuffer {
     void* p = nullptr;
@@ -217,6 +237,33 @@ void DynamicIcmWithIlsNoAbsNoNormalCuda(const ColMajorMatrix<float>& X, const Pr
                                         std::uint64_t sample_id_offset, int device) {
     (void)print_progress;
     IcmCommon(X, precomp, xC, icm_iters, ils_iters, perturb_k, seed, B, a, X_norm2, cost, sample_id_offset, device, 0);
+}
+
+void EncodeBaseLargeRoot(const PrecompLargeRoot& pre, const ColMajorMatrix<float>& Xblk, int H_beam, int icm_iters,
+                         int ils_iters, int perturb_k, bool use_abs, std::uint32_t seed,
+                         std::uint64_t sample_id_offset, std::vector<std::uint32_t>* cluster_id,
+                         ColMajorMatrix<Code>* B_small, ColMajorMatrix<float>* a, std::vector<float>* cost,
+                         float* out_beam_mse, float* out_final_mse, int device) {
+    if (!cluster_id || !B_small || !a) return;
+    const int n = Xblk.cols, m = pre.m;
+    cluster_id->resize(static_cast<size_t>(n));
+    B_small->rows = std::max(0, m - 1);
+    B_small->cols = n;
+    B_small->data.resize(static_cast<size_t>(B_small->rows) * n);
+    a->rows = m;
+    a->cols = n;
+    a->data.resize(static_cast<size_t>(m) * n);
+    std::vector<float> c(static_cast<size_t>(n));
+    if (n <= 0) return;
+    stlq_b200_encoder* enc = LargeRootEncoderFor(pre, device);
+    double sums[2] = {0.0, 0.0};
+    Check(stlq_b200_encode_base_large_root(enc, Xblk.data.data(), STLQ_B200_F32, n, std::max(1, H_beam), icm_iters,
+                                           ils_iters, perturb_k, use_abs ? 1 : 0, seed, sample_id_offset,
+                                           cluster_id->data(), B_small->data.data(), a->data.data(), c.data(), sums),
+          "stlq_b200_encode_base_large_root");
+    if (cost) *cost = std::move(c);
+    if (out_beam_mse) *out_beam_mse = static_cast<float>(sums[0] / n);
+    if (out_final_mse) *out_final_mse = static_cast<float>(sums[1] / n);
 }
 
 void ReleaseThreadEncoders() {

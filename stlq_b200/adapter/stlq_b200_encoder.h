@@ -21,6 +21,7 @@
 
 #include "stlq/common/config.h"
 #include "stlq/common/types.h"
+#include "stlq/quantizer/precomp_large_root.h"
 
 namespace stlq {
 
@@ -50,6 +51,18 @@ void DynamicIcmWithIlsNoAbsNoNormalCuda(const ColMajorMatrix<float>& X, const Pr
                                         std::vector<float>* X_norm2, std::vector<float>* cost,
                                         bool print_progress = true, std::uint64_t sample_id_offset = 0,
                                         int device = 0);
+
+// The large pipeline's basic encode of one block (encode_base_streaming.cpp:1040-1300, CPU
+// branch): BeamSearchPrefixLSLargeRoot (beam_search.h:26-32) + SolveLeastSquaresAllLargeRoot +
+// ComputeCostsLargeRoot + DynamicIcmWithIls{Abs,NoAbs}NoNormalLargeRoot, on the GPU from the block's
+// vectors.  Outputs are resized as the reference resizes them; out_beam_mse / out_final_mse (may be
+// null) are the means of the beam-stage and final costs (MeanMseFromCosts).  h_vec[0] <= 256.
+// Throws std::runtime_error on failure.
+void EncodeBaseLargeRoot(const PrecompLargeRoot& pre, const ColMajorMatrix<float>& Xblk, int H_beam, int icm_iters,
+                         int ils_iters, int perturb_k, bool use_abs, std::uint32_t seed,
+                         std::uint64_t sample_id_offset, std::vector<std::uint32_t>* cluster_id,
+                         ColMajorMatrix<Code>* B_small, ColMajorMatrix<float>* a, std::vector<float>* cost,
+                         float* out_beam_mse, float* out_final_mse, int device = 0);
 
 // Drops this thread's cached encoder handles (e.g. before the device is reset).
 void ReleaseThreadEncoders();

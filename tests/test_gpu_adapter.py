@@ -44,3 +44,17 @@ def test_adapter_stage_seams(harness, name):
                                           c["perturb_k"], bool(c["use_abs"]), c["seed"])
     assert np.array_equal(Bb, c["B_beam"]) and np.array_equal(ab, c["a_beam"])
     assert np.array_equal(Bi, c["B"]) and np.array_equal(ai, c["a"]) and np.array_equal(cost, c["cost"])
+
+
+@pytest.mark.parametrize("name", ["lr_d128_m8_k256_b16", "lr_m5_k64_ils_noabs", "lr_ragged_d30"])
+def test_adapter_large_root(harness, name):
+    """stlq::b200::EncodeBaseLargeRoot on the reference's own PrecompLargeRoot: the large-root
+    fixtures' codes, coefficients and costs, bit for bit."""
+    from conftest import load_lr_case
+
+    c = load_lr_case(name)
+    r = harness.large_root_encode(c["h_vec"], c["C_all"], c["X"], c["beam"], c["icm_iters"], c["ils_iters"],
+                                  c["perturb_k"], bool(c["use_abs"]), c["seed"])
+    for k in ("cluster", "B_small", "a", "cost"):
+        assert np.array_equal(r[k], c[k]), k
+    assert abs(r["final_mse"] - float(np.mean(c["cost"].astype(np.float64)))) <= 1e-6 * abs(r["final_mse"])
