@@ -147,6 +147,19 @@ int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const 
 int stlq_b200_beam_search_noalloc(stlq_b200_encoder* enc, const float* xnorm2_dev, const float* xC_dev, int64_t n,
                                   int beam, uint8_t* B_dev, void* stream);
 
+/* Input rotation X <- R X (ApplyRotationInPlace, src/pipeline/app_utils.cpp:203-227; the OPQ
+ * rotation of the train result, applied to the base set before encoding,
+ * stlq_non_large_pipeline_flow.cpp:58).  R: d x d column-major; NULL or the exact identity turns it
+ * off (the reference skips the product then, IsIdentityRotation :186-201).  When set, the
+ * whole-stage entry points (stlq_b200_encode_base*, the large-root ones included) rotate each
+ * slice on the device with the reference's GEMM order before encoding; the stage entry points take
+ * already rotated vectors, as the reference's stage functions do. */
+int stlq_b200_set_rotation(stlq_b200_encoder* enc, const float* R);
+
+/* out_dev (d x n floats) = R X_dev (or X_dev converted to float when no rotation is set), the
+ * reference's ConvertU8ToF32AndRotate (include/stlq/core/kernel_provider.h:48-54). */
+int stlq_b200_rotate(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* out_dev, void* stream);
+
 /* ---- Large-root encoder (the large pipeline's basic encode) ----
  * Replaces BuildPrecompLargeRoot (src/quantizer/precomp_large_root.cpp:27-160),
  * BeamSearchPrefixLSLargeRoot (src/quantizer/beam_search.cpp:579-992, declared in

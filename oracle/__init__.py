@@ -205,6 +205,14 @@ class Reference:
     def precomp(self, h_vec, C_all):
         return RefPrecomp(self, h_vec, C_all)
 
+    def rotate(self, R, X):
+        """ApplyRotationInPlace's GEMM: R (d x d) given as numpy R_np[col, row] (column-major), X (n, d)."""
+        R, X = _f32(R), _f32(X)
+        out = np.empty_like(X)
+        self.lib.ref_rotate(_p(R, _f32p), ctypes.c_int(X.shape[1]), _p(X, _f32p), ctypes.c_int(X.shape[0]),
+                            _p(out, _f32p))
+        return out
+
     def large_root_encode(self, h_vec, C_all, X, beam, icm_iters, ils_iters=0, perturb_k=0, use_abs=True,
                           seed=38251450, sample_id_offset=0):
         """The large pipeline's basic encode (BuildPrecompLargeRoot + BeamSearchPrefixLSLargeRoot +

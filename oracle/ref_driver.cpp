@@ -250,6 +250,14 @@ int ref_encode_base(void* h, const float* X, int n, int beam, int icm_iters, int
     return 0;
 }
 
+// ApplyRotationInPlace's product (src/pipeline/app_utils.cpp:203-227): X_rot = R X with the
+// reference's GemmRaw (no transposes), R d x d and X d x n column-major.  (The identity test that
+// skips it is left to the caller.)
+void ref_rotate(const float* R, int d, const float* X, int n, float* out) {
+    stlq::ScopedBlasThreads blas_scope(stlq::OmpMaxThreads());
+    stlq::GemmRaw(false, false, d, n, d, 1.0f, R, d, X, d, 0.0f, out, d);
+}
+
 // Large-root basic encode: BuildPrecompLargeRoot (codebook 0 is the root), ComputeXcSmall,
 // BeamSearchPrefixLSLargeRoot, SolveLeastSquaresAllLargeRoot + ComputeCostsLargeRoot (the beam
 // costs), DynamicIcmWithIls{Abs,NoAbs}NoNormalLargeRoot (final codes, coefficients and costs).

@@ -133,8 +133,11 @@ struct stlq_b200_encoder {
     DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
     // Tensor-core modes: C_all split into TF32 hi / lo parts once at create.
     DevBuf Chi, Clo;
+    // Input rotation X <- R X (ApplyRotationInPlace), R stored by rows; off when R is the identity.
+    DevBuf Rrow;
+    bool rotate = false;
     // Per-call scratch, grown on demand and kept for the handle's lifetime.
-    DevBuf xC, xn, xnd, partials, orders, redo, Xhi, Xlo, Bfull;
+    DevBuf xC, xn, xnd, partials, orders, redo, Xhi, Xlo, Bfull, Xrot;
     std::vector<int> orders_host;
     int64_t orders_key[4] = {-1, -1, -1, -1};
     // Host path.
@@ -246,17 +249,25 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
     const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), SliceVectors(enc));
     STLQ_TRY(EnsureScratch(enc, S));
     const size_t esz = ElemSize(x_dtype);
+    if (enc->rotate) STLQ_TRY(enc->Xrot.Ensure(static_cast<size_t>(S) * dims.d * sizeof(float)));
     for (int64_t s0 = 0; s0 < n; s0 += S) {
         const int64_t ns = std::min(S, n - s0);
         const void* Xs = static_cast<const char*>(X) + static_cast<size_t>(s0) * dims.d * esz;
-        STLQ_TRY(LaunchXc(enc, Xs, x_dtype, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
+        int xt = x_dtype;
+        if (enc->rotate) {  // X <- R X as the reference's GemmRaw computes it, then encode the result
+            STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->Rrow.as<float>(), dims.d, dims.d, Xs, x_dtype, ns,
+                                                 enc->Xrot.as<float>(), dims.d, nullptr, nullptr, stream));
+            Xs = enc->Xrot.p;
+            xt = STLQ_B200_F32;
+        }
+        STLQ_TRY(LaunchXc(enc, Xs, xt, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
                           enc->xnd.as<double>(), stream));
         STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
                                             enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->redo.as<int>(),
                                             enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
         if (dims.large_root)  // LS, cost and ICM take the root term from the SIMD-order dot
-            STLQ_CK(stlq_b200::LaunchRootDot(dims, enc->C.as<float>(), Xs, x_dtype, B + s0 * dims.m, ns,
+            STLQ_CK(stlq_b200::LaunchRootDot(dims, enc->C.as<float>(), Xs, xt, B + s0 * dims.m, ns,
                                              enc->xC.as<float>(), stream));
         stlq_b200::RefineArgs ra{};
         ra.dims = dims;
@@ -414,7 +425,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
     for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
-                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
+                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->Xrot, &enc->Rrow, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
         enc->xin[i].Release();
@@ -637,6 +648,55 @@ int stlq_b200_encode_base_large_root_device(stlq_b200_encoder* enc, const void* 
     STLQ_TRY(EncodeDevice(enc, X_dev, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
                           sample_id_offset, enc->Bfull.as<uint8_t>(), a_dev, cost_dev, cost_sums_dev, s));
     STLQ_CK(stlq_b200::LaunchSplitRootCodes(enc->dims.m, enc->Bfull.as<uint8_t>(), n, cluster_dev, B_small_dev, s));
+    return 0;
+}
+
+int stlq_b200_set_rotation(stlq_b200_encoder* enc, const float* R) {
+    STLQ_TRY(CheckEnc(enc));
+    const int d = enc->dims.d;
+    bool identity = true;
+    if (R) {
+        for (int c = 0; c < d && identity; ++c)
+            for (int r = 0; r < d; ++r)
+                if (R[static_cast<size_t>(c) * d + r] != (r == c ? 1.0f : 0.0f)) {
+                    identity = false;
+                    break;
+                }
+    }
+    DeviceScope scope(enc->device);
+    STLQ_CK(cudaStreamSynchronize(enc->compute));
+    enc->rotate = false;
+    if (!R || identity) return 0;  // IsIdentityRotation: the reference skips the product
+    std::vector<float> rows(static_cast<size_t>(d) * d);
+    for (int i = 0; i < d; ++i)
+        for (int k = 0; k < d; ++k) rows[static_cast<size_t>(i) * d + k] = R[static_cast<size_t>(k) * d + i];
+    STLQ_TRY(enc->Rrow.Ensure(rows.size() * sizeof(float)));
+    STLQ_CK(cudaMemcpy(enc->Rrow.p, rows.data(), rows.size() * sizeof(float), cudaMemcpyHostToDevice));
+    enc->rotate = true;
+    return 0;
+}
+
+int stlq_b200_rotate(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, float* out_dev, void* stream) {
+    STLQ_TRY(CheckEnc(enc));
+    if (x_dtype != STLQ_B200_F32 && x_dtype != STLQ_B200_U8) return Fail(STLQ_B200_EINVAL, "x_dtype must be F32 or U8");
+    if (n > 0 && (!X_dev || !out_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
+    DeviceScope scope(enc->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int d = enc->dims.d;
+    const size_t esz = ElemSize(x_dtype);
+    const int64_t S = stlq_b200::MaxGemmSliceVectors();
+    for (int64_t s0 = 0; s0 < n; s0 += S) {
+        const int64_t ns = std::min(S, n - s0);
+        const void* Xs = static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * d * esz;
+        if (enc->rotate) {
+            STLQ_CK(stlq_b200::LaunchXcGemmExact(enc->Rrow.as<float>(), d, d, Xs, x_dtype, ns, out_dev + s0 * d, d,
+                                                 nullptr, nullptr, s));
+        } else if (x_dtype == STLQ_B200_F32) {
+            STLQ_CK(cudaMemcpyAsync(out_dev + s0 * d, Xs, sizeof(float) * ns * d, cudaMemcpyDeviceToDevice, s));
+        } else {  // identity: the u8 -> f32 conversion alone
+            STLQ_CK(stlq_b200::LaunchU8ToF32(static_cast<const uint8_t*>(Xs), ns * d, out_dev + s0 * d, s));
+        }
+    }
     return 0;
 }
 

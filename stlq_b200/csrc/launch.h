@@ -71,6 +71,7 @@ struct BeamInputs {
 cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream);
 cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream);
 cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream);
+cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStream_t stream);
 cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gcol, float* Grow, float* Gdiag,
                                    float* invnorm, cudaStream_t stream);
 // Large-root mode: xC[vec][root] = the reference's SIMD-order dot of the chosen root codeword with

@@ -1,6 +1,7 @@
 // Device-side parts of BuildPrecomp (reference src/quantizer/encoder_precomp.inc:1-53) that the
 // encoder derives from C_all and G: the row-major copy of G used by the beam kernel's coalesced
 // cross-term gathers, the diagonal alpha = G(h, h), and 1/||c_h||.
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -57,7 +58,20 @@ __global__ void LargeRootPrecompKernel(const float* __restrict__ norms, int h0, 
     }
 }
 
+__global__ void U8ToF32Kernel(const uint8_t* __restrict__ x, int64_t count, float* __restrict__ out) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = static_cast<float>(x[i]);
+}
+
 }  // namespace
+
+cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStream_t stream) {
+    if (count <= 0) return cudaSuccess;
+    const int grid = static_cast<int>(std::min<int64_t>((count + 255) / 256, 148 * 32));
+    U8ToF32Kernel<<<grid, 256, 0, stream>>>(x, count, out);
+    return cudaGetLastError();
+}
 
 cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gcol, float* Grow, float* Gdiag,
                                    float* invnorm, cudaStream_t stream) {

@@ -63,6 +63,8 @@ def load_library():
                                                      c_u64, vp, vp, vp, vp, vp]
     lib.stlq_b200_encode_base_large_root_device.argtypes = [vp, vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_int,
                                                             c_u32, c_u64, vp, vp, vp, vp, vp, vp]
+    lib.stlq_b200_set_rotation.argtypes = [vp, vp]
+    lib.stlq_b200_rotate.argtypes = [vp, vp, c_int, c_i64, vp, vp]
     _LIB = lib
     return lib
 
@@ -219,6 +221,19 @@ class Encoder:
                                                    ctypes.c_void_p(s))
         _check(self.lib, rc, "stlq_b200_encode_base_device")
         return B, a, cost, sse
+
+    def set_rotation(self, R):
+        """R: (d, d) array holding the reference's column-major R (R_np[col, row]); None clears it."""
+        Rc = None if R is None else np.ascontiguousarray(R, np.float32)
+        _check(self.lib, self.lib.stlq_b200_set_rotation(self.handle, _np_ptr(Rc)), "stlq_b200_set_rotation")
+
+    def rotate(self, X):
+        import torch
+
+        out = torch.empty((X.shape[0], self.d), dtype=torch.float32, device=X.device)
+        _check(self.lib, self.lib.stlq_b200_rotate(self.handle, _t_ptr(X), _dtype_code(X), X.shape[0], _t_ptr(out),
+                                                   self._stream(X)), "stlq_b200_rotate")
+        return out
 
     # ---- stage-level entry points (device tensors) ---------------------------------------
     def _stream(self, t):
