@@ -49,7 +49,8 @@ enum { STLQ_B200_F32 = 0, STLQ_B200_U8 = 1 };
 
 /* Limits of this build. */
 #define STLQ_B200_MAX_M 16      /* codebooks (layers) */
-#define STLQ_B200_MAX_K 256     /* codewords per codebook (uint8 codes) */
+#define STLQ_B200_MAX_K 256     /* codewords per codebook with uint8 codes */
+#define STLQ_B200_MAX_K_WIDE 1024 /* codewords per codebook with uint16 codes (the _u16 entry points) */
 #define STLQ_B200_MAX_BEAM 32   /* beam width */
 
 /* Message for the last failed call on this host thread ("" if none). */
@@ -65,7 +66,11 @@ const char* stlq_b200_version(void);
  *   G       optional H x H column-major Gram matrix (the reference's Precomp::G); when NULL it is
  *           computed on the device as C_all^T C_all in the order selected by gemm_mode.
  *   invnorm optional H floats (Precomp::invnorm_flat); computed when NULL.
- * h_vec[l] in [1, 256], m in [1, 16], d >= 1. */
+ * h_vec[l] in [1, 1024], m in [1, 16], d >= 1.  With every h_vec[l] <= 256 codes are uint8 (the
+ * reference's FullCode) and the uint8 entry points apply; a codebook above 256 codewords makes them
+ * uint16 (the _u16 entry points, which the reference has no counterpart for: its codes are uint8;
+ * the results follow the reference's algorithm with wider codes), limited to beam x max(h_vec) <=
+ * 16384. */
 int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_all, const float* G,
                      const float* invnorm, int gemm_mode, stlq_b200_encoder** out);
 
@@ -85,6 +90,11 @@ int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, in
                           int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
                           uint8_t* B_out, float* a_out, float* cost_out, double* sse_out);
 
+/* stlq_b200_encode_base with uint16 codes (B_out m x n), for codebooks above 256 codewords. */
+int stlq_b200_encode_base_u16(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
+                              int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                              uint16_t* B_out, float* a_out, float* cost_out, double* sse_out);
+
 /* Same stage on DEVICE buffers (all pointers on the encoder's device), enqueued on `stream`
  * (a cudaStream_t; NULL = the legacy default stream).  Asynchronous: returns after enqueueing.
  * sse_out_dev: 2 doubles on the device (may be NULL). */
@@ -92,6 +102,10 @@ int stlq_b200_encode_base_device(stlq_b200_encoder* enc, const void* X_dev, int 
                                  int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
                                  uint64_t sample_id_offset, uint8_t* B_dev, float* a_dev, float* cost_dev,
                                  double* sse_out_dev, void* stream);
+int stlq_b200_encode_base_device_u16(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, int beam,
+                                     int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                     uint64_t sample_id_offset, uint16_t* B_dev, float* a_dev, float* cost_dev,
+                                     double* sse_out_dev, void* stream);
 
 /* ---- Stage-level entry points (device buffers, asynchronous on `stream`) ---- */
 

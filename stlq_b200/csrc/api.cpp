@@ -125,6 +125,7 @@ constexpr size_t kFlagBytes = 64;
 struct stlq_b200_encoder {
     int device = 0;
     int num_sms = 148;
+    size_t max_block_smem = 232448;  // opt-in dynamic shared memory per block (B200: 227 KB)
     int gemm_mode = STLQ_B200_GEMM_EXACT;
     // Self-check of the beam pre-filter (environment STLQ_B200_CHECK_FILTER=1 at create time):
     // every candidate is also evaluated exactly and a wrongly dropped one raises EDEVICE.
@@ -148,6 +149,8 @@ struct stlq_b200_encoder {
 };
 
 namespace {
+
+size_t CodeBytes(const stlq_b200_encoder* enc) { return enc->dims.wide ? 2 : 1; }
 
 // Vectors per encode slice: bounds the xC scratch (H floats per vector) to ~2 GiB.
 int64_t SliceVectors(const stlq_b200_encoder* enc) {
@@ -175,6 +178,23 @@ int CheckEncodeArgs(const stlq_b200_encoder* enc, int x_dtype, int64_t n, int be
         return Fail(STLQ_B200_EINVAL, "beam must be in [1, " + std::to_string(STLQ_B200_MAX_BEAM) + "]");
     if (icm_iters < 0 || ils_iters < 0 || perturb_k < 0)
         return Fail(STLQ_B200_EINVAL, "icm_iters, ils_iters and perturb_k must be >= 0");
+    // The beam kernels keep one float per candidate of a layer (beam x codebook size) in shared
+    // memory; every beam <= 32 with codebooks <= 1024 fits a B200's 227 KB.
+    if (BeamFastSmemBytes(enc->dims, beam) > enc->max_block_smem)
+        return Fail(STLQ_B200_EINVAL, "beam x (largest codebook) needs more shared memory than a block of this "
+                                      "device has");
+    return 0;
+}
+
+// Entry points with uint8 codes serve encoders whose codebooks have at most 256 codewords; the
+// _u16 ones the others.
+int CheckCodeWidth(const stlq_b200_encoder* enc, bool wide) {
+    STLQ_TRY(CheckEnc(enc));
+    if (enc->dims.wide != static_cast<int>(wide))
+        return Fail(STLQ_B200_EINVAL, wide ? "this encoder has uint8 codes (codebooks of at most 256 codewords); use "
+                                             "the uint8 entry points"
+                                           : "this encoder has codebooks above 256 codewords (uint16 codes); use the "
+                                             "_u16 entry points");
     return 0;
 }
 
@@ -241,9 +261,11 @@ int EnsureScratch(stlq_b200_encoder* enc, int64_t slice) {
 
 // The encode stage on device buffers for n vectors, sliced; sse_dev (2 doubles) accumulates.
 int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters, int ils_iters,
-                 int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset, uint8_t* B, float* a,
+                 int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset, void* Bv, float* a,
                  float* cost, double* sse_dev, cudaStream_t stream) {
     const Dims& dims = enc->dims;
+    char* B = static_cast<char*>(Bv);  // codes of CodeBytes(enc) bytes each
+    const size_t cb = CodeBytes(enc);
     const int n_ils = (ils_iters <= 0 || perturb_k <= 0 || dims.m <= 1) ? 0 : ils_iters;
     if (icm_iters > 0) STLQ_TRY(UploadOrders(enc, icm_iters, n_ils, seed, stream));
     const int64_t S = std::min<int64_t>(std::max<int64_t>(n, 1), SliceVectors(enc));
@@ -263,11 +285,11 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         STLQ_TRY(LaunchXc(enc, Xs, xt, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
                           enc->xnd.as<double>(), stream));
         STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
-                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m, enc->redo.as<int>(),
+                                            enc->xC.as<float>(), ns, beam, B + s0 * dims.m * cb, enc->redo.as<int>(),
                                             enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
         if (dims.large_root)  // LS, cost and ICM take the root term from the SIMD-order dot
-            STLQ_CK(stlq_b200::LaunchRootDot(dims, enc->C.as<float>(), Xs, xt, B + s0 * dims.m, ns,
+            STLQ_CK(stlq_b200::LaunchRootDot(dims, enc->C.as<float>(), Xs, xt, B + s0 * dims.m * cb, ns,
                                              enc->xC.as<float>(), stream));
         stlq_b200::RefineArgs ra{};
         ra.dims = dims;
@@ -285,7 +307,7 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         ra.seed = seed;
         ra.sample_id_offset = sample_id_offset + static_cast<uint64_t>(s0);
         ra.orders = icm_iters > 0 ? enc->orders.as<int>() : nullptr;
-        ra.B = B + s0 * dims.m;
+        ra.B = B + s0 * dims.m * cb;
         ra.a = a ? a + s0 * dims.m : nullptr;
         ra.cost = cost ? cost + s0 : nullptr;
         ra.partials = sse_dev ? enc->partials.as<double>() : nullptr;
@@ -339,8 +361,9 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     dims.m = m;
     int H = 0, maxK = 0;
     for (int l = 0; l < m; ++l) {
-        if (h_vec[l] < 1 || h_vec[l] > STLQ_B200_MAX_K)
-            return Fail(STLQ_B200_EINVAL, "h_vec[" + std::to_string(l) + "] must be in [1, 256] (uint8 codes)");
+        if (h_vec[l] < 1 || h_vec[l] > STLQ_B200_MAX_K_WIDE)
+            return Fail(STLQ_B200_EINVAL, "h_vec[" + std::to_string(l) +
+                                              "] must be in [1, 1024] (uint8 codes up to 256, uint16 above)");
         dims.h_vec[l] = h_vec[l];
         dims.off[l] = H;
         H += h_vec[l];
@@ -348,6 +371,7 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     }
     dims.H = H;
     dims.maxK = maxK;
+    dims.wide = maxK > STLQ_B200_MAX_K;
     int ndev = 0;
     STLQ_CK(cudaGetDeviceCount(&ndev));
     if (device < 0 || device >= ndev) return Fail(STLQ_B200_EINVAL, "device ordinal out of range");
@@ -363,7 +387,10 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
         return rc;
     };
     cudaDeviceProp prop{};
-    if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) enc->num_sms = prop.multiProcessorCount;
+    if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) {
+        enc->num_sms = prop.multiProcessorCount;
+        enc->max_block_smem = prop.sharedMemPerBlockOptin;
+    }
     const size_t HH = static_cast<size_t>(H) * H;
     int rc = 0;
     if ((rc = enc->C.Ensure(sizeof(float) * H * d)) || (rc = enc->Gcol.Ensure(sizeof(float) * HH)) ||
@@ -487,6 +514,7 @@ int stlq_b200_encode_base_device(stlq_b200_encoder* enc, const void* X_dev, int 
                                  int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
                                  uint64_t sample_id_offset, uint8_t* B_dev, float* a_dev, float* cost_dev,
                                  double* sse_out_dev, void* stream) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
     STLQ_TRY(CheckEncodeArgs(enc, x_dtype, n, beam, icm_iters, ils_iters, perturb_k));
     if (n > 0 && (!X_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "X_dev and B_dev must be non-null");
     DeviceScope scope(enc->device);
@@ -496,13 +524,34 @@ int stlq_b200_encode_base_device(stlq_b200_encoder* enc, const void* X_dev, int 
                         B_dev, a_dev, cost_dev, sse_out_dev, s);
 }
 
-// Host buffers: slices of up to `kHostSlice` vectors go through two pinned/device buffer pairs.
-// The copy stream carries H2D of slice s+1 and D2H of slice s-1 while the compute stream encodes
-// slice s; host staging into pinned memory is skipped when the caller's buffers are pinned.
-int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
-                          int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
-                          uint8_t* B_out, float* a_out, float* cost_out, double* sse_out) {
+int stlq_b200_encode_base_device_u16(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int64_t n, int beam,
+                                 int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                 uint64_t sample_id_offset, uint16_t* B_dev, float* a_dev, float* cost_dev,
+                                 double* sse_out_dev, void* stream) {
+    STLQ_TRY(CheckCodeWidth(enc, true));
     STLQ_TRY(CheckEncodeArgs(enc, x_dtype, n, beam, icm_iters, ils_iters, perturb_k));
+    if (n > 0 && (!X_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "X_dev and B_dev must be non-null");
+    DeviceScope scope(enc->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (sse_out_dev) STLQ_CK(cudaMemsetAsync(sse_out_dev, 0, 2 * sizeof(double), s));
+    return EncodeDevice(enc, X_dev, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed, sample_id_offset,
+                        B_dev, a_dev, cost_dev, sse_out_dev, s);
+}
+
+}  // extern "C"
+
+namespace {
+
+// The host-buffer stage for codes of CodeBytes(enc) bytes.  Slices of up to `kHostSlice` vectors
+// go through two pinned/device buffer pairs: the copy stream carries H2D of slice s+1 and D2H of
+// slice s-1 while the compute stream encodes slice s; host staging into pinned memory is skipped
+// when the caller's buffers are pinned.
+int EncodeHost(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters, int ils_iters,
+               int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset, void* B_outv, float* a_out,
+               float* cost_out, double* sse_out) {
+    STLQ_TRY(CheckEncodeArgs(enc, x_dtype, n, beam, icm_iters, ils_iters, perturb_k));
+    char* B_out = static_cast<char*>(B_outv);
+    const size_t cb = CodeBytes(enc);
     if (n > 0 && (!X || !B_out)) return Fail(STLQ_B200_EINVAL, "X and B_out must be non-null");
     DeviceScope scope(enc->device);
     const Dims& dims = enc->dims;
@@ -516,11 +565,11 @@ int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, in
     const bool pin_c = !cost_out || IsPinnedHost(cost_out);
     for (int b = 0; b < 2; ++b) {
         STLQ_TRY(enc->xin[b].Ensure(in_bytes));
-        STLQ_TRY(enc->Bd[b].Ensure(static_cast<size_t>(S) * dims.m));
+        STLQ_TRY(enc->Bd[b].Ensure(static_cast<size_t>(S) * dims.m * cb));
         STLQ_TRY(enc->ad[b].Ensure(static_cast<size_t>(S) * dims.m * sizeof(float)));
         STLQ_TRY(enc->costd[b].Ensure(static_cast<size_t>(S) * sizeof(float)));
         if (!pin_x) STLQ_TRY(enc->pin_in[b].Ensure(in_bytes));
-        if (!pin_B) STLQ_TRY(enc->pin_B[b].Ensure(static_cast<size_t>(S) * dims.m));
+        if (!pin_B) STLQ_TRY(enc->pin_B[b].Ensure(static_cast<size_t>(S) * dims.m * cb));
         if (!pin_a) STLQ_TRY(enc->pin_a[b].Ensure(static_cast<size_t>(S) * dims.m * sizeof(float)));
         if (!pin_c) STLQ_TRY(enc->pin_cost[b].Ensure(static_cast<size_t>(S) * sizeof(float)));
     }
@@ -534,7 +583,7 @@ int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, in
         const int b = static_cast<int>(s % 2);
         const int64_t s0 = s * S, ns = std::min(S, n - s0);
         STLQ_CK(cudaEventSynchronize(enc->ev_d2h[b]));
-        if (!pin_B) std::memcpy(B_out + s0 * dims.m, enc->pin_B[b].p, static_cast<size_t>(ns) * dims.m);
+        if (!pin_B) std::memcpy(B_out + s0 * dims.m * cb, enc->pin_B[b].p, static_cast<size_t>(ns) * dims.m * cb);
         if (!pin_a) std::memcpy(a_out + s0 * dims.m, enc->pin_a[b].p, static_cast<size_t>(ns) * dims.m * sizeof(float));
         if (!pin_c) std::memcpy(cost_out + s0, enc->pin_cost[b].p, static_cast<size_t>(ns) * sizeof(float));
         return 0;
@@ -553,13 +602,13 @@ int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, in
         STLQ_CK(cudaEventRecord(enc->ev_h2d[b], ps));
         STLQ_CK(cudaStreamWaitEvent(cs, enc->ev_h2d[b], 0));
         STLQ_TRY(EncodeDevice(enc, enc->xin[b].p, x_dtype, ns, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
-                              sample_id_offset + static_cast<uint64_t>(s0), enc->Bd[b].as<uint8_t>(),
+                              sample_id_offset + static_cast<uint64_t>(s0), enc->Bd[b].p,
                               a_out ? enc->ad[b].as<float>() : nullptr, cost_out ? enc->costd[b].as<float>() : nullptr,
                               sse_out ? enc->sse_d.as<double>() : nullptr, cs));
         STLQ_CK(cudaEventRecord(enc->ev_comp[b], cs));
         STLQ_CK(cudaStreamWaitEvent(ps, enc->ev_comp[b], 0));
-        void* dB = pin_B ? static_cast<void*>(B_out + s0 * dims.m) : enc->pin_B[b].p;
-        STLQ_CK(cudaMemcpyAsync(dB, enc->Bd[b].p, static_cast<size_t>(ns) * dims.m, cudaMemcpyDeviceToHost, ps));
+        void* dB = pin_B ? static_cast<void*>(B_out + s0 * dims.m * cb) : enc->pin_B[b].p;
+        STLQ_CK(cudaMemcpyAsync(dB, enc->Bd[b].p, static_cast<size_t>(ns) * dims.m * cb, cudaMemcpyDeviceToHost, ps));
         if (a_out) {
             void* da = pin_a ? static_cast<void*>(a_out + s0 * dims.m) : enc->pin_a[b].p;
             STLQ_CK(cudaMemcpyAsync(da, enc->ad[b].p, static_cast<size_t>(ns) * dims.m * sizeof(float),
@@ -581,11 +630,34 @@ int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, in
     return stlq_b200_sync(enc, cs);
 }
 
+}  // namespace
+
+extern "C" {
+
+int stlq_b200_encode_base(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
+                          int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                          uint8_t* B_out, float* a_out, float* cost_out, double* sse_out) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
+    return EncodeHost(enc, X, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed, sample_id_offset, B_out,
+                      a_out, cost_out, sse_out);
+}
+
+int stlq_b200_encode_base_u16(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
+                              int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                              uint16_t* B_out, float* a_out, float* cost_out, double* sse_out) {
+    STLQ_TRY(CheckCodeWidth(enc, true));
+    return EncodeHost(enc, X, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed, sample_id_offset, B_out,
+                      a_out, cost_out, sse_out);
+}
+
 int stlq_b200_create_large_root(int device, int d, int m, const int* h_vec, const float* C_all, int gemm_mode,
                                 stlq_b200_encoder** out) {
     if (!out) return Fail(STLQ_B200_EINVAL, "out is null");
     *out = nullptr;
     if (m < 2) return Fail(STLQ_B200_EINVAL, "a large-root encoder needs m >= 2 (a root and at least one small codebook)");
+    for (int l = 0; l < m && h_vec; ++l)
+        if (h_vec[l] > STLQ_B200_MAX_K)
+            return Fail(STLQ_B200_EINVAL, "a large-root encoder supports codebooks of at most 256 codewords");
     STLQ_TRY(stlq_b200_create(device, d, m, h_vec, C_all, nullptr, nullptr, gemm_mode, out));
     stlq_b200_encoder* enc = *out;
     DeviceScope scope(enc->device);
@@ -727,6 +799,7 @@ int stlq_b200_xnorm2(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int
 
 int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const float* xC_dev, int64_t n, int beam,
                           uint8_t* B_dev, void* stream) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
     STLQ_TRY(CheckEncodeArgs(enc, STLQ_B200_F32, n, beam, 0, 0, 0));
     if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
@@ -739,6 +812,7 @@ int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const
 
 int stlq_b200_solve_ls(stlq_b200_encoder* enc, const float* xC_dev, const uint8_t* B_dev, int64_t n, float* a_dev,
                        void* stream) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
     STLQ_TRY(CheckEnc(enc));
     if (n > 0 && (!xC_dev || !B_dev || !a_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
@@ -758,6 +832,7 @@ int stlq_b200_solve_ls(stlq_b200_encoder* enc, const float* xC_dev, const uint8_
 int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnorm2_dev, int64_t n, int icm_iters,
                   int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset, uint8_t* B_dev,
                   float* a_dev, float* cost_dev, void* stream) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
     STLQ_TRY(CheckEncodeArgs(enc, STLQ_B200_F32, n, 1, icm_iters, ils_iters, perturb_k));
     if (n > 0 && (!xC_dev || !xnorm2_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
@@ -788,6 +863,7 @@ int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnor
 
 int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const float* xC_dev, const uint8_t* B_dev,
                   const float* a_dev, int64_t n, double* sse_dev, void* stream) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
     STLQ_TRY(CheckEnc(enc));
     if (n > 0 && (!X_dev || !xC_dev || !B_dev || !a_dev || !sse_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);

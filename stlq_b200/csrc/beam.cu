@@ -209,33 +209,36 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
                                            const float* __restrict__ xc, float* lo, float* hi_out, int check,
                                            unsigned int* err_flag, bool recip) {
     const int tid = threadIdx.x;
-    float alpha[kCpt], gamma[kCpt];
-    int col[kCpt];
-    bool ok[kCpt];
-#pragma unroll
-    for (int c = 0; c < kCpt; ++c) {
-        const int k = tid + c * kThreads;
-        ok[c] = k < K;
-        col[c] = offL + k;
-        alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
-        gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
-    }
-    const float* gq[kCpt];
-#pragma unroll
-    for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
     float hmin = PosInf();  // never NaN: a bound is finite or +-inf
-    for (int h = 0; h < curH; ++h) {
-        float l[kCpt], hi[kCpt];
-        CheapBounds<MAXM, L>(cur, h, gq, ok, alpha, gamma, l, hi);
+    // Codebooks above 256 codewords are walked in chunks of kMaxK (kCpt codewords per thread).
+    for (int kc = 0; kc < K; kc += kMaxK) {
+        float alpha[kCpt], gamma[kCpt];
+        int col[kCpt];
+        bool ok[kCpt];
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) {
-            if (ok[c]) {
-                lo[h * K + tid + c * kThreads] = l[c];
-                if (kHi) hi_out[h * K + tid + c * kThreads] = hi[c];
-                hmin = fminf(hmin, hi[c]);
-            }
+            const int k = kc + tid + c * kThreads;
+            ok[c] = k < K;
+            col[c] = offL + k;
+            alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
+            gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
         }
-        if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag, recip);
+        const float* gq[kCpt];
+#pragma unroll
+        for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
+        for (int h = 0; h < curH; ++h) {
+            float l[kCpt], hi[kCpt];
+            CheapBounds<MAXM, L>(cur, h, gq, ok, alpha, gamma, l, hi);
+#pragma unroll
+            for (int c = 0; c < kCpt; ++c) {
+                if (ok[c]) {
+                    lo[h * K + kc + tid + c * kThreads] = l[c];
+                    if (kHi) hi_out[h * K + kc + tid + c * kThreads] = hi[c];
+                    hmin = fminf(hmin, hi[c]);
+                }
+            }
+            if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag, recip);
+        }
     }
     return OrderKey(hmin);
 }
@@ -342,7 +345,9 @@ struct Replay {
 
 // One layer of the replay: cheap bounds for every candidate, the pre-scan that finds the
 // candidates able to enter, exact errors for those only (all others are +inf, which enters no
-// slot), then the reference's replacement scan over the exact errors.
+// slot), then the reference's replacement scan over the exact errors.  Without room for the upper
+// bounds (his == nullptr: beam x codebook size too large for shared memory) every candidate is
+// evaluated exactly; the scan's result is the same.
 template <int MAXM>
 __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
@@ -350,19 +355,22 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
     const int n_cand = curH * K;
-    CheapDispatch<MAXM, true>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, errs, his, 0, nullptr, dims.large_root != 0);
-    __syncthreads();
     int* list = reinterpret_cast<int*>(his);
-    if (tid < 32) {
-        Replay rp;
-        rp.Init(beam);
-        const int need = rp.PreScan(errs, his, n_cand, list);
-        if (tid == 0) lt.n_surv = need;
+    if (his) {
+        CheapDispatch<MAXM, true>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, errs, his, 0, nullptr,
+                                  dims.large_root != 0);
+        __syncthreads();
+        if (tid < 32) {
+            Replay rp;
+            rp.Init(beam);
+            const int need = rp.PreScan(errs, his, n_cand, list);
+            if (tid == 0) lt.n_surv = need;
+        }
+        __syncthreads();
     }
-    __syncthreads();
-    const int need = lt.n_surv;
+    const int need = his ? lt.n_surv : n_cand;
     for (int p = tid; p < need; p += kThreads) {
-        const int idx = list[p];
+        const int idx = his ? list[p] : p;
         const int h = idx / K, k = idx - h * K;
         errs[idx] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
                                      __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr, dims.large_root != 0);
@@ -391,14 +399,14 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
                                                              const float* __restrict__ Gdiag,
                                                              const float* __restrict__ xnorm2,
                                                              const float* __restrict__ xC, int64_t n, int beam,
-                                                             uint8_t* __restrict__ Bout, const int* vec_list,
-                                                             const int* count) {
+                                                             void* __restrict__ Bout, const int* vec_list,
+                                                             const int* count, bool prescan) {
     extern __shared__ __align__(16) unsigned char smem[];
     const size_t sv = SlotView<MAXM>::Bytes(beam);
     size_t off = (2 * sv + 15) & ~size_t(15);
     LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
     float* errs = reinterpret_cast<float*>(smem + ((off + sizeof(LayerTable) + 15) & ~size_t(15)));
-    float* his = errs + beam * dims.maxK;
+    float* his = prescan ? errs + beam * dims.maxK : nullptr;
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     const int64_t total = vec_list ? static_cast<int64_t>(*count) : n;
@@ -435,7 +443,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
             const uint32_t key = tid < curH ? OrderKey(cur.E[tid]) : 0xffffffffu;
             const uint32_t kmin = __reduce_min_sync(kFull, key);
             const int best = __ffs(__ballot_sync(kFull, key == kmin)) - 1;
-            if (tid < m) Bout[vec * m + tid] = static_cast<uint8_t>(cur.rowh(best)[tid] / dims.H - dims.off[tid]);
+            if (tid < m) StoreCode(Bout, vec * m + tid, cur.rowh(best)[tid] / dims.H - dims.off[tid], dims.wide);
         }
         __syncthreads();
     }
@@ -625,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
                                                            const float* __restrict__ Gdiag,
                                                            const float* __restrict__ xnorm2,
                                                            const float* __restrict__ xC, int64_t n, int beam,
-                                                           uint8_t* __restrict__ Bout, int* redo_list, int* redo_count,
+                                                           void* __restrict__ Bout, int* redo_list, int* redo_count,
                                                            int check, unsigned int* err_flag,
                                                            unsigned long long* stats) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -646,14 +654,10 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         const float nx2 = __ldg(xnorm2 + vec);
         // Layer 0: exact errors are cheap; they serve as their own bounds.
         uint32_t hmin = 0xffffffffu;
-#pragma unroll
-        for (int c = 0; c < kCpt; ++c) {
-            const int k = tid + c * kThreads;
-            if (k < K0) {
-                const float e1 = Layer0Error(Gdiag, xc, nx2, k);
-                lo[k] = e1;
-                hmin = min(hmin, OrderKey(e1));
-            }
+        for (int k = tid; k < K0; k += kThreads) {
+            const float e1 = Layer0Error(Gdiag, xc, nx2, k);
+            lo[k] = e1;
+            hmin = min(hmin, OrderKey(e1));
         }
         int curH = SelectSurvivors(lo, K0, hmin, beam, lt, surv);
         if (curH >= 0) {
@@ -685,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         if (redo) {
             if (tid == 0) redo_list[atomicAdd(redo_count, 1)] = static_cast<int>(vec);
         } else if (tid < m) {
-            Bout[vec * m + tid] = static_cast<uint8_t>(cur.rowh(0)[tid] / dims.H - dims.off[tid]);
+            StoreCode(Bout, vec * m + tid, cur.rowh(0)[tid] / dims.H - dims.off[tid], dims.wide);
         }
         __syncthreads();
     }
@@ -705,11 +709,27 @@ size_t FastSmemBytes(int beam, int maxK) {
            sizeof(float) * kKeep * KeepStride<MAXM>() + 16;
 }
 
+// With the pre-scan: errors (lower bounds first) and upper bounds; without: errors only.
 template <int MAXM>
-size_t ReplaySmemBytes(int beam, int maxK) {
+size_t ReplaySmemBytes(int beam, int maxK, bool prescan) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
-    return b + 2 * sizeof(float) * beam * maxK + 16;  // errors (lower bounds first) and upper bounds
+    return b + (prescan ? 2 : 1) * sizeof(float) * beam * maxK + 16;
+}
+
+// The largest dynamic shared memory a block of the current device may opt into.
+size_t MaxBlockSmem() {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return 0;
+    return static_cast<size_t>(v);
+}
+
+// The replay runs its pre-scan whenever the upper bounds fit beside the errors.
+template <int MAXM>
+bool ReplayPrescan(int beam, int maxK) {
+    return ReplaySmemBytes<MAXM>(beam, maxK, true) <= MaxBlockSmem();
 }
 
 // Sets the kernel's shared-memory size, finds how many CTAs fit on an SM, then asks for the
@@ -748,7 +768,7 @@ cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* gr
 
 template <int MAXM>
 cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2, const float* xC,
-                        int64_t n, int beam, uint8_t* Bout, int* redo, int check, unsigned int* err_flag,
+                        int64_t n, int beam, void* Bout, int* redo, int check, unsigned int* err_flag,
                         unsigned long long* stats, int num_sms, cudaStream_t stream) {
     int grid = 0;
     const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
@@ -760,18 +780,19 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
                                                           check, err_flag, stats);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK);
+    const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxK);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK, prescan);
     e = Prepare(BeamReplayKernel<MAXM>, rsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     BeamReplayKernel<MAXM><<<grid, kThreads, rsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
-                                                            redo);
+                                                            redo, prescan);
     return cudaGetLastError();
 }
 
 template <int MAXM>
 cudaError_t PrepareT(const Dims& dims, int beam) {
     const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK, ReplayPrescan<MAXM>(beam, dims.maxK));
     cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(fsm));
     if (e != cudaSuccess) return e;
@@ -781,13 +802,17 @@ cudaError_t PrepareT(const Dims& dims, int beam) {
 
 }  // namespace
 
+size_t BeamFastSmemBytes(const Dims& dims, int beam) {
+    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxK) : FastSmemBytes<16>(beam, dims.maxK);
+}
+
 cudaError_t PrepareBeamKernels(const Dims& dims, int beam) {
     return dims.m <= 8 ? PrepareT<8>(dims, beam) : PrepareT<16>(dims, beam);
 }
 
 // redo: n + 1 ints of scratch (a count, then vector ids handed from the fast to the replay kernel).
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
-                             const float* xC, int64_t n, int beam, uint8_t* Bout, int* redo, int check,
+                             const float* xC, int64_t n, int beam, void* Bout, int* redo, int check,
                              unsigned int* err_flag, int num_sms, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     // The encoder's flag word is followed by four 64-bit counters (BeamStats).

@@ -9,6 +9,15 @@
 namespace stlq_b200 {
 
 // Monotone map from float to uint32 so that unsigned order equals float order (-inf < ... < +inf).
+// Codes are stored as uint8 or, for codebooks above 256 codewords, uint16.
+__device__ __forceinline__ int LoadCode(const void* B, int64_t i, int wide) {
+    return wide ? static_cast<const uint16_t*>(B)[i] : static_cast<const uint8_t*>(B)[i];
+}
+__device__ __forceinline__ void StoreCode(void* B, int64_t i, int code, int wide) {
+    if (wide) static_cast<uint16_t*>(B)[i] = static_cast<uint16_t>(code);
+    else static_cast<uint8_t*>(B)[i] = static_cast<uint8_t>(code);
+}
+
 __device__ __forceinline__ uint32_t OrderKey(float f) {
     const uint32_t u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);

@@ -22,8 +22,10 @@ cudaError_t LaunchSplitTf32(const void* x, int x_dtype, int64_t count, float* hi
 // ||x||^2 per vector in float (the reference's 4-lane SIMD order) and in double; either may be null.
 cudaError_t LaunchNorms(const void* X, int x_dtype, int64_t n, int d, float* xn, double* xnd, cudaStream_t stream);
 
+// Dynamic shared memory of the fast beam kernel (the larger of the two beam kernels).
+size_t BeamFastSmemBytes(const Dims& dims, int beam);
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
-                             const float* xC, int64_t n, int beam, uint8_t* Bout, int* redo, int check,
+                             const float* xC, int64_t n, int beam, void* Bout, int* redo, int check,
                              unsigned int* err_flag, int num_sms, cudaStream_t stream);
 
 struct RefineArgs {
@@ -42,7 +44,7 @@ struct RefineArgs {
     uint32_t seed;
     uint64_t sample_id_offset;
     const int* orders;  // [(n_ils + 1)][icm_iters][m]
-    uint8_t* B;
+    void* B;  // m x n codes, uint8 or (dims.wide) uint16
     float* a;
     float* cost;
     double* partials;  // [grid][2] (beam SSE, final SSE) or null
@@ -50,7 +52,7 @@ struct RefineArgs {
 
 cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream);
 cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* out, cudaStream_t stream);
-cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const uint8_t* B,
+cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const void* B,
                       const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
 int RefineWarpsPerBlock();
 
@@ -76,7 +78,7 @@ cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gco
                                    float* invnorm, cudaStream_t stream);
 // Large-root mode: xC[vec][root] = the reference's SIMD-order dot of the chosen root codeword with
 // x (Dot, least_squares.cpp:35-42), which its LS, cost and ICM use for the root term.
-cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const uint8_t* B, int64_t n,
+cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const void* B, int64_t n,
                           float* xC, cudaStream_t stream);
 cudaError_t LaunchSplitRootCodes(int m, const uint8_t* B, int64_t n, uint32_t* cluster, uint8_t* B_small,
                                  cudaStream_t stream);

@@ -59,6 +59,10 @@ extern "C" int stlq_b200_beam_search_noalloc(stlq_b200_encoder* enc, const float
                                              int64_t n, int beam, uint8_t* B_dev, void* stream) {
     stlq_b200::BeamInputs in{};
     if (int rc = stlq_b200::GetBeamInputs(enc, &in)) return rc;
+    if (in.dims.wide)
+        return stlq_b200::SetError(STLQ_B200_EINVAL,
+                                   "stlq_b200_beam_search_noalloc writes uint8 codes; this encoder has a codebook above "
+                                   "256 codewords");
     if (n < 0) return stlq_b200::SetError(STLQ_B200_EINVAL, "n must be >= 0");
     if (n > STLQ_B200_NOALLOC_MAX_VECTORS) {
         const std::string msg = "stlq_b200_beam_search_noalloc: n = " + std::to_string(n) + " exceeds " +

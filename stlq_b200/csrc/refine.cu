@@ -455,7 +455,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
     for (int64_t vec = static_cast<int64_t>(blockIdx.x) * kWarps + warp; vec < p.n;
          vec += static_cast<int64_t>(gridDim.x) * kWarps) {
         const float* xc = p.xC + vec * dims.H;
-        if (lane < m) ws.code[lane] = p.B[vec * m + lane];
+        if (lane < m) ws.code[lane] = LoadCode(p.B, vec * m + lane, dims.wide);
         __syncwarp();
         if (p.mode == 0) {
             LoadGram(dims, p.Gcol, ws.code, ws.Gs);
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
             if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
         }
         if (lane < m) {
-            p.B[vec * m + lane] = static_cast<uint8_t>(ws.code[lane]);
+            StoreCode(p.B, vec * m + lane, ws.code[lane], dims.wide);
             if (p.a) p.a[vec * m + lane] = ws.a[lane];
         }
         if (lane == 0 && p.cost) p.cost[vec] = cost;
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
 // then added (no contraction).  4 threads per vector.
 template <typename T>
 __global__ void RootDotKernel(Dims dims, const float* __restrict__ C, const T* __restrict__ X,
-                              const uint8_t* __restrict__ B, int64_t n, float* __restrict__ xC) {
+                              const void* __restrict__ B, int64_t n, float* __restrict__ xC) {
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t vec = t >> 2;
     const int l = static_cast<int>(t & 3);
@@ -560,7 +560,7 @@ __global__ void RootDotKernel(Dims dims, const float* __restrict__ C, const T* _
     int root = 0;
     float s = 0.0f;
     if (ok) {
-        root = B[vec * dims.m];
+        root = LoadCode(B, vec * dims.m, dims.wide);
         const float* c = C + static_cast<size_t>(root) * d;
         const T* x = X + vec * d;
         const int body = (d / 4) * 4;
@@ -589,14 +589,14 @@ __global__ void ReducePartialsKernel(const double* partials, int nblocks, double
 }
 
 // Per-vector MSE term alone (stlq_b200_sse): one thread per vector.
-__global__ void SseKernel(Dims dims, const float* Gcol, const float* xC, const double* xnorm2_d, const uint8_t* B,
+__global__ void SseKernel(Dims dims, const float* Gcol, const float* xC, const double* xnorm2_d, const void* B,
                           const float* a, int64_t n, double* partials) {
     __shared__ double red[256];
     double s = 0.0;
     for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n;
          v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         int code[kMaxM];
-        for (int l = 0; l < dims.m; ++l) code[l] = B[v * dims.m + l];
+        for (int l = 0; l < dims.m; ++l) code[l] = LoadCode(B, v * dims.m + l, dims.wide);
         s += VectorSse(dims, GramGlobal{Gcol, dims.H, dims.off, code}, xC + v * dims.H, code, a + v * dims.m,
                        xnorm2_d[v]);
     }
@@ -621,7 +621,7 @@ cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* ou
     return cudaGetLastError();
 }
 
-cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const uint8_t* B,
+cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const void* B,
                       const float* a, int64_t n, double* partials, int grid, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     SseKernel<<<grid, 256, 0, stream>>>(dims, Gcol, xC, xnorm2_d, B, a, n, partials);
@@ -649,7 +649,7 @@ cudaError_t LaunchSplitRootCodes(int m, const uint8_t* B, int64_t n, uint32_t* c
     return cudaGetLastError();
 }
 
-cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const uint8_t* B, int64_t n,
+cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const void* B, int64_t n,
                           float* xC, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     const int grid = static_cast<int>((n * 4 + 255) / 256);

@@ -8,6 +8,7 @@ namespace stlq_b200 {
 constexpr int kMaxM = 16;
 constexpr int kMaxK = 256;
 constexpr int kMaxBeam = 32;
+constexpr int kMaxKWide = 1024;  // codewords per codebook with uint16 codes
 constexpr float kIcmEps = 1e-6f;  // icm.cpp:29, least_squares.cpp:19
 
 // Device-side error flags (bit set by a kernel that met a state it cannot handle; read by the
@@ -32,6 +33,8 @@ struct Dims {
     // codebook 0 is the root; the beam's triangular solves multiply by 1/R_ii
     // (beam_search.cpp:517-575) and costs follow SampleCostLargeRoot (cost_utils.cpp:160-209).
     int large_root;
+    // Codes are uint16 (some codebook has more than 256 codewords) instead of uint8.
+    int wide;
 };
 
 }  // namespace stlq_b200

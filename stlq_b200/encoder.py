@@ -48,6 +48,8 @@ def load_library():
                                           vp, vp, vp, vp]
     lib.stlq_b200_encode_base_device.argtypes = [vp, vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_int, c_u32,
                                                  c_u64, vp, vp, vp, vp, vp]
+    lib.stlq_b200_encode_base_u16.argtypes = lib.stlq_b200_encode_base.argtypes
+    lib.stlq_b200_encode_base_device_u16.argtypes = lib.stlq_b200_encode_base_device.argtypes
     lib.stlq_b200_xc_gemm.argtypes = [vp, vp, c_int, c_i64, vp, vp]
     lib.stlq_b200_xnorm2.argtypes = [vp, vp, c_int, c_i64, vp, vp]
     lib.stlq_b200_beam_search.argtypes = [vp, vp, vp, c_i64, c_int, vp, vp]
@@ -111,6 +113,8 @@ class Encoder:
         if int(self.h_vec.sum()) != self.H:
             raise StlqB200Error("sum(h_vec) must equal C_all.shape[0]")
         self.device = int(device)
+        # Codebooks above 256 codewords take uint16 codes (the _u16 entry points).
+        self.wide = self.m > 0 and int(self.h_vec.max()) > 256
         mode = _MODES[gemm_mode] if isinstance(gemm_mode, str) else int(gemm_mode)
         Gc = None if G is None else np.ascontiguousarray(G, np.float32)
         inv = None if invnorm is None else np.ascontiguousarray(invnorm, np.float32)
@@ -150,16 +154,17 @@ class Encoder:
         n = X.shape[0]
         out = dict(out or {})
         B = out.get("B")
-        B = np.empty((n, self.m), np.uint8) if B is None else B
+        B = np.empty((n, self.m), np.uint16 if self.wide else np.uint8) if B is None else B
         a = out.get("a") if want_a else None
         a = np.empty((n, self.m), np.float32) if (want_a and a is None) else a
         cost = out.get("cost") if want_cost else None
         cost = np.empty(n, np.float32) if (want_cost and cost is None) else cost
         sse = np.zeros(2, np.float64)
-        rc = self.lib.stlq_b200_encode_base(self.handle, _np_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters,
-                                            perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF, sample_id_offset,
-                                            _np_ptr(B), _np_ptr(a), _np_ptr(cost), _np_ptr(sse))
-        _check(self.lib, rc, "stlq_b200_encode_base")
+        name = "stlq_b200_encode_base_u16" if self.wide else "stlq_b200_encode_base"
+        rc = getattr(self.lib, name)(self.handle, _np_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters,
+                                     perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF, sample_id_offset,
+                                     _np_ptr(B), _np_ptr(a), _np_ptr(cost), _np_ptr(sse))
+        _check(self.lib, rc, name)
         nn = max(n, 1)
         return dict(B=B, a=a, cost=cost, beam_mse=sse[0] / nn, final_mse=sse[1] / nn, sse=sse)
 
@@ -207,19 +212,21 @@ class Encoder:
     def encode_base_device(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,
                            seed: int = 38251450, sample_id_offset: int = 0, B=None, a=None, cost=None, sse=None,
                            stream=None):
-        """Asynchronous on ``stream`` (default: torch's current stream).  Returns (B, a, cost, sse)."""
+        """Asynchronous on ``stream`` (default: torch's current stream).  Returns (B, a, cost, sse); B is
+        uint16 when a codebook has more than 256 codewords, else uint8."""
         import torch
 
         n = X.shape[0]
         dev = X.device
-        B = torch.empty((n, self.m), dtype=torch.uint8, device=dev) if B is None else B
+        code_t = torch.uint16 if self.wide else torch.uint8
+        B = torch.empty((n, self.m), dtype=code_t, device=dev) if B is None else B
         sse = torch.zeros(2, dtype=torch.float64, device=dev) if sse is None else sse
         s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
-        rc = self.lib.stlq_b200_encode_base_device(self.handle, _t_ptr(X), _dtype_code(X), n, beam, icm_iters,
-                                                   ils_iters, perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF,
-                                                   sample_id_offset, _t_ptr(B), _t_ptr(a), _t_ptr(cost), _t_ptr(sse),
-                                                   ctypes.c_void_p(s))
-        _check(self.lib, rc, "stlq_b200_encode_base_device")
+        name = "stlq_b200_encode_base_device_u16" if self.wide else "stlq_b200_encode_base_device"
+        rc = getattr(self.lib, name)(self.handle, _t_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters,
+                                     perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF, sample_id_offset, _t_ptr(B),
+                                     _t_ptr(a), _t_ptr(cost), _t_ptr(sse), ctypes.c_void_p(s))
+        _check(self.lib, rc, name)
         return B, a, cost, sse
 
     def set_rotation(self, R):

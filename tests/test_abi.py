@@ -38,7 +38,7 @@ def test_version_and_empty_error():
 @pytest.mark.parametrize("m,h,d,mode,msg", [
     (0, [], 8, 0, b"m must be"),
     (17, [4] * 17, 8, 0, b"m must be"),
-    (2, [4, 257], 8, 0, b"h_vec[1]"),
+    (2, [4, 1025], 8, 0, b"h_vec[1]"),
     (2, [4, 0], 8, 0, b"h_vec[1]"),
     (2, [4, 4], 0, 0, b"d must be"),
     (2, [4, 4], 8, 3, b"gemm_mode must be"),
