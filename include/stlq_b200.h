@@ -52,6 +52,7 @@ enum { STLQ_B200_F32 = 0, STLQ_B200_U8 = 1 };
 #define STLQ_B200_MAX_K 256     /* codewords per codebook with uint8 codes */
 #define STLQ_B200_MAX_K_WIDE 1024 /* codewords per codebook with uint16 codes (the _u16 entry points) */
 #define STLQ_B200_MAX_BEAM 32   /* beam width */
+#define STLQ_B200_MAX_ROOT 65536 /* root codewords of a large-root encoder */
 
 /* Message for the last failed call on this host thread ("" if none). */
 const char* stlq_b200_last_error(void);
@@ -181,11 +182,14 @@ int stlq_b200_rotate(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, int
  * (least_squares.cpp:567-745), ComputeCostsLargeRoot (cost_utils.cpp:160-235) and
  * DynamicIcmWithIls{Abs,NoAbs}NoNormalLargeRoot (icm.cpp:347-870, 1005-1210), as the large
  * pipeline runs them per block (src/quantizer/encode_base_streaming.cpp:1040-1300).
- * Codebook 0 of C_all is the root (cluster ids); this build supports h_vec[0] <= 256.  The
- * large-root arithmetic differs from the regular encoder's in the root codewords' norms and the
- * root dot products (the reference's SIMD-order loops), the beam's triangular solves (multiplied
- * by 1/R_ii) and the cost's summation order; the codes equal the reference's large-root codes.
- * The stage entry points above also accept such a handle (codes as m x n, root first). */
+ * Codebook 0 of C_all is the root (cluster ids): h_vec[0] in [1, 65536], the other codebooks
+ * in [1, 256] (uint8 codes, as the reference's B_small).  Like PrecompLargeRoot the handle holds
+ * no root-root Gram block: only the G0S and G_small columns ((H - h0) x H floats) and the root
+ * norms.  The large-root arithmetic differs from the regular encoder's in the root codewords'
+ * norms and the root dot products (the reference's SIMD-order loops), the beam's triangular
+ * solves (multiplied by 1/R_ii) and the cost's summation order; the codes equal the reference's
+ * large-root codes.  With h_vec[0] <= 256 the uint8 stage entry points above also accept such a
+ * handle (codes as m x n, root first). */
 int stlq_b200_create_large_root(int device, int d, int m, const int* h_vec, const float* C_all, int gemm_mode,
                                 stlq_b200_encoder** out);
 

@@ -152,6 +152,11 @@ namespace {
 
 size_t CodeBytes(const stlq_b200_encoder* enc) { return enc->dims.wide ? 2 : 1; }
 
+// The beam's Gram array: the row-major copy, or the large-root encoder's one symmetric array.
+const float* BeamGram(const stlq_b200_encoder* enc) {
+    return enc->Grow.p ? enc->Grow.as<float>() : enc->Gcol.as<float>();
+}
+
 // Vectors per encode slice: bounds the xC scratch (H floats per vector) to ~2 GiB.
 int64_t SliceVectors(const stlq_b200_encoder* enc) {
     const int64_t by_mem = (int64_t{1} << 31) / (static_cast<int64_t>(enc->dims.H) * 4);
@@ -284,7 +289,7 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         }
         STLQ_TRY(LaunchXc(enc, Xs, xt, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
                           enc->xnd.as<double>(), stream));
-        STLQ_CK(stlq_b200::LaunchBeamSearch(dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), enc->xn.as<float>(),
+        STLQ_CK(stlq_b200::LaunchBeamSearch(dims, BeamGram(enc), enc->Gdiag.as<float>(), enc->xn.as<float>(),
                                             enc->xC.as<float>(), ns, beam, B + s0 * dims.m * cb, enc->redo.as<int>(),
                                             enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
@@ -294,6 +299,7 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         stlq_b200::RefineArgs ra{};
         ra.dims = dims;
         ra.Gcol = enc->Gcol.as<float>();
+        ra.Gdiag = enc->Gdiag.as<float>();
         ra.invnorm = enc->invnorm.as<float>();
         ra.xC = enc->xC.as<float>();
         ra.xnorm2 = enc->xn.as<float>();
@@ -326,7 +332,7 @@ namespace stlq_b200 {
 int GetBeamInputs(const stlq_b200_encoder* enc, BeamInputs* out) {
     if (!enc) return Fail(STLQ_B200_EINVAL, "encoder handle is null");
     out->dims = enc->dims;
-    out->Grow = enc->Grow.as<float>();
+    out->Grow = BeamGram(enc);
     out->Gdiag = enc->Gdiag.as<float>();
     out->err_flag = enc->err_flag.as<unsigned int>();
     out->check_filter = enc->check_filter;
@@ -345,8 +351,15 @@ const char* stlq_b200_last_error(void) { return g_last_error.c_str(); }
 
 const char* stlq_b200_version(void) { return "stlq_b200 0.1.0 sm_100a"; }
 
-int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_all, const float* G,
-                     const float* invnorm, int gemm_mode, stlq_b200_encoder** out) {
+}  // extern "C"
+
+namespace {
+
+// Both encoder kinds.  Regular: the full Gram G = C_all^T C_all in both orientations (or the
+// caller's G).  Large root (BuildPrecompLargeRoot): only the columns of codebooks 1..m-1, one
+// symmetric array, with the root codewords' norms as their diagonal.
+int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, const float* G, const float* invnorm,
+               int gemm_mode, bool large_root, stlq_b200_encoder** out) {
     if (!out) return Fail(STLQ_B200_EINVAL, "out is null");
     *out = nullptr;
     if (!h_vec || !C_all) return Fail(STLQ_B200_EINVAL, "h_vec and C_all must be non-null");
@@ -359,19 +372,33 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     Dims dims{};
     dims.d = d;
     dims.m = m;
-    int H = 0, maxK = 0;
+    if (large_root && m < 2)
+        return Fail(STLQ_B200_EINVAL, "a large-root encoder needs m >= 2 (a root and at least one small codebook)");
+    int H = 0, maxK = 0, maxKs = 1;
     for (int l = 0; l < m; ++l) {
-        if (h_vec[l] < 1 || h_vec[l] > STLQ_B200_MAX_K_WIDE)
+        if (large_root) {
+            const int lim = l == 0 ? STLQ_B200_MAX_ROOT : STLQ_B200_MAX_K;
+            if (h_vec[l] < 1 || h_vec[l] > lim)
+                return Fail(STLQ_B200_EINVAL, "h_vec[" + std::to_string(l) + "] must be in [1, " + std::to_string(lim) +
+                                                  "] for a large-root encoder");
+        } else if (h_vec[l] < 1 || h_vec[l] > STLQ_B200_MAX_K_WIDE) {
             return Fail(STLQ_B200_EINVAL, "h_vec[" + std::to_string(l) +
                                               "] must be in [1, 1024] (uint8 codes up to 256, uint16 above)");
+        }
         dims.h_vec[l] = h_vec[l];
         dims.off[l] = H;
         H += h_vec[l];
         maxK = std::max(maxK, h_vec[l]);
+        if (l > 0) maxKs = std::max(maxKs, h_vec[l]);
     }
     dims.H = H;
     dims.maxK = maxK;
-    dims.wide = maxK > STLQ_B200_MAX_K;
+    dims.maxKs = maxKs;
+    dims.large_root = large_root ? 1 : 0;
+    dims.wide = maxK > STLQ_B200_MAX_K;  // large root: only the root can exceed 256
+    dims.c0 = large_root ? h_vec[0] : 0;
+    dims.ldg = H - dims.c0;
+    const int Hs = dims.ldg;
     int ndev = 0;
     STLQ_CK(cudaGetDeviceCount(&ndev));
     if (device < 0 || device >= ndev) return Fail(STLQ_B200_EINVAL, "device ordinal out of range");
@@ -391,10 +418,10 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
         enc->num_sms = prop.multiProcessorCount;
         enc->max_block_smem = prop.sharedMemPerBlockOptin;
     }
-    const size_t HH = static_cast<size_t>(H) * H;
+    const size_t HH = static_cast<size_t>(H) * Hs;  // Gram entries held
     int rc = 0;
     if ((rc = enc->C.Ensure(sizeof(float) * H * d)) || (rc = enc->Gcol.Ensure(sizeof(float) * HH)) ||
-        (rc = enc->Grow.Ensure(sizeof(float) * HH)) || (rc = enc->Gdiag.Ensure(sizeof(float) * H)) ||
+        (!large_root && (rc = enc->Grow.Ensure(sizeof(float) * HH))) || (rc = enc->Gdiag.Ensure(sizeof(float) * H)) ||
         (rc = enc->invnorm.Ensure(sizeof(float) * H)) || (rc = enc->err_flag.Ensure(kFlagBytes)))
         return fail(rc);
     if (cudaStreamCreateWithFlags(&enc->compute, cudaStreamNonBlocking) != cudaSuccess ||
@@ -413,7 +440,13 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
     };
     if ((rc = ck(cudaMemcpyAsync(enc->C.p, C_all, sizeof(float) * H * d, cudaMemcpyHostToDevice, s), "upload C_all")))
         return fail(rc);
-    if (G) {
+    if (large_root) {
+        // G(r, h0 + j) = C_all[r] . C_small[j] at Gcol[r * Hs + j], the GEMM's summation order
+        // (BuildPrecompLargeRoot's G0S and G_small GEMMs; the products commute).
+        rc = ck(stlq_b200::LaunchXcGemmExact(enc->C.as<float>() + static_cast<size_t>(dims.c0) * d, Hs, d, enc->C.p,
+                                             STLQ_B200_F32, H, enc->Gcol.as<float>(), Hs, nullptr, nullptr, s),
+                "G0S / G_small gemm");
+    } else if (G) {
         rc = ck(cudaMemcpyAsync(enc->Gcol.p, G, sizeof(float) * HH, cudaMemcpyHostToDevice, s), "upload G");
     } else {
         // G = C_all^T C_all in the same summation order as xC (BuildPrecomp calls the same Gemm).
@@ -431,19 +464,44 @@ int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_
                 "split C_all");
         if (rc) return fail(rc);
     }
-    if (invnorm) {
-        rc = ck(cudaMemcpyAsync(enc->invnorm.p, invnorm, sizeof(float) * H, cudaMemcpyHostToDevice, s), "upload invnorm");
+    if (large_root) {
+        // invnorm and the root norms from the reference's SIMD-order Norm2.
+        DevBuf norms;
+        if ((rc = norms.Ensure(sizeof(float) * H))) return fail(rc);
+        rc = ck(stlq_b200::LaunchNorms(enc->C.p, STLQ_B200_F32, H, d, norms.as<float>(), nullptr, s), "codeword norms");
+        if (!rc)
+            rc = ck(stlq_b200::LaunchLargeRootPrecomp(norms.as<float>(), dims.c0, H, enc->Gcol.as<float>(),
+                                                      enc->Gdiag.as<float>(), enc->invnorm.as<float>(), s),
+                    "large-root precompute");
+        if (!rc) rc = ck(cudaStreamSynchronize(s), "create sync");
+        norms.Release();
+        if (rc) return fail(rc);
     } else {
-        rc = ck(stlq_b200::LaunchInvnorm(enc->C.as<float>(), H, d, enc->invnorm.as<float>(), s), "invnorm");
+        if (invnorm) {
+            rc = ck(cudaMemcpyAsync(enc->invnorm.p, invnorm, sizeof(float) * H, cudaMemcpyHostToDevice, s),
+                    "upload invnorm");
+        } else {
+            rc = ck(stlq_b200::LaunchInvnorm(enc->C.as<float>(), H, d, enc->invnorm.as<float>(), s), "invnorm");
+        }
+        if (rc) return fail(rc);
+        if ((rc = ck(stlq_b200::LaunchTranspose(enc->Gcol.as<float>(), enc->Grow.as<float>(), H, H, s), "transpose G")) ||
+            (rc = ck(stlq_b200::LaunchDiag(enc->Gcol.as<float>(), enc->Gdiag.as<float>(), H, s), "diag G")))
+            return fail(rc);
     }
-    if (rc) return fail(rc);
-    if ((rc = ck(stlq_b200::LaunchTranspose(enc->Gcol.as<float>(), enc->Grow.as<float>(), H, H, s), "transpose G")) ||
-        (rc = ck(stlq_b200::LaunchDiag(enc->Gcol.as<float>(), enc->Gdiag.as<float>(), H, s), "diag G")) ||
-        (rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, kFlagBytes, s), "memset")) ||
+    if ((rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, kFlagBytes, s), "memset")) ||
         (rc = ck(cudaStreamSynchronize(s), "create sync")))
         return fail(rc);
     *out = enc;
     return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int stlq_b200_create(int device, int d, int m, const int* h_vec, const float* C_all, const float* G,
+                     const float* invnorm, int gemm_mode, stlq_b200_encoder** out) {
+    return CreateImpl(device, d, m, h_vec, C_all, G, invnorm, gemm_mode, false, out);
 }
 
 int stlq_b200_destroy(stlq_b200_encoder* enc) {
@@ -652,36 +710,7 @@ int stlq_b200_encode_base_u16(stlq_b200_encoder* enc, const void* X, int x_dtype
 
 int stlq_b200_create_large_root(int device, int d, int m, const int* h_vec, const float* C_all, int gemm_mode,
                                 stlq_b200_encoder** out) {
-    if (!out) return Fail(STLQ_B200_EINVAL, "out is null");
-    *out = nullptr;
-    if (m < 2) return Fail(STLQ_B200_EINVAL, "a large-root encoder needs m >= 2 (a root and at least one small codebook)");
-    for (int l = 0; l < m && h_vec; ++l)
-        if (h_vec[l] > STLQ_B200_MAX_K)
-            return Fail(STLQ_B200_EINVAL, "a large-root encoder supports codebooks of at most 256 codewords");
-    STLQ_TRY(stlq_b200_create(device, d, m, h_vec, C_all, nullptr, nullptr, gemm_mode, out));
-    stlq_b200_encoder* enc = *out;
-    DeviceScope scope(enc->device);
-    enc->dims.large_root = 1;
-    DevBuf norms;
-    int rc = norms.Ensure(sizeof(float) * enc->dims.H);
-    cudaStream_t s = enc->compute;
-    auto ck = [&](cudaError_t e, const char* what) {
-        if (e == cudaSuccess) return 0;
-        return Fail(STLQ_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
-    };
-    if (!rc) rc = ck(stlq_b200::LaunchNorms(enc->C.p, STLQ_B200_F32, enc->dims.H, d, norms.as<float>(), nullptr, s),
-                     "codeword norms");
-    if (!rc) rc = ck(stlq_b200::LaunchLargeRootPrecomp(norms.as<float>(), enc->dims.h_vec[0], enc->dims.H,
-                                                       enc->Gcol.as<float>(), enc->Grow.as<float>(),
-                                                       enc->Gdiag.as<float>(), enc->invnorm.as<float>(), s),
-                     "large-root precompute");
-    if (!rc) rc = ck(cudaStreamSynchronize(s), "create sync");
-    norms.Release();
-    if (rc) {
-        stlq_b200_destroy(enc);
-        *out = nullptr;
-    }
-    return rc;
+    return CreateImpl(device, d, m, h_vec, C_all, nullptr, nullptr, gemm_mode, true, out);
 }
 
 int stlq_b200_encode_base_large_root(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, int beam,
@@ -692,13 +721,16 @@ int stlq_b200_encode_base_large_root(stlq_b200_encoder* enc, const void* X, int 
     if (!enc->dims.large_root) return Fail(STLQ_B200_EINVAL, "encoder was not created by stlq_b200_create_large_root");
     if (n > 0 && (!cluster_out || !B_small_out)) return Fail(STLQ_B200_EINVAL, "cluster_out and B_small_out must be non-null");
     const int m = enc->dims.m;
-    std::vector<uint8_t> B(static_cast<size_t>(std::max<int64_t>(n, 0)) * m);
-    STLQ_TRY(stlq_b200_encode_base(enc, X, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
-                                   sample_id_offset, B.data(), a_out, cost_out, cost_sums_out));
+    const bool wide = enc->dims.wide != 0;  // root codes above 255 are held as uint16
+    std::vector<uint8_t> B(static_cast<size_t>(std::max<int64_t>(n, 0)) * m * CodeBytes(enc));
+    STLQ_TRY(EncodeHost(enc, X, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed, sample_id_offset,
+                        B.data(), a_out, cost_out, cost_sums_out));
+    const uint16_t* B16 = reinterpret_cast<const uint16_t*>(B.data());
     for (int64_t v = 0; v < n; ++v) {
-        const uint8_t* b = B.data() + v * m;
-        cluster_out[v] = b[0];
-        std::memcpy(B_small_out + v * (m - 1), b + 1, m - 1);
+        const size_t o = static_cast<size_t>(v) * m;
+        cluster_out[v] = wide ? B16[o] : B[o];
+        for (int l = 1; l < m; ++l)
+            B_small_out[v * (m - 1) + l - 1] = static_cast<uint8_t>(wide ? B16[o + l] : B[o + l]);
     }
     return 0;
 }
@@ -715,11 +747,11 @@ int stlq_b200_encode_base_large_root_device(stlq_b200_encoder* enc, const void* 
     DeviceScope scope(enc->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (n <= 0) return 0;
-    STLQ_TRY(enc->Bfull.Ensure(static_cast<size_t>(n) * enc->dims.m));
+    STLQ_TRY(enc->Bfull.Ensure(static_cast<size_t>(n) * enc->dims.m * CodeBytes(enc)));
     if (cost_sums_dev) STLQ_CK(cudaMemsetAsync(cost_sums_dev, 0, 2 * sizeof(double), s));
     STLQ_TRY(EncodeDevice(enc, X_dev, x_dtype, n, beam, icm_iters, ils_iters, perturb_k, use_abs, seed,
-                          sample_id_offset, enc->Bfull.as<uint8_t>(), a_dev, cost_dev, cost_sums_dev, s));
-    STLQ_CK(stlq_b200::LaunchSplitRootCodes(enc->dims.m, enc->Bfull.as<uint8_t>(), n, cluster_dev, B_small_dev, s));
+                          sample_id_offset, enc->Bfull.p, a_dev, cost_dev, cost_sums_dev, s));
+    STLQ_CK(stlq_b200::LaunchSplitRootCodes(enc->dims.m, enc->Bfull.p, enc->dims.wide, n, cluster_dev, B_small_dev, s));
     return 0;
 }
 
@@ -804,7 +836,7 @@ int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const
     if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
     STLQ_TRY(enc->redo.Ensure(static_cast<size_t>(n + 1) * sizeof(int)));
-    STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, enc->Grow.as<float>(), enc->Gdiag.as<float>(), xnorm2_dev, xC_dev, n,
+    STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, BeamGram(enc), enc->Gdiag.as<float>(), xnorm2_dev, xC_dev, n,
                                         beam, B_dev, enc->redo.as<int>(), enc->check_filter, enc->err_flag.as<unsigned int>(), enc->num_sms,
                                         static_cast<cudaStream_t>(stream)));
     return 0;
@@ -819,6 +851,7 @@ int stlq_b200_solve_ls(stlq_b200_encoder* enc, const float* xC_dev, const uint8_
     stlq_b200::RefineArgs ra{};
     ra.dims = enc->dims;
     ra.Gcol = enc->Gcol.as<float>();
+    ra.Gdiag = enc->Gdiag.as<float>();
     ra.invnorm = enc->invnorm.as<float>();
     ra.xC = xC_dev;
     ra.n = n;
@@ -842,6 +875,7 @@ int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnor
     stlq_b200::RefineArgs ra{};
     ra.dims = enc->dims;
     ra.Gcol = enc->Gcol.as<float>();
+    ra.Gdiag = enc->Gdiag.as<float>();
     ra.invnorm = enc->invnorm.as<float>();
     ra.xC = xC_dev;
     ra.xnorm2 = xnorm2_dev;
@@ -878,7 +912,7 @@ int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const 
         STLQ_CK(stlq_b200::LaunchNorms(static_cast<const char*>(X_dev) + static_cast<size_t>(s0) * enc->dims.d * esz,
                                        x_dtype, ns, enc->dims.d, nullptr, enc->xnd.as<double>(), s));
         const int g = static_cast<int>(std::min<int64_t>((ns + 255) / 256, grid));
-        STLQ_CK(stlq_b200::LaunchSse(enc->dims, enc->Gcol.as<float>(), xC_dev + s0 * enc->dims.H, enc->xnd.as<double>(),
+        STLQ_CK(stlq_b200::LaunchSse(enc->dims, enc->Gcol.as<float>(), enc->Gdiag.as<float>(), xC_dev + s0 * enc->dims.H, enc->xnd.as<double>(),
                                      B_dev + s0 * enc->dims.m, a_dev + s0 * enc->dims.m, ns, enc->partials.as<double>(),
                                      g, s));
         STLQ_CK(stlq_b200::LaunchReducePartials(enc->partials.as<double>(), g, sse_dev, s));

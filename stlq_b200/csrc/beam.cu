@@ -67,7 +67,7 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
                             const float* keep = nullptr, const float* ex = nullptr) {
     constexpr int NL = MAXM - 1;
     const int tid = threadIdx.x;
-    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    const int K = dims.h_vec[L], offL = dims.off[L], ldg = dims.ldg, colL = offL - dims.c0;
     // R prefix of each winner's parent: rows r <= c < L, one (winner, column) pair per thread.
     for (int e = tid; e < newH * L; e += kThreads) {
         const int o = e / L, c = e - o * L;
@@ -93,7 +93,7 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
             a_last = st[2 * MAXM + 1];
             e = ex[p];
         } else {
-            e = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, ak,
+            e = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, ldg, colL + k, ak,
                                  __ldg(xc + offL + k), y, v, &denom, &a_last, dims.large_root != 0);
         }
 #pragma unroll
@@ -105,7 +105,7 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
             nxt.rinvh(o)[t] = cur.rinvh(h)[t];
         }
         const float rll = __fsqrt_rn(denom);
-        nxt.rowh(o)[L] = (offL + k) * H;
+        nxt.rowh(o)[L] = (offL + k) * ldg;
         nxt.ah(o)[L] = a_last;
         nxt.Rh(o)[L * MAXM + L] = rll;
         nxt.rinvh(o)[L] = __frcp_rn(rll);
@@ -115,7 +115,7 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
 }
 
 // No finite candidate in a layer (beam_search.cpp:385-400): the previous slots are kept.  The code
-// of this layer is written as 0 (Grow row row0 = offL * H); the reference copies a stale buffer
+// of this layer is written as 0 (Grow row row0 = offL * ldg); the reference copies a stale buffer
 // value there.
 template <int MAXM>
 __device__ int KeepPrevious(int L, int row0, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
@@ -138,13 +138,13 @@ __device__ int KeepPrevious(int L, int row0, const SlotView<MAXM>& cur, const Sl
 
 // Layer 0 state of slot o holding codeword k (beam_search.cpp:248-258).
 template <int MAXM>
-__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, int H, const float* Gdiag, const float* xc,
+__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, int ldg, const float* Gdiag, const float* xc,
                           float nx2) {
     const float alpha = __ldg(Gdiag + k);
     const float gamma = __ldg(xc + k);
     const float a1 = div_rn(gamma, alpha);
     const float r00 = __fsqrt_rn(alpha);
-    s.rowh(o)[0] = k * H;  // layer 0 starts at flat index 0
+    s.rowh(o)[0] = k * ldg;  // layer 0 starts at flat index 0
     s.ah(o)[0] = a1;
     s.E[o] = sub_rn(nx2, mul_rn(gamma, a1));
     s.Rh(o)[0] = r00;
@@ -159,7 +159,7 @@ template <int MAXM>
 __device__ void DeadSlot0(const Dims& dims, const SlotView<MAXM>& s) {
     const int tid = threadIdx.x;
     if (tid < MAXM) {
-        s.rowh(0)[tid] = tid < dims.m ? dims.off[tid] * dims.H : 0;
+        s.rowh(0)[tid] = tid < dims.m ? dims.off[tid] * dims.ldg : 0;
         s.ah(0)[tid] = 0.0f;
         s.rinvh(0)[tid] = 0.0f;
     }
@@ -179,6 +179,24 @@ __device__ __forceinline__ float Layer0Error(const float* Gdiag, const float* xc
     return (alpha != 0.0f && e1 < PosInf()) ? e1 : PosInf();
 }
 
+// Where the selection reads a candidate's error (or lower bound): a shared-memory array
+// (16-byte aligned, read four at a time), or, for a layer-0 codebook too large to keep one float
+// per codeword, recomputed from xC.
+struct ArraySource {
+    const float* v;
+    static constexpr bool kVec = true;
+    __device__ float operator()(int idx) const { return v[idx]; }
+    __device__ const float* v0() const { return v; }
+};
+struct Layer0Source {
+    const float* Gdiag;
+    const float* xc;
+    float nx2;
+    static constexpr bool kVec = false;
+    __device__ float operator()(int k) const { return Layer0Error(Gdiag, xc, nx2, k); }
+    __device__ const float* v0() const { return nullptr; }  // no array: never read four at a time
+};
+
 // ---------------------------------------------------------------------------------------------
 // Cheap pass shared by both kernels.
 
@@ -186,14 +204,14 @@ __device__ __forceinline__ float Layer0Error(const float* Gdiag, const float* xc
 // lie inside them; a miss raises kErrFilterMiss.  Inlined: a call site inside the hot loop, even
 // one never taken, costs the loop registers.
 template <int MAXM>
-__device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int H,
+__device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int ldg,
                                          const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
                                          const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
                                          unsigned int* err_flag, bool recip) {
     const RowArr<MAXM> flat = RowsOf<MAXM>(cur, h, L);
     for (int c = 0; c < kCpt; ++c) {
         if (!ok[c]) continue;
-        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, H, col[c], alpha[c], gamma[c], nullptr, nullptr,
+        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, ldg, col[c], alpha[c], gamma[c], nullptr, nullptr,
                                          nullptr, nullptr, recip);
         if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
     }
@@ -204,7 +222,7 @@ __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int
 // compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
 // call boundary costs more than the copies save).
 template <int MAXM, int L, bool kHi>
-__device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int H,
+__device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int colL,
                                            const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                                            const float* __restrict__ xc, float* lo, float* hi_out, int check,
                                            unsigned int* err_flag, bool recip) {
@@ -219,7 +237,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
         for (int c = 0; c < kCpt; ++c) {
             const int k = kc + tid + c * kThreads;
             ok[c] = k < K;
-            col[c] = offL + k;
+            col[c] = colL + k;  // Gram column; Gdiag and xc are indexed by the flat index
             alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
             gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
         }
@@ -237,20 +255,20 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
                     hmin = fminf(hmin, hi[c]);
                 }
             }
-            if (check) CheckBounds<MAXM>(cur, h, L, Grow, H, col, ok, alpha, gamma, l, hi, err_flag, recip);
+            if (check) CheckBounds<MAXM>(cur, h, L, Grow, 0, col, ok, alpha, gamma, l, hi, err_flag, recip);
         }
     }
     return OrderKey(hmin);
 }
 
 template <int MAXM, bool kHi>
-__device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int H,
+__device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
                                   int check, unsigned int* err, bool recip) {
 #define STLQ_B200_CHEAP(LL)                                                                          \
     case LL:                                                                                         \
         if constexpr (LL < MAXM)                                                                     \
-            return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, H, Grow, Gdiag, xc, lo, hi_out, check, err, recip); \
+            return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err, recip); \
         break;
     switch (L) {
         STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
@@ -283,11 +301,13 @@ struct Replay {
         widx = __ffs(__ballot_sync(kFull, key == wkey)) - 1;
         worst = KeyToFloat(wkey);
     }
-    // Scans errs[0..n) in order: one ballot per 32 candidates, entering ones replayed in order.
-    __device__ void Scan(const float* errs, int n) {
+    // Scans errors 0..n of `src` in order: one ballot per 32 candidates, entering ones replayed in
+    // order.
+    template <class Src>
+    __device__ void Scan(Src src, int n) {
         const int lane = threadIdx.x & 31;
         for (int base = 0; base < n; base += 32) {
-            const float e = base + lane < n ? errs[base + lane] : PosInf();
+            const float e = base + lane < n ? src(base + lane) : PosInf();
             unsigned mask = __ballot_sync(kFull, e < worst);
             while (mask) {
                 const int l = __ffs(mask) - 1;
@@ -353,11 +373,11 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                             const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt) {
     const int tid = threadIdx.x;
-    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
     const int n_cand = curH * K;
     int* list = reinterpret_cast<int*>(his);
     if (his) {
-        CheapDispatch<MAXM, true>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, errs, his, 0, nullptr,
+        CheapDispatch<MAXM, true>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
                                   dims.large_root != 0);
         __syncthreads();
         if (tid < 32) {
@@ -372,20 +392,20 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     for (int p = tid; p < need; p += kThreads) {
         const int idx = his ? list[p] : p;
         const int h = idx / K, k = idx - h * K;
-        errs[idx] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+        errs[idx] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, dims.ldg, colL + k, __ldg(Gdiag + offL + k),
                                      __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr, dims.large_root != 0);
     }
     __syncthreads();
     if (tid < 32) {
         Replay rp;
         rp.Init(beam);
-        rp.Scan(errs, n_cand);
+        rp.Scan(ArraySource{errs}, n_cand);
         rp.Publish(beam, lt);
     }
     __syncthreads();
     const int newH = lt.n_slots;
     if (newH == 0) {
-        curH = KeepPrevious<MAXM>(L, offL * H, cur, nxt, curH, beam);
+        curH = KeepPrevious<MAXM>(L, offL * dims.ldg, cur, nxt, curH, beam);
     } else {
         Materialize<MAXM>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc);
         curH = newH;
@@ -406,7 +426,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
     size_t off = (2 * sv + 15) & ~size_t(15);
     LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
     float* errs = reinterpret_cast<float*>(smem + ((off + sizeof(LayerTable) + 15) & ~size_t(15)));
-    float* his = prescan ? errs + beam * dims.maxK : nullptr;
+    float* his = prescan ? errs + beam * dims.maxKs : nullptr;
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     const int64_t total = vec_list ? static_cast<int64_t>(*count) : n;
@@ -414,18 +434,22 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         const int64_t vec = vec_list ? vec_list[i] : i;
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
-        for (int k = tid; k < K0; k += kThreads) errs[k] = Layer0Error(Gdiag, xc, nx2, k);
+        // Layer 0 keeps its errors in errs[] when they fit (beam x maxKs floats), else recomputes them.
+        const bool stored0 = K0 <= beam * dims.maxKs;
+        if (stored0)
+            for (int k = tid; k < K0; k += kThreads) errs[k] = Layer0Error(Gdiag, xc, nx2, k);
         __syncthreads();
         if (tid < 32) {
             Replay rp;
             rp.Init(beam);
-            rp.Scan(errs, K0);
+            if (stored0) rp.Scan(ArraySource{errs}, K0);
+            else rp.Scan(Layer0Source{Gdiag, xc, nx2}, K0);
             rp.Publish(beam, lt);
         }
         __syncthreads();
         int curH = lt.n_slots;
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.H, Gdiag, xc, nx2);
+        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.ldg, Gdiag, xc, nx2);
         if (curH == 0) {
             DeadSlot0<MAXM>(dims, s0);
             curH = 1;
@@ -443,7 +467,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
             const uint32_t key = tid < curH ? OrderKey(cur.E[tid]) : 0xffffffffu;
             const uint32_t kmin = __reduce_min_sync(kFull, key);
             const int best = __ffs(__ballot_sync(kFull, key == kmin)) - 1;
-            if (tid < m) StoreCode(Bout, vec * m + tid, cur.rowh(best)[tid] / dims.H - dims.off[tid], dims.wide);
+            if (tid < m) StoreCode(Bout, vec * m + tid, cur.rowh(best)[tid] / dims.ldg - dims.off[tid], dims.wide);
         }
         __syncthreads();
     }
@@ -468,13 +492,14 @@ __device__ __forceinline__ uint32_t WarpSortAsc(uint32_t v) {
 }
 
 // Selection shared by every layer of the fast kernel, out of line so that one copy serves every
-// layer.  Inputs: lo[idx] (a lower bound of each candidate's exact error; the exact error itself
-// in layer 0; 16-byte aligned) and this thread's smallest upper bound `hmin`.  The 128 per-thread
+// layer.  Inputs: src(idx) (a lower bound of each candidate's exact error; the exact error itself
+// in layer 0) and this thread's smallest upper bound `hmin`.  The 128 per-thread
 // minima belong to distinct candidates, so their B-th smallest, tau, bounds the B-th smallest
 // exact error from above; every candidate with lo <= tau is a survivor (all others are provably
 // larger than the B-th smallest exact error).  Returns the survivor count, or -1 when the list
 // overflows.
-__device__ __noinline__ int SelectSurvivors(const float* lo, int n_cand, uint32_t hmin, int beam, LayerTable& lt,
+template <class Src>
+__device__ __noinline__ int SelectSurvivors(Src src, int n_cand, uint32_t hmin, int beam, LayerTable& lt,
                                             uint16_t* surv) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Each warp sorts its 32 minima; only a warp's B smallest can be among the B smallest of all
@@ -513,14 +538,14 @@ __device__ __noinline__ int SelectSurvivors(const float* lo, int n_cand, uint32_
     const float tau = tb >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tb);  // < B finite bounds: keep all
     // Count this thread's survivors (four candidates per 128-bit load), scan the counts across the
     // block, then write the survivors at their offsets.
-    const float4* lo4 = reinterpret_cast<const float4*>(lo);
-    const int n4 = n_cand >> 2;
+    const float4* lo4 = reinterpret_cast<const float4*>(src.v0());
+    const int n4 = Src::kVec ? n_cand >> 2 : 0;
     int cnt = 0;
     for (int c = tid; c < n4; c += kThreads) {
         const float4 v = lo4[c];
         cnt += (v.x <= tau) + (v.y <= tau) + (v.z <= tau) + (v.w <= tau);
     }
-    for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads) cnt += lo[idx] <= tau;
+    for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads) cnt += src(idx) <= tau;
     int incl = cnt;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -546,7 +571,7 @@ __device__ __noinline__ int SelectSurvivors(const float* lo, int n_cand, uint32_
             if (v.w <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 3);
         }
         for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads)
-            if (lo[idx] <= tau) surv[p++] = static_cast<uint16_t>(idx);
+            if (src(idx) <= tau) surv[p++] = static_cast<uint16_t>(idx);
     }
     __syncthreads();
     if (tid == 0) lt.n_surv = S;
@@ -600,18 +625,18 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
                          int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, uint64_t* keys, float* keep,
                          int check, unsigned int* err_flag) {
     const int tid = threadIdx.x;
-    const int K = dims.h_vec[L], offL = dims.off[L], H = dims.H;
+    const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
     const uint32_t hmin =
-        CheapDispatch<MAXM, false>(L, cur, curH, K, offL, H, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
+        CheapDispatch<MAXM, false>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
                                    dims.large_root != 0);
-    const int S = SelectSurvivors(lo, curH * K, hmin, beam, lt, surv);
+    const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     for (int p = tid; p < S; p += kThreads) {
         const int idx = surv[p];
         const int h = idx / K, k = idx - h * K;
         float* st = keep + p * KeepStride<MAXM>();
         const bool kp = p < kKeep;
-        ex[p] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, H, offL + k, __ldg(Gdiag + offL + k),
+        ex[p] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, dims.ldg, colL + k, __ldg(Gdiag + offL + k),
                                  __ldg(xc + offL + k), kp ? st : nullptr, kp ? st + MAXM : nullptr,
                                  kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr, dims.large_root != 0);
     }
@@ -619,7 +644,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
     const int newH = RankSurvivors(ex, surv, S, beam, lt, keys);
     if (newH < 0) return -1;
     if (newH == 0) {
-        const int kept = KeepPrevious<MAXM>(L, offL * H, cur, nxt, curH, beam);
+        const int kept = KeepPrevious<MAXM>(L, offL * dims.ldg, cur, nxt, curH, beam);
         __syncthreads();
         return kept;
     }
@@ -643,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     off = (off + sizeof(LayerTable) + 15) & ~size_t(15);
     uint64_t* keys = reinterpret_cast<uint64_t*>(smem + off);
     float* lo = reinterpret_cast<float*>(keys + kSurvCap);
-    float* ex = lo + beam * dims.maxK;
+    float* ex = lo + beam * dims.maxKs;
     float* keep = ex + kSurvCap;
     uint16_t* surv = reinterpret_cast<uint16_t*>(keep + kKeep * KeepStride<MAXM>());
     const int tid = threadIdx.x;
@@ -652,21 +677,25 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     for (int64_t vec = blockIdx.x; vec < n; vec += gridDim.x) {
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
-        // Layer 0: exact errors are cheap; they serve as their own bounds.
+        // Layer 0: exact errors are cheap; they serve as their own bounds.  They are kept in lo[]
+        // when they fit (beam x maxKs floats), else recomputed where the selection reads them.
+        const bool stored0 = K0 <= beam * dims.maxKs;
         uint32_t hmin = 0xffffffffu;
         for (int k = tid; k < K0; k += kThreads) {
             const float e1 = Layer0Error(Gdiag, xc, nx2, k);
-            lo[k] = e1;
+            if (stored0) lo[k] = e1;
             hmin = min(hmin, OrderKey(e1));
         }
-        int curH = SelectSurvivors(lo, K0, hmin, beam, lt, surv);
+        int curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
+                           : SelectSurvivors(Layer0Source{Gdiag, xc, nx2}, K0, hmin, beam, lt, surv);
         if (curH >= 0) {
-            for (int p = tid; p < curH; p += kThreads) ex[p] = lo[surv[p]];
+            for (int p = tid; p < curH; p += kThreads)
+                ex[p] = stored0 ? lo[surv[p]] : Layer0Error(Gdiag, xc, nx2, surv[p]);
             __syncthreads();
             curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
         }
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.H, Gdiag, xc, nx2);
+        if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.ldg, Gdiag, xc, nx2);
         if (curH == 0) {
             DeadSlot0<MAXM>(dims, s0);
             curH = 1;
@@ -689,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         if (redo) {
             if (tid == 0) redo_list[atomicAdd(redo_count, 1)] = static_cast<int>(vec);
         } else if (tid < m) {
-            StoreCode(Bout, vec * m + tid, cur.rowh(0)[tid] / dims.H - dims.off[tid], dims.wide);
+            StoreCode(Bout, vec * m + tid, cur.rowh(0)[tid] / dims.ldg - dims.off[tid], dims.wide);
         }
         __syncthreads();
     }
@@ -771,7 +800,7 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
                         int64_t n, int beam, void* Bout, int* redo, int check, unsigned int* err_flag,
                         unsigned long long* stats, int num_sms, cudaStream_t stream) {
     int grid = 0;
-    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs);
     cudaError_t e = Prepare(BeamFastKernel<MAXM>, fsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
@@ -780,8 +809,8 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
                                                           check, err_flag, stats);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxK);
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK, prescan);
+    const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
     e = Prepare(BeamReplayKernel<MAXM>, rsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     BeamReplayKernel<MAXM><<<grid, kThreads, rsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
@@ -791,8 +820,8 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
 
 template <int MAXM>
 cudaError_t PrepareT(const Dims& dims, int beam) {
-    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxK);
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxK, ReplayPrescan<MAXM>(beam, dims.maxK));
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, ReplayPrescan<MAXM>(beam, dims.maxKs));
     cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(fsm));
     if (e != cudaSuccess) return e;
@@ -803,7 +832,7 @@ cudaError_t PrepareT(const Dims& dims, int beam) {
 }  // namespace
 
 size_t BeamFastSmemBytes(const Dims& dims, int beam) {
-    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxK) : FastSmemBytes<16>(beam, dims.maxK);
+    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxKs) : FastSmemBytes<16>(beam, dims.maxKs);
 }
 
 cudaError_t PrepareBeamKernels(const Dims& dims, int beam) {

@@ -30,7 +30,8 @@ cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* G
 
 struct RefineArgs {
     Dims dims;
-    const float* Gcol;
+    const float* Gcol;   // Gram array of the refinement (layout: Dims::ldg, Dims::c0)
+    const float* Gdiag;  // G(h, h) for every flat index h
     const float* invnorm;
     const float* xC;
     const float* xnorm2;
@@ -52,8 +53,8 @@ struct RefineArgs {
 
 cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream);
 cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* out, cudaStream_t stream);
-cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const void* B,
-                      const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
+cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, const float* xC, const double* xnorm2_d,
+                      const void* B, const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
 int RefineWarpsPerBlock();
 
 // Loads both beam kernels and sets their shared-memory attributes (no launch).
@@ -74,13 +75,15 @@ cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cud
 cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream);
 cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream);
 cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStream_t stream);
-cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gcol, float* Grow, float* Gdiag,
-                                   float* invnorm, cudaStream_t stream);
+// Large-root precompute: invnorm from the SIMD-order norms; Gdiag = norm0 for the h0 root codewords
+// and the compact Gram's diagonal (G[h * Hs + h - h0]) for the others.
+cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, const float* G, float* Gdiag, float* invnorm,
+                                   cudaStream_t stream);
 // Large-root mode: xC[vec][root] = the reference's SIMD-order dot of the chosen root codeword with
 // x (Dot, least_squares.cpp:35-42), which its LS, cost and ICM use for the root term.
 cudaError_t LaunchRootDot(const Dims& dims, const float* C, const void* X, int x_dtype, const void* B, int64_t n,
                           float* xC, cudaStream_t stream);
-cudaError_t LaunchSplitRootCodes(int m, const uint8_t* B, int64_t n, uint32_t* cluster, uint8_t* B_small,
+cudaError_t LaunchSplitRootCodes(int m, const void* B, int wide, int64_t n, uint32_t* cluster, uint8_t* B_small,
                                  cudaStream_t stream);
 
 }  // namespace stlq_b200

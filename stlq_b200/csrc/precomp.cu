@@ -43,19 +43,16 @@ __global__ void InvnormKernel(const float* __restrict__ C, int H, int d, float* 
 }
 
 // Large-root precompute from the codewords' norms in the reference's SIMD order (Norm2,
-// precomp_large_root.cpp:15-23): invnorm = 1/sqrt(norm) (0 for a zero codeword), and for the h0 root
-// codewords the Gram diagonal is norm0 (BuildPrecompLargeRoot :85-91) instead of the GEMM value.
-__global__ void LargeRootPrecompKernel(const float* __restrict__ norms, int h0, int H, float* Gcol, float* Grow,
+// precomp_large_root.cpp:15-23): invnorm = 1/sqrt(norm) (0 for a zero codeword); the diagonal is
+// norm0 for the h0 root codewords (BuildPrecompLargeRoot :85-91) and G_small's for the others (the
+// compact Gram G[h * (H - h0) + (h - h0)]).
+__global__ void LargeRootPrecompKernel(const float* __restrict__ norms, int h0, int H, const float* __restrict__ G,
                                        float* Gdiag, float* invnorm) {
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
     if (h >= H) return;
     const float n2 = norms[h];
     invnorm[h] = n2 > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(n2)) : 0.0f;
-    if (h < h0) {
-        Gdiag[h] = n2;
-        Gcol[static_cast<size_t>(h) * H + h] = n2;
-        Grow[static_cast<size_t>(h) * H + h] = n2;
-    }
+    Gdiag[h] = h < h0 ? n2 : G[static_cast<size_t>(h) * (H - h0) + (h - h0)];
 }
 
 __global__ void U8ToF32Kernel(const uint8_t* __restrict__ x, int64_t count, float* __restrict__ out) {
@@ -73,9 +70,9 @@ cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStrea
     return cudaGetLastError();
 }
 
-cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, float* Gcol, float* Grow, float* Gdiag,
-                                   float* invnorm, cudaStream_t stream) {
-    LargeRootPrecompKernel<<<(H + 255) / 256, 256, 0, stream>>>(norms, h0, H, Gcol, Grow, Gdiag, invnorm);
+cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, const float* G, float* Gdiag, float* invnorm,
+                                   cudaStream_t stream) {
+    LargeRootPrecompKernel<<<(H + 255) / 256, 256, 0, stream>>>(norms, h0, H, G, Gdiag, invnorm);
     return cudaGetLastError();
 }
 

@@ -44,17 +44,31 @@ struct WarpState {
     float Gbak[2 * kMaxM];    // row and column of a trial code change, for the rollback
 };
 
-__device__ __forceinline__ float GAt(const float* Gcol, int H, int row, int col) {
-    return Gcol[static_cast<size_t>(col) * H + row];
+// G(row, col) of two flat indices from the refinement's Gram array: G(r, c), r >= c0, at
+// g[c * ldg + (r - c0)] (the layout is described with Dims).  Regular encoders have c0 = 0; in a
+// large-root encoder a root row is read through symmetry, and two root codewords are only ever
+// the root's own diagonal.
+struct GramRef {
+    const float* g;
+    const float* diag;
+    int ldg, c0;
+    __device__ float operator()(int row, int col) const {
+        if (row >= c0) return g[static_cast<size_t>(col) * ldg + (row - c0)];
+        if (col >= c0) return g[static_cast<size_t>(row) * ldg + (col - c0)];
+        return diag[row];
+    }
+};
+
+__device__ __forceinline__ GramRef MakeGram(const Dims& dims, const float* g, const float* diag) {
+    return GramRef{g, diag, dims.ldg, dims.c0};
 }
 
 // Gram entry G(flat_r, flat_c) of layers r and c, from the global matrix or the warp's cache.
 struct GramGlobal {
-    const float* Gcol;
-    int H;
+    GramRef g;
     const int* off;
     const int* code;
-    __device__ float operator()(int r, int c) const { return GAt(Gcol, H, off[r] + code[r], off[c] + code[c]); }
+    __device__ float operator()(int r, int c) const { return g(off[r] + code[r], off[c] + code[c]); }
 };
 struct GramShared {
     const float* Gs;
@@ -63,25 +77,25 @@ struct GramShared {
 };
 
 // All lanes: ws.Gs for `code`.
-__device__ void LoadGram(const Dims& dims, const float* Gcol, const int* code, float* Gs) {
+__device__ void LoadGram(const Dims& dims, const GramRef& Gr, const int* code, float* Gs) {
     const int lane = threadIdx.x & 31, m = dims.m;
     __syncwarp();
     for (int e = lane; e < m * m; e += 32) {
         const int r = e / m, c = e - r * m;
-        Gs[e] = GAt(Gcol, dims.H, dims.off[r] + code[r], dims.off[c] + code[c]);
+        Gs[e] = Gr(dims.off[r] + code[r], dims.off[c] + code[c]);
     }
     __syncwarp();
 }
 
 // All lanes: row and column j of Gs for code[j]'s new value, the old ones saved in bak.
-__device__ void UpdateGram(const Dims& dims, const float* Gcol, const int* code, int j, float* Gs, float* bak) {
+__device__ void UpdateGram(const Dims& dims, const GramRef& Gr, const int* code, int j, float* Gs, float* bak) {
     const int lane = threadIdx.x & 31, m = dims.m;
     __syncwarp();
     if (lane < m) {
         const int fj = dims.off[j] + code[j], fk = dims.off[lane] + code[lane];
         bak[lane] = Gs[j * m + lane];
         bak[m + lane] = Gs[lane * m + j];
-        const float row = GAt(Gcol, dims.H, fj, fk), col = GAt(Gcol, dims.H, fk, fj);
+        const float row = Gr(fj, fk), col = Gr(fk, fj);
         __syncwarp(0xffffffffu >> (32 - m));
         Gs[j * m + lane] = row;
         Gs[lane * m + j] = col;
@@ -359,14 +373,14 @@ __device__ __forceinline__ uint32_t UniformBelow(SplitMix64& r, uint32_t bound) 
 // One RunIcm call (icm.cpp:89-344) on `code` (in/out) for the warp's vector; a and cost out.
 // With do_init false the caller has already solved LS and the cost for `code` (RunIcm's first
 // step, icm.cpp:109-114), so only the sweeps run.
-__device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* invnorm, const float* xc, float xn2,
+__device__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc, float xn2,
                            int icm_iters, const int* orders, bool use_abs, int* code, float* a, float* cost,
                            WarpState& ws, bool do_init = true) {
     const int lane = threadIdx.x & 31;
-    const int m = dims.m, H = dims.H;
+    const int m = dims.m;
     const GramShared G{ws.Gs, m};
     if (do_init) {
-        LoadGram(dims, Gcol, code, ws.Gs);
+        LoadGram(dims, Gr, code, ws.Gs);
         if (lane == 0) {
             if (!SolveLs(dims, G, xc, code, ws, a))
                 for (int l = 0; l < m; ++l) a[l] = 0.0f;
@@ -391,7 +405,8 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
                 for (int l = 0; l < m; ++l) {
                     if (l == j) continue;
                     const int fl = dims.off[l] + code[l];
-                    v = sub_rn(v, mul_rn(a[l], __ldg(Gcol + static_cast<size_t>(fl) * H + startf + t)));
+                    // G(startf + t, fl): codebook j >= 1, so the row is always stored (>= c0).
+                    v = sub_rn(v, mul_rn(a[l], __ldg(Gr.g + static_cast<size_t>(fl) * Gr.ldg + (startf - Gr.c0) + t)));
                 }
                 const float val = mul_rn(v, __ldg(invnorm + startf + t));
                 const float s = use_abs ? fabsf(val) : val;
@@ -413,7 +428,7 @@ __device__ void RunIcmWarp(const Dims& dims, const float* Gcol, const float* inv
             if (best == old_code) continue;
             __syncwarp();
             if (lane == 0) code[j] = best;
-            UpdateGram(dims, Gcol, code, j, ws.Gs, ws.Gbak);
+            UpdateGram(dims, Gr, code, j, ws.Gs, ws.Gbak);
             bool keep = false;
             if (lane == 0) {
                 for (int l = 0; l < m; ++l) ws.backup[l] = a[l];
@@ -451,6 +466,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
     WarpState& ws = wss[warp];
     const Dims& dims = p.dims;
     const int m = dims.m;
+    const GramRef Gr = MakeGram(dims, p.Gcol, p.Gdiag);
     double sse_beam = 0.0, sse_final = 0.0;
     for (int64_t vec = static_cast<int64_t>(blockIdx.x) * kWarps + warp; vec < p.n;
          vec += static_cast<int64_t>(gridDim.x) * kWarps) {
@@ -458,7 +474,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
         if (lane < m) ws.code[lane] = LoadCode(p.B, vec * m + lane, dims.wide);
         __syncwarp();
         if (p.mode == 0) {
-            LoadGram(dims, p.Gcol, ws.code, ws.Gs);
+            LoadGram(dims, Gr, ws.code, ws.Gs);
             if (lane == 0) {
                 if (!SolveLs(dims, GramShared{ws.Gs, m}, xc, ws.code, ws, ws.a))
                     for (int l = 0; l < m; ++l) ws.a[l] = 0.0f;
@@ -472,7 +488,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
         float cost = 0.0f;
         // RunIcm's first step recomputes LS and cost for the beam codes (icm.cpp:109-114); with
         // the MSE requested, the LS result is also the beam-stage coefficients.
-        RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, 0, p.orders, p.use_abs, ws.code, ws.a, &cost, ws);
+        RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, 0, p.orders, p.use_abs, ws.code, ws.a, &cost, ws);
         // Beam-stage error: MeanMseFromPrecomp's term, or for a large-root encoder the float cost
         // itself (the large pipeline averages ComputeCostsLargeRoot, encode_base_streaming.cpp:301-311).
         if (p.partials && lane == 0)
@@ -480,7 +496,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
                                         : VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
         __syncwarp();
         if (p.icm_iters > 0)
-            RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
+            RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
                        /*do_init=*/false);
         cost = __shfl_sync(0xffffffffu, cost, 0);
         const int ksel = min(p.perturb_k, m);
@@ -502,7 +518,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
             }
             __syncwarp();
             float ccost = 0.0f;
-            RunIcmWarp(dims, p.Gcol, p.invnorm, xc, xn2, p.icm_iters,
+            RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters,
                        p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, ws.cand, ws.acand,
                        &ccost, ws);
             ccost = __shfl_sync(0xffffffffu, ccost, 0);
@@ -518,7 +534,7 @@ __global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
         if (p.partials && dims.large_root) {
             if (lane == 0) sse_final += static_cast<double>(cost);
         } else if (p.partials) {
-            if (p.n_ils > 0) LoadGram(dims, p.Gcol, ws.code, ws.Gs);  // the cache holds the last ILS candidate
+            if (p.n_ils > 0) LoadGram(dims, Gr, ws.code, ws.Gs);  // the cache holds the last ILS candidate
             if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
         }
         if (lane < m) {
@@ -589,15 +605,15 @@ __global__ void ReducePartialsKernel(const double* partials, int nblocks, double
 }
 
 // Per-vector MSE term alone (stlq_b200_sse): one thread per vector.
-__global__ void SseKernel(Dims dims, const float* Gcol, const float* xC, const double* xnorm2_d, const void* B,
-                          const float* a, int64_t n, double* partials) {
+__global__ void SseKernel(Dims dims, const float* Gcol, const float* Gdiag, const float* xC, const double* xnorm2_d,
+                          const void* B, const float* a, int64_t n, double* partials) {
     __shared__ double red[256];
     double s = 0.0;
     for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n;
          v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         int code[kMaxM];
         for (int l = 0; l < dims.m; ++l) code[l] = LoadCode(B, v * dims.m + l, dims.wide);
-        s += VectorSse(dims, GramGlobal{Gcol, dims.H, dims.off, code}, xC + v * dims.H, code, a + v * dims.m,
+        s += VectorSse(dims, GramGlobal{MakeGram(dims, Gcol, Gdiag), dims.off, code}, xC + v * dims.H, code, a + v * dims.m,
                        xnorm2_d[v]);
     }
     red[threadIdx.x] = s;
@@ -621,10 +637,10 @@ cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* ou
     return cudaGetLastError();
 }
 
-cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* xC, const double* xnorm2_d, const void* B,
-                      const float* a, int64_t n, double* partials, int grid, cudaStream_t stream) {
+cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, const float* xC, const double* xnorm2_d,
+                      const void* B, const float* a, int64_t n, double* partials, int grid, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    SseKernel<<<grid, 256, 0, stream>>>(dims, Gcol, xC, xnorm2_d, B, a, n, partials);
+    SseKernel<<<grid, 256, 0, stream>>>(dims, Gcol, Gdiag, xC, xnorm2_d, B, a, n, partials);
     return cudaGetLastError();
 }
 
@@ -632,20 +648,21 @@ int RefineWarpsPerBlock() { return kWarps; }
 
 // Large-root outputs from the internal m x n codes: cluster id (the root code) and the (m-1) small
 // codes of each vector (BeamSearchPrefixLSLargeRoot's cluster_id / B_small, beam_search.h:26-32).
-__global__ void SplitRootCodesKernel(int m, const uint8_t* __restrict__ B, int64_t n, uint32_t* __restrict__ cluster,
-                                     uint8_t* __restrict__ B_small) {
+// Internal codes are uint16 when the root has more than 256 codewords.
+__global__ void SplitRootCodesKernel(int m, const void* __restrict__ B, int wide, int64_t n,
+                                     uint32_t* __restrict__ cluster, uint8_t* __restrict__ B_small) {
     for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n;
          v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        cluster[v] = B[v * m];
-        for (int l = 1; l < m; ++l) B_small[v * (m - 1) + l - 1] = B[v * m + l];
+        cluster[v] = static_cast<uint32_t>(LoadCode(B, v * m, wide));
+        for (int l = 1; l < m; ++l) B_small[v * (m - 1) + l - 1] = static_cast<uint8_t>(LoadCode(B, v * m + l, wide));
     }
 }
 
-cudaError_t LaunchSplitRootCodes(int m, const uint8_t* B, int64_t n, uint32_t* cluster, uint8_t* B_small,
+cudaError_t LaunchSplitRootCodes(int m, const void* B, int wide, int64_t n, uint32_t* cluster, uint8_t* B_small,
                                  cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 32));
-    SplitRootCodesKernel<<<grid, 256, 0, stream>>>(m, B, n, cluster, B_small);
+    SplitRootCodesKernel<<<grid, 256, 0, stream>>>(m, B, wide, n, cluster, B_small);
     return cudaGetLastError();
 }
 

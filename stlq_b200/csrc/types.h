@@ -27,8 +27,17 @@ struct Dims {
     int m;        // codebooks
     int H;        // sum of h_vec
     int maxK;     // max of h_vec
+    int maxKs;    // max of h_vec[1..m-1] (1 when m == 1): candidates per beam slot and layer
     int h_vec[kMaxM];
     int off[kMaxM];
+    // Gram storage.  The beam reads G(r, c), c >= c0, at Grow[r * ldg + (c - c0)]; the refinement
+    // reads G(r, c), r >= c0, at Gcol[c * ldg + (r - c0)].  Regular encoders hold all of G in both
+    // orientations (ldg = H, c0 = 0).  Large-root encoders hold one array for both (G is computed
+    // on the device and symmetric) with only the columns of codebooks 1..m-1 (ldg = H - h0,
+    // c0 = h0): the reference's G0S and G_small blocks.  The root codewords' own diagonal is in
+    // the diagonal array; no other root-root entry is ever needed.
+    int ldg;
+    int c0;
     // Large-root encoder (PrecompLargeRoot, reference include/stlq/quantizer/precomp_large_root.h):
     // codebook 0 is the root; the beam's triangular solves multiply by 1/R_ii
     // (beam_search.cpp:517-575) and costs follow SampleCostLargeRoot (cost_utils.cpp:160-209).

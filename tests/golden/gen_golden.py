@@ -109,6 +109,38 @@ def large_root_cases():
     make_lr_case("lr_edge_vectors", E, books, beam=4, icm=2)
 
 
+def rvq_with_root(X, h0, m_small, k_small, seed, root=None):
+    """A root of h0 codewords (k-means, or the given array) and m_small residual codebooks trained
+    on X minus each vector's nearest root codeword."""
+    if root is None:
+        root = synth.train_rvq(X, 1, h0, iters=4, seed=seed)[0]
+    lab = np.empty(X.shape[0], np.int64)
+    r2 = (root.astype(np.float64) ** 2).sum(1)
+    for i in range(0, X.shape[0], 256):
+        xb = X[i:i + 256].astype(np.float64)
+        lab[i:i + 256] = (r2[None, :] - 2.0 * xb @ root.T.astype(np.float64)).argmin(1)
+    R = (X - root[lab]).astype(np.float32)
+    return [root.astype(np.float32)] + synth.train_rvq(R, m_small, k_small, iters=5, seed=seed + 1)
+
+
+def big_root_cases():
+    # Roots above 256 codewords (cluster ids beyond a byte).  A 300-code root (layer-0 errors fit
+    # the beam's shared-memory list), config 3's shape with a 5000-code root (5000 > beam x 256: the
+    # layer-0 errors are recomputed where the selection reads them) and a 1024-code root with ILS.
+    X = synth.sift_like(20300, d=128, seed=21)
+    make_lr_case("lr_root5000_d128_m8_b16", X[:300], rvq_with_root(X[300:], 5000, 7, 256, seed=21), beam=16, icm=1)
+    X = synth.sift_like(6300, d=32, seed=22, n_centres=200)
+    make_lr_case("lr_root300_d32_b16", X[:300], rvq_with_root(X[300:], 300, 3, 64, seed=22), beam=16, icm=1)
+    make_lr_case("lr_root1024_d32_ils", X[:300], rvq_with_root(X[300:], 1024, 4, 64, seed=23), beam=4, icm=2,
+                 ils=2, perturb=2)
+    # The largest root the encoder takes: 65,536 codewords (data points, not trained).
+    X = synth.sift_like(70000, d=16, seed=24, n_centres=500)
+    rng = np.random.default_rng(24)
+    root = X[64:][rng.permutation(X.shape[0] - 64)[:65536]]
+    make_lr_case("lr_root65536_d16", X[:64], rvq_with_root(X[64:4064], 65536, 2, 32, seed=24, root=root), beam=8,
+                 icm=1)
+
+
 def main():
     # The reference's own test setup (tests/test_streaming_encode_base.cpp:67-134): m=3, K=16,
     # d=16, beam 2, ICM 2, ILS 3, perturb 2, seed 1234 -- at n=600.
@@ -153,6 +185,10 @@ def main():
 
 if __name__ == "__main__":
     oracle.build(reference=True)
+    if "--big-root-only" in sys.argv:
+        big_root_cases()
+        sys.exit(0)
     if "--large-root-only" not in sys.argv:
         main()
     large_root_cases()
+    big_root_cases()

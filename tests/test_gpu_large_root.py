@@ -1,8 +1,9 @@
 """GPU: the large-root encoder (the large pipeline's basic encode) against the reference.
 
 Bar: bit-exact root codes (cluster ids), small codes, coefficients and final costs against the
-fixtures the reference's own large-root code produced (tests/golden/lr_*.npz); the cost sums equal
-the double sums of those costs.  The device entry point equals the host one.
+fixtures the reference's own large-root code produced (tests/golden/lr_*.npz), roots of 32 to
+65,536 codewords; the cost sums equal the double sums of those costs.  The device entry point
+equals the host one.
 """
 import numpy as np
 import pytest
@@ -41,10 +42,11 @@ def test_large_root_matches_reference(cuda, name):
     assert abs(r["sums"][0] - float(np.sum(c["cost_beam"].astype(np.float64)))) <= 1e-9 * abs(r["sums"][0])
 
 
-def test_large_root_device_equals_host(cuda):
+@pytest.mark.parametrize("name", ["lr_d128_m8_k256_b16", "lr_root5000_d128_m8_b16", "lr_root65536_d16"])
+def test_large_root_device_equals_host(cuda, name):
     import stlq_b200
 
-    c = load_lr_case("lr_d128_m8_k256_b16")
+    c = load_lr_case(name)
     enc = stlq_b200.Encoder(c["C_all"], c["h_vec"], device=0, large_root=True)
     h = enc.encode_base_large_root(c["X"], *args(c))
     cl, Bs, a, cost, sums = enc.encode_base_large_root_device(torch.from_numpy(c["X"]).to(cuda), *args(c))

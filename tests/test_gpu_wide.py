@@ -103,5 +103,6 @@ def test_code_width_is_enforced(cuda):
                                        None, sse.ctypes.data)
     assert rc != 0 and b"uint8" in lib.stlq_b200_last_error()
     narrow.close()
-    with pytest.raises(stlq_b200.StlqB200Error, match="at most 256"):
-        stlq_b200.Encoder(C_all, h_vec, device=0, large_root=True)
+    # A large-root encoder takes a root up to 65536 codewords, the other codebooks up to 256.
+    with pytest.raises(stlq_b200.StlqB200Error, match="for a large-root encoder"):
+        stlq_b200.Encoder(C_all, [64, 512], device=0, large_root=True)
