@@ -132,6 +132,7 @@ struct stlq_b200_encoder {
     int check_filter = 0;
     Dims dims{};
     DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
+    DevBuf Bdiag;  // the beam's diagonal (LaunchBeamDiag)
     // Tensor-core modes: C_all split into TF32 hi / lo parts once at create.
     DevBuf Chi, Clo;
     // Input rotation X <- R X (ApplyRotationInPlace), R stored by rows; off when R is the identity.
@@ -289,7 +290,7 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         }
         STLQ_TRY(LaunchXc(enc, Xs, xt, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
                           enc->xnd.as<double>(), stream));
-        STLQ_CK(stlq_b200::LaunchBeamSearch(dims, BeamGram(enc), enc->Gdiag.as<float>(), enc->xn.as<float>(),
+        STLQ_CK(stlq_b200::LaunchBeamSearch(dims, BeamGram(enc), enc->Bdiag.as<float>(), enc->xn.as<float>(),
                                             enc->xC.as<float>(), ns, beam, B + s0 * dims.m * cb, enc->redo.as<int>(),
                                             enc->check_filter,
                                             enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
@@ -333,7 +334,7 @@ int GetBeamInputs(const stlq_b200_encoder* enc, BeamInputs* out) {
     if (!enc) return Fail(STLQ_B200_EINVAL, "encoder handle is null");
     out->dims = enc->dims;
     out->Grow = BeamGram(enc);
-    out->Gdiag = enc->Gdiag.as<float>();
+    out->Gdiag = enc->Bdiag.as<float>();
     out->err_flag = enc->err_flag.as<unsigned int>();
     out->check_filter = enc->check_filter;
     out->num_sms = enc->num_sms;
@@ -422,7 +423,8 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
     int rc = 0;
     if ((rc = enc->C.Ensure(sizeof(float) * H * d)) || (rc = enc->Gcol.Ensure(sizeof(float) * HH)) ||
         (!large_root && (rc = enc->Grow.Ensure(sizeof(float) * HH))) || (rc = enc->Gdiag.Ensure(sizeof(float) * H)) ||
-        (rc = enc->invnorm.Ensure(sizeof(float) * H)) || (rc = enc->err_flag.Ensure(kFlagBytes)))
+        (rc = enc->Bdiag.Ensure(sizeof(float) * H)) || (rc = enc->invnorm.Ensure(sizeof(float) * H)) ||
+        (rc = enc->err_flag.Ensure(kFlagBytes)))
         return fail(rc);
     if (cudaStreamCreateWithFlags(&enc->compute, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&enc->copy, cudaStreamNonBlocking) != cudaSuccess)
@@ -488,7 +490,10 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
             (rc = ck(stlq_b200::LaunchDiag(enc->Gcol.as<float>(), enc->Gdiag.as<float>(), H, s), "diag G")))
             return fail(rc);
     }
-    if ((rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, kFlagBytes, s), "memset")) ||
+    if ((rc = ck(stlq_b200::LaunchBeamDiag(dims, enc->Gcol.as<float>(), enc->Gdiag.as<float>(), enc->Bdiag.as<float>(),
+                                           s),
+                 "beam diagonal")) ||
+        (rc = ck(cudaMemsetAsync(enc->err_flag.p, 0, kFlagBytes, s), "memset")) ||
         (rc = ck(cudaStreamSynchronize(s), "create sync")))
         return fail(rc);
     *out = enc;
@@ -509,7 +514,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     DeviceScope scope(enc->device);
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
-    for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
+    for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->Bdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
                       &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->Xrot, &enc->Rrow, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
@@ -836,7 +841,7 @@ int stlq_b200_beam_search(stlq_b200_encoder* enc, const float* xnorm2_dev, const
     if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return Fail(STLQ_B200_EINVAL, "null buffer");
     DeviceScope scope(enc->device);
     STLQ_TRY(enc->redo.Ensure(static_cast<size_t>(n + 1) * sizeof(int)));
-    STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, BeamGram(enc), enc->Gdiag.as<float>(), xnorm2_dev, xC_dev, n,
+    STLQ_CK(stlq_b200::LaunchBeamSearch(enc->dims, BeamGram(enc), enc->Bdiag.as<float>(), xnorm2_dev, xC_dev, n,
                                         beam, B_dev, enc->redo.as<int>(), enc->check_filter, enc->err_flag.as<unsigned int>(), enc->num_sms,
                                         static_cast<cudaStream_t>(stream)));
     return 0;

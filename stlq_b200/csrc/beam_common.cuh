@@ -22,6 +22,12 @@ constexpr float kDenomGuard = 1e-3f;
 
 __device__ __forceinline__ float PosInf() { return __int_as_float(0x7f800000); }
 
+// The beam's diagonal marks a codeword of codebooks 1..m-1 whose Gram column is exactly zero
+// (a zero codeword) with alpha = -0.0f.  Every prefix then has A = 0, so y, v and delta are 0 and
+// denom = alpha - delta == 0: the reference skips the candidate (beam_search.cpp:309), in every
+// slot.  -0.0f and +0.0f take the same branch in every comparison the reference makes.
+__device__ __forceinline__ bool IsZeroColumn(float alpha) { return __float_as_uint(alpha) == 0x80000000u; }
+
 // Beam slots in dynamic shared memory, sized by the runtime beam width.
 template <int MAXM>
 struct SlotView {
@@ -177,7 +183,8 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 // L ulp in diff (scale |gamma| + sum|A_t a_t|) and in denom (scale alpha + delta), propagated
 // through r = diff^2/denom, plus the final subtraction; kept with a factor 16.  A candidate
 // whose cheap value is unreliable (ill-conditioned slot, denom <= kDenomGuard * alpha, NaN)
-// gets [-inf, +inf].
+// gets [-inf, +inf].  A codeword whose whole Gram column is zero (alpha is -0.0f in the beam's
+// diagonal, see IsZeroColumn) gets [+inf, +inf]: the reference always skips it.
 template <int MAXM, int L>
 __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* const (&gq)[kCpt],
                                             const bool (&ok)[kCpt],
@@ -232,8 +239,9 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
         const float w = fmaf(2.0f * fabsf(diff) * seta[q] + fabsf(r) * (alpha[q] + delta[q]), u16 * fabsf(rden),
                              e16 * (Eo + fabsf(r)));
         const bool force = ill || !(denom > kDenomGuard * alpha[q]) || !(w < PosInf()) || !(ep < PosInf());
-        lo[q] = force ? -PosInf() : ep - w;
-        hi[q] = force ? PosInf() : ep + w;
+        const bool zero = IsZeroColumn(alpha[q]);
+        lo[q] = zero ? PosInf() : force ? -PosInf() : ep - w;
+        hi[q] = force || zero ? PosInf() : ep + w;
     }
 }
 

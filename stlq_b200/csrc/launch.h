@@ -74,6 +74,10 @@ struct BeamInputs {
 cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cudaStream_t stream);
 cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream);
 cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStream_t stream);
+// The beam's diagonal: Gdiag with -0.0f for codewords of codebooks 1..m-1 whose Gram column is
+// exactly zero (skipped by the reference in every slot) and +0.0f for any other zero.
+cudaError_t LaunchBeamDiag(const Dims& dims, const float* Gcol, const float* Gdiag, float* Bdiag,
+                           cudaStream_t stream);
 cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStream_t stream);
 // Large-root precompute: invnorm from the SIMD-order norms; Gdiag = norm0 for the h0 root codewords
 // and the compact Gram's diagonal (G[h * Hs + h - h0]) for the others.

@@ -31,6 +31,31 @@ __global__ void DiagKernel(const float* __restrict__ Gcol, float* __restrict__ d
     if (h < H) diag[h] = Gcol[static_cast<size_t>(h) * H + h];
 }
 
+// The beam's copy of the Gram diagonal: -0.0f marks a codeword of codebooks 1..m-1 whose Gram
+// column G(., c) is exactly zero (it can never enter a beam); a diagonal 0 of any other codeword
+// is written as +0.0f, and every other value is copied.  One warp per codeword; the column is read
+// through the refinement's layout (Gcol[c * ldg + r - c0] = G(r, c) for r >= c0; a large-root
+// encoder's root rows G(r, c), r < c0, at Gcol[r * ldg + c - c0]).
+__global__ void BeamDiagKernel(Dims dims, const float* __restrict__ Gcol, const float* __restrict__ Gdiag,
+                               float* __restrict__ Bdiag) {
+    const int lane = threadIdx.x & 31;
+    const int c = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= dims.H) return;
+    const float g = Gdiag[c];
+    bool zero = dims.m > 1 && c >= dims.off[1] && g == 0.0f;
+    if (zero) {  // warp-uniform: c is the warp's, and `zero` only changes through __all_sync
+        const size_t ld = static_cast<size_t>(dims.ldg);
+        for (int r0 = 0; r0 < dims.H; r0 += 32) {
+            const int r = r0 + lane;
+            float v = 0.0f;
+            if (r < dims.H) v = r >= dims.c0 ? Gcol[c * ld + (r - dims.c0)] : Gcol[r * ld + (c - dims.c0)];
+            zero = __all_sync(0xffffffffu, v == 0.0f);
+            if (!zero) break;
+        }
+    }
+    if (lane == 0) Bdiag[c] = zero ? -0.0f : (g == 0.0f ? 0.0f : g);
+}
+
 // invnorm_flat[h] = 1/sqrt(sum_r c_r^2) with the reference's sequential float sum
 // (encoder_precomp.inc:31-39); 0 for a zero codeword.
 __global__ void InvnormKernel(const float* __restrict__ C, int H, int d, float* __restrict__ invnorm) {
@@ -84,6 +109,12 @@ cudaError_t LaunchTranspose(const float* in, float* out, int rows, int cols, cud
 
 cudaError_t LaunchDiag(const float* Gcol, float* diag, int H, cudaStream_t stream) {
     DiagKernel<<<(H + 255) / 256, 256, 0, stream>>>(Gcol, diag, H);
+    return cudaGetLastError();
+}
+
+cudaError_t LaunchBeamDiag(const Dims& dims, const float* Gcol, const float* Gdiag, float* Bdiag,
+                           cudaStream_t stream) {
+    BeamDiagKernel<<<(dims.H + 7) / 8, 256, 0, stream>>>(dims, Gcol, Gdiag, Bdiag);
     return cudaGetLastError();
 }
 
