@@ -10,6 +10,7 @@ NCCL all-reduce of the per-shard MSE sums when N > 1.  Weak scaling: every GPU e
 reference's trainer) and broadcast over NCCL.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --sweep [--gpus N]     # config 4's grid: throughput and code agreement per point
 """
 from __future__ import annotations
 
@@ -44,6 +45,10 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-fp32-peak", action="store_true", help="skip the SGEMM FP32 peak measurement")
     p.add_argument("--no-strict", action="store_true", help="skip the STRICT (tensor-core GEMM) mode leg")
+    p.add_argument("--sweep", action="store_true",
+                   help="config 4's grid (M in {8,16}, K in {256,1024}, beam in {1,4,16,32}, ICM 0/1): one JSON "
+                        "line with every point's throughput and code agreement")
+    p.add_argument("--sweep-seconds", type=float, default=0.5, help="target GPU time of one timed sweep step")
     p.add_argument("--gemm-only", choices=["exact", "strict", "fast"], default=None,
                    help="profiling aid: run only the xC GEMM of this mode on one 262,144-vector slice")
     return p.parse_args()
@@ -507,6 +512,124 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+SWEEP_BOOKS = ((8, 256), (8, 1024), (16, 256), (16, 1024))
+SWEEP_BEAMS = (1, 4, 16, 32)
+SWEEP_ICM = (0, 1)
+
+
+def sweep_sizes(m, k, beam, seconds):
+    """(device vectors per GPU, CPU-check sample) for one sweep point, scaled by the beam's
+    candidate work (beam * K * M^2) from a 3M vectors/s reference point at M=8, K=256, beam 16."""
+    rel = 262_144 / (beam * k * m * m)
+    n = int(min(1 << 20, max(16_384, 3e6 * rel * seconds)))
+    n = (n + 1023) // 1024 * 1024
+    sample = int(min(1024, max(32, 512 * rel))) if k <= 256 else int(min(256, max(4, 64 * rel)))
+    return n, sample
+
+
+def run_sweep(args):
+    """Config 4: a 10M-vector D=128 f32 base (config-0 generator, seed 4) over the grid M in {8, 16},
+    K in {256, 1024}, beam width in {1, 4, 16, 32}, 0 or 1 ICM sweep, at N GPUs (each GPU its own
+    shard: weak scaling, max over ranks).  A point's timed step encodes a device-resident slice of
+    that base sized for about --sweep-seconds of GPU work (10M vectors per point would take
+    minutes at the slow points; the per-vector work does not depend on n).  Code agreement: the
+    first vectors of the slice against the reference's own CPU encoder (oracle/_ref) for K = 256, and
+    against the CPU restatement (oracle/stlq_oracle.cpp, uint16 codes) for K = 1024, which the
+    reference cannot represent (its codes are uint8)."""
+    import torch
+    import torch.distributed as dist
+
+    import stlq_b200
+    from stlq_b200 import synth
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    points = []
+    t_all = time.perf_counter()
+    for m, k in SWEEP_BOOKS:
+        H = m * k
+        if rank == 0:
+            train = synth.sift_like(50_000, d=args.d, seed=0)
+            C = torch.from_numpy(synth.flatten_books(synth.train_rvq(train, m, k, iters=8, seed=0,
+                                                                     device=device))).to(device)
+        else:
+            C = torch.empty((H, args.d), dtype=torch.float32, device=device)
+        if world > 1:
+            dist.broadcast(C, src=0)
+        C_np = C.cpu().numpy()
+        h_vec = [k] * m
+        enc = stlq_b200.Encoder(C_np, h_vec, device=local)
+        n_max = max(sweep_sizes(m, k, b, args.sweep_seconds)[0] for b in SWEEP_BEAMS)
+        offset = rank * n_max
+        X_np = synth.sift_like(n_max, d=args.d, seed=4, start=offset)
+        Xd = torch.from_numpy(X_np).to(device)
+        ref_P = None
+        for beam in SWEEP_BEAMS:
+            n, sample = sweep_sizes(m, k, beam, args.sweep_seconds)
+            for icm in SWEEP_ICM:
+                X = Xd[:n]
+                B = a = None
+
+                def step():
+                    nonlocal B, a
+                    B, a, _, _ = enc.encode_base_device(X, beam, icm, 0, 0, True, 38251450, offset)
+
+                step()
+                torch.cuda.synchronize()
+                enc.sync()
+                if world > 1:
+                    dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 2
+                e0.record()
+                for _ in range(reps):
+                    step()
+                e1.record()
+                torch.cuda.synchronize()
+                t = torch.tensor([e0.elapsed_time(e1) / 1e3 / reps], dtype=torch.float64, device=device)
+                if world > 1:
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                t_max = float(t.item())
+                pt = {"M": m, "K": k, "beam": beam, "icm": icm, "vectors_per_gpu": n,
+                      "vectors_per_s": world * n / t_max, "ms_per_step": 1e3 * t_max}
+                if rank == 0 and not args.no_cpu:
+                    import oracle
+
+                    Bg = B[:sample].cpu().numpy()
+                    if k <= 256:
+                        if ref_P is None:
+                            ref_P = oracle.Reference(threads=os.cpu_count()).precomp(h_vec, C_np)
+                        r = ref_P.encode_base(X_np[:sample], beam, icm)
+                        checker = "reference CPU encoder (oracle/_ref)"
+                    else:
+                        r = oracle.Oracle().encode_base(h_vec, C_np, X_np[:sample], beam, icm)
+                        checker = "CPU restatement (reference cannot represent K > 256)"
+                    same = (Bg.astype(np.int64) == np.asarray(r["B"]).astype(np.int64)).all(1)
+                    pt["code_match"] = {"frac": float(same.mean()), "vectors": sample, "checker": checker}
+                points.append(pt)
+                if rank == 0:
+                    print(json.dumps(pt), file=sys.stderr, flush=True)
+        enc.close()
+        del Xd, C
+    if rank == 0:
+        line = {"metric": "encoded vectors/sec (config-4 sweep)", "unit": "vectors/s", "n_gpus": world,
+                "higher_is_better": True, "scaling": "weak", "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "D=128 f32 SIFT-like base (seed 4), codebooks: seeded residual k-means on "
+                                       "50,000 vectors; ILS 0, use_abs, seed 38251450; each point a device-resident "
+                                       "slice per GPU, 1 warm-up + 2 timed steps, CUDA events, max over ranks",
+                           "parallelism": f"dp{world} (shards of base vectors)"},
+                "wall_s": time.perf_counter() - t_all, "sweep": points}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_gemm_only(args):
     """Profiling aid (not a bench line): the xC GEMM of one mode on a slice, three launches."""
     import torch
@@ -529,6 +652,9 @@ def main():
     args = parse_args()
     if args.gemm_only:
         run_gemm_only(args)
+        return
+    if args.sweep and args.impl == "ours":
+        run_sweep(args)
         return
     if args.impl == "reference":
         run_reference(args)

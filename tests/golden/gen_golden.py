@@ -141,6 +141,21 @@ def big_root_cases():
                  icm=1)
 
 
+def zero_codeword_cases():
+    # Zero and duplicated codewords (what k-means leaves behind in empty clusters): the reference
+    # skips a zero codeword in every beam slot (denom == 0) and breaks exact ties by scan order.
+    X = synth.sift_like(6400, d=32, seed=25, n_centres=120)
+    books = synth.train_rvq(X[400:], 5, 64, iters=5, seed=25)
+    books[1][5] = 0.0
+    books[2][0:3] = 0.0
+    books[3][7] = books[3][9]
+    books[4][:16] = 0.0
+    make_case("zero_codewords", X[:400], books, beam=16, icm=2, ils=1, perturb=2)
+    lr = [b.copy() for b in books]
+    lr[0][11] = 0.0
+    make_lr_case("lr_zero_codewords", X[:400], lr, beam=8, icm=1)
+
+
 def main():
     # The reference's own test setup (tests/test_streaming_encode_base.cpp:67-134): m=3, K=16,
     # d=16, beam 2, ICM 2, ILS 3, perturb 2, seed 1234 -- at n=600.
@@ -188,7 +203,11 @@ if __name__ == "__main__":
     if "--big-root-only" in sys.argv:
         big_root_cases()
         sys.exit(0)
+    if "--zero-only" in sys.argv:
+        zero_codeword_cases()
+        sys.exit(0)
     if "--large-root-only" not in sys.argv:
         main()
     large_root_cases()
     big_root_cases()
+    zero_codeword_cases()

@@ -169,3 +169,19 @@ def test_exact_gemm_u8_and_unaligned_input(cuda, oracle_lib):
     want = oracle_lib.gemm_xc(C, Xu.astype(np.float32).reshape(-1)[1:1 + n * d].reshape(n, d))
     assert np.array_equal(enc.xc_gemm(shifted).cpu().numpy(), want)
     enc.sync()
+
+
+def test_zero_codewords_stay_on_fast_path(cuda):
+    """Zero codewords are skipped by the fast kernel's cheap pass instead of forcing exact
+    evaluations (which overflowed the survivor list at large codebooks and sent every vector to
+    the replay kernel); codes stay bit-exact (test_stages_match_reference covers the fixture)."""
+    c = load_case("zero_codewords")
+    enc = make_encoder(c)
+    enc.beam_stats(reset=True)
+    r = enc.encode_base(c["X"], c["beam"], c["icm_iters"], c["ils_iters"], c["perturb_k"], bool(c["use_abs"]),
+                        c["seed"])
+    st = enc.beam_stats(reset=True)
+    assert np.array_equal(r["B"], c["B"])
+    assert st["replayed_fraction"] < 0.5, st
+    # 16 slots x 16 zero codewords of the last codebook alone would be 256 forced survivors.
+    assert st["exact_per_layer"] < 128, st
