@@ -261,14 +261,63 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
     return OrderKey(hmin);
 }
 
+// CheapPass with each thread's two codewords adjacent (k = kc + 2 t, k + 1): aligned 8-byte
+// gathers and packed FP32x2 arithmetic (CheapBoundsPair); `table` holds the slots' pair tables.
+// Only the 16-layer kernel has it: there the L^2 substitution dominates and the pass is 7%
+// faster; the 8-layer kernel is bound by dependency latency and the table's extra barrier per
+// layer, and measured 2% slower with it.
+template <int MAXM>
+constexpr bool kPairPath = MAXM > 8;
+static_assert(kCpt == 2, "the paired cheap pass takes two codewords per thread");
+template <int MAXM, int L, bool kHi>
+__device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
+                                               int offL, int colL, const float* __restrict__ Grow,
+                                               const float* __restrict__ Gdiag, const float* __restrict__ xc,
+                                               float* lo, float* hi_out, int check, unsigned int* err_flag,
+                                               bool recip) {
+    const int tid = threadIdx.x;
+    float hmin = PosInf();
+    for (int kc = 0; kc < K; kc += 2 * kThreads) {
+        const int k = kc + 2 * tid;
+        const bool ok = k < K;  // K is even: k + 1 < K as well
+        const float2 alpha = ok ? __ldg(reinterpret_cast<const float2*>(Gdiag + offL + k)) : make_float2(0.0f, 0.0f);
+        const float2 gamma = ok ? __ldg(reinterpret_cast<const float2*>(xc + offL + k)) : make_float2(0.0f, 0.0f);
+        const float* gq = Grow + colL + k;
+        for (int h = 0; h < curH; ++h) {
+            float2 l, hi;
+            CheapBoundsPair<MAXM, L>(table + h * PairTableStride<MAXM>(), cur.rowh(h), cur.E[h], cur.ill[h] != 0, gq,
+                                     ok, alpha, gamma, l, hi);
+            if (ok) {
+                *reinterpret_cast<float2*>(lo + h * K + k) = l;
+                if (kHi) *reinterpret_cast<float2*>(hi_out + h * K + k) = hi;
+                hmin = fminf(hmin, fminf(hi.x, hi.y));
+            }
+            if (check) {
+                const int col[kCpt] = {colL + k, colL + k + 1};
+                const bool okc[kCpt] = {ok, ok};
+                const float al[kCpt] = {alpha.x, alpha.y}, ga[kCpt] = {gamma.x, gamma.y};
+                const float la[kCpt] = {l.x, l.y}, ha[kCpt] = {hi.x, hi.y};
+                CheckBounds<MAXM>(cur, h, L, Grow, 0, col, okc, al, ga, la, ha, err_flag, recip);
+            }
+        }
+    }
+    return OrderKey(hmin);
+}
+
+// `table` non-null: the paired pass (Dims::pair) over the slots' pair tables.
 template <int MAXM, bool kHi>
 __device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
-                                  int check, unsigned int* err, bool recip) {
+                                  int check, unsigned int* err, bool recip, const float2* table) {
 #define STLQ_B200_CHEAP(LL)                                                                          \
     case LL:                                                                                         \
-        if constexpr (LL < MAXM)                                                                     \
+        if constexpr (LL < MAXM) {                                                                   \
+            if constexpr (kPairPath<MAXM>)                                                           \
+                if (table)                                                                           \
+                    return CheapPassPair<MAXM, LL, kHi>(cur, table, curH, K, offL, colL, Grow, Gdiag, xc, lo, \
+                                                        hi_out, check, err, recip);                  \
             return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err, recip); \
+        }                                                                                            \
         break;
     switch (L) {
         STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
@@ -371,14 +420,21 @@ struct Replay {
 template <int MAXM>
 __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
-                            const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt) {
+                            const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt,
+                            float2* table) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
     const int n_cand = curH * K;
     int* list = reinterpret_cast<int*>(his);
     if (his) {
+        if constexpr (kPairPath<MAXM>) {
+            if (table) {
+                BuildPairTable<MAXM>(cur, curH, L, table);
+                __syncthreads();
+            }
+        }
         CheapDispatch<MAXM, true>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
-                                  dims.large_root != 0);
+                                  dims.large_root != 0, table);
         __syncthreads();
         if (tid < 32) {
             Replay rp;
@@ -427,6 +483,10 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
     LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
     float* errs = reinterpret_cast<float*>(smem + ((off + sizeof(LayerTable) + 15) & ~size_t(15)));
     float* his = prescan ? errs + beam * dims.maxKs : nullptr;
+    float2* table = nullptr;  // pair tables after the candidate arrays (Dims::pair, pre-scan only)
+    if (dims.pair && prescan)
+        table = reinterpret_cast<float2*>(
+            (reinterpret_cast<uintptr_t>(errs + 2 * beam * dims.maxKs) + 15) & ~uintptr_t(15));
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     const int64_t total = vec_list ? static_cast<int64_t>(*count) : n;
@@ -459,7 +519,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         for (int L = 1; L < m; ++L) {
             ReplayLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
                               SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, his,
-                              lt);
+                              lt, table);
             ci ^= 1;
         }
         if (tid < 32) {  // first slot with the smallest error (beam_search.cpp:409-416)
@@ -623,12 +683,18 @@ template <int MAXM>
 __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
                          const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
                          int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, uint64_t* keys, float* keep,
-                         int check, unsigned int* err_flag) {
+                         int check, unsigned int* err_flag, float2* table) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
+    if constexpr (kPairPath<MAXM>) {
+        if (table) {
+            BuildPairTable<MAXM>(cur, curH, L, table);
+            __syncthreads();
+        }
+    }
     const uint32_t hmin =
         CheapDispatch<MAXM, false>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
-                                   dims.large_root != 0);
+                                   dims.large_root != 0, table);
     const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     for (int p = tid; p < S; p += kThreads) {
@@ -671,6 +737,9 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     float* ex = lo + beam * dims.maxKs;
     float* keep = ex + kSurvCap;
     uint16_t* surv = reinterpret_cast<uint16_t*>(keep + kKeep * KeepStride<MAXM>());
+    float2* table = dims.pair ? reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(surv + kSurvCap) + 15) &
+                                                          ~uintptr_t(15))
+                              : nullptr;
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     unsigned long long n_surv = 0, n_layers = 0, n_vec = 0, n_redo = 0;  // thread 0's tallies
@@ -705,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         for (int L = 1; L < m && curH > 0; ++L) {
             curH = FastLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
                                    SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo, lt,
-                                   surv, ex, keys, keep, check, err_flag);
+                                   surv, ex, keys, keep, check, err_flag, table);
             ci ^= 1;
             n_surv += lt.n_surv;
             ++n_layers;
@@ -730,20 +799,26 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     }
 }
 
+// The pair tables of every slot (Dims::pair), with 16 bytes of alignment slack.
 template <int MAXM>
-size_t FastSmemBytes(int beam, int maxK) {
+size_t PairTableBytes(int beam) {
+    return 16 + sizeof(float2) * static_cast<size_t>(beam) * PairTableStride<MAXM>();
+}
+
+template <int MAXM>
+size_t FastSmemBytes(int beam, int maxK, bool pair = false) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
     return b + sizeof(uint64_t) * kSurvCap + sizeof(float) * beam * maxK + (sizeof(float) + sizeof(uint16_t)) * kSurvCap +
-           sizeof(float) * kKeep * KeepStride<MAXM>() + 16;
+           sizeof(float) * kKeep * KeepStride<MAXM>() + 16 + (pair ? PairTableBytes<MAXM>(beam) : 0);
 }
 
 // With the pre-scan: errors (lower bounds first) and upper bounds; without: errors only.
 template <int MAXM>
-size_t ReplaySmemBytes(int beam, int maxK, bool prescan) {
+size_t ReplaySmemBytes(int beam, int maxK, bool prescan, bool pair = false) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
-    return b + (prescan ? 2 : 1) * sizeof(float) * beam * maxK + 16;
+    return b + (prescan ? 2 : 1) * sizeof(float) * beam * maxK + 16 + (pair && prescan ? PairTableBytes<MAXM>(beam) : 0);
 }
 
 // The largest dynamic shared memory a block of the current device may opt into.
@@ -753,6 +828,24 @@ size_t MaxBlockSmem() {
         cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
         return 0;
     return static_cast<size_t>(v);
+}
+
+// The fast kernel takes the pair tables (Dims::pair) when they fit and cost no resident CTA.
+template <typename KernelT>
+bool PairKeepsOccupancy(KernelT kernel, size_t smem_scalar, size_t smem_pair) {
+    if (smem_pair > MaxBlockSmem()) return false;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_pair)) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    int a = 0, b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, kernel, kThreads, smem_scalar) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kThreads, smem_pair) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return b > 0 && b >= a;
 }
 
 // The replay runs its pre-scan whenever the upper bounds fit beside the errors.
@@ -800,28 +893,40 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
                         int64_t n, int beam, void* Bout, int* redo, int check, unsigned int* err_flag,
                         unsigned long long* stats, int num_sms, cudaStream_t stream) {
     int grid = 0;
-    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs);
+    Dims df = dims;
+    df.pair = kPairPath<MAXM> && dims.pair &&
+              PairKeepsOccupancy(BeamFastKernel<MAXM>, FastSmemBytes<MAXM>(beam, dims.maxKs),
+                                 FastSmemBytes<MAXM>(beam, dims.maxKs, true));
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs, df.pair != 0);
     cudaError_t e = Prepare(BeamFastKernel<MAXM>, fsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
-    BeamFastKernel<MAXM><<<grid, kThreads, fsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
+    BeamFastKernel<MAXM><<<grid, kThreads, fsm, stream>>>(df, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
                                                           check, err_flag, stats);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
+    Dims dr = dims;
+    dr.pair = kPairPath<MAXM> && dims.pair && prescan &&
+              ReplaySmemBytes<MAXM>(beam, dims.maxKs, true, true) <= MaxBlockSmem();
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, dr.pair != 0);
     e = Prepare(BeamReplayKernel<MAXM>, rsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
-    BeamReplayKernel<MAXM><<<grid, kThreads, rsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
+    BeamReplayKernel<MAXM><<<grid, kThreads, rsm, stream>>>(dr, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
                                                             redo, prescan);
     return cudaGetLastError();
 }
 
 template <int MAXM>
 cudaError_t PrepareT(const Dims& dims, int beam) {
-    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs);
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, ReplayPrescan<MAXM>(beam, dims.maxKs));
+    // The largest sizes a launch may ask for (the pair tables included when they fit).
+    const bool pair = kPairPath<MAXM> && dims.pair != 0;
+    const size_t f1 = FastSmemBytes<MAXM>(beam, dims.maxKs, pair);
+    const size_t fsm = f1 <= MaxBlockSmem() ? f1 : FastSmemBytes<MAXM>(beam, dims.maxKs);
+    const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
+    const size_t r1 = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, pair);
+    const size_t rsm = r1 <= MaxBlockSmem() ? r1 : ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
     cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(fsm));
     if (e != cudaSuccess) return e;

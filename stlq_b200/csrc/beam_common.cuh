@@ -174,6 +174,27 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 #undef STLQ_B200_EXACT
 }
 
+// The error bounds of one candidate from its cheap delta, eta and seta (see CheapBounds).
+template <int L>
+__device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta, float eta, float seta, float Eo,
+                                           bool ill, float& lo, float& hi) {
+    // Half-width w = 16 * de with de as documented at CheapBounds; the factor 16 is folded into the
+    // constants.
+    constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
+    constexpr float e16 = 16.0f * 1.2e-7f;
+    const float denom = alpha - delta;
+    const float diff = gamma - eta;
+    const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
+    const float r = diff * diff * rden;
+    const float ep = fmaxf(Eo - r, 0.0f);
+    const float w = fmaf(2.0f * fabsf(diff) * seta + fabsf(r) * (alpha + delta), u16 * fabsf(rden),
+                         e16 * (Eo + fabsf(r)));
+    const bool force = ill || !(denom > kDenomGuard * alpha) || !(w < PosInf()) || !(ep < PosInf());
+    const bool zero = IsZeroColumn(alpha);
+    lo = zero ? PosInf() : force ? -PosInf() : ep - w;
+    hi = force || zero ? PosInf() : ep + w;
+}
+
 // Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
 // kCpt codewords (Gram column pointers gq[q] = Grow + col[q]; the values of a codeword with !ok[q]
 // are meaningless and unused).  L is a compile-time constant here: this is the hot
@@ -226,23 +247,65 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     }
     const float Eo = cur.E[h];
     const bool ill = cur.ill[h] != 0;
-    // Half-width w = 16 * de with de as documented above; the factor 16 is folded into the constants.
-    constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
-    constexpr float e16 = 16.0f * 1.2e-7f;
 #pragma unroll
-    for (int q = 0; q < kCpt; ++q) {
-        const float denom = alpha[q] - delta[q];
-        const float diff = gamma[q] - eta[q];
-        const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
-        const float r = diff * diff * rden;
-        const float ep = fmaxf(Eo - r, 0.0f);
-        const float w = fmaf(2.0f * fabsf(diff) * seta[q] + fabsf(r) * (alpha[q] + delta[q]), u16 * fabsf(rden),
-                             e16 * (Eo + fabsf(r)));
-        const bool force = ill || !(denom > kDenomGuard * alpha[q]) || !(w < PosInf()) || !(ep < PosInf());
-        const bool zero = IsZeroColumn(alpha[q]);
-        lo[q] = zero ? PosInf() : force ? -PosInf() : ep - w;
-        hi[q] = force || zero ? PosInf() : ep + w;
+    for (int q = 0; q < kCpt; ++q) BoundsTail<L>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, lo[q], hi[q]);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Paired cheap bounds: a thread's two candidates are adjacent codewords k, k + 1 of one slot, so
+// their Gram gathers, alpha and gamma are single 8-byte loads and the substitution, delta and eta
+// run on packed FP32x2 (two correctly rounded fma / mul per instruction, bit-identical per lane to
+// the scalar CheapBounds).  The slot's scalars reach both lanes as duplicated pairs from a
+// per-layer table built by BuildPairTable.  Used when every codebook has an even number of
+// codewords (so every row offset, column and flat index of a pair is even: 8-byte aligned).
+
+// Table of one slot at layer L, in the order the substitution consumes it: for i = 0..L-1 the
+// entries -R(k, i) for k < i, then 1/R_ii, then a_i, each as the pair {v, v}.  Row i starts at
+// i(i-1)/2 + 2i.
+template <int MAXM>
+__host__ __device__ constexpr int PairTableStride() { return (MAXM - 1) * (MAXM - 2) / 2 + 2 * (MAXM - 1); }
+
+template <int MAXM>
+__device__ void BuildPairTable(const SlotView<MAXM>& cur, int curH, int L, float2* table) {
+    for (int e = threadIdx.x; e < curH * L; e += blockDim.x) {
+        const int h = e / L, i = e - h * L;
+        float2* row = table + h * PairTableStride<MAXM>() + i * (i - 1) / 2 + 2 * i;
+        const float* Rh = cur.Rh(h);
+        for (int k = 0; k < i; ++k) {
+            const float v = -Rh[i * MAXM + k];
+            row[k] = make_float2(v, v);
+        }
+        const float ri = cur.rinvh(h)[i], ai = cur.ah(h)[i];
+        row[i] = make_float2(ri, ri);
+        row[i + 1] = make_float2(ai, ai);
     }
+}
+
+template <int MAXM, int L>
+__device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, const int* rw, float Eo, bool ill,
+                                                const float* gq, bool ok, float2 alpha, float2 gamma, float2& lo,
+                                                float2& hi) {
+    float2 A[L], y[L];
+#pragma unroll
+    for (int i = 0; i < L; ++i)
+        A[i] = ok ? __ldg(reinterpret_cast<const float2*>(gq + rw[i])) : make_float2(0.0f, 0.0f);
+    float2 delta = make_float2(0.0f, 0.0f), eta = make_float2(0.0f, 0.0f);
+    float seta0 = fabsf(gamma.x), seta1 = fabsf(gamma.y);
+#pragma unroll
+    for (int i = 0; i < L; ++i) {
+        const float2* row = tab + i * (i - 1) / 2 + 2 * i;
+        float2 s = A[i];
+#pragma unroll
+        for (int k = 0; k < i; ++k) s = __ffma2_rn(row[k], y[k], s);
+        const float2 ri = row[i], ai = row[i + 1];
+        y[i] = __fmul2_rn(s, ri);
+        delta = __ffma2_rn(y[i], y[i], delta);
+        eta = __ffma2_rn(A[i], ai, eta);
+        seta0 = fmaf(fabsf(A[i].x), fabsf(ai.x), seta0);
+        seta1 = fmaf(fabsf(A[i].y), fabsf(ai.x), seta1);
+    }
+    BoundsTail<L>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, lo.x, hi.x);
+    BoundsTail<L>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, lo.y, hi.y);
 }
 
 }  // namespace beam
