@@ -209,6 +209,35 @@ int stlq_b200_encode_base_large_root_device(stlq_b200_encoder* enc, const void* 
                                             uint8_t* B_small_dev, float* a_dev, float* cost_dev,
                                             double* cost_sums_dev, void* stream);
 
+/* ---- Kernel-provider primitives ----
+ * The device operations behind StreamKernelProvider (include/stlq/core/kernel_provider.h:28-221,
+ * the reference's GPU backend seam; its CUDA implementation is src/core/kernel_provider_cuda_stream*
+ * over cuBLAS).  The C++ provider class stlq::b200::B200StreamKernels
+ * (stlq_b200/adapter/stlq_b200_kernels.h) implements that interface on them.  All pointers are on
+ * the handle's device; work is enqueued on `stream` (NULL: the legacy default stream). */
+typedef struct stlq_b200_kernels stlq_b200_kernels;
+int stlq_b200_kernels_create(int device, stlq_b200_kernels** out);
+int stlq_b200_kernels_destroy(stlq_b200_kernels* k);
+
+/* C = alpha op(A) op(B) + beta C, column-major, BLAS sgemm semantics (replaces stlq::GemmRaw /
+ * cblas_sgemm, src/core/blas.cpp:61-80, and the providers' Gemm*).  The result is bit-identical to
+ * the reference's single-thread OpenBLAS 0.3.15 sgemm: K split into blocks of 448 (a remainder in
+ * (448, 896) halved and rounded up to 16), one FMA chain per block, C = fl(beta C) (0 when beta is 0)
+ * and then C = fma(alpha, chain, C) per block in order.  k == 0 or alpha == 0 scales C by beta. */
+int stlq_b200_sgemm(stlq_b200_kernels* k, int trans_a, int trans_b, int m, int n, int kdim, float alpha,
+                    const float* A, int lda, const float* B, int ldb, float beta, float* C, int ldc, void* stream);
+
+/* out (rows x cols, leading dimension rows) = float(in) for a uint8 tile with leading dimension
+ * ld_in (ConvertU8ToF32, ConvertU8ToF32AndRotatePtr's first step). */
+int stlq_b200_u8_to_f32(stlq_b200_kernels* k, const uint8_t* in, int ld_in, int rows, int64_t cols, float* out,
+                        void* stream);
+
+/* Per column of scores (rows x cols, leading dimension ld): idx = the first row holding the maximum,
+ * val = that maximum (NaN never wins; no value above -inf gives row 0, -inf) (ArgmaxColsF32[Device]).
+ * idx or val may be NULL. */
+int stlq_b200_argmax_cols(stlq_b200_kernels* k, const float* scores, int ld, int rows, int64_t cols, int* idx,
+                          float* val, void* stream);
+
 /* Block until all work this encoder enqueued on `stream` has finished; returns
  * STLQ_B200_EDEVICE if a kernel flagged an internal error since the last check. */
 int stlq_b200_sync(stlq_b200_encoder* enc, void* stream);

@@ -205,6 +205,20 @@ class Reference:
     def precomp(self, h_vec, C_all):
         return RefPrecomp(self, h_vec, C_all)
 
+    def gemm(self, trans_a, trans_b, alpha, A, B, beta=0.0, C=None, threads=1):
+        """stlq::GemmRaw on column-major operands given as numpy arrays M_np[col, row] (so the
+        (rows x cols) matrix M is M_np.T); returns C_np[col, row] for C = alpha op(A) op(B) + beta C."""
+        A, B = _f32(A), _f32(B)
+        a_rows, a_cols = A.shape[1], A.shape[0]
+        b_rows, b_cols = B.shape[1], B.shape[0]
+        m, k = (a_cols, a_rows) if trans_a else (a_rows, a_cols)
+        n = b_rows if trans_b else b_cols
+        out = np.zeros((n, m), np.float32) if C is None else np.array(C, np.float32, copy=True, order="C")
+        self.lib.ref_gemm(int(trans_a), int(trans_b), m, n, k, ctypes.c_float(alpha), _p(A, _f32p), a_rows,
+                          _p(B, _f32p), b_rows, ctypes.c_float(beta), _p(out, _f32p), m, int(threads))
+        self.lib.ref_set_threads(self.threads)
+        return out
+
     def rotate(self, R, X):
         """ApplyRotationInPlace's GEMM: R (d x d) given as numpy R_np[col, row] (column-major), X (n, d)."""
         R, X = _f32(R), _f32(X)
@@ -347,6 +361,67 @@ class AdapterHarness:
         out = np.empty((X.shape[0], H), np.float32)
         self.lib.ref_gemm_xc(pre, _p(X, _f32p), X.shape[0], _p(out, _f32p))
         return out
+
+    # ---- kernel provider (stlq::b200::B200StreamKernels; None: the reference's CpuStreamKernels) ----
+    def provider(self, device=0):
+        err = ctypes.create_string_buffer(512)
+        self.lib.prov_create.restype = ctypes.c_void_p
+        h = self.lib.prov_create(int(device), err, 512)
+        if not h:
+            raise RuntimeError(err.value.decode())
+        return ctypes.c_void_p(h)
+
+    def provider_destroy(self, h):
+        self.lib.prov_destroy.argtypes = [ctypes.c_void_p]
+        self.lib.prov_destroy(h)
+
+    def provider_gemm(self, h, which, trans_a, trans_b, alpha, A, B, beta=0.0, C=None):
+        """C = alpha op(A) op(B) + beta C through the provider; matrices as M_np[col, row]."""
+        A, B = _f32(A), _f32(B)
+        ar, ac = A.shape[1], A.shape[0]
+        br, bc = B.shape[1], B.shape[0]
+        m = ac if trans_a else ar
+        n = br if trans_b else bc
+        out = np.zeros((n, m), np.float32) if C is None else np.array(C, np.float32, copy=True, order="C")
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.prov_gemm(h, int(which), int(trans_a), int(trans_b), ctypes.c_float(alpha), _p(A, _f32p), ar,
+                                ac, _p(B, _f32p), br, bc, ctypes.c_float(beta), _p(out, _f32p), m, n, err, 512)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def provider_convert(self, h, mode, U, rows, R=None, C_small=None):
+        """mode 0 ConvertU8ToF32, 1 ConvertU8ToF32AndRotate, 2 ConvertU8ToF32AndRotatePtr.  U: uint8
+        (cols, ld_in) (column-major tile of leading dimension ld_in, the first `rows` bytes used).
+        Returns (out as out_np[col, row], cached flags)."""
+        U = np.ascontiguousarray(U, np.uint8)
+        cols, ld_in = U.shape
+        Rm = None if R is None else _f32(R)
+        rr, rc_ = (0, 0) if Rm is None else (Rm.shape[1], Rm.shape[0])
+        out_rows = rows if mode == 0 else rr
+        out = np.empty((cols, out_rows), np.float32)
+        Cs = None if C_small is None else _f32(C_small)
+        hs = 0 if Cs is None else Cs.shape[0]
+        cached = np.zeros(2, np.int32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.prov_convert(h, int(mode), _p(U, _u8p), ld_in, rows, cols,
+                                   None if Rm is None else _p(Rm, _f32p), rr, rc_, _p(out, _f32p),
+                                   None if Cs is None else _p(Cs, _f32p), hs, _p(cached, _i32p), err, 512)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return out, cached
+
+    def provider_argmax(self, h, S):
+        """ArgmaxColsF32 of S (rows x cols) given as S_np[col, row]."""
+        S = _f32(S)
+        cols, rows = S.shape
+        idx = np.empty(cols, np.int32)
+        val = np.empty(cols, np.float32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.prov_argmax(h, _p(S, _f32p), rows, cols, _p(idx, _i32p), _p(val, _f32p), err, 512)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return idx, val
 
     def large_root_encode(self, h_vec, C_all, X, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450,
                           device=0):

@@ -3,6 +3,7 @@
 // on the same Precomp object (created by ref_precomp_create in ref_driver.cpp).
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -120,4 +121,139 @@ extern "C" int adapter_large_root_encode(int d, int m, const int* h_vec, const f
         return 1;
     }
     return 0;
+}
+
+// ---- Kernel provider: stlq::b200::B200StreamKernels next to the reference's CpuStreamKernels ----
+#include "stlq/core/kernel_provider_cpu.h"
+#include "stlq_b200_kernels.h"
+
+namespace {
+
+template <typename T>
+stlq::ColMajorMatrix<T> MatOf(const T* p, int rows, int cols) {
+    stlq::ColMajorMatrix<T> m(rows, cols);
+    if (p && rows > 0 && cols > 0) std::memcpy(m.data.data(), p, sizeof(T) * static_cast<size_t>(rows) * cols);
+    return m;
+}
+
+void CopyErr(const std::exception& e, char* err, int errlen) {
+    std::strncpy(err, e.what(), static_cast<size_t>(errlen) - 1);
+    err[errlen - 1] = 0;
+}
+
+}  // namespace
+
+extern "C" void* prov_create(int device, char* err, int errlen) {
+    try {
+        return new stlq::b200::B200StreamKernels(device);
+    } catch (const std::exception& e) {
+        CopyErr(e, err, errlen);
+        return nullptr;
+    }
+}
+
+extern "C" void prov_destroy(void* p) { delete static_cast<stlq::b200::B200StreamKernels*>(p); }
+
+// C (cr x cc, in/out) through one of the provider's GEMM entries (B200 when p is non-null, else the
+// reference's CpuStreamKernels::Gemm): 0 Gemm, 1 GemmDevice, 2 GemmDeviceHostPtrB,
+// 3 EnsureDeviceF32(B) then GemmDeviceDevicePtrB; 1-3 read the result back with DownloadF32.
+extern "C" int prov_gemm(void* p, int which, int ta, int tb, float alpha, const float* A, int ar, int ac,
+                         const float* B, int br, int bc, float beta, float* C, int cr, int cc, char* err, int errlen) {
+    try {
+        const auto Am = MatOf(A, ar, ac), Bm = MatOf(B, br, bc);
+        auto Cm = MatOf(C, cr, cc);
+        if (!p) {
+            stlq::CpuStreamKernels cpu;
+            cpu.Gemm(ta != 0, tb != 0, alpha, Am, Bm, beta, &Cm);
+        } else {
+            auto* k = static_cast<stlq::b200::B200StreamKernels*>(p);
+            stlq::DeviceMatF32View v;
+            if (which == 0) {
+                k->Gemm(ta != 0, tb != 0, alpha, Am, Bm, beta, &Cm);
+            } else {
+                if (which == 1) {
+                    k->GemmDevice(ta != 0, tb != 0, alpha, Am, Bm, beta, &v);
+                } else if (which == 2) {
+                    k->GemmDeviceHostPtrB(ta != 0, tb != 0, alpha, Am, Bm.data.data(), br, br, bc, beta, &v);
+                } else {
+                    stlq::DeviceMatF32View dB;
+                    if (!k->EnsureDeviceF32(Bm, &dB)) throw std::runtime_error("EnsureDeviceF32 failed");
+                    k->GemmDeviceDevicePtrB(ta != 0, tb != 0, alpha, Am, dB.ptr, dB.ld, br, bc, beta, &v);
+                }
+                k->DownloadF32(v, &Cm);
+            }
+        }
+        if (Cm.rows != cr || Cm.cols != cc) throw std::runtime_error("result shape differs");
+        std::memcpy(C, Cm.data.data(), sizeof(float) * static_cast<size_t>(cr) * cc);
+        return 0;
+    } catch (const std::exception& e) {
+        CopyErr(e, err, errlen);
+        return 1;
+    }
+}
+
+// ConvertU8ToF32 (mode 0), ConvertU8ToF32AndRotate (1) or ConvertU8ToF32AndRotatePtr (2, `in` with
+// leading dimension ld_in) on the B200 provider (p non-null) or the CPU one.  out: (R rows or
+// rows) x cols.  cached: TryGetCachedDeviceF32 of the result, then 1 if a GemmDevice of
+// C_small^T with it equals Gemm on the host copy (-1 when not asked: C_small null).
+extern "C" int prov_convert(void* p, int mode, const std::uint8_t* in, int ld_in, int rows, int cols, const float* R,
+                            int rr, int rc, float* out, const float* C_small, int hs, int* cached, char* err,
+                            int errlen) {
+    try {
+        std::unique_ptr<stlq::StreamKernelProvider> own;
+        stlq::StreamKernelProvider* k = static_cast<stlq::b200::B200StreamKernels*>(p);
+        if (!k) {
+            own = std::make_unique<stlq::CpuStreamKernels>();
+            k = own.get();
+        }
+        const auto Rm = MatOf(R, rr, rc);
+        stlq::ColMajorMatrix<float> X;
+        if (mode == 0 || mode == 1) {
+            stlq::ColMajorMatrix<std::uint8_t> U(rows, cols);
+            for (int j = 0; j < cols; ++j)
+                std::memcpy(U.Col(j), in + static_cast<size_t>(j) * ld_in, static_cast<size_t>(rows));
+            if (mode == 0) k->ConvertU8ToF32(U, &X);
+            else k->ConvertU8ToF32AndRotate(U, Rm, &X);
+        } else {
+            k->ConvertU8ToF32AndRotatePtr(in, ld_in, rows, cols, Rm, &X);
+        }
+        std::memcpy(out, X.data.data(), sizeof(float) * X.data.size());
+        if (cached) {
+            stlq::DeviceMatF32View v;
+            cached[0] = k->TryGetCachedDeviceF32(X, &v) ? 1 : 0;
+            cached[1] = -1;
+            if (C_small && hs > 0) {
+                const auto Cs = MatOf(C_small, X.rows, hs);
+                stlq::ColMajorMatrix<float> host_xc(hs, X.cols), dev_xc;
+                k->Gemm(true, false, 1.0f, Cs, X, 0.0f, &host_xc);
+                stlq::DeviceMatF32View xv;
+                k->GemmDevice(true, false, 1.0f, Cs, X, 0.0f, &xv);
+                k->DownloadF32(xv, &dev_xc);
+                cached[1] = dev_xc.data == host_xc.data ? 1 : 0;
+            }
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        CopyErr(e, err, errlen);
+        return 1;
+    }
+}
+
+// ArgmaxColsF32 of a host score matrix (rows x cols) uploaded with EnsureDeviceF32.
+extern "C" int prov_argmax(void* p, const float* S, int rows, int cols, int* idx, float* val, char* err, int errlen) {
+    try {
+        auto* k = static_cast<stlq::b200::B200StreamKernels*>(p);
+        const auto Sm = MatOf(S, rows, cols);
+        stlq::DeviceMatF32View v;
+        if (!k->EnsureDeviceF32(Sm, &v)) throw std::runtime_error("EnsureDeviceF32 failed");
+        std::vector<int> a;
+        std::vector<float> b;
+        k->ArgmaxColsF32(v, &a, &b);
+        std::memcpy(idx, a.data(), sizeof(int) * a.size());
+        std::memcpy(val, b.data(), sizeof(float) * b.size());
+        return 0;
+    } catch (const std::exception& e) {
+        CopyErr(e, err, errlen);
+        return 1;
+    }
 }

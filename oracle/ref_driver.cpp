@@ -58,6 +58,8 @@ double Now() {
 
 }  // namespace
 
+extern "C" void openblas_set_num_threads(int);
+
 extern "C" {
 
 const char* ref_blas_core(void) { return openblas_get_corename(); }
@@ -253,6 +255,16 @@ int ref_encode_base(void* h, const float* X, int n, int beam, int icm_iters, int
 // ApplyRotationInPlace's product (src/pipeline/app_utils.cpp:203-227): X_rot = R X with the
 // reference's GemmRaw (no transposes), R d x d and X d x n column-major.  (The identity test that
 // skips it is left to the caller.)
+// The reference's BLAS wrapper as the kernel providers call it (stlq::GemmRaw,
+// src/core/blas.cpp:61-80): column-major sgemm with `threads` BLAS threads.  The thread count goes
+// straight to OpenBLAS: BlasSetThreads caches the last value per copy of blas.cpp, and the tests
+// load two libraries with their own copies over one OpenBLAS.
+void ref_gemm(int trans_a, int trans_b, int m, int n, int k, float alpha, const float* A, int lda, const float* B,
+              int ldb, float beta, float* C, int ldc, int threads) {
+    openblas_set_num_threads(threads);
+    stlq::GemmRaw(trans_a != 0, trans_b != 0, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
 void ref_rotate(const float* R, int d, const float* X, int n, float* out) {
     stlq::ScopedBlasThreads blas_scope(stlq::OmpMaxThreads());
     stlq::GemmRaw(false, false, d, n, d, 1.0f, R, d, X, d, 0.0f, out, d);

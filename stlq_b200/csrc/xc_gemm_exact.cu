@@ -15,6 +15,13 @@
 // steps; a partial last step runs only its kn terms, so no output gets an extra (+0) term.
 // Output layout: xC[vec * ldo + codeword].  ||x||^2 comes from LaunchNorms (same order as the
 // reference's SIMD loop).
+//
+// The same kernel is the general sgemm of the kernel-provider seam (LaunchSgemmExact): with row
+// strides lda / ldb and OpenBLAS's alpha / beta epilogue, C starts at fl(beta * C) (0 when beta is 0)
+// and each K block's chain is folded as C = fma(alpha, chain, C), in block order (the single-thread
+// OpenBLAS 0.3.15 result for every transpose, checked against the reference's GemmRaw).  With
+// alpha = 1 and beta = 0 that is exactly the xC product above.
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -38,8 +45,8 @@ __host__ __device__ __forceinline__ int NextKBlock(int rem) {
 template <typename T>
 struct TileLoader {
     float v[2][4];
-    __device__ __forceinline__ void Load(const T* __restrict__ M, int64_t nrows, int d, int64_t row0, int k0,
-                                         bool vec4) {  // vec4: 4-element loads are aligned
+    __device__ __forceinline__ void Load(const T* __restrict__ M, int64_t nrows, int64_t ld, int d, int64_t row0,
+                                         int k0, bool vec4) {  // row r at M + r * ld; vec4: aligned 4-loads
         const int tid = threadIdx.x;
         const int kq = 4 * (tid & 3);
 #pragma unroll
@@ -47,7 +54,7 @@ struct TileLoader {
             const int64_t r = row0 + (tid >> 2) + 64 * h;
             const int k = k0 + kq;
             if (r < nrows && vec4 && k + 3 < d) {
-                const T* p = M + r * d + k;
+                const T* p = M + r * ld + k;
                 if constexpr (sizeof(T) == 4) {
                     const float4 q = __ldg(reinterpret_cast<const float4*>(p));
                     v[h][0] = q.x, v[h][1] = q.y, v[h][2] = q.z, v[h][3] = q.w;
@@ -58,7 +65,7 @@ struct TileLoader {
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
-                    v[h][c] = (r < nrows && k + c < d) ? static_cast<float>(M[r * d + k + c]) : 0.0f;
+                    v[h][c] = (r < nrows && k + c < d) ? static_cast<float>(M[r * ld + k + c]) : 0.0f;
             }
         }
     }
@@ -73,10 +80,21 @@ struct TileLoader {
     }
 };
 
+// Output element (row i, vector j) of this thread's 8 x 8 tile before the product: fl(beta * C),
+// or 0 when beta is 0 (C not read).
+__device__ __forceinline__ float InitialC(const float* out, int ldo, int r0, int64_t j0, int i, int j, int rows,
+                                         int64_t n, float beta, int tx, int ty) {
+    if (beta == 0.0f) return 0.0f;
+    const int r = r0 + (i < 4 ? tx * 4 + i : 64 + tx * 4 + (i - 4));
+    const int64_t gj = j0 + (j < 4 ? ty * 4 + j : 64 + ty * 4 + (j - 4));
+    return (r < rows && gj < n) ? __fmul_rn(beta, out[gj * ldo + r]) : 0.0f;
+}
+
 template <typename T, bool kMulti>
 __global__ void __launch_bounds__(kGemmThreads, kMulti ? 1 : 2)
     XcGemmExactKernel(const float* __restrict__ C, int rows, int d, const T* __restrict__ X, int64_t n,
-                      float* __restrict__ out, int ldo, bool cvec, bool xvec, bool ovec) {
+                      float* __restrict__ out, int ldo, bool cvec, bool xvec, bool ovec, int64_t ldc_in,
+                      int64_t ldx, float alpha, float beta) {
     __shared__ __align__(16) float Cs[2][kBK][kTM];
     __shared__ __align__(16) float Xs[2][kBK][kTN];
     const int tid = threadIdx.x;
@@ -95,8 +113,8 @@ __global__ void __launch_bounds__(kGemmThreads, kMulti ? 1 : 2)
 
     TileLoader<float> lc;
     TileLoader<T> lx;
-    lc.Load(C, rows, d, r0, 0, cvec);
-    lx.Load(X, n, d, j0, 0, xvec);
+    lc.Load(C, rows, ldc_in, d, r0, 0, cvec);
+    lx.Load(X, n, ldx, d, j0, 0, xvec);
     lc.Store(Cs[0]);
     lx.Store(Xs[0]);
     __syncthreads();
@@ -104,15 +122,18 @@ __global__ void __launch_bounds__(kGemmThreads, kMulti ? 1 : 2)
     for (int s = 0; s < steps; ++s) {
         const int k0 = s * kBK, buf = s & 1;
         if (s + 1 < steps) {
-            lc.Load(C, rows, d, r0, k0 + kBK, cvec);
-            lx.Load(X, n, d, j0, k0 + kBK, xvec);
+            lc.Load(C, rows, ldc_in, d, r0, k0 + kBK, cvec);
+            lx.Load(X, n, ldx, d, j0, k0 + kBK, xvec);
         }
         if (kMulti && k0 == kb_end) {  // a new K block: fold the finished block's chains
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    if constexpr (kMulti) tot[i][j] = first ? part[i][j] : __fadd_rn(tot[i][j], part[i][j]);
+                    if constexpr (kMulti) {
+                        if (first) tot[i][j] = InitialC(out, ldo, r0, j0, i, j, rows, n, beta, tx, ty);
+                        tot[i][j] = __fmaf_rn(alpha, part[i][j], tot[i][j]);
+                    }
                     part[i][j] = 0.0f;
                 }
             first = false;
@@ -151,8 +172,10 @@ __global__ void __launch_bounds__(kGemmThreads, kMulti ? 1 : 2)
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            if constexpr (kMulti) v[i] = first ? part[i][j] : __fadd_rn(tot[i][j], part[i][j]);
-            else v[i] = part[i][j];
+            float c;
+            if constexpr (kMulti) c = first ? InitialC(out, ldo, r0, j0, i, j, rows, n, beta, tx, ty) : tot[i][j];
+            else c = InitialC(out, ldo, r0, j0, i, j, rows, n, beta, tx, ty);
+            v[i] = __fmaf_rn(alpha, part[i][j], c);
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -169,19 +192,23 @@ __global__ void __launch_bounds__(kGemmThreads, kMulti ? 1 : 2)
     }
 }
 
+// C rows at C + r * ldc_in, X rows at X + j * ldx (both contiguous over the d products).
 template <typename T>
-cudaError_t LaunchT(const float* C, int rows, int d, const T* X, int64_t n, float* out, int ldo, cudaStream_t stream) {
+cudaError_t LaunchT(const float* C, int rows, int d, const T* X, int64_t n, float* out, int ldo, cudaStream_t stream,
+                    int64_t ldc_in, int64_t ldx, float alpha = 1.0f, float beta = 0.0f) {
     const int64_t gy = (n + kTN - 1) / kTN;
     if (gy > 65535) return cudaErrorInvalidValue;  // callers slice n
     dim3 grid((rows + kTM - 1) / kTM, static_cast<unsigned>(gy));
-    // Vector loads need every row to start aligned: d % 4 == 0 and an aligned base.
-    const bool cvec = d % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0;
-    const bool xvec = d % 4 == 0 && reinterpret_cast<uintptr_t>(X) % (4 * sizeof(T)) == 0;
+    // Vector loads need every row to start aligned: d and the row stride multiples of 4, an aligned base.
+    const bool cvec = d % 4 == 0 && ldc_in % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0;
+    const bool xvec = d % 4 == 0 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % (4 * sizeof(T)) == 0;
     const bool ovec = ldo % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
     if (d > 448)
-        XcGemmExactKernel<T, true><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, X, n, out, ldo, cvec, xvec, ovec);
+        XcGemmExactKernel<T, true><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, X, n, out, ldo, cvec, xvec, ovec,
+                                                                      ldc_in, ldx, alpha, beta);
     else
-        XcGemmExactKernel<T, false><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, X, n, out, ldo, cvec, xvec, ovec);
+        XcGemmExactKernel<T, false><<<grid, kGemmThreads, 0, stream>>>(C, rows, d, X, n, out, ldo, cvec, xvec, ovec,
+                                                                       ldc_in, ldx, alpha, beta);
     return cudaGetLastError();
 }
 
@@ -191,13 +218,27 @@ cudaError_t LaunchT(const float* C, int rows, int d, const T* X, int64_t n, floa
 cudaError_t LaunchXcGemmExact(const float* C, int rows, int d, const void* X, int x_dtype, int64_t n, float* out,
                               int ldo, float* xnorm2, double* xnorm2_d, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    cudaError_t e = x_dtype == 0 ? LaunchT(C, rows, d, static_cast<const float*>(X), n, out, ldo, stream)
-                                 : LaunchT(C, rows, d, static_cast<const uint8_t*>(X), n, out, ldo, stream);
+    cudaError_t e = x_dtype == 0 ? LaunchT(C, rows, d, static_cast<const float*>(X), n, out, ldo, stream, d, d)
+                                 : LaunchT(C, rows, d, static_cast<const uint8_t*>(X), n, out, ldo, stream, d, d);
     if (e != cudaSuccess) return e;
     if (xnorm2 || xnorm2_d) return LaunchNorms(X, x_dtype, n, d, xnorm2, xnorm2_d, stream);
     return cudaSuccess;
 }
 
 int MaxGemmSliceVectors() { return 65535 * 64; }
+
+// out(rows x n, ldo) = alpha * A B + beta * out with A's rows at A + i * lda and B's columns at
+// B + j * ldb, both contiguous over the k products (an op(A) of a transposed A, an op(B) of a
+// plain B); n is sliced to the grid limit here.
+cudaError_t LaunchSgemmExact(const float* A, int64_t lda, int rows, int k, const float* B, int64_t ldb, int64_t n,
+                             float alpha, float beta, float* out, int ldo, cudaStream_t stream) {
+    const int64_t S = int64_t{65535} * kTN;
+    for (int64_t j0 = 0; j0 < n; j0 += S) {
+        const int64_t nj = std::min<int64_t>(S, n - j0);
+        cudaError_t e = LaunchT(A, rows, k, B + j0 * ldb, nj, out + j0 * ldo, ldo, stream, lda, ldb, alpha, beta);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
 
 }  // namespace stlq_b200
