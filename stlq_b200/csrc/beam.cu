@@ -221,16 +221,17 @@ __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int
 // the upper bounds into hi_out), and the thread's smallest upper bound as the return value.  One copy per layer, inlined (with L a
 // compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
 // call boundary costs more than the copies save).
-template <int MAXM, int L, bool kHi>
+template <int MAXM, int L, bool kHi, bool kWide>
 __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int colL,
                                            const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                                            const float* __restrict__ xc, float* lo, float* hi_out, int check,
                                            unsigned int* err_flag, bool recip) {
     const int tid = threadIdx.x;
     float hmin = PosInf();  // never NaN: a bound is finite or +-inf
-    // Codebooks above 256 codewords are walked in chunks of kMaxK (kCpt codewords per thread).
-    for (int kc = 0; kc < K; kc += kMaxK) {
-        float alpha[kCpt], gamma[kCpt];
+    // Codebooks above 256 codewords (the kWide kernels) are walked in chunks of kMaxK, kCpt
+    // codewords per thread; the other kernels make one pass with kc = 0 known at compile time.
+    for (int kc = 0; kc < (kWide ? K : 1); kc += kMaxK) {
+        float alpha[kCpt], gamma[kCpt], lof[kCpt];
         int col[kCpt];
         bool ok[kCpt];
 #pragma unroll
@@ -240,13 +241,14 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
             col[c] = colL + k;  // Gram column; Gdiag and xc are indexed by the flat index
             alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
             gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
+            lof[c] = IsZeroColumn(alpha[c]) ? PosInf() : -PosInf();
         }
         const float* gq[kCpt];
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
         for (int h = 0; h < curH; ++h) {
             float l[kCpt], hi[kCpt];
-            CheapBounds<MAXM, L>(cur, h, gq, ok, alpha, gamma, l, hi);
+            CheapBounds<MAXM, L>(cur, h, gq, ok, alpha, gamma, lof, l, hi);
 #pragma unroll
             for (int c = 0; c < kCpt; ++c) {
                 if (ok[c]) {
@@ -269,7 +271,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
 template <int MAXM>
 constexpr bool kPairPath = MAXM > 8;
 static_assert(kCpt == 2, "the paired cheap pass takes two codewords per thread");
-template <int MAXM, int L, bool kHi>
+template <int MAXM, int L, bool kHi, bool kWide>
 __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
                                                int offL, int colL, const float* __restrict__ Grow,
                                                const float* __restrict__ Gdiag, const float* __restrict__ xc,
@@ -277,16 +279,18 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
                                                bool recip) {
     const int tid = threadIdx.x;
     float hmin = PosInf();
-    for (int kc = 0; kc < K; kc += 2 * kThreads) {
+    for (int kc = 0; kc < (kWide ? K : 1); kc += 2 * kThreads) {
         const int k = kc + 2 * tid;
         const bool ok = k < K;  // K is even: k + 1 < K as well
         const float2 alpha = ok ? __ldg(reinterpret_cast<const float2*>(Gdiag + offL + k)) : make_float2(0.0f, 0.0f);
         const float2 gamma = ok ? __ldg(reinterpret_cast<const float2*>(xc + offL + k)) : make_float2(0.0f, 0.0f);
+        const float2 lof = make_float2(IsZeroColumn(alpha.x) ? PosInf() : -PosInf(),
+                                       IsZeroColumn(alpha.y) ? PosInf() : -PosInf());
         const float* gq = Grow + colL + k;
         for (int h = 0; h < curH; ++h) {
             float2 l, hi;
             CheapBoundsPair<MAXM, L>(table + h * PairTableStride<MAXM>(), cur.rowh(h), cur.E[h], cur.ill[h] != 0, gq,
-                                     ok, alpha, gamma, l, hi);
+                                     ok, alpha, gamma, lof, l, hi);
             if (ok) {
                 *reinterpret_cast<float2*>(lo + h * K + k) = l;
                 if (kHi) *reinterpret_cast<float2*>(hi_out + h * K + k) = hi;
@@ -305,7 +309,7 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
 }
 
 // `table` non-null: the paired pass (Dims::pair) over the slots' pair tables.
-template <int MAXM, bool kHi>
+template <int MAXM, bool kHi, bool kWide>
 __device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
                                   int check, unsigned int* err, bool recip, const float2* table) {
@@ -314,9 +318,10 @@ __device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, in
         if constexpr (LL < MAXM) {                                                                   \
             if constexpr (kPairPath<MAXM>)                                                           \
                 if (table)                                                                           \
-                    return CheapPassPair<MAXM, LL, kHi>(cur, table, curH, K, offL, colL, Grow, Gdiag, xc, lo, \
+                    return CheapPassPair<MAXM, LL, kHi, kWide>(cur, table, curH, K, offL, colL, Grow, Gdiag, xc, lo, \
                                                         hi_out, check, err, recip);                  \
-            return CheapPass<MAXM, LL, kHi>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err, recip); \
+            return CheapPass<MAXM, LL, kHi, kWide>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err, \
+                                                   recip);                                           \
         }                                                                                            \
         break;
     switch (L) {
@@ -417,7 +422,7 @@ struct Replay {
 // slot), then the reference's replacement scan over the exact errors.  Without room for the upper
 // bounds (his == nullptr: beam x codebook size too large for shared memory) every candidate is
 // evaluated exactly; the scan's result is the same.
-template <int MAXM>
+template <int MAXM, bool kWide>
 __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                             const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt,
@@ -433,7 +438,7 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
                 __syncthreads();
             }
         }
-        CheapDispatch<MAXM, true>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
+        CheapDispatch<MAXM, true, kWide>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
                                   dims.large_root != 0, table);
         __syncthreads();
         if (tid < 32) {
@@ -469,8 +474,10 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     __syncthreads();
 }
 
-// Encodes the vectors listed in vec_list[0 .. *count) (or 0 .. n when vec_list is null).
-template <int MAXM>
+// Encodes the vectors listed in vec_list[0 .. *count) (or 0 .. n when vec_list is null).  kWide
+// (BigCodebooks): a codebook of layers 1..m-1 has more than kMaxK codewords, or layer 0's errors do
+// not fit the candidate array; the other kernels, the common sizes, compile neither case in.
+template <int MAXM, bool kWide>
 __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const float* __restrict__ Grow,
                                                              const float* __restrict__ Gdiag,
                                                              const float* __restrict__ xnorm2,
@@ -495,15 +502,19 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
         // Layer 0 keeps its errors in errs[] when they fit (beam x maxKs floats), else recomputes them.
-        const bool stored0 = K0 <= beam * dims.maxKs;
+        const bool stored0 = !kWide || K0 <= beam * dims.maxKs;
         if (stored0)
             for (int k = tid; k < K0; k += kThreads) errs[k] = Layer0Error(Gdiag, xc, nx2, k);
         __syncthreads();
         if (tid < 32) {
             Replay rp;
             rp.Init(beam);
-            if (stored0) rp.Scan(ArraySource{errs}, K0);
-            else rp.Scan(Layer0Source{Gdiag, xc, nx2}, K0);
+            if constexpr (kWide) {
+                if (stored0) rp.Scan(ArraySource{errs}, K0);
+                else rp.Scan(Layer0Source{Gdiag, xc, nx2}, K0);
+            } else {
+                rp.Scan(ArraySource{errs}, K0);
+            }
             rp.Publish(beam, lt);
         }
         __syncthreads();
@@ -517,7 +528,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         __syncthreads();
         int ci = 0;
         for (int L = 1; L < m; ++L) {
-            ReplayLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
+            ReplayLayer<MAXM, kWide>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
                               SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, his,
                               lt, table);
             ci ^= 1;
@@ -679,7 +690,7 @@ __device__ __noinline__ int RankSurvivors(const float* ex, const uint16_t* surv,
     return min(n_valid, beam);
 }
 
-template <int MAXM>
+template <int MAXM, bool kWide>
 __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
                          const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
                          int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, uint64_t* keys, float* keep,
@@ -693,7 +704,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
         }
     }
     const uint32_t hmin =
-        CheapDispatch<MAXM, false>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
+        CheapDispatch<MAXM, false, kWide>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
                                    dims.large_root != 0, table);
     const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
@@ -719,7 +730,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
     return newH;
 }
 
-template <int MAXM>
+template <int MAXM, bool kWide>
 __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
                                                            const float* __restrict__ Gdiag,
                                                            const float* __restrict__ xnorm2,
@@ -748,15 +759,19 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         const float nx2 = __ldg(xnorm2 + vec);
         // Layer 0: exact errors are cheap; they serve as their own bounds.  They are kept in lo[]
         // when they fit (beam x maxKs floats), else recomputed where the selection reads them.
-        const bool stored0 = K0 <= beam * dims.maxKs;
+        const bool stored0 = !kWide || K0 <= beam * dims.maxKs;
         uint32_t hmin = 0xffffffffu;
         for (int k = tid; k < K0; k += kThreads) {
             const float e1 = Layer0Error(Gdiag, xc, nx2, k);
             if (stored0) lo[k] = e1;
             hmin = min(hmin, OrderKey(e1));
         }
-        int curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
+        int curH;
+        if constexpr (kWide)
+            curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
                            : SelectSurvivors(Layer0Source{Gdiag, xc, nx2}, K0, hmin, beam, lt, surv);
+        else
+            curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
         if (curH >= 0) {
             for (int p = tid; p < curH; p += kThreads)
                 ex[p] = stored0 ? lo[surv[p]] : Layer0Error(Gdiag, xc, nx2, surv[p]);
@@ -772,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         __syncthreads();
         int ci = 0;
         for (int L = 1; L < m && curH > 0; ++L) {
-            curH = FastLayer<MAXM>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
+            curH = FastLayer<MAXM, kWide>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
                                    SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo, lt,
                                    surv, ex, keys, keep, check, err_flag, table);
             ci ^= 1;
@@ -888,21 +903,21 @@ cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* gr
     return cudaSuccess;
 }
 
-template <int MAXM>
+template <int MAXM, bool kWide>
 cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2, const float* xC,
                         int64_t n, int beam, void* Bout, int* redo, int check, unsigned int* err_flag,
                         unsigned long long* stats, int num_sms, cudaStream_t stream) {
     int grid = 0;
     Dims df = dims;
     df.pair = kPairPath<MAXM> && dims.pair &&
-              PairKeepsOccupancy(BeamFastKernel<MAXM>, FastSmemBytes<MAXM>(beam, dims.maxKs),
+              PairKeepsOccupancy(BeamFastKernel<MAXM, kWide>, FastSmemBytes<MAXM>(beam, dims.maxKs),
                                  FastSmemBytes<MAXM>(beam, dims.maxKs, true));
     const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs, df.pair != 0);
-    cudaError_t e = Prepare(BeamFastKernel<MAXM>, fsm, num_sms, n, &grid);
+    cudaError_t e = Prepare(BeamFastKernel<MAXM, kWide>, fsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
-    BeamFastKernel<MAXM><<<grid, kThreads, fsm, stream>>>(df, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
+    BeamFastKernel<MAXM, kWide><<<grid, kThreads, fsm, stream>>>(df, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
                                                           check, err_flag, stats);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -911,14 +926,14 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
     dr.pair = kPairPath<MAXM> && dims.pair && prescan &&
               ReplaySmemBytes<MAXM>(beam, dims.maxKs, true, true) <= MaxBlockSmem();
     const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, dr.pair != 0);
-    e = Prepare(BeamReplayKernel<MAXM>, rsm, num_sms, n, &grid);
+    e = Prepare(BeamReplayKernel<MAXM, kWide>, rsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
-    BeamReplayKernel<MAXM><<<grid, kThreads, rsm, stream>>>(dr, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
+    BeamReplayKernel<MAXM, kWide><<<grid, kThreads, rsm, stream>>>(dr, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
                                                             redo, prescan);
     return cudaGetLastError();
 }
 
-template <int MAXM>
+template <int MAXM, bool kWide>
 cudaError_t PrepareT(const Dims& dims, int beam) {
     // The largest sizes a launch may ask for (the pair tables included when they fit).
     const bool pair = kPairPath<MAXM> && dims.pair != 0;
@@ -927,10 +942,10 @@ cudaError_t PrepareT(const Dims& dims, int beam) {
     const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
     const size_t r1 = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, pair);
     const size_t rsm = r1 <= MaxBlockSmem() ? r1 : ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
-    cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM, kWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(fsm));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(BeamReplayKernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(BeamReplayKernel<MAXM, kWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(rsm));
 }
 
@@ -940,8 +955,16 @@ size_t BeamFastSmemBytes(const Dims& dims, int beam) {
     return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxKs) : FastSmemBytes<16>(beam, dims.maxKs);
 }
 
+// The kWide kernels: a codebook of layers 1..m-1 above kMaxK codewords (chunked cheap passes) or
+// layer-0 errors that do not fit the beam x maxKs candidate array (recomputed from xC).
+bool BigCodebooks(const Dims& dims, int beam) {
+    return dims.maxKs > kMaxK || dims.h_vec[0] > beam * dims.maxKs;
+}
+
 cudaError_t PrepareBeamKernels(const Dims& dims, int beam) {
-    return dims.m <= 8 ? PrepareT<8>(dims, beam) : PrepareT<16>(dims, beam);
+    const bool wide = BigCodebooks(dims, beam);
+    if (dims.m <= 8) return wide ? PrepareT<8, true>(dims, beam) : PrepareT<8, false>(dims, beam);
+    return wide ? PrepareT<16, true>(dims, beam) : PrepareT<16, false>(dims, beam);
 }
 
 // redo: n + 1 ints of scratch (a count, then vector ids handed from the fast to the replay kernel).
@@ -951,11 +974,12 @@ cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* G
     if (n <= 0) return cudaSuccess;
     // The encoder's flag word is followed by four 64-bit counters (BeamStats).
     unsigned long long* stats = err_flag ? reinterpret_cast<unsigned long long*>(err_flag + 4) : nullptr;
-    if (dims.m <= 8)
-        return LaunchBeamT<8>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms,
-                              stream);
-    return LaunchBeamT<16>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms,
-                           stream);
+    const bool wide = BigCodebooks(dims, beam);  // separate kernels: the common sizes keep the simple paths
+#define STLQ_B200_LAUNCH(MM, WW) \
+    LaunchBeamT<MM, WW>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms, stream)
+    if (dims.m <= 8) return wide ? STLQ_B200_LAUNCH(8, true) : STLQ_B200_LAUNCH(8, false);
+    return wide ? STLQ_B200_LAUNCH(16, true) : STLQ_B200_LAUNCH(16, false);
+#undef STLQ_B200_LAUNCH
 }
 
 }  // namespace stlq_b200

@@ -175,9 +175,11 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 }
 
 // The error bounds of one candidate from its cheap delta, eta and seta (see CheapBounds).
+// lof: the lower bound of a forced candidate: -inf, or +inf for a zero codeword, which is always
+// forced (its cheap denominator is -0 - 0) and which the reference always skips.
 template <int L>
 __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta, float eta, float seta, float Eo,
-                                           bool ill, float& lo, float& hi) {
+                                           bool ill, float lof, float& lo, float& hi) {
     // Half-width w = 16 * de with de as documented at CheapBounds; the factor 16 is folded into the
     // constants.
     constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
@@ -190,9 +192,8 @@ __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta
     const float w = fmaf(2.0f * fabsf(diff) * seta + fabsf(r) * (alpha + delta), u16 * fabsf(rden),
                          e16 * (Eo + fabsf(r)));
     const bool force = ill || !(denom > kDenomGuard * alpha) || !(w < PosInf()) || !(ep < PosInf());
-    const bool zero = IsZeroColumn(alpha);
-    lo = zero ? PosInf() : force ? -PosInf() : ep - w;
-    hi = force || zero ? PosInf() : ep + w;
+    lo = force ? lof : ep - w;
+    hi = force ? PosInf() : ep + w;
 }
 
 // Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
@@ -210,7 +211,7 @@ template <int MAXM, int L>
 __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* const (&gq)[kCpt],
                                             const bool (&ok)[kCpt],
                                             const float (&alpha)[kCpt], const float (&gamma)[kCpt],
-                                            float (&lo)[kCpt], float (&hi)[kCpt]) {
+                                            const float (&lof)[kCpt], float (&lo)[kCpt], float (&hi)[kCpt]) {
     const float* Rh = cur.Rh(h);
     const float* rinv = cur.rinvh(h);
     const float* ah = cur.ah(h);
@@ -248,7 +249,8 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     const float Eo = cur.E[h];
     const bool ill = cur.ill[h] != 0;
 #pragma unroll
-    for (int q = 0; q < kCpt; ++q) BoundsTail<L>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, lo[q], hi[q]);
+    for (int q = 0; q < kCpt; ++q)
+        BoundsTail<L>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, lof[q], lo[q], hi[q]);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -283,8 +285,8 @@ __device__ void BuildPairTable(const SlotView<MAXM>& cur, int curH, int L, float
 
 template <int MAXM, int L>
 __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, const int* rw, float Eo, bool ill,
-                                                const float* gq, bool ok, float2 alpha, float2 gamma, float2& lo,
-                                                float2& hi) {
+                                                const float* gq, bool ok, float2 alpha, float2 gamma, float2 lof,
+                                                float2& lo, float2& hi) {
     float2 A[L], y[L];
 #pragma unroll
     for (int i = 0; i < L; ++i)
@@ -304,8 +306,8 @@ __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, 
         seta0 = fmaf(fabsf(A[i].x), fabsf(ai.x), seta0);
         seta1 = fmaf(fabsf(A[i].y), fabsf(ai.x), seta1);
     }
-    BoundsTail<L>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, lo.x, hi.x);
-    BoundsTail<L>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, lo.y, hi.y);
+    BoundsTail<L>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, lof.x, lo.x, hi.x);
+    BoundsTail<L>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, lof.y, lo.y, hi.y);
 }
 
 }  // namespace beam
