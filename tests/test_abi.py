@@ -74,3 +74,24 @@ def test_python_layer_refuses_without_library(monkeypatch, tmp_path):
     monkeypatch.setenv("STLQ_B200_LIB", str(tmp_path / "missing.so"))
     with pytest.raises(stlq_b200.StlqB200Error, match="no CPU fallback"):
         stlq_b200.load_library()
+
+
+def test_kernel_provider_entries_reject_bad_arguments():
+    """The kernel-provider primitives validate on the host: no handle, negative sizes, leading
+    dimensions below the row count."""
+    lib = stlq_b200.load_library()
+    vp, ci = ctypes.c_void_p, ctypes.c_int
+    lib.stlq_b200_sgemm.argtypes = [vp, ci, ci, ci, ci, ci, ctypes.c_float, vp, ci, vp, ci, ctypes.c_float, vp, ci, vp]
+    lib.stlq_b200_u8_to_f32.argtypes = [vp, vp, ci, ci, ctypes.c_int64, vp, vp]
+    lib.stlq_b200_argmax_cols.argtypes = [vp, vp, ci, ci, ctypes.c_int64, vp, vp, vp]
+    lib.stlq_b200_kernels_create.argtypes = [ci, ctypes.POINTER(vp)]
+    assert lib.stlq_b200_sgemm(None, 0, 0, 4, 4, 4, 1.0, None, 4, None, 4, 0.0, None, 4, None) == 1
+    assert b"handle is null" in lib.stlq_b200_last_error()
+    assert lib.stlq_b200_u8_to_f32(None, None, 4, 4, 4, None, None) == 1
+    assert lib.stlq_b200_argmax_cols(None, None, 4, 4, 4, None, None, None) == 1
+    out = vp()
+    rc = lib.stlq_b200_kernels_create(-1, ctypes.byref(out))
+    assert rc != 0 and not out.value
+    if rc == 1:
+        assert b"device ordinal" in lib.stlq_b200_last_error()
+    assert lib.stlq_b200_kernels_destroy(None) == 0
