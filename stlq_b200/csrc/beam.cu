@@ -377,6 +377,30 @@ struct Replay {
             }
         }
     }
+    // Scan over the candidates list[0..n) only (their indices, in scan order), every other
+    // candidate's error being +inf: +inf never enters (it is not below any worst), so the
+    // replacement history, slot order included, is Scan's over all candidates.
+    __device__ void ScanList(const float* errs, const int* list, int n) {
+        const int lane = threadIdx.x & 31;
+        for (int base = 0; base < n; base += 32) {
+            const int idx = base + lane < n ? list[base + lane] : -1;
+            const float e = idx >= 0 ? errs[idx] : PosInf();
+            unsigned mask = __ballot_sync(kFull, e < worst);
+            while (mask) {
+                const int l = __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float el = __shfl_sync(kFull, e, l);
+                const int il = __shfl_sync(kFull, idx, l);
+                if (el < worst) {
+                    if (lane == widx) {
+                        es = el;
+                        cs = il;
+                    }
+                    Refresh();
+                }
+            }
+        }
+    }
     // Pre-scan on the cheap bounds.  Scanning hi[] with the same rule makes `worst` the B-th
     // smallest upper bound of the prefix, an upper bound of the exact scan's worst at the same
     // position (each exact error is <= its hi).  A candidate whose lo is not below that bound at the
@@ -460,7 +484,8 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     if (tid < 32) {
         Replay rp;
         rp.Init(beam);
-        rp.Scan(ArraySource{errs}, n_cand);
+        if (his) rp.ScanList(errs, list, need);  // the pre-scan's candidates, in scan order
+        else rp.Scan(ArraySource{errs}, n_cand);
         rp.Publish(beam, lt);
     }
     __syncthreads();
