@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import shutil
 import subprocess
 
 import numpy as np
@@ -58,6 +59,8 @@ def build(reference: bool = True) -> None:
         targets.append("ref")
         if os.path.exists(os.path.join(os.path.dirname(HERE), "stlq_b200", "libstlq_b200.so")):
             targets.append("adapter")
+        if shutil.which("nvcc") or os.path.exists("/usr/local/cuda/bin/nvcc"):
+            targets.append("refcuda")  # the reference's own CUDA ICM, for timing against ours
     env = dict(os.environ)
     if "STLQ_REF_DIR" in env:
         env["REF"] = env["STLQ_REF_DIR"]
@@ -335,6 +338,45 @@ class RefPrecomp:
 
 
 ADAPTER_SO = os.path.join(HERE, "_ref", "libstlq_adapter_test.so")
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libstlq_ref_cuda.so")
+
+
+class RefCudaIcm:
+    """The reference's own CUDA ICM (DynamicIcmWithIls*NoNormalCuda, icm_cuda.cu compiled for
+    sm_100a by the Makefile's refcuda target), on a Precomp built by the reference."""
+
+    def __init__(self, path: str = REF_CUDA_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: build it with `make -C oracle refcuda`")
+        self.lib = ctypes.CDLL(path)
+        self.lib.ref_precomp_create.restype = ctypes.c_void_p
+        self.lib.ref_precomp_destroy.argtypes = [ctypes.c_void_p]
+
+    def precomp(self, h_vec, C_all):
+        h = np.asarray(h_vec, np.int32)
+        C = _f32(C_all)
+        return ctypes.c_void_p(self.lib.ref_precomp_create(C.shape[1], len(h), _p(h, _i32p), _p(C, _f32p)))
+
+    def icm(self, pre, m, X, xC, B, icm_iters, ils_iters=0, perturb_k=0, use_abs=True, seed=38251450,
+            sample_id_offset=0):
+        """Returns (B, a, cost, timing): timing = seconds of uploads, B upload, initial ICM, ILS
+        copy+perturb, ILS ICM, ILS accept, downloads, as the reference's CudaIcmTiming reports them."""
+        X, xC = _f32(X), _f32(xC)
+        n = X.shape[0]
+        Bo = np.array(B, np.uint8, copy=True, order="C")
+        a = np.empty((n, m), np.float32)
+        cost = np.empty(n, np.float32)
+        t = np.zeros(7, np.float64)
+        rc = self.lib.ref_icm_cuda(pre, _p(X, _f32p), n, _p(xC, _f32p), int(icm_iters), int(ils_iters),
+                                   int(perturb_k), int(bool(use_abs)), ctypes.c_uint32(seed),
+                                   ctypes.c_uint64(sample_id_offset), _p(Bo, _u8p), _p(a, _f32p), _p(cost, _f32p),
+                                   _p(t, _f64p))
+        if rc:
+            raise RuntimeError("ref_icm_cuda failed")
+        return Bo, a, cost, t
+
+    def release(self, pre):
+        self.lib.ref_precomp_destroy(pre)
 
 
 class AdapterHarness:

@@ -28,6 +28,7 @@ namespace stlq_b200 {
 namespace {
 
 constexpr int kWarps = 4;
+constexpr int kScoreT = 8;  // ICM codewords per lane held in registers (a chunk of 256 per warp)
 constexpr int kRefineThreads = 32 * kWarps;
 
 struct WarpState {
@@ -116,7 +117,7 @@ __device__ void RestoreGram(int m, int j, float* Gs, const float* bak) {
 }
 
 // Fixed-size Cholesky for m in {5, 10} (CholeskyUpperFixed, least_squares.cpp:44-66), row-major.
-__device__ bool CholFixed(float* A, int m) {
+__device__ __noinline__ bool CholFixed(float* A, int m) {
     for (int k = 0; k < m; ++k) {
         float sum = A[k * m + k];
         for (int j = 0; j < k; ++j) {
@@ -175,7 +176,7 @@ __device__ float PotfLeftover(float y, const float* a, const float* x, int m1, i
     return add_rn(y, e);
 }
 
-__device__ bool CholLapack(float* A, int m) {  // column-major A[r + c*m], upper triangle
+__device__ __noinline__ bool CholLapack(float* A, int m) {  // column-major A[r + c*m], upper triangle
     for (int j = 0; j < m; ++j) {
         const float* xj = A + j * m;
         double acc = 0.0;
@@ -227,7 +228,7 @@ __device__ void TrsmBwdBlock(const float* A, int m, float* c, int r0, int bs) {
     }
 }
 
-__device__ void SolveLapack(const float* A, int m, float* c) {  // U^T y = b, U x = y, in place
+__device__ __noinline__ void SolveLapack(const float* A, int m, float* c) {  // U^T y = b, U x = y, in place
     constexpr int UM = 16;
     int kk = 0;
     for (int b = 0; b < m / UM; ++b) {
@@ -258,8 +259,11 @@ __device__ void SolveLapack(const float* A, int m, float* c) {  // U^T y = b, U 
 }
 
 // One vector's LS solve with the reference's retry policy (3 diagonal bumps 1e-6 x10^i).
+// Out of line, like the other per-vector serial routines of this file: inlined at every call site
+// (initial solve, each ICM change, each ILS round) they made the kernel large enough for
+// instruction fetch to be its main stall.
 template <class Gram>
-__device__ bool SolveLs(const Dims& dims, const Gram& G, const float* xc, const int* code, WarpState& ws,
+__device__ __noinline__ bool SolveLs(const Dims& dims, const Gram& G, const float* xc, const int* code, WarpState& ws,
                         float* a_out) {
     const int m = dims.m;
     const bool fixed = (m == 5 || m == 10);
@@ -304,7 +308,7 @@ __device__ bool SolveLs(const Dims& dims, const Gram& G, const float* xc, const 
 
 // SampleCost (cost_utils.cpp:112-137).
 template <class Gram>
-__device__ float SampleCost(const Dims& dims, const Gram& G, const float* xc, const int* code, const float* a,
+__device__ __noinline__ float SampleCost(const Dims& dims, const Gram& G, const float* xc, const int* code, const float* a,
                             float xn2) {
     const int m = dims.m;
     float term1 = 0.0f, term2 = 0.0f;
@@ -321,7 +325,7 @@ __device__ float SampleCost(const Dims& dims, const Gram& G, const float* xc, co
 // xc[flat_0] holds the reference's SIMD-order dot of the root codeword with x (LaunchRootDot) and
 // G(0, 0) the root codeword's norm0.
 template <class Gram>
-__device__ float SampleCostLargeRoot(const Dims& dims, const Gram& G, const float* xc, const int* code,
+__device__ __noinline__ float SampleCostLargeRoot(const Dims& dims, const Gram& G, const float* xc, const int* code,
                                      const float* a, float xn2) {
     const int m = dims.m;
     float term1 = mul_rn(a[0], xc[dims.off[0] + code[0]]);
@@ -373,7 +377,7 @@ __device__ __forceinline__ uint32_t UniformBelow(SplitMix64& r, uint32_t bound) 
 // One RunIcm call (icm.cpp:89-344) on `code` (in/out) for the warp's vector; a and cost out.
 // With do_init false the caller has already solved LS and the cost for `code` (RunIcm's first
 // step, icm.cpp:109-114), so only the sweeps run.
-__device__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc, float xn2,
+__device__ __noinline__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc, float xn2,
                            int icm_iters, const int* orders, bool use_abs, int* code, float* a, float* cost,
                            WarpState& ws, bool do_init = true) {
     const int lane = threadIdx.x & 31;
@@ -397,22 +401,41 @@ __device__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, const float* inv
             if (j == 0 || hj <= 1) continue;
             const int startf = dims.off[j];
             const int old_code = code[j];
-            // score(t) = (xC(t) - sum_{l != j} a_l G(t, flat_l)) * invnorm(t)   (icm.cpp:272-300)
+            // score(t) = (xC(t) - sum_{l != j} a_l G(t, flat_l)) * invnorm(t)   (icm.cpp:272-300).
+            // Each lane holds kScoreT codewords t = t0 + lane + 32 i; the layers l run outermost
+            // (the same per-t subtraction order), so a lane's kScoreT gathers of one Gram row are
+            // issued together instead of one L2 round trip per term.
             float best_s = __int_as_float(0xff800000);  // -inf
             int best_t = 0x7fffffff;
-            for (int t = lane; t < hj; t += 32) {
-                float v = xc[startf + t];
+            for (int t0 = 0; t0 < hj; t0 += 32 * kScoreT) {
+                float v[kScoreT];
+#pragma unroll
+                for (int i = 0; i < kScoreT; ++i) {
+                    const int t = t0 + lane + 32 * i;
+                    v[i] = t < hj ? xc[startf + t] : 0.0f;
+                }
                 for (int l = 0; l < m; ++l) {
                     if (l == j) continue;
-                    const int fl = dims.off[l] + code[l];
-                    // G(startf + t, fl): codebook j >= 1, so the row is always stored (>= c0).
-                    v = sub_rn(v, mul_rn(a[l], __ldg(Gr.g + static_cast<size_t>(fl) * Gr.ldg + (startf - Gr.c0) + t)));
+                    const float al = a[l];
+                    // G(startf + t, flat_l): codebook j >= 1, so the row is always stored (>= c0).
+                    const float* grow = Gr.g + static_cast<size_t>(dims.off[l] + code[l]) * Gr.ldg +
+                                        (startf - Gr.c0) + t0 + lane;
+                    float g[kScoreT];
+#pragma unroll
+                    for (int i = 0; i < kScoreT; ++i) g[i] = t0 + lane + 32 * i < hj ? __ldg(grow + 32 * i) : 0.0f;
+#pragma unroll
+                    for (int i = 0; i < kScoreT; ++i) v[i] = sub_rn(v[i], mul_rn(al, g[i]));
                 }
-                const float val = mul_rn(v, __ldg(invnorm + startf + t));
-                const float s = use_abs ? fabsf(val) : val;
-                if (s > best_s) {  // first strict maximum in t order
-                    best_s = s;
-                    best_t = t;
+#pragma unroll
+                for (int i = 0; i < kScoreT; ++i) {
+                    const int t = t0 + lane + 32 * i;
+                    if (t >= hj) continue;
+                    const float val = mul_rn(v[i], __ldg(invnorm + startf + t));
+                    const float s = use_abs ? fabsf(val) : val;
+                    if (s > best_s) {  // first strict maximum in t order (t increases with i and t0)
+                        best_s = s;
+                        best_t = t;
+                    }
                 }
             }
 #pragma unroll
@@ -459,7 +482,7 @@ __device__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, const float* inv
 
 
 
-__global__ void __launch_bounds__(kRefineThreads) RefineKernel(RefineArgs p) {
+__global__ void __launch_bounds__(kRefineThreads, 4) RefineKernel(RefineArgs p) {
     __shared__ WarpState wss[kWarps];
     __shared__ double sse_w[kWarps][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
