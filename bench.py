@@ -40,6 +40,9 @@ def parse_args():
     p.add_argument("--k", type=int, default=256)
     p.add_argument("--beam", type=int, default=16)
     p.add_argument("--icm", type=int, default=1)
+    p.add_argument("--data", choices=["sift", "deep", "gist"], default="sift",
+                   help="seeded generator: SIFT-like integers 0..255 (configs 0, 3, 4 and the headline), "
+                        "Deep-like unit-norm (config 1, D=96), GIST-like in [0, 1] (config 2, D=960)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the CPU-baseline sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
@@ -69,12 +72,24 @@ def load_measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def base_vectors(args, n, seed, start=0):
+    """n base vectors of the chosen generator; `start` selects a later part of the set (a rank's
+    shard).  The SIFT-like stream is sliced; the other generators draw each shard from its own
+    seed."""
+    from stlq_b200 import synth
+
+    if args.data == "sift":
+        return synth.sift_like(n, d=args.d, seed=seed, start=start)
+    gen = synth.deep_like if args.data == "deep" else synth.gist_like
+    return gen(n, d=args.d, seed=seed + 7919 * (start // max(n, 1)))
+
+
 def make_codebooks(args, device):
     """Seeded residual k-means on a 50,000-vector subsample (seed 0): the stand-in for codebooks
     frozen from the reference's trainer."""
     from stlq_b200 import synth
 
-    train = synth.sift_like(50_000, d=args.d, seed=0)
+    train = base_vectors(args, 50_000, 0)
     books = synth.train_rvq(train, args.m, args.k, iters=8, seed=0, device=device)
     return synth.flatten_books(books)
 
@@ -191,7 +206,7 @@ def run_reference(args):
 
     dev = "cuda" if torch.cuda.is_available() else None
     C = make_codebooks(args, dev)
-    X = synth.sift_like(min(args.n, 200_000), d=args.d, seed=4)
+    X = base_vectors(args, min(args.n, 200_000), 4)
     import oracle
 
     ref = oracle.Reference(threads=os.cpu_count())
@@ -215,7 +230,7 @@ def run_reference(args):
         "impl": "reference", "metric": "encoded vectors/sec", "value": value, "unit": "vectors/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.n} x D={args.d} f32 (SIFT-like, seed 4), M={args.m}, K={args.k}, "
+        "config": {"workload": f"{args.n} x D={args.d} f32 ({args.data.upper()}-like, seed 4), M={args.m}, K={args.k}, "
                                f"beam={args.beam}, ICM={args.icm}, ILS=0; reference CPU encoder on a "
                                f"{per_step}-vector sample per step",
                    "cache": "sample per step"},
@@ -323,7 +338,7 @@ def run_ours(args):
     enc = stlq_b200.Encoder(C_np, h_vec, device=local)
     n = args.n
     offset = rank * n
-    X_np = synth.sift_like(n, d=args.d, seed=4, start=offset)
+    X_np = base_vectors(args, n, 4, start=offset)
     X = torch.from_numpy(X_np).to(device)
     B = torch.empty((n, args.m), dtype=torch.uint8, device=device)
     a = torch.empty((n, args.m), dtype=torch.float32, device=device)
@@ -474,11 +489,12 @@ def run_ours(args):
             "metric": "encoded vectors/sec", "value": value, "unit": "vectors/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded SIFT-like D=128, values 0..255; codebooks: seeded residual k-means)",
+            "data": f"synthetic (seeded {args.data.upper()}-like D={args.d}; codebooks: seeded residual k-means)",
             "config": {"workload": f"{n} x D={args.d} f32 per GPU, M={args.m}, K={args.k}, beam={args.beam}, "
                                    f"ICM={args.icm}, ILS=0, use_abs, seed 38251450",
                        "vectors_per_gpu": n, "gemm_mode": "exact",
-                       "cache": "inputs larger than L2 (X 512 MB, xC 2 GiB per slice)",
+                       "cache": f"inputs larger than L2 (X {X_np.nbytes / 2**20:.0f} MiB per GPU, xC up to 2 GiB "
+                                "per slice)",
                        "parallelism": f"dp{world} (shards of base vectors)"},
             "gpu_launches": launches_per_step * args.steps,
             "mse": total_mse,
@@ -640,7 +656,7 @@ def run_gemm_only(args):
     device = torch.device("cuda", 0)
     C = make_codebooks(args, device)
     enc = stlq_b200.Encoder(C, [args.k] * args.m, device=0, gemm_mode=args.gemm_only)
-    X = torch.from_numpy(synth.sift_like(min(args.n, 262_144), d=args.d, seed=4)).to(device)
+    X = torch.from_numpy(base_vectors(args, min(args.n, 262_144), 4)).to(device)
     for _ in range(3):
         xc = enc.xc_gemm(X)
     torch.cuda.synchronize()
