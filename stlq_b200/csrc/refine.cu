@@ -45,6 +45,23 @@ struct WarpState {
     float Gbak[2 * kMaxM];    // row and column of a trial code change, for the rollback
 };
 
+// One lane's scratch for the solve of GroupStart (local memory: the lanes' copies interleave,
+// so a warp's accesses to one element coalesce).
+struct LaneScratch {
+    float A[kMaxM * kMaxM];
+    float b[kMaxM];
+    float x[kMaxM];
+    float y[kMaxM];
+};
+
+// Results of GroupStart for the 32 vectors of a warp's group, lane-major, in global scratch (one
+// per warp of the grid): kept in shared memory they took L1 capacity the ICM gathers use.
+struct GroupState {
+    float a[kMaxM][32];
+    float cost[32];
+    double sse[32];
+};
+
 // G(row, col) of two flat indices from the refinement's Gram array: G(r, c), r >= c0, at
 // g[c * ldg + (r - c0)] (the layout is described with Dims).  Regular encoders have c0 = 0; in a
 // large-root encoder a root row is read through symmetry, and two root codewords are only ever
@@ -262,8 +279,8 @@ __device__ __noinline__ void SolveLapack(const float* A, int m, float* c) {  // 
 // Out of line, like the other per-vector serial routines of this file: inlined at every call site
 // (initial solve, each ICM change, each ILS round) they made the kernel large enough for
 // instruction fetch to be its main stall.
-template <class Gram>
-__device__ __noinline__ bool SolveLs(const Dims& dims, const Gram& G, const float* xc, const int* code, WarpState& ws,
+template <class Gram, class Scratch>
+__device__ __noinline__ bool SolveLs(const Dims& dims, const Gram& G, const float* xc, const int* code, Scratch& ws,
                         float* a_out) {
     const int m = dims.m;
     const bool fixed = (m == 5 || m == 10);
@@ -478,94 +495,119 @@ __device__ __noinline__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, con
     }
 }
 
+// RunIcm's first step (icm.cpp:109-114), or with mode 0 the whole LS stage, for the vector of
+// each lane: lane i takes vec0 + i * stride (the warp's next 32 vectors), solves LS and the cost
+// serially from the global Gram, and leaves a, cost and the beam-stage SSE term in gs (mode 0:
+// a straight to p.a).  The same routines and the same Gram values as the warp's own solve, so the
+// results are identical; the serial solves run 32 at a time instead of on lane 0 alone.
+__device__ __noinline__ void GroupStart(const RefineArgs& p, const GramRef& Gr, int64_t vec0, int64_t stride,
+                                        GroupState* gs) {
+    const Dims& dims = p.dims;
+    const int m = dims.m, lane = threadIdx.x & 31;
+    const int64_t vec = vec0 + lane * stride;
+    if (vec >= p.n) return;
+    int code[kMaxM];
+    float a[kMaxM];
+    LaneScratch sc;
+    for (int l = 0; l < m; ++l) code[l] = LoadCode(p.B, vec * m + l, dims.wide);
+    const float* xc = p.xC + vec * dims.H;
+    const GramGlobal G{Gr, dims.off, code};
+    if (!SolveLs(dims, G, xc, code, sc, a))
+        for (int l = 0; l < m; ++l) a[l] = 0.0f;
+    if (p.mode == 0) {
+        for (int l = 0; l < m; ++l) p.a[vec * m + l] = a[l];
+        return;
+    }
+    const float c = Cost(dims, G, xc, code, a, p.xnorm2[vec]);
+    for (int l = 0; l < m; ++l) gs->a[l][lane] = a[l];
+    gs->cost[lane] = c;
+    // Beam-stage error: MeanMseFromPrecomp's term, or for a large-root encoder the float cost
+    // itself (the large pipeline averages ComputeCostsLargeRoot, encode_base_streaming.cpp:301-311).
+    if (p.partials)
+        gs->sse[lane] = dims.large_root ? static_cast<double>(c) : VectorSse(dims, G, xc, code, a, p.xnorm2_d[vec]);
+}
+
 }  // namespace
-
-
 
 __global__ void __launch_bounds__(kRefineThreads, 4) RefineKernel(RefineArgs p) {
     __shared__ WarpState wss[kWarps];
     __shared__ double sse_w[kWarps][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WarpState& ws = wss[warp];
+    GroupState* gs = p.mode == 0 ? nullptr : static_cast<GroupState*>(p.group) + blockIdx.x * kWarps + warp;
     const Dims& dims = p.dims;
     const int m = dims.m;
     const GramRef Gr = MakeGram(dims, p.Gcol, p.Gdiag);
     double sse_beam = 0.0, sse_final = 0.0;
-    for (int64_t vec = static_cast<int64_t>(blockIdx.x) * kWarps + warp; vec < p.n;
-         vec += static_cast<int64_t>(gridDim.x) * kWarps) {
-        const float* xc = p.xC + vec * dims.H;
-        if (lane < m) ws.code[lane] = LoadCode(p.B, vec * m + lane, dims.wide);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    // The warp's vectors are blockIdx.x * kWarps + warp + i * stride, taken 32 at a time: the
+    // group's solves run lane-parallel (GroupStart), then the warp refines them one by one.
+    for (int64_t g0 = static_cast<int64_t>(blockIdx.x) * kWarps + warp; g0 < p.n; g0 += 32 * stride) {
         __syncwarp();
-        if (p.mode == 0) {
-            LoadGram(dims, Gr, ws.code, ws.Gs);
-            if (lane == 0) {
-                if (!SolveLs(dims, GramShared{ws.Gs, m}, xc, ws.code, ws, ws.a))
-                    for (int l = 0; l < m; ++l) ws.a[l] = 0.0f;
+        GroupStart(p, Gr, g0, stride, gs);
+        __syncwarp();
+        if (p.mode == 0) continue;
+        for (int gi = 0; gi < 32 && g0 + gi * stride < p.n; ++gi) {
+            const int64_t vec = g0 + gi * stride;
+            const float* xc = p.xC + vec * dims.H;
+            if (lane < m) {
+                ws.code[lane] = LoadCode(p.B, vec * m + lane, dims.wide);
+                ws.a[lane] = gs->a[lane][gi];
             }
-            __syncwarp();
-            if (lane < m) p.a[vec * m + lane] = ws.a[lane];
-            __syncwarp();
-            continue;
-        }
-        const float xn2 = p.xnorm2[vec];
-        float cost = 0.0f;
-        // RunIcm's first step recomputes LS and cost for the beam codes (icm.cpp:109-114); with
-        // the MSE requested, the LS result is also the beam-stage coefficients.
-        RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, 0, p.orders, p.use_abs, ws.code, ws.a, &cost, ws);
-        // Beam-stage error: MeanMseFromPrecomp's term, or for a large-root encoder the float cost
-        // itself (the large pipeline averages ComputeCostsLargeRoot, encode_base_streaming.cpp:301-311).
-        if (p.partials && lane == 0)
-            sse_beam += dims.large_root ? static_cast<double>(cost)
-                                        : VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
-        __syncwarp();
-        if (p.icm_iters > 0)
-            RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
-                       /*do_init=*/false);
-        cost = __shfl_sync(0xffffffffu, cost, 0);
-        const int ksel = min(p.perturb_k, m);
-        for (int outer = 0; outer < p.n_ils; ++outer) {
-            if (lane < m) ws.cand[lane] = ws.code[lane];
-            __syncwarp();
-            if (lane == 0) {  // icm.cpp:953-972
-                const uint64_t ig = p.sample_id_offset + static_cast<uint64_t>(vec);
-                SplitMix64 r{static_cast<uint64_t>(p.seed) ^ (static_cast<uint64_t>(outer + 1) * 0x9e3779b97f4a7c15ULL) ^
-                             ((ig + 1) * 0xbf58476d1ce4e5b9ULL)};
-                for (int s = 0; s < ksel; ++s) {
-                    const int layer = 1 + static_cast<int>(UniformBelow(r, static_cast<uint32_t>(m - 1)));
-                    const int h = dims.h_vec[layer];
-                    if (h <= 1) continue;
-                    const int old_code = ws.cand[layer];
-                    const int raw = static_cast<int>(UniformBelow(r, static_cast<uint32_t>(h - 1)));
-                    ws.cand[layer] = raw >= old_code ? raw + 1 : raw;
+            LoadGram(dims, Gr, ws.code, ws.Gs);  // syncs the warp before and after
+            const float xn2 = p.xnorm2[vec];
+            float cost = gs->cost[gi];
+            if (p.partials && lane == 0) sse_beam += gs->sse[gi];
+            if (p.icm_iters > 0)
+                RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
+                           /*do_init=*/false);
+            cost = __shfl_sync(0xffffffffu, cost, 0);
+            const int ksel = min(p.perturb_k, m);
+            for (int outer = 0; outer < p.n_ils; ++outer) {
+                if (lane < m) ws.cand[lane] = ws.code[lane];
+                __syncwarp();
+                if (lane == 0) {  // icm.cpp:953-972
+                    const uint64_t ig = p.sample_id_offset + static_cast<uint64_t>(vec);
+                    SplitMix64 r{static_cast<uint64_t>(p.seed) ^
+                                 (static_cast<uint64_t>(outer + 1) * 0x9e3779b97f4a7c15ULL) ^
+                                 ((ig + 1) * 0xbf58476d1ce4e5b9ULL)};
+                    for (int s = 0; s < ksel; ++s) {
+                        const int layer = 1 + static_cast<int>(UniformBelow(r, static_cast<uint32_t>(m - 1)));
+                        const int h = dims.h_vec[layer];
+                        if (h <= 1) continue;
+                        const int old_code = ws.cand[layer];
+                        const int raw = static_cast<int>(UniformBelow(r, static_cast<uint32_t>(h - 1)));
+                        ws.cand[layer] = raw >= old_code ? raw + 1 : raw;
+                    }
                 }
-            }
-            __syncwarp();
-            float ccost = 0.0f;
-            RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters,
-                       p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, ws.cand, ws.acand,
-                       &ccost, ws);
-            ccost = __shfl_sync(0xffffffffu, ccost, 0);
-            if (add_rn(ccost, kIcmEps) < cost) {  // icm.cpp:979-990
-                if (lane < m) {
-                    ws.code[lane] = ws.cand[lane];
-                    ws.a[lane] = ws.acand[lane];
+                __syncwarp();
+                float ccost = 0.0f;
+                RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters,
+                           p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, ws.cand, ws.acand,
+                           &ccost, ws);
+                ccost = __shfl_sync(0xffffffffu, ccost, 0);
+                if (add_rn(ccost, kIcmEps) < cost) {  // icm.cpp:979-990
+                    if (lane < m) {
+                        ws.code[lane] = ws.cand[lane];
+                        ws.a[lane] = ws.acand[lane];
+                    }
+                    cost = ccost;
                 }
-                cost = ccost;
+                __syncwarp();
             }
+            if (p.partials && dims.large_root) {
+                if (lane == 0) sse_final += static_cast<double>(cost);
+            } else if (p.partials) {
+                if (p.n_ils > 0) LoadGram(dims, Gr, ws.code, ws.Gs);  // the cache holds the last ILS candidate
+                if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
+            }
+            if (lane < m) {
+                StoreCode(p.B, vec * m + lane, ws.code[lane], dims.wide);
+                if (p.a) p.a[vec * m + lane] = ws.a[lane];
+            }
+            if (lane == 0 && p.cost) p.cost[vec] = cost;
             __syncwarp();
         }
-        if (p.partials && dims.large_root) {
-            if (lane == 0) sse_final += static_cast<double>(cost);
-        } else if (p.partials) {
-            if (p.n_ils > 0) LoadGram(dims, Gr, ws.code, ws.Gs);  // the cache holds the last ILS candidate
-            if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
-        }
-        if (lane < m) {
-            StoreCode(p.B, vec * m + lane, ws.code[lane], dims.wide);
-            if (p.a) p.a[vec * m + lane] = ws.a[lane];
-        }
-        if (lane == 0 && p.cost) p.cost[vec] = cost;
-        __syncwarp();
     }
     if (p.partials) {
         if (lane == 0) {
@@ -668,6 +710,8 @@ cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, c
 }
 
 int RefineWarpsPerBlock() { return kWarps; }
+
+size_t RefineGroupBytes() { return sizeof(GroupState); }
 
 // Large-root outputs from the internal m x n codes: cluster id (the root code) and the (m-1) small
 // codes of each vector (BeamSearchPrefixLSLargeRoot's cluster_id / B_small, beam_search.h:26-32).
