@@ -139,7 +139,7 @@ struct stlq_b200_encoder {
     DevBuf Rrow;
     bool rotate = false;
     // Per-call scratch, grown on demand and kept for the handle's lifetime.
-    DevBuf xC, xn, xnd, partials, group, orders, redo, Xhi, Xlo, Bfull, Xrot;
+    DevBuf xC, xn, xnd, partials, orders, redo, Xhi, Xlo, Bfull, Xrot;
     std::vector<int> orders_host;
     int64_t orders_key[4] = {-1, -1, -1, -1};
     // Host path.
@@ -168,12 +168,6 @@ int RefineGrid(const stlq_b200_encoder* enc, int64_t n) {
     const int64_t per_block = stlq_b200::RefineWarpsPerBlock();
     const int64_t want = (n + per_block - 1) / per_block;
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t{enc->num_sms} * 16)));
-}
-
-// The refinement kernel's per-warp scratch for a grid of `grid` CTAs.
-int EnsureRefineGroup(stlq_b200_encoder* enc, int grid) {
-    return enc->group.Ensure(static_cast<size_t>(grid) * stlq_b200::RefineWarpsPerBlock() *
-                             stlq_b200::RefineGroupBytes());
 }
 
 int CheckEnc(const stlq_b200_encoder* enc) {
@@ -267,7 +261,6 @@ int EnsureScratch(stlq_b200_encoder* enc, int64_t slice) {
     STLQ_TRY(enc->xn.Ensure(static_cast<size_t>(slice) * sizeof(float)));
     STLQ_TRY(enc->xnd.Ensure(static_cast<size_t>(slice) * sizeof(double)));
     STLQ_TRY(enc->partials.Ensure(static_cast<size_t>(RefineGrid(enc, slice)) * 2 * sizeof(double)));
-    STLQ_TRY(EnsureRefineGroup(enc, RefineGrid(enc, slice)));
     STLQ_TRY(enc->redo.Ensure(static_cast<size_t>(slice + 1) * sizeof(int)));
     return 0;
 }
@@ -325,7 +318,6 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         ra.a = a ? a + s0 * dims.m : nullptr;
         ra.cost = cost ? cost + s0 : nullptr;
         ra.partials = sse_dev ? enc->partials.as<double>() : nullptr;
-        ra.group = enc->group.p;
         const int grid = RefineGrid(enc, ns);
         STLQ_CK(stlq_b200::LaunchRefine(ra, grid, stream));
         if (sse_dev) STLQ_CK(stlq_b200::LaunchReducePartials(enc->partials.as<double>(), grid, sse_dev, stream));
@@ -525,7 +517,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
     for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->Bdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
-                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->Xrot, &enc->Rrow, &enc->xnd, &enc->partials, &enc->group, &enc->orders, &enc->redo, &enc->sse_d})
+                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->Xrot, &enc->Rrow, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
         enc->xin[i].Release();
@@ -906,10 +898,7 @@ int stlq_b200_icm(stlq_b200_encoder* enc, const float* xC_dev, const float* xnor
     ra.B = B_dev;
     ra.a = a_dev;
     ra.cost = cost_dev;
-    const int grid = RefineGrid(enc, n);
-    STLQ_TRY(EnsureRefineGroup(enc, grid));
-    ra.group = enc->group.p;
-    STLQ_CK(stlq_b200::LaunchRefine(ra, grid, s));
+    STLQ_CK(stlq_b200::LaunchRefine(ra, RefineGrid(enc, n), s));
     return 0;
 }
 

@@ -49,7 +49,6 @@ struct RefineArgs {
     float* a;
     float* cost;
     double* partials;  // [grid][2] (beam SSE, final SSE) or null
-    void* group;       // mode 1: scratch of RefineGroupBytes() per warp of the grid
 };
 
 cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream);
@@ -57,7 +56,6 @@ cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* ou
 cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, const float* xC, const double* xnorm2_d,
                       const void* B, const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
 int RefineWarpsPerBlock();
-size_t RefineGroupBytes();
 
 // Loads both beam kernels and sets their shared-memory attributes (no launch).
 cudaError_t PrepareBeamKernels(const Dims& dims, int beam);

@@ -12,11 +12,11 @@
 // without returning to the host: the reference launches one kernel per layer per sweep and
 // copies state through the host between them (icm_cuda_kernels.inc:2183-2261).
 //
-// Layout: one warp per vector, 4 warps per CTA.  The ICM scores of a layer are spread over the
-// 32 lanes (coalesced reads of G's column segment); the argmax reduces with shuffles; the small
-// SPD solves run on lane 0 from a per-warp shared-memory matrix.  The m x m Gram submatrix of the
-// current codes is cached per warp in shared memory (loaded by all lanes, two rows/columns per
-// trial code change), so lane 0's solves, costs and MSE terms read no global memory.
+// Layout: 4 warps per CTA; a warp refines its vectors 32 at a time, lane i holding the codes,
+// coefficients and cost of the i-th.  The ICM scores of a layer are computed by the whole warp
+// for one vector at a time (coalesced reads of G's column segment, argmax by shuffles); the
+// serial parts (LS solves, costs, trial changes, ILS perturbations, MSE terms) then run on every
+// lane at once, each for its own vector, reading Gram entries from the global matrix.
 #include <algorithm>
 #include <cstdint>
 
@@ -31,35 +31,19 @@ constexpr int kWarps = 4;
 constexpr int kScoreT = 8;  // ICM codewords per lane held in registers (a chunk of 256 per warp)
 constexpr int kRefineThreads = 32 * kWarps;
 
-struct WarpState {
-    float A[kMaxM * kMaxM];
-    float b[kMaxM];
-    float x[kMaxM];
-    float y[kMaxM];
-    float a[kMaxM];
-    float backup[kMaxM];
+// The codes and coefficients of the vector the warp is scoring, staged by the lane that holds it.
+struct WarpStage {
     int code[kMaxM];
-    int cand[kMaxM];
-    float acand[kMaxM];
-    float Gs[kMaxM * kMaxM];  // Gs[r*m + c] = G(flat_r, flat_c) for the codes being refined
-    float Gbak[2 * kMaxM];    // row and column of a trial code change, for the rollback
+    float a[kMaxM];
 };
 
-// One lane's scratch for the solve of GroupStart (local memory: the lanes' copies interleave,
-// so a warp's accesses to one element coalesce).
+// One lane's scratch for an LS solve (local memory: the lanes' copies interleave, so a warp's
+// accesses to one element coalesce).
 struct LaneScratch {
     float A[kMaxM * kMaxM];
     float b[kMaxM];
     float x[kMaxM];
     float y[kMaxM];
-};
-
-// Results of GroupStart for the 32 vectors of a warp's group, lane-major, in global scratch (one
-// per warp of the grid): kept in shared memory they took L1 capacity the ICM gathers use.
-struct GroupState {
-    float a[kMaxM][32];
-    float cost[32];
-    double sse[32];
 };
 
 // G(row, col) of two flat indices from the refinement's Gram array: G(r, c), r >= c0, at
@@ -81,58 +65,13 @@ __device__ __forceinline__ GramRef MakeGram(const Dims& dims, const float* g, co
     return GramRef{g, diag, dims.ldg, dims.c0};
 }
 
-// Gram entry G(flat_r, flat_c) of layers r and c, from the global matrix or the warp's cache.
+// Gram entry G(flat_r, flat_c) of layers r and c for the codes `code`.
 struct GramGlobal {
     GramRef g;
     const int* off;
     const int* code;
     __device__ float operator()(int r, int c) const { return g(off[r] + code[r], off[c] + code[c]); }
 };
-struct GramShared {
-    const float* Gs;
-    int m;
-    __device__ float operator()(int r, int c) const { return Gs[r * m + c]; }
-};
-
-// All lanes: ws.Gs for `code`.
-__device__ void LoadGram(const Dims& dims, const GramRef& Gr, const int* code, float* Gs) {
-    const int lane = threadIdx.x & 31, m = dims.m;
-    __syncwarp();
-    for (int e = lane; e < m * m; e += 32) {
-        const int r = e / m, c = e - r * m;
-        Gs[e] = Gr(dims.off[r] + code[r], dims.off[c] + code[c]);
-    }
-    __syncwarp();
-}
-
-// All lanes: row and column j of Gs for code[j]'s new value, the old ones saved in bak.
-__device__ void UpdateGram(const Dims& dims, const GramRef& Gr, const int* code, int j, float* Gs, float* bak) {
-    const int lane = threadIdx.x & 31, m = dims.m;
-    __syncwarp();
-    if (lane < m) {
-        const int fj = dims.off[j] + code[j], fk = dims.off[lane] + code[lane];
-        bak[lane] = Gs[j * m + lane];
-        bak[m + lane] = Gs[lane * m + j];
-        const float row = Gr(fj, fk), col = Gr(fk, fj);
-        __syncwarp(0xffffffffu >> (32 - m));
-        Gs[j * m + lane] = row;
-        Gs[lane * m + j] = col;
-    }
-    __syncwarp();
-}
-
-// All lanes: undoes UpdateGram.
-__device__ void RestoreGram(int m, int j, float* Gs, const float* bak) {
-    const int lane = threadIdx.x & 31;
-    __syncwarp();
-    if (lane < m) {
-        Gs[j * m + lane] = bak[lane];
-        __syncwarp(0xffffffffu >> (32 - m));
-        Gs[lane * m + j] = bak[m + lane];
-    }
-    __syncwarp();
-}
-
 // Fixed-size Cholesky for m in {5, 10} (CholeskyUpperFixed, least_squares.cpp:44-66), row-major.
 __device__ __noinline__ bool CholFixed(float* A, int m) {
     for (int k = 0; k < m; ++k) {
@@ -391,223 +330,226 @@ __device__ __forceinline__ uint32_t UniformBelow(SplitMix64& r, uint32_t bound) 
     return static_cast<uint32_t>(__umul64hi(r.Next(), static_cast<uint64_t>(bound)));
 }
 
-// One RunIcm call (icm.cpp:89-344) on `code` (in/out) for the warp's vector; a and cost out.
-// With do_init false the caller has already solved LS and the cost for `code` (RunIcm's first
-// step, icm.cpp:109-114), so only the sweeps run.
-__device__ __noinline__ void RunIcmWarp(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc, float xn2,
-                           int icm_iters, const int* orders, bool use_abs, int* code, float* a, float* cost,
-                           WarpState& ws, bool do_init = true) {
+// The ICM choice for layer j of the staged vector, by the whole warp (icm.cpp:272-300): the
+// codeword t with the largest score (xC(t) - sum_{l != j} a_l G(t, flat_l)) * invnorm(t),
+// absolute with use_abs, the first strict maximum in t order; code[j] when no score beats -inf.
+// Each lane holds kScoreT codewords t = t0 + lane + 32 i; the layers l run outermost (the same
+// per-t subtraction order), so a lane's kScoreT gathers of one Gram row are issued together.
+__device__ __forceinline__ int ScoreLayer(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc,
+                                          int j, const int* code, const float* a, bool use_abs) {
     const int lane = threadIdx.x & 31;
-    const int m = dims.m;
-    const GramShared G{ws.Gs, m};
-    if (do_init) {
-        LoadGram(dims, Gr, code, ws.Gs);
-        if (lane == 0) {
-            if (!SolveLs(dims, G, xc, code, ws, a))
-                for (int l = 0; l < m; ++l) a[l] = 0.0f;
-            *cost = Cost(dims, G, xc, code, a, xn2);
+    const int m = dims.m, hj = dims.h_vec[j], startf = dims.off[j];
+    float best_s = __int_as_float(0xff800000);  // -inf
+    int best_t = 0x7fffffff;
+    for (int t0 = 0; t0 < hj; t0 += 32 * kScoreT) {
+        float v[kScoreT];
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) {
+            const int t = t0 + lane + 32 * i;
+            v[i] = t < hj ? xc[startf + t] : 0.0f;
+        }
+        for (int l = 0; l < m; ++l) {
+            if (l == j) continue;
+            const float al = a[l];
+            // G(startf + t, flat_l): codebook j >= 1, so the row is always stored (>= c0).
+            const float* grow =
+                Gr.g + static_cast<size_t>(dims.off[l] + code[l]) * Gr.ldg + (startf - Gr.c0) + t0 + lane;
+            float g[kScoreT];
+#pragma unroll
+            for (int i = 0; i < kScoreT; ++i) g[i] = t0 + lane + 32 * i < hj ? __ldg(grow + 32 * i) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < kScoreT; ++i) v[i] = sub_rn(v[i], mul_rn(al, g[i]));
+        }
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) {
+            const int t = t0 + lane + 32 * i;
+            if (t >= hj) continue;
+            const float val = mul_rn(v[i], __ldg(invnorm + startf + t));
+            const float s = use_abs ? fabsf(val) : val;
+            if (s > best_s) {  // first strict maximum in t order (t increases with i and t0)
+                best_s = s;
+                best_t = t;
+            }
         }
     }
-    __syncwarp();
-    bool active = true;
-    for (int it = 0; it < icm_iters && active; ++it) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float s2 = __shfl_xor_sync(0xffffffffu, best_s, o);
+        const int t2 = __shfl_xor_sync(0xffffffffu, best_t, o);
+        if (s2 > best_s || (s2 == best_s && t2 < best_t)) {
+            best_s = s2;
+            best_t = t2;
+        }
+    }
+    return (best_s > __int_as_float(0xff800000)) ? best_t : code[j];
+}
+
+// One lane's trial change of layer j to `best` for its own vector (icm.cpp:300-340): LS for the
+// new codes and their cost; the change is kept only if the cost drops by more than kIcmEps,
+// otherwise code and a are restored.  Returns whether it was kept.
+__device__ __noinline__ bool TryChange(const Dims& dims, const GramRef& Gr, const float* xc, float xn2, int j, int best,
+                                       int* code, float* a, float* cost, LaneScratch& sc) {
+    const int m = dims.m;
+    const int old_code = code[j];
+    float backup[kMaxM];
+    for (int l = 0; l < m; ++l) backup[l] = a[l];
+    code[j] = best;
+    const GramGlobal G{Gr, dims.off, code};
+    bool keep = SolveLs(dims, G, xc, code, sc, a);
+    if (keep) {
+        const float nc = Cost(dims, G, xc, code, a, xn2);
+        keep = add_rn(nc, kIcmEps) < *cost;
+        if (keep) *cost = nc;
+    }
+    if (!keep) {
+        code[j] = old_code;
+        for (int l = 0; l < m; ++l) a[l] = backup[l];
+    }
+    return keep;
+}
+
+__device__ __forceinline__ const float* ShflPtr(const float* ptr, int src) {
+    return reinterpret_cast<const float*>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ptr), src));
+}
+
+// RunIcm's sweeps (icm.cpp:116-344) for the vectors of a warp's group after its first step: lane
+// i < ng holds the i-th vector's codes, coefficients and cost (in/out) and its xC row.  For each
+// layer of the order, the warp scores the active vectors one at a time from the codes their lanes
+// stage in `st`; then every lane tries its own vector's change at once.  A vector stops after a
+// sweep without a kept change, as RunIcm does.
+__device__ __noinline__ void RunIcmGroup(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc,
+                                         float xn2, int ng, int icm_iters, const int* orders, bool use_abs,
+                                         int* code, float* a, float* cost, WarpStage& st, LaneScratch& sc) {
+    const int lane = threadIdx.x & 31;
+    const int m = dims.m;
+    bool active = lane < ng;
+    for (int it = 0; it < icm_iters; ++it) {
+        if (!__any_sync(0xffffffffu, active)) break;
         bool changed = false;
         for (int oi = 0; oi < m; ++oi) {
             const int j = orders[it * m + oi];
-            const int hj = dims.h_vec[j];
-            if (j == 0 || hj <= 1) continue;
-            const int startf = dims.off[j];
-            const int old_code = code[j];
-            // score(t) = (xC(t) - sum_{l != j} a_l G(t, flat_l)) * invnorm(t)   (icm.cpp:272-300).
-            // Each lane holds kScoreT codewords t = t0 + lane + 32 i; the layers l run outermost
-            // (the same per-t subtraction order), so a lane's kScoreT gathers of one Gram row are
-            // issued together instead of one L2 round trip per term.
-            float best_s = __int_as_float(0xff800000);  // -inf
-            int best_t = 0x7fffffff;
-            for (int t0 = 0; t0 < hj; t0 += 32 * kScoreT) {
-                float v[kScoreT];
-#pragma unroll
-                for (int i = 0; i < kScoreT; ++i) {
-                    const int t = t0 + lane + 32 * i;
-                    v[i] = t < hj ? xc[startf + t] : 0.0f;
-                }
-                for (int l = 0; l < m; ++l) {
-                    if (l == j) continue;
-                    const float al = a[l];
-                    // G(startf + t, flat_l): codebook j >= 1, so the row is always stored (>= c0).
-                    const float* grow = Gr.g + static_cast<size_t>(dims.off[l] + code[l]) * Gr.ldg +
-                                        (startf - Gr.c0) + t0 + lane;
-                    float g[kScoreT];
-#pragma unroll
-                    for (int i = 0; i < kScoreT; ++i) g[i] = t0 + lane + 32 * i < hj ? __ldg(grow + 32 * i) : 0.0f;
-#pragma unroll
-                    for (int i = 0; i < kScoreT; ++i) v[i] = sub_rn(v[i], mul_rn(al, g[i]));
-                }
-#pragma unroll
-                for (int i = 0; i < kScoreT; ++i) {
-                    const int t = t0 + lane + 32 * i;
-                    if (t >= hj) continue;
-                    const float val = mul_rn(v[i], __ldg(invnorm + startf + t));
-                    const float s = use_abs ? fabsf(val) : val;
-                    if (s > best_s) {  // first strict maximum in t order (t increases with i and t0)
-                        best_s = s;
-                        best_t = t;
+            if (j == 0 || dims.h_vec[j] <= 1) continue;
+            int mine = 0;
+            for (unsigned act = __ballot_sync(0xffffffffu, active); act; act &= act - 1) {
+                const int gi = __ffs(act) - 1;
+                __syncwarp();
+                if (lane == gi)
+                    for (int l = 0; l < m; ++l) {
+                        st.code[l] = code[l];
+                        st.a[l] = a[l];
                     }
-                }
+                const float* xg = ShflPtr(xc, gi);
+                __syncwarp();
+                const int best = ScoreLayer(dims, Gr, invnorm, xg, j, st.code, st.a, use_abs);
+                if (lane == gi) mine = best;
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float s2 = __shfl_xor_sync(0xffffffffu, best_s, o);
-                const int t2 = __shfl_xor_sync(0xffffffffu, best_t, o);
-                if (s2 > best_s || (s2 == best_s && t2 < best_t)) {
-                    best_s = s2;
-                    best_t = t2;
-                }
-            }
-            const int best = (best_s > __int_as_float(0xff800000)) ? best_t : old_code;
-            if (best == old_code) continue;
-            __syncwarp();
-            if (lane == 0) code[j] = best;
-            UpdateGram(dims, Gr, code, j, ws.Gs, ws.Gbak);
-            bool keep = false;
-            if (lane == 0) {
-                for (int l = 0; l < m; ++l) ws.backup[l] = a[l];
-                keep = SolveLs(dims, G, xc, code, ws, a);
-                if (keep) {
-                    const float nc = Cost(dims, G, xc, code, a, xn2);
-                    keep = add_rn(nc, kIcmEps) < *cost;
-                    if (keep) {
-                        *cost = nc;
-                        changed = true;
-                    }
-                }
-                if (!keep) {
-                    code[j] = old_code;
-                    for (int l = 0; l < m; ++l) a[l] = ws.backup[l];
-                }
-            }
-            changed = __shfl_sync(0xffffffffu, changed, 0);
-            keep = __shfl_sync(0xffffffffu, keep, 0);
-            if (!keep) RestoreGram(m, j, ws.Gs, ws.Gbak);
-            __syncwarp();
+            if (active && mine != code[j]) changed |= TryChange(dims, Gr, xc, xn2, j, mine, code, a, cost, sc);
         }
-        if (!changed) active = false;
+        active = active && changed;
     }
-}
-
-// RunIcm's first step (icm.cpp:109-114), or with mode 0 the whole LS stage, for the vector of
-// each lane: lane i takes vec0 + i * stride (the warp's next 32 vectors), solves LS and the cost
-// serially from the global Gram, and leaves a, cost and the beam-stage SSE term in gs (mode 0:
-// a straight to p.a).  The same routines and the same Gram values as the warp's own solve, so the
-// results are identical; the serial solves run 32 at a time instead of on lane 0 alone.
-__device__ __noinline__ void GroupStart(const RefineArgs& p, const GramRef& Gr, int64_t vec0, int64_t stride,
-                                        GroupState* gs) {
-    const Dims& dims = p.dims;
-    const int m = dims.m, lane = threadIdx.x & 31;
-    const int64_t vec = vec0 + lane * stride;
-    if (vec >= p.n) return;
-    int code[kMaxM];
-    float a[kMaxM];
-    LaneScratch sc;
-    for (int l = 0; l < m; ++l) code[l] = LoadCode(p.B, vec * m + l, dims.wide);
-    const float* xc = p.xC + vec * dims.H;
-    const GramGlobal G{Gr, dims.off, code};
-    if (!SolveLs(dims, G, xc, code, sc, a))
-        for (int l = 0; l < m; ++l) a[l] = 0.0f;
-    if (p.mode == 0) {
-        for (int l = 0; l < m; ++l) p.a[vec * m + l] = a[l];
-        return;
-    }
-    const float c = Cost(dims, G, xc, code, a, p.xnorm2[vec]);
-    for (int l = 0; l < m; ++l) gs->a[l][lane] = a[l];
-    gs->cost[lane] = c;
-    // Beam-stage error: MeanMseFromPrecomp's term, or for a large-root encoder the float cost
-    // itself (the large pipeline averages ComputeCostsLargeRoot, encode_base_streaming.cpp:301-311).
-    if (p.partials)
-        gs->sse[lane] = dims.large_root ? static_cast<double>(c) : VectorSse(dims, G, xc, code, a, p.xnorm2_d[vec]);
 }
 
 }  // namespace
 
 __global__ void __launch_bounds__(kRefineThreads, 4) RefineKernel(RefineArgs p) {
-    __shared__ WarpState wss[kWarps];
+    __shared__ WarpStage stage[kWarps];
     __shared__ double sse_w[kWarps][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    WarpState& ws = wss[warp];
-    GroupState* gs = p.mode == 0 ? nullptr : static_cast<GroupState*>(p.group) + blockIdx.x * kWarps + warp;
     const Dims& dims = p.dims;
     const int m = dims.m;
     const GramRef Gr = MakeGram(dims, p.Gcol, p.Gdiag);
     double sse_beam = 0.0, sse_final = 0.0;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
-    // The warp's vectors are blockIdx.x * kWarps + warp + i * stride, taken 32 at a time: the
-    // group's solves run lane-parallel (GroupStart), then the warp refines them one by one.
+    // The warp's vectors are blockIdx.x * kWarps + warp + i * stride, taken 32 at a time (lane i
+    // holds the i-th of a group), the order in which one vector at a time would take them.
     for (int64_t g0 = static_cast<int64_t>(blockIdx.x) * kWarps + warp; g0 < p.n; g0 += 32 * stride) {
-        __syncwarp();
-        GroupStart(p, Gr, g0, stride, gs);
-        __syncwarp();
-        if (p.mode == 0) continue;
-        for (int gi = 0; gi < 32 && g0 + gi * stride < p.n; ++gi) {
-            const int64_t vec = g0 + gi * stride;
-            const float* xc = p.xC + vec * dims.H;
-            if (lane < m) {
-                ws.code[lane] = LoadCode(p.B, vec * m + lane, dims.wide);
-                ws.a[lane] = gs->a[lane][gi];
+        const int ng = static_cast<int>(min(int64_t{32}, (p.n - g0 + stride - 1) / stride));
+        const bool own = lane < ng;
+        const int64_t vec = own ? g0 + lane * stride : 0;
+        const float* xc = p.xC + vec * dims.H;
+        int code[kMaxM];
+        float a[kMaxM];
+        LaneScratch sc;
+        float cost = 0.0f, xn2 = 0.0f;
+        double tb = 0.0, tf = 0.0;
+        if (own) {
+            // RunIcm's first step (icm.cpp:109-114), or with mode 0 the whole LS stage.
+            for (int l = 0; l < m; ++l) code[l] = LoadCode(p.B, vec * m + l, dims.wide);
+            const GramGlobal G{Gr, dims.off, code};
+            if (!SolveLs(dims, G, xc, code, sc, a))
+                for (int l = 0; l < m; ++l) a[l] = 0.0f;
+            if (p.mode == 0) {
+                for (int l = 0; l < m; ++l) p.a[vec * m + l] = a[l];
+            } else {
+                xn2 = p.xnorm2[vec];
+                cost = Cost(dims, G, xc, code, a, xn2);
+                // Beam-stage error: MeanMseFromPrecomp's term, or for a large-root encoder the float
+                // cost itself (the large pipeline averages ComputeCostsLargeRoot,
+                // encode_base_streaming.cpp:301-311).
+                if (p.partials)
+                    tb = dims.large_root ? static_cast<double>(cost)
+                                         : VectorSse(dims, G, xc, code, a, p.xnorm2_d[vec]);
             }
-            LoadGram(dims, Gr, ws.code, ws.Gs);  // syncs the warp before and after
-            const float xn2 = p.xnorm2[vec];
-            float cost = gs->cost[gi];
-            if (p.partials && lane == 0) sse_beam += gs->sse[gi];
-            if (p.icm_iters > 0)
-                RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters, p.orders, p.use_abs, ws.code, ws.a, &cost, ws,
-                           /*do_init=*/false);
-            cost = __shfl_sync(0xffffffffu, cost, 0);
-            const int ksel = min(p.perturb_k, m);
-            for (int outer = 0; outer < p.n_ils; ++outer) {
-                if (lane < m) ws.cand[lane] = ws.code[lane];
-                __syncwarp();
-                if (lane == 0) {  // icm.cpp:953-972
-                    const uint64_t ig = p.sample_id_offset + static_cast<uint64_t>(vec);
-                    SplitMix64 r{static_cast<uint64_t>(p.seed) ^
-                                 (static_cast<uint64_t>(outer + 1) * 0x9e3779b97f4a7c15ULL) ^
-                                 ((ig + 1) * 0xbf58476d1ce4e5b9ULL)};
-                    for (int s = 0; s < ksel; ++s) {
-                        const int layer = 1 + static_cast<int>(UniformBelow(r, static_cast<uint32_t>(m - 1)));
-                        const int h = dims.h_vec[layer];
-                        if (h <= 1) continue;
-                        const int old_code = ws.cand[layer];
-                        const int raw = static_cast<int>(UniformBelow(r, static_cast<uint32_t>(h - 1)));
-                        ws.cand[layer] = raw >= old_code ? raw + 1 : raw;
-                    }
-                }
-                __syncwarp();
-                float ccost = 0.0f;
-                RunIcmWarp(dims, Gr, p.invnorm, xc, xn2, p.icm_iters,
-                           p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, ws.cand, ws.acand,
-                           &ccost, ws);
-                ccost = __shfl_sync(0xffffffffu, ccost, 0);
-                if (add_rn(ccost, kIcmEps) < cost) {  // icm.cpp:979-990
-                    if (lane < m) {
-                        ws.code[lane] = ws.cand[lane];
-                        ws.a[lane] = ws.acand[lane];
-                    }
-                    cost = ccost;
-                }
-                __syncwarp();
-            }
-            if (p.partials && dims.large_root) {
-                if (lane == 0) sse_final += static_cast<double>(cost);
-            } else if (p.partials) {
-                if (p.n_ils > 0) LoadGram(dims, Gr, ws.code, ws.Gs);  // the cache holds the last ILS candidate
-                if (lane == 0) sse_final += VectorSse(dims, GramShared{ws.Gs, m}, xc, ws.code, ws.a, p.xnorm2_d[vec]);
-            }
-            if (lane < m) {
-                StoreCode(p.B, vec * m + lane, ws.code[lane], dims.wide);
-                if (p.a) p.a[vec * m + lane] = ws.a[lane];
-            }
-            if (lane == 0 && p.cost) p.cost[vec] = cost;
-            __syncwarp();
         }
+        if (p.mode == 0) continue;
+        WarpStage& st = stage[warp];
+        if (p.icm_iters > 0)
+            RunIcmGroup(dims, Gr, p.invnorm, xc, xn2, ng, p.icm_iters, p.orders, p.use_abs, code, a, &cost, st, sc);
+        const int ksel = min(p.perturb_k, m);
+        for (int outer = 0; outer < p.n_ils; ++outer) {
+            int cand[kMaxM];
+            float acand[kMaxM];
+            float ccost = 0.0f;
+            if (own) {
+                for (int l = 0; l < m; ++l) cand[l] = code[l];
+                const uint64_t ig = p.sample_id_offset + static_cast<uint64_t>(vec);  // icm.cpp:953-972
+                SplitMix64 r{static_cast<uint64_t>(p.seed) ^
+                             (static_cast<uint64_t>(outer + 1) * 0x9e3779b97f4a7c15ULL) ^
+                             ((ig + 1) * 0xbf58476d1ce4e5b9ULL)};
+                for (int s = 0; s < ksel; ++s) {
+                    const int layer = 1 + static_cast<int>(UniformBelow(r, static_cast<uint32_t>(m - 1)));
+                    const int h = dims.h_vec[layer];
+                    if (h <= 1) continue;
+                    const int old_code = cand[layer];
+                    const int raw = static_cast<int>(UniformBelow(r, static_cast<uint32_t>(h - 1)));
+                    cand[layer] = raw >= old_code ? raw + 1 : raw;
+                }
+                const GramGlobal G{Gr, dims.off, cand};
+                if (!SolveLs(dims, G, xc, cand, sc, acand))
+                    for (int l = 0; l < m; ++l) acand[l] = 0.0f;
+                ccost = Cost(dims, G, xc, cand, acand, xn2);
+            }
+            if (p.icm_iters > 0)
+                RunIcmGroup(dims, Gr, p.invnorm, xc, xn2, ng, p.icm_iters,
+                            p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, cand, acand,
+                            &ccost, st, sc);
+            if (own && add_rn(ccost, kIcmEps) < cost) {  // icm.cpp:979-990
+                for (int l = 0; l < m; ++l) {
+                    code[l] = cand[l];
+                    a[l] = acand[l];
+                }
+                cost = ccost;
+            }
+        }
+        if (own) {
+            if (p.partials)
+                tf = dims.large_root ? static_cast<double>(cost)
+                                     : VectorSse(dims, GramGlobal{Gr, dims.off, code}, xc, code, a, p.xnorm2_d[vec]);
+            for (int l = 0; l < m; ++l) {
+                StoreCode(p.B, vec * m + l, code[l], dims.wide);
+                if (p.a) p.a[vec * m + l] = a[l];
+            }
+            if (p.cost) p.cost[vec] = cost;
+        }
+        if (p.partials)  // added in the warp's vector order
+            for (int gi = 0; gi < ng; ++gi) {
+                const double b = __shfl_sync(0xffffffffu, tb, gi), f = __shfl_sync(0xffffffffu, tf, gi);
+                if (lane == 0) {
+                    sse_beam += b;
+                    sse_final += f;
+                }
+            }
     }
     if (p.partials) {
         if (lane == 0) {
@@ -710,8 +652,6 @@ cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, c
 }
 
 int RefineWarpsPerBlock() { return kWarps; }
-
-size_t RefineGroupBytes() { return sizeof(GroupState); }
 
 // Large-root outputs from the internal m x n codes: cluster id (the root code) and the (m-1) small
 // codes of each vector (BeamSearchPrefixLSLargeRoot's cluster_id / B_small, beam_search.h:26-32).
