@@ -164,10 +164,12 @@ int64_t SliceVectors(const stlq_b200_encoder* enc) {
     return std::max<int64_t>(1024, std::min<int64_t>(by_mem, stlq_b200::MaxGemmSliceVectors()));
 }
 
+// One resident wave of refinement CTAs (each warp loops over its vectors), fewer for small n.
 int RefineGrid(const stlq_b200_encoder* enc, int64_t n) {
     const int64_t per_block = stlq_b200::RefineWarpsPerBlock();
     const int64_t want = (n + per_block - 1) / per_block;
-    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t{enc->num_sms} * 16)));
+    const int64_t wave = int64_t{enc->num_sms} * stlq_b200::RefineBlocksPerSm();
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, wave)));
 }
 
 int CheckEnc(const stlq_b200_encoder* enc) {

@@ -56,6 +56,7 @@ cudaError_t LaunchReducePartials(const double* partials, int nblocks, double* ou
 cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, const float* xC, const double* xnorm2_d,
                       const void* B, const float* a, int64_t n, double* partials, int grid, cudaStream_t stream);
 int RefineWarpsPerBlock();
+int RefineBlocksPerSm();
 
 // Loads both beam kernels and sets their shared-memory attributes (no launch).
 cudaError_t PrepareBeamKernels(const Dims& dims, int beam);

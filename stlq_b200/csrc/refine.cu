@@ -30,6 +30,10 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kScoreT = 8;  // ICM codewords per lane held in registers (a chunk of 256 per warp)
 constexpr int kRefineThreads = 32 * kWarps;
+// Resident CTAs per SM the kernel is compiled for (64 registers a thread): the scoring's Gram
+// gathers are latency-bound, and 32 warps per SM hide twice what 16 do, which outweighs the
+// spills of the serial routines.
+constexpr int kRefineBlocksPerSm = 8;
 
 // The codes and coefficients of the vector the warp is scoring, staged by the lane that holds it.
 struct WarpStage {
@@ -452,7 +456,7 @@ __device__ __noinline__ void RunIcmGroup(const Dims& dims, const GramRef& Gr, co
 
 }  // namespace
 
-__global__ void __launch_bounds__(kRefineThreads, 4) RefineKernel(RefineArgs p) {
+__global__ void __launch_bounds__(kRefineThreads, kRefineBlocksPerSm) RefineKernel(RefineArgs p) {
     __shared__ WarpStage stage[kWarps];
     __shared__ double sse_w[kWarps][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -652,6 +656,8 @@ cudaError_t LaunchSse(const Dims& dims, const float* Gcol, const float* Gdiag, c
 }
 
 int RefineWarpsPerBlock() { return kWarps; }
+
+int RefineBlocksPerSm() { return kRefineBlocksPerSm; }
 
 // Large-root outputs from the internal m x n codes: cluster id (the root code) and the (m-1) small
 // codes of each vector (BeamSearchPrefixLSLargeRoot's cluster_id / B_small, beam_search.h:26-32).
