@@ -480,6 +480,11 @@ def run_ours(args):
         F_cand = cand_flops_per_vector(args.m, args.k, args.beam)
         beam_bytes = S * (4 * H + 4 + args.m)
         achieved_gbs = beam_bytes / beam_s / 1e9
+        # DRAM traffic of BeamFastKernel<8>, measured by ncu (dram__bytes_read.sum +
+        # dram__bytes_write.sum) on one launch of 65,536 vectors of the headline shape: 544.7 MB
+        # read, 5.1 MB written; it grows with the vectors a launch processes, so it is scaled to S.
+        headline_shape = (args.d, args.m, args.k, args.beam) == (128, 8, 256, 16)
+        traffic = S * (544.7e6 + 5.1e6) / 65536 if headline_shape else None
         F_gemm = 2 * args.d * H
         hbm_bytes_vec = 4 * args.d + args.m + 4 * args.m
         t_gemm = F_gemm / (peaks["bf16_tflops"] * 1e12)
@@ -501,7 +506,9 @@ def run_ours(args):
             "roofline": {
                 "bound": "hbm", "kernel": "BeamFastKernel<8>", "achieved": achieved_gbs,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"],
-                "traffic": None, "peak_source": peaks_src,
+                "traffic": traffic, "peak_source": peaks_src,
+                "traffic_source": "ncu capture of one 65,536-vector launch of the same shape, scaled to the "
+                                  "launch's vectors" if traffic else "not captured for this shape",
                 "note": "algorithmic bytes per vector = xC row (4H) + ||x||^2 (4) + codes (M); the kernel is "
                         "bound by FP32 issue, see simt",
                 "simt": {"achieved": F_cand * S / beam_s / 1e12, "peak": fp32_peak, "unit": "TFLOP/s",
