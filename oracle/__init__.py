@@ -379,6 +379,34 @@ class RefCudaIcm:
         self.lib.ref_precomp_destroy(pre)
 
 
+class RefCudaBeam:
+    """The reference's own large-root CUDA beam search (BeamSearchPrefixLSLargeRootCudaH2/H4,
+    beam_search_cuda.cu compiled for sm_100a by the Makefile's refcuda target; beam 2 or 4 only)."""
+
+    def __init__(self, path: str = REF_CUDA_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: build it with `make -C oracle refcuda`")
+        self.lib = ctypes.CDLL(path)
+
+    def beam(self, h_vec, C_all, X, beam, allow_tf32=False):
+        """C_all: (H, d), root codewords first; X: (n, d).  Returns (cluster (n,) uint32, B_small
+        (n, m-1) uint8, timing): timing = seconds of norms, root GEMM, root top-H update and the
+        expansion of layers 1..m-1, as the reference's BeamSearchLargeRootTiming reports them."""
+        h = np.asarray(h_vec, np.int32)
+        C, Xf = _f32(C_all), _f32(X)
+        m, (n, d) = len(h), Xf.shape
+        cluster = np.empty(n, np.uint32)
+        B_small = np.empty((n, m - 1), np.uint8)
+        t = np.zeros(4, np.float64)
+        rc = self.lib.ref_beam_large_root_cuda(
+            ctypes.c_int(d), ctypes.c_int(m), _p(h, _i32p), _p(C, _f32p), _p(Xf, _f32p), ctypes.c_int(n),
+            ctypes.c_int(beam), ctypes.c_int(int(bool(allow_tf32))),
+            cluster.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), _p(B_small, _u8p), _p(t, _f64p))
+        if rc != 0:
+            raise RuntimeError(f"ref_beam_large_root_cuda failed ({rc})")
+        return cluster, B_small, t
+
+
 class AdapterHarness:
     """The drop-in C++ adapter (stlq_b200/adapter) driven with the reference's own types: the
     library holds the reference objects too, so a Precomp built here feeds both sides."""
