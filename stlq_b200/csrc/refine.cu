@@ -8,7 +8,7 @@
 //
 // Every step of ICM and ILS is independent across vectors once the layer orders are known (the
 // reference draws them on the host from one std::mt19937 and the same orders apply to every
-// vector), so one warp carries a vector through LS, cost, all ICM sweeps and all ILS rounds
+// vector), so one warp carries its vectors through LS, cost, all ICM sweeps and all ILS rounds
 // without returning to the host: the reference launches one kernel per layer per sweep and
 // copies state through the host between them (icm_cuda_kernels.inc:2183-2261).
 //
