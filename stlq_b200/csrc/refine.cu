@@ -229,7 +229,9 @@ __device__ __noinline__ bool SolveLs(const Dims& dims, const Gram& G, const floa
     const bool fixed = (m == 5 || m == 10);
     float lambda = 0.0f;
     for (int attempt = 0; attempt < 4; ++attempt) {
-        for (int e = 0; e < m * m; ++e) ws.A[e] = 0.0f;
+        // Only the upper triangle is written and read (both Cholesky variants and both solves
+        // index k <= j), so the strict lower triangle is never set: one solve touches fewer
+        // words of the lane's scratch.
         for (int j = 0; j < m; ++j) {
             const int fj = dims.off[j] + code[j];
             ws.b[j] = xc[fj];
