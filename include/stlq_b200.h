@@ -155,7 +155,10 @@ int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const 
  * The encoder handle (which allocates its codebook tables) and the inputs and outputs are the
  * caller's, created beforehand.
  * The first call on each device sets up that device (it looks up the array's device address and
- * loads the beam kernels); make that first call before any stream capture.  All calls share the
+ * loads every beam kernel variant, for any encoder shape); make that first call before any stream
+ * capture.  The address is kept for the process: do not reset the device (cudaDeviceReset) while
+ * the library is loaded.  Arguments are checked as stlq_b200_beam_search checks them (the same
+ * STLQ_B200_EINVAL results), plus the size limit.  All calls share the
  * one array: each clears it before use, and calls whose work overlaps on the GPU (concurrent
  * streams, several host threads) race and must not be issued. */
 #define STLQ_B200_NOALLOC_MAX_VECTORS (1 << 20)

@@ -52,18 +52,34 @@ _u8p = ctypes.POINTER(ctypes.c_uint8)
 _u16p = ctypes.POINTER(ctypes.c_uint16)
 
 
+def reference_dir() -> str | None:
+    """Where the reference's sources are: the STLQ_REF_DIR environment variable, else the
+    ``reference_path`` recorded in the repository's BASELINE.json.  None when neither names an
+    existing directory (a GPU box, which only uses the prebuilt libraries)."""
+    cand = os.environ.get("STLQ_REF_DIR")
+    if not cand:
+        try:
+            import json
+
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return cand if cand and os.path.isdir(cand) else None
+
+
 def build(reference: bool = True) -> None:
     """Compile the restatement (always) and the reference library (when its sources exist)."""
     targets = ["oracle"]
-    if reference and os.path.isdir(os.environ.get("STLQ_REF_DIR", "/root/reference")):
+    env = dict(os.environ)
+    ref = reference_dir() if reference else None
+    if ref:
+        env["REF"] = ref
         targets.append("ref")
         if os.path.exists(os.path.join(os.path.dirname(HERE), "stlq_b200", "libstlq_b200.so")):
             targets.append("adapter")
         if shutil.which("nvcc") or os.path.exists("/usr/local/cuda/bin/nvcc"):
             targets.append("refcuda")  # the reference's own CUDA ICM, for timing against ours
-    env = dict(os.environ)
-    if "STLQ_REF_DIR" in env:
-        env["REF"] = env["STLQ_REF_DIR"]
     subprocess.run(["make", "-s", "-C", HERE, "-j8", *targets], check=True, env=env)
 
 

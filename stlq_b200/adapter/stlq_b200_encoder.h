@@ -56,7 +56,8 @@ void DynamicIcmWithIlsNoAbsNoNormalCuda(const ColMajorMatrix<float>& X, const Pr
 // branch): BeamSearchPrefixLSLargeRoot (beam_search.h:26-32) + SolveLeastSquaresAllLargeRoot +
 // ComputeCostsLargeRoot + DynamicIcmWithIls{Abs,NoAbs}NoNormalLargeRoot, on the GPU from the block's
 // vectors.  Outputs are resized as the reference resizes them; out_beam_mse / out_final_mse (may be
-// null) are the means of the beam-stage and final costs (MeanMseFromCosts).  h_vec[0] <= 256.
+// null) are the means of the beam-stage and final costs (MeanMseFromCosts).  The root (h_vec[0])
+// may hold up to STLQ_B200_MAX_ROOT (65,536) codewords; codebooks 1..m-1 up to 256.
 // Throws std::runtime_error on failure.
 void EncodeBaseLargeRoot(const PrecompLargeRoot& pre, const ColMajorMatrix<float>& Xblk, int H_beam, int icm_iters,
                          int ils_iters, int perturb_k, bool use_abs, std::uint32_t seed,

@@ -346,6 +346,13 @@ int GetBeamInputs(const stlq_b200_encoder* enc, BeamInputs* out) {
 
 int SetError(int code, const char* msg) { return Fail(code, msg); }
 
+// The argument checks of stlq_b200_beam_search (uint8 codes, n, beam, and the beam kernels'
+// shared memory for this encoder's codebooks), for entry points in other translation units.
+int CheckBeamCall(const stlq_b200_encoder* enc, int64_t n, int beam) {
+    STLQ_TRY(CheckCodeWidth(enc, false));
+    return CheckEncodeArgs(enc, STLQ_B200_F32, n, beam, 0, 0, 0);
+}
+
 }  // namespace stlq_b200
 
 extern "C" {

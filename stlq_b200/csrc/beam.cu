@@ -992,6 +992,22 @@ cudaError_t PrepareBeamKernels(const Dims& dims, int beam) {
     return wide ? PrepareT<16, true>(dims, beam) : PrepareT<16, false>(dims, beam);
 }
 
+// Querying a kernel's attributes makes the runtime load it (under lazy module loading too), so
+// no later launch of any beam kernel variant does that first-use work.
+cudaError_t LoadAllBeamKernels() {
+    cudaFuncAttributes a{};
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(BeamFastKernel<8, false>),    reinterpret_cast<const void*>(BeamFastKernel<8, true>),
+        reinterpret_cast<const void*>(BeamFastKernel<16, false>),   reinterpret_cast<const void*>(BeamFastKernel<16, true>),
+        reinterpret_cast<const void*>(BeamReplayKernel<8, false>),  reinterpret_cast<const void*>(BeamReplayKernel<8, true>),
+        reinterpret_cast<const void*>(BeamReplayKernel<16, false>), reinterpret_cast<const void*>(BeamReplayKernel<16, true>)};
+    for (const void* k : kernels) {
+        const cudaError_t e = cudaFuncGetAttributes(&a, k);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 // redo: n + 1 ints of scratch (a count, then vector ids handed from the fast to the replay kernel).
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
                              const float* xC, int64_t n, int beam, void* Bout, int* redo, int check,

@@ -60,6 +60,8 @@ int RefineBlocksPerSm();
 
 // Loads both beam kernels and sets their shared-memory attributes (no launch).
 cudaError_t PrepareBeamKernels(const Dims& dims, int beam);
+// Loads every instantiation of the beam kernels on the current device (no launch).
+cudaError_t LoadAllBeamKernels();
 
 // What the beam-search launch needs from an encoder handle (api.cpp).
 struct BeamInputs {

@@ -16,6 +16,7 @@
 namespace stlq_b200 {
 int GetBeamInputs(const stlq_b200_encoder* enc, BeamInputs* out);
 int SetError(int code, const char* msg);
+int CheckBeamCall(const stlq_b200_encoder* enc, int64_t n, int beam);
 }  // namespace stlq_b200
 
 namespace {
@@ -28,11 +29,15 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) int g_handoff[STLQ_B200_NOALLOC_MAX_VECTORS + 1];
 
 std::mutex g_setup_mutex;
+// The array's device address per device, looked up once.  It stays valid for the process's CUDA
+// context on that device: the library does not support resetting a device (cudaDeviceReset) while
+// it is loaded, which would leave this address stale.
 int* g_handoff_addr[kMaxDevices] = {};
 
 // Once per device, with that device current: the device address of g_handoff (the host-side
-// name of the array is only a stand-in, never a device pointer).
-int SetupDevice(int device, const stlq_b200::BeamInputs& in, int beam) {
+// name of the array is only a stand-in, never a device pointer), and every beam kernel variant
+// loaded, so that no later call on this device, for any encoder shape, does first-use work.
+int SetupDevice(int device) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (g_handoff_addr[device]) return 0;
     int* p = nullptr;
@@ -42,12 +47,11 @@ int SetupDevice(int device, const stlq_b200::BeamInputs& in, int beam) {
         return stlq_b200::SetError(STLQ_B200_ECUDA,
                                    (std::string("cudaGetSymbolAddress(hand-off scratch): ") + cudaGetErrorString(e)).c_str());
     }
-    // Load both beam kernels now, so that later calls do no first-use work at all.
-    const cudaError_t e2 = stlq_b200::PrepareBeamKernels(in.dims, beam);
+    const cudaError_t e2 = stlq_b200::LoadAllBeamKernels();
     if (e2 != cudaSuccess) {
         cudaGetLastError();
         return stlq_b200::SetError(STLQ_B200_ECUDA,
-                                   (std::string("preparing the beam kernels: ") + cudaGetErrorString(e2)).c_str());
+                                   (std::string("loading the beam kernels: ") + cudaGetErrorString(e2)).c_str());
     }
     g_handoff_addr[device] = p;
     return 0;
@@ -63,20 +67,21 @@ extern "C" int stlq_b200_beam_search_noalloc(stlq_b200_encoder* enc, const float
         return stlq_b200::SetError(STLQ_B200_EINVAL,
                                    "stlq_b200_beam_search_noalloc writes uint8 codes; this encoder has a codebook above "
                                    "256 codewords");
-    if (n < 0) return stlq_b200::SetError(STLQ_B200_EINVAL, "n must be >= 0");
     if (n > STLQ_B200_NOALLOC_MAX_VECTORS) {
         const std::string msg = "stlq_b200_beam_search_noalloc: n = " + std::to_string(n) + " exceeds " +
                                 std::to_string(STLQ_B200_NOALLOC_MAX_VECTORS) +
                                 " vectors, the size of its static scratch; split the call";
         return stlq_b200::SetError(STLQ_B200_EINVAL, msg.c_str());
     }
-    if (beam < 1 || beam > STLQ_B200_MAX_BEAM) return stlq_b200::SetError(STLQ_B200_EINVAL, "beam must be in [1, 32]");
+    // The same checks as stlq_b200_beam_search (n, beam, shared memory for this beam width and
+    // these codebooks), with the same EINVAL results.
+    if (int rc = stlq_b200::CheckBeamCall(enc, n, beam)) return rc;
     if (n > 0 && (!xnorm2_dev || !xC_dev || !B_dev)) return stlq_b200::SetError(STLQ_B200_EINVAL, "null buffer");
     if (in.device < 0 || in.device >= kMaxDevices) return stlq_b200::SetError(STLQ_B200_EINVAL, "device ordinal too large");
     int prev = -1;
     if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
     if (cudaSetDevice(in.device) != cudaSuccess) return stlq_b200::SetError(STLQ_B200_ECUDA, "cudaSetDevice failed");
-    int rc = SetupDevice(in.device, in, beam);
+    int rc = SetupDevice(in.device);
     if (rc == 0 && n > 0) {
         const cudaError_t e = stlq_b200::LaunchBeamSearch(in.dims, in.Grow, in.Gdiag, xnorm2_dev, xC_dev, n, beam, B_dev,
                                                           g_handoff_addr[in.device], in.check_filter, in.err_flag,

@@ -84,6 +84,28 @@ def _t_ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
+def _check_noalloc_args(xnorm2, xC, out, H: int, m: int) -> None:
+    """Shapes, types, layout and device of the tensors given to the no-alloc beam search: xC
+    (n, H) float32, xnorm2 (n,) float32, out (n, m) uint8 or None; all contiguous, all on one CUDA
+    device.  Raises ValueError; checks nothing on the GPU."""
+    import torch
+
+    if xC.dim() != 2 or xC.shape[1] != H or xC.dtype != torch.float32:
+        raise ValueError(f"xC must be float32 of shape (n, {H}), got {tuple(xC.shape)} {xC.dtype}")
+    n = xC.shape[0]
+    if xnorm2.dtype != torch.float32 or xnorm2.numel() != n or xnorm2.dim() != 1:
+        raise ValueError(f"xnorm2 must be float32 of shape ({n},), got {tuple(xnorm2.shape)} {xnorm2.dtype}")
+    tensors = [xC, xnorm2]
+    if out is not None:
+        if out.dtype != torch.uint8 or tuple(out.shape) != (n, m):
+            raise ValueError(f"out must be uint8 of shape ({n}, {m}), got {tuple(out.shape)} {out.dtype}")
+        tensors.append(out)
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("xC, xnorm2 and out must be contiguous")
+    if any(t.device != xC.device for t in tensors) or xC.device.type != "cuda":
+        raise ValueError("xC, xnorm2 and out must be on the same CUDA device")
+
+
 def _dtype_code(x) -> int:
     name = str(x.dtype)
     if name.endswith("uint8"):
@@ -275,9 +297,14 @@ class Encoder:
 
     def beam_search_noalloc(self, xnorm2, xC, beam: int, out=None):
         """The same beam search through the entry point that allocates no device memory; ``out``
-        (uint8, n x m) may be supplied by callers that cannot let torch allocate either."""
+        (uint8, n x m) may be supplied by callers that cannot let torch allocate either.
+
+        The kernel writes through raw pointers, so every tensor is checked here first (a wrong
+        shape, type, layout or device would be an out-of-bounds device write, not an error):
+        raises ValueError before anything is launched."""
         import torch
 
+        _check_noalloc_args(xnorm2, xC, out, self.H, self.m)
         B = torch.empty((xC.shape[0], self.m), dtype=torch.uint8, device=xC.device) if out is None else out
         _check(self.lib, self.lib.stlq_b200_beam_search_noalloc(self.handle, _t_ptr(xnorm2), _t_ptr(xC), xC.shape[0],
                                                                 beam, _t_ptr(B), self._stream(xC)),

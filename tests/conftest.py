@@ -38,6 +38,8 @@ def load_lr_case(name):
 def load_case(name):
     with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
         c = {k: z[k] for k in z.files}
+    # Large codebooks are stored as float16 values; widening them to float32 is exact.
+    c["C_all"] = np.ascontiguousarray(c["C_all"], np.float32)
     for k in ("beam", "icm_iters", "ils_iters", "perturb_k", "use_abs", "seed"):
         c[k] = int(c[k])
     for k in ("beam_mse", "final_mse"):

@@ -42,7 +42,8 @@ def sha(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
-def make_case(name, X, books, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, store_xc=None):
+def make_case(name, X, books, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, store_xc=None,
+              f16_books=False):
     ref = oracle.Reference(threads=os.cpu_count())
     C = synth.flatten_books(books)
     h = np.array([b.shape[0] for b in books], np.int32)
@@ -58,7 +59,9 @@ def make_case(name, X, books, beam, icm, ils=0, perturb=0, use_abs=True, seed=38
     full = P.encode_base(X, beam, icm, ils, perturb, use_abs, seed)
     assert np.array_equal(full["B"], B), name
     small = store_xc if store_xc is not None else xC.size <= 40_000
-    out = dict(X=X, C_all=C, h_vec=h, beam=beam, icm_iters=icm, ils_iters=ils, perturb_k=perturb,
+    if f16_books:  # stored as float16; tests/conftest.py's load_case widens it back (exactly)
+        assert np.array_equal(C.astype(np.float16).astype(np.float32), C), name
+    out = dict(X=X, C_all=C.astype(np.float16) if f16_books else C, h_vec=h, beam=beam, icm_iters=icm, ils_iters=ils, perturb_k=perturb,
                use_abs=int(bool(use_abs)), seed=np.uint32(seed), xC_sha=sha(xC), G_sha=sha(G), invnorm=inv,
                xnorm2=xn, B_beam=B_beam, a_beam=a_beam, beam_mse=beam_mse, B=B, a=a, cost=cost,
                final_mse=final_mse, blas_core=ref.blas_core())
@@ -156,6 +159,20 @@ def zero_codeword_cases():
     make_lr_case("lr_zero_codewords", X[:400], lr, beam=8, icm=1)
 
 
+def config_cases():
+    # BASELINE config 2's shape (GIST-like D=960, M=16, K=256, beam 16, 2 ICM sweeps): the deepest
+    # beam (layers up to L=15) and the 16-codebook kernel's paired pass at K=256.  The codebooks
+    # are rounded to float16 values (exact in float32; every product and sum is still float32) so
+    # that the 4096 x 960 codebook is stored as float16 and the fixture stays a few MB.
+    X = synth.gist_like(8200, d=960, seed=2, n_centres=400)
+    books = [b.astype(np.float16).astype(np.float32) for b in synth.train_rvq(X[200:], 16, 256, iters=4, seed=2)]
+    make_case("cfg2_d960_m16_k256_b16_icm2", X[:200], books, beam=16, icm=2, store_xc=False, f16_books=True)
+    # BASELINE config 0's encode settings (SIFT-like D=128 integers, M=8, K=256, beam 8, no ICM).
+    X = synth.sift_like(20400, d=128, seed=30)
+    make_case("cfg0_d128_m8_k256_b8_icm0", X[:400], synth.train_rvq(X[400:], 8, 256, iters=6, seed=30), beam=8,
+              icm=0, store_xc=False)
+
+
 def main():
     # The reference's own test setup (tests/test_streaming_encode_base.cpp:67-134): m=3, K=16,
     # d=16, beam 2, ICM 2, ILS 3, perturb 2, seed 1234 -- at n=600.
@@ -206,8 +223,12 @@ if __name__ == "__main__":
     if "--zero-only" in sys.argv:
         zero_codeword_cases()
         sys.exit(0)
+    if "--config-only" in sys.argv:
+        config_cases()
+        sys.exit(0)
     if "--large-root-only" not in sys.argv:
         main()
     large_root_cases()
     big_root_cases()
     zero_codeword_cases()
+    config_cases()

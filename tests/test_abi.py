@@ -95,3 +95,28 @@ def test_kernel_provider_entries_reject_bad_arguments():
     if rc == 1:
         assert b"device ordinal" in lib.stlq_b200_last_error()
     assert lib.stlq_b200_kernels_destroy(None) == 0
+
+
+def test_noalloc_python_layer_rejects_bad_tensors_before_launch():
+    """The no-alloc beam search writes through raw pointers into the caller's `out`; the Python
+    layer rejects a wrong shape, type, layout or device with ValueError before the library is
+    called (a CPU tensor never reaches a kernel)."""
+    import torch
+
+    H, m, n = 64, 4, 10
+    xC = torch.zeros((n, H), dtype=torch.float32)
+    xn = torch.zeros(n, dtype=torch.float32)
+    good = torch.zeros((n, m), dtype=torch.uint8)
+    bad = [
+        (xC, xn, torch.zeros((n - 1, m), dtype=torch.uint8), "out must be uint8 of shape"),
+        (xC, xn, torch.zeros((n, m + 1), dtype=torch.uint8), "out must be uint8 of shape"),
+        (xC, xn, torch.zeros((n, m), dtype=torch.int32), "out must be uint8 of shape"),
+        (xC, xn, torch.zeros((m, n), dtype=torch.uint8).t(), "contiguous"),
+        (xC, torch.zeros(n + 1, dtype=torch.float32), good, "xnorm2 must be"),
+        (xC[:, :H - 1], xn, good, "xC must be float32 of shape"),
+        (xC.double(), xn, good, "xC must be float32 of shape"),
+        (xC, xn, good, "same CUDA device"),  # all on the CPU
+    ]
+    for x_c, x_n, out, msg in bad:
+        with pytest.raises(ValueError, match=msg):
+            enc_mod._check_noalloc_args(x_n, x_c, out, H, m)

@@ -61,3 +61,24 @@ def test_noalloc_rejects_oversized_calls(cuda):
     rc = lib.stlq_b200_beam_search_noalloc(enc.handle, p, p, (1 << 20) + 1, 4, p, None)
     assert rc == 1
     assert b"exceeds 1048576 vectors" in lib.stlq_b200_last_error()
+
+
+@pytest.mark.parametrize("beam", [0, 33])
+def test_noalloc_rejects_what_the_regular_entry_point_rejects(cuda, beam):
+    """Both entry points run the same argument checks and return the same EINVAL and message."""
+    import ctypes
+
+    import torch
+
+    import stlq_b200
+
+    c = load_case("single_vector")
+    enc = stlq_b200.Encoder(c["C_all"], c["h_vec"], device=0)
+    lib = stlq_b200.load_library()
+    dummy = torch.zeros(64, device=cuda)
+    p = ctypes.c_void_p(dummy.data_ptr())
+    rc_reg = lib.stlq_b200_beam_search(enc.handle, p, p, 1, beam, p, None)
+    msg_reg = lib.stlq_b200_last_error()
+    rc_na = lib.stlq_b200_beam_search_noalloc(enc.handle, p, p, 1, beam, p, None)
+    assert rc_reg == rc_na == 1
+    assert lib.stlq_b200_last_error() == msg_reg
