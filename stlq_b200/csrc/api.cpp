@@ -133,8 +133,9 @@ struct stlq_b200_encoder {
     Dims dims{};
     DevBuf C, Gcol, Grow, Gdiag, invnorm, err_flag;
     DevBuf Bdiag;  // the beam's diagonal (LaunchBeamDiag)
-    // Tensor-core modes: C_all split into TF32 hi / lo parts once at create.
-    DevBuf Chi, Clo;
+    // Tensor-core modes: C_all split into TF32 hi / lo parts once at create; STRICT mode also keeps
+    // upper bounds of the codeword norms (its tensor-core error bound is kappa ||c|| ||x||).
+    DevBuf Chi, Clo, cn;
     // Input rotation X <- R X (ApplyRotationInPlace), R stored by rows; off when R is the identity.
     DevBuf Rrow;
     bool rotate = false;
@@ -188,7 +189,7 @@ int CheckEncodeArgs(const stlq_b200_encoder* enc, int x_dtype, int64_t n, int be
         return Fail(STLQ_B200_EINVAL, "icm_iters, ils_iters and perturb_k must be >= 0");
     // The beam kernels keep one float per candidate of a layer (beam x codebook size) in shared
     // memory; every beam <= 32 with codebooks <= 1024 fits a B200's 227 KB.
-    if (BeamFastSmemBytes(enc->dims, beam) > enc->max_block_smem)
+    if (BeamFastSmemBytes(enc->dims, beam, enc->gemm_mode == STLQ_B200_GEMM_STRICT) > enc->max_block_smem)
         return Fail(STLQ_B200_EINVAL, "beam x (largest codebook) needs more shared memory than a block of this "
                                       "device has");
     return 0;
@@ -234,6 +235,13 @@ int UploadOrders(stlq_b200_encoder* enc, int icm_iters, int n_ils, uint32_t seed
 }
 
 bool TensorCoreMode(const stlq_b200_encoder* enc) { return enc->gemm_mode != STLQ_B200_GEMM_EXACT; }
+
+// STRICT mode's bound on |xC_tensor - xC_exact| / (||c|| ||x||): (0.4 d + 16) 2^-24.  Measured on
+// B200 at the benchmark shapes (134M entries at d = 128, 67M at d = 96 and d = 960): at most
+// 1.3e-6 (d = 128), 7.3e-7 (d = 96), 7.2e-6 (d = 960), i.e. 3.1x, 4.4x and 3.3x below this bound.
+// The kernels check the bound on every entry they compute exactly and report kErrTcBound
+// (STLQ_B200_EDEVICE) if it is ever exceeded.
+float StrictKappa(int d) { return (0.4f * static_cast<float>(d) + 16.0f) * 0x1p-24f; }
 
 // xC (rows x n, ldo-strided per vector) and optional norms for n <= MaxGemmSliceVectors() vectors
 // in the encoder's GEMM mode.
@@ -292,10 +300,15 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         }
         STLQ_TRY(LaunchXc(enc, Xs, xt, ns, dims.H, enc->xC.as<float>(), dims.H, enc->xn.as<float>(),
                           enc->xnd.as<double>(), stream));
+        // STRICT: xC is the tensor cores'; the beam and refinement kernels recompute, in the exact
+        // GEMM's order, every entry a decision or an output depends on.
+        stlq_b200::ExactDotArgs ea{};
+        if (enc->gemm_mode == STLQ_B200_GEMM_STRICT)
+            ea = stlq_b200::ExactDotArgs{enc->C.as<float>(), Xs, xt, enc->cn.as<float>(), StrictKappa(dims.d)};
         STLQ_CK(stlq_b200::LaunchBeamSearch(dims, BeamGram(enc), enc->Bdiag.as<float>(), enc->xn.as<float>(),
                                             enc->xC.as<float>(), ns, beam, B + s0 * dims.m * cb, enc->redo.as<int>(),
                                             enc->check_filter,
-                                            enc->err_flag.as<unsigned int>(), enc->num_sms, stream));
+                                            enc->err_flag.as<unsigned int>(), enc->num_sms, stream, &ea));
         if (dims.large_root)  // LS, cost and ICM take the root term from the SIMD-order dot
             STLQ_CK(stlq_b200::LaunchRootDot(dims, enc->C.as<float>(), Xs, xt, B + s0 * dims.m * cb, ns,
                                              enc->xC.as<float>(), stream));
@@ -320,6 +333,8 @@ int EncodeDevice(stlq_b200_encoder* enc, const void* X, int x_dtype, int64_t n, 
         ra.a = a ? a + s0 * dims.m : nullptr;
         ra.cost = cost ? cost + s0 : nullptr;
         ra.partials = sse_dev ? enc->partials.as<double>() : nullptr;
+        ra.ex = ea;
+        ra.err_flag = enc->err_flag.as<unsigned int>();
         const int grid = RefineGrid(enc, ns);
         STLQ_CK(stlq_b200::LaunchRefine(ra, grid, stream));
         if (sse_dev) STLQ_CK(stlq_b200::LaunchReducePartials(enc->partials.as<double>(), grid, sse_dev, stream));
@@ -476,6 +491,11 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
                                            strict ? enc->Clo.as<float>() : nullptr, s),
                 "split C_all");
         if (rc) return fail(rc);
+        if (strict) {
+            if ((rc = enc->cn.Ensure(sizeof(float) * H))) return fail(rc);
+            rc = ck(stlq_b200::LaunchNormBounds(enc->C.as<float>(), H, d, enc->cn.as<float>(), s), "codeword norm bounds");
+            if (rc) return fail(rc);
+        }
     }
     if (large_root) {
         // invnorm and the root norms from the reference's SIMD-order Norm2.
@@ -526,7 +546,7 @@ int stlq_b200_destroy(stlq_b200_encoder* enc) {
     if (enc->compute) cudaStreamSynchronize(enc->compute);
     if (enc->copy) cudaStreamSynchronize(enc->copy);
     for (DevBuf* b : {&enc->C, &enc->Gcol, &enc->Grow, &enc->Gdiag, &enc->Bdiag, &enc->invnorm, &enc->err_flag, &enc->xC, &enc->xn,
-                      &enc->Chi, &enc->Clo, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->Xrot, &enc->Rrow, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
+                      &enc->Chi, &enc->Clo, &enc->cn, &enc->Xhi, &enc->Xlo, &enc->Bfull, &enc->Xrot, &enc->Rrow, &enc->xnd, &enc->partials, &enc->orders, &enc->redo, &enc->sse_d})
         b->Release();
     for (int i = 0; i < 2; ++i) {
         enc->xin[i].Release();
@@ -579,6 +599,7 @@ int stlq_b200_sync(stlq_b200_encoder* enc, void* stream) {
         if (flag & stlq_b200::kErrBadShape) what += " bad-shape";
         if (flag & stlq_b200::kErrFilterMiss) what += " beam-filter-miss";
         if (flag & stlq_b200::kErrWaitTimeout) what += " tensor-core-gemm-wait-timeout";
+        if (flag & stlq_b200::kErrTcBound) what += " tensor-core-xc-outside-its-error-bound";
         return Fail(STLQ_B200_EDEVICE, "a kernel reported internal errors:" + what);
     }
     return 0;

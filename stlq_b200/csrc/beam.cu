@@ -27,6 +27,13 @@
 // bounds cannot exclude from entering the scan (ReplayLayer).
 //
 // The layer index is a run-time argument of every routine (see beam_common.cuh).
+//
+// STRICT mode (the kStrict instantiations): xC comes from the tensor cores and differs from the
+// exact GEMM's by at most dg = kappa ||c|| ||x|| per entry.  Every bound is widened by that term
+// (layer 0: Layer0Bounds; later layers: BoundsTail), and every value the selection or the
+// outputs depend on -- the survivors' exact errors, the winners' state, the replay's scans -- is
+// computed from the exact xC entry, recomputed on demand in the exact GEMM's order (ExactCtx::Gamma,
+// with the vector staged in shared memory).  The codes are therefore the exact mode's.
 #include <cstdint>
 
 #include "beam_common.cuh"
@@ -41,9 +48,22 @@ namespace {
 constexpr int kSurvCap = 512;  // exactly evaluated survivors per layer in the fast kernel
 constexpr int kKeep = 64;      // survivors whose exact-evaluation results are kept for Materialize
 
+// The exact xC entry of flat codeword `flat`: the row itself (EXACT and FAST modes take xC as exact)
+// or, in STRICT mode, recomputed in the exact GEMM's order.
+template <bool kStrict>
+__device__ __forceinline__ float ExactGamma(const ExactCtx& ctx, const float* xc, int flat) {
+    if constexpr (kStrict) return ctx.Gamma(flat);
+    else return __ldg(xc + flat);
+}
+
 // Per kept survivor: y[MAXM], v[MAXM], denom, a_last.
 template <int MAXM>
 __host__ __device__ constexpr int KeepStride() { return 2 * MAXM + 2; }
+
+// Floats of each candidate array of the replay kernel: beam x maxKs, at least 64 (STRICT mode's
+// layer 0 splits the first array into a list and its errors, chunks of at least 32).
+__host__ __device__ inline int ReplayCandFloats(int beam, int maxKs) { return beam * maxKs > 64 ? beam * maxKs : 64; }
+__host__ __device__ inline int Align4(int d) { return (d + 3) & ~3; }
 
 struct LayerTable {
     int cand[kMaxBeam];   // candidate (scan index) held by each slot, slot order
@@ -59,12 +79,13 @@ struct LayerTable {
 // Copies the winners' state into the next slot buffer (beam_search.cpp:337-383): parent prefix of
 // R, then each winner's own R column (y, sqrt(denom)), coefficients a_t - v_t a_last, a_last, code.
 // With `keep` (fast kernel) a winner whose survivor position is below kKeep takes y, v, denom,
-// a_last and its error from the exact evaluation already made; otherwise they are recomputed.
-template <int MAXM>
+// a_last and its error from the exact evaluation already made; otherwise they are recomputed (in
+// STRICT mode from the exact xC entry: the fast kernel's gex[survivor position], else recomputed).
+template <int MAXM, bool kStrict>
 __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt,
                             const LayerTable& lt, int newH, const float* __restrict__ Grow,
-                            const float* __restrict__ Gdiag, const float* __restrict__ xc,
-                            const float* keep = nullptr, const float* ex = nullptr) {
+                            const float* __restrict__ Gdiag, const float* __restrict__ xc, const ExactCtx& ctx,
+                            const float* keep = nullptr, const float* ex = nullptr, const float* gex = nullptr) {
     constexpr int NL = MAXM - 1;
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], ldg = dims.ldg, colL = offL - dims.c0;
@@ -93,8 +114,11 @@ __device__ void Materialize(const Dims& dims, int L, const SlotView<MAXM>& cur, 
             a_last = st[2 * MAXM + 1];
             e = ex[p];
         } else {
-            e = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, ldg, colL + k, ak,
-                                 __ldg(xc + offL + k), y, v, &denom, &a_last, dims.large_root != 0);
+            float gamma;
+            if constexpr (kStrict) gamma = gex ? gex[lt.candp[o]] : ctx.Gamma(offL + k);
+            else gamma = __ldg(xc + offL + k);
+            e = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, ldg, colL + k, ak, gamma, y, v, &denom,
+                                 &a_last, dims.large_root != 0);
         }
 #pragma unroll
         for (int t = 0; t < NL; ++t) {
@@ -136,12 +160,11 @@ __device__ int KeepPrevious(int L, int row0, const SlotView<MAXM>& cur, const Sl
     return max(1, keep);
 }
 
-// Layer 0 state of slot o holding codeword k (beam_search.cpp:248-258).
+// Layer 0 state of slot o holding codeword k with exact xC entry gamma (beam_search.cpp:248-258).
 template <int MAXM>
-__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, int ldg, const float* Gdiag, const float* xc,
+__device__ void InitSlot0(const SlotView<MAXM>& s, int o, int k, int ldg, const float* Gdiag, float gamma,
                           float nx2) {
     const float alpha = __ldg(Gdiag + k);
-    const float gamma = __ldg(xc + k);
     const float a1 = div_rn(gamma, alpha);
     const float r00 = __fsqrt_rn(alpha);
     s.rowh(o)[0] = k * ldg;  // layer 0 starts at flat index 0
@@ -172,12 +195,53 @@ __device__ void DeadSlot0(const Dims& dims, const SlotView<MAXM>& s) {
 
 // Layer-0 error of codeword k: a1 = gamma/alpha, e1 = ||x||^2 - gamma*a1, not clamped; a zero
 // codeword (alpha == 0) is skipped (beam_search.cpp:240-252).
-__device__ __forceinline__ float Layer0Error(const float* Gdiag, const float* xc, float nx2, int k) {
+__device__ __forceinline__ float Layer0ErrorG(const float* Gdiag, float gamma, float nx2, int k) {
     const float alpha = __ldg(Gdiag + k);
-    const float gamma = __ldg(xc + k);
     const float e1 = sub_rn(nx2, mul_rn(gamma, div_rn(gamma, alpha)));
     return (alpha != 0.0f && e1 < PosInf()) ? e1 : PosInf();
 }
+__device__ __forceinline__ float Layer0Error(const float* Gdiag, const float* xc, float nx2, int k) {
+    return Layer0ErrorG(Gdiag, __ldg(xc + k), nx2, k);
+}
+
+// STRICT mode: bounds [lo, hi] on Layer0Error of codeword k from the tensor-core entry g (the exact
+// one lies within dg of it): e1 = nx2 - g^2/alpha over |g| in [|g| - dg, |g| + dg], widened by
+// 1e-6 (|nx2| + q_max), far more than the roundings of both this and the exact sequence.  A zero
+// codeword (skipped by the reference) gets [+inf, +inf]; anything non-finite [-inf, +inf].
+__device__ __forceinline__ void Layer0Bounds(const float* Gdiag, const float* xc, const ExactCtx& ctx, float nx2,
+                                             int k, float& lo, float& hi) {
+    const float alpha = __ldg(Gdiag + k);
+    if (alpha == 0.0f) {
+        lo = hi = PosInf();
+        return;
+    }
+    const float ag = fabsf(__ldg(xc + k)), dg = ctx.Bound(k);
+    const float gmax = ag + dg, gmin = fmaxf(ag - dg, 0.0f);
+    const float qmax = gmax * gmax / alpha, qmin = gmin * gmin / alpha;
+    const float slack = 1e-6f * (fabsf(nx2) + qmax);
+    lo = (nx2 - qmax) - slack;
+    hi = (nx2 - qmin) + slack;
+    if (!(lo == lo) || !(hi == hi) || !(slack < PosInf())) {
+        lo = -PosInf();
+        hi = PosInf();
+    }
+}
+
+// STRICT mode, a root too large to keep one bound per codeword: lower bounds recomputed where the
+// selection reads them.
+struct Layer0LoSource {
+    const float* Gdiag;
+    const float* xc;
+    ExactCtx ctx;
+    float nx2;
+    static constexpr bool kVec = false;
+    __device__ float operator()(int k) const {
+        float lo, hi;
+        Layer0Bounds(Gdiag, xc, ctx, nx2, k, lo, hi);
+        return lo;
+    }
+    __device__ const float* v0() const { return nullptr; }
+};
 
 // Where the selection reads a candidate's error (or lower bound): a shared-memory array
 // (16-byte aligned, read four at a time), or, for a layer-0 codebook too large to keep one float
@@ -203,15 +267,18 @@ struct Layer0Source {
 // Self-check of the cheap bounds (STLQ_B200_CHECK_FILTER): the exact error of each candidate must
 // lie inside them; a miss raises kErrFilterMiss.  Inlined: a call site inside the hot loop, even
 // one never taken, costs the loop registers.
-template <int MAXM>
+// In STRICT mode the exact error comes from the exact xC entry (flat index = Gram column + coff).
+template <int MAXM, bool kStrict>
 __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int L, const float* __restrict__ Grow, int ldg,
                                          const int (&col)[kCpt], const bool (&ok)[kCpt], const float (&alpha)[kCpt],
                                          const float (&gamma)[kCpt], const float (&l)[kCpt], const float (&hi)[kCpt],
-                                         unsigned int* err_flag, bool recip) {
+                                         unsigned int* err_flag, bool recip, const ExactCtx& ctx, int coff) {
     const RowArr<MAXM> flat = RowsOf<MAXM>(cur, h, L);
     for (int c = 0; c < kCpt; ++c) {
         if (!ok[c]) continue;
-        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, ldg, col[c], alpha[c], gamma[c], nullptr, nullptr,
+        float g = gamma[c];
+        if constexpr (kStrict) g = ctx.Gamma(col[c] + coff);
+        const float e = EvalExactL<MAXM>(cur, h, L, flat, Grow, ldg, col[c], alpha[c], g, nullptr, nullptr,
                                          nullptr, nullptr, recip);
         if (e < PosInf() && !(e >= l[c] && e <= hi[c])) atomicOr(err_flag, kErrFilterMiss);
     }
@@ -221,17 +288,17 @@ __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int
 // the upper bounds into hi_out), and the thread's smallest upper bound as the return value.  One copy per layer, inlined (with L a
 // compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
 // call boundary costs more than the copies save).
-template <int MAXM, int L, bool kHi, bool kWide>
+template <int MAXM, int L, bool kHi, bool kWide, bool kStrict>
 __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int colL,
                                            const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                                            const float* __restrict__ xc, float* lo, float* hi_out, int check,
-                                           unsigned int* err_flag, bool recip) {
+                                           unsigned int* err_flag, bool recip, const ExactCtx& ctx) {
     const int tid = threadIdx.x;
     float hmin = PosInf();  // never NaN: a bound is finite or +-inf
     // Codebooks above 256 codewords (the kWide kernels) are walked in chunks of kMaxK, kCpt
     // codewords per thread; the other kernels make one pass with kc = 0 known at compile time.
     for (int kc = 0; kc < (kWide ? K : 1); kc += kMaxK) {
-        float alpha[kCpt], gamma[kCpt], lof[kCpt];
+        float alpha[kCpt], gamma[kCpt], lof[kCpt], dg[kCpt];
         int col[kCpt];
         bool ok[kCpt];
 #pragma unroll
@@ -242,13 +309,14 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
             alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
             gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
             lof[c] = IsZeroColumn(alpha[c]) ? PosInf() : -PosInf();
+            dg[c] = (kStrict && ok[c]) ? ctx.Bound(offL + k) : 0.0f;
         }
         const float* gq[kCpt];
 #pragma unroll
         for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
         for (int h = 0; h < curH; ++h) {
             float l[kCpt], hi[kCpt];
-            CheapBounds<MAXM, L>(cur, h, gq, ok, alpha, gamma, lof, l, hi);
+            CheapBounds<MAXM, L, kStrict>(cur, h, gq, ok, alpha, gamma, lof, dg, l, hi);
 #pragma unroll
             for (int c = 0; c < kCpt; ++c) {
                 if (ok[c]) {
@@ -257,7 +325,9 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
                     hmin = fminf(hmin, hi[c]);
                 }
             }
-            if (check) CheckBounds<MAXM>(cur, h, L, Grow, 0, col, ok, alpha, gamma, l, hi, err_flag, recip);
+            if (check)
+                CheckBounds<MAXM, kStrict>(cur, h, L, Grow, 0, col, ok, alpha, gamma, l, hi, err_flag, recip, ctx,
+                                           offL - colL);
         }
     }
     return OrderKey(hmin);
@@ -271,12 +341,12 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
 template <int MAXM>
 constexpr bool kPairPath = MAXM > 8;
 static_assert(kCpt == 2, "the paired cheap pass takes two codewords per thread");
-template <int MAXM, int L, bool kHi, bool kWide>
+template <int MAXM, int L, bool kHi, bool kWide, bool kStrict>
 __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
                                                int offL, int colL, const float* __restrict__ Grow,
                                                const float* __restrict__ Gdiag, const float* __restrict__ xc,
                                                float* lo, float* hi_out, int check, unsigned int* err_flag,
-                                               bool recip) {
+                                               bool recip, const ExactCtx& ctx) {
     const int tid = threadIdx.x;
     float hmin = PosInf();
     for (int kc = 0; kc < (kWide ? K : 1); kc += 2 * kThreads) {
@@ -286,11 +356,13 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
         const float2 gamma = ok ? __ldg(reinterpret_cast<const float2*>(xc + offL + k)) : make_float2(0.0f, 0.0f);
         const float2 lof = make_float2(IsZeroColumn(alpha.x) ? PosInf() : -PosInf(),
                                        IsZeroColumn(alpha.y) ? PosInf() : -PosInf());
+        const float2 dg = (kStrict && ok) ? make_float2(ctx.Bound(offL + k), ctx.Bound(offL + k + 1))
+                                          : make_float2(0.0f, 0.0f);
         const float* gq = Grow + colL + k;
         for (int h = 0; h < curH; ++h) {
             float2 l, hi;
-            CheapBoundsPair<MAXM, L>(table + h * PairTableStride<MAXM>(), cur.rowh(h), cur.E[h], cur.ill[h] != 0, gq,
-                                     ok, alpha, gamma, lof, l, hi);
+            CheapBoundsPair<MAXM, L, kStrict>(table + h * PairTableStride<MAXM>(), cur.rowh(h), cur.E[h],
+                                              cur.ill[h] != 0, gq, ok, alpha, gamma, lof, dg, l, hi);
             if (ok) {
                 *reinterpret_cast<float2*>(lo + h * K + k) = l;
                 if (kHi) *reinterpret_cast<float2*>(hi_out + h * K + k) = hi;
@@ -301,7 +373,8 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
                 const bool okc[kCpt] = {ok, ok};
                 const float al[kCpt] = {alpha.x, alpha.y}, ga[kCpt] = {gamma.x, gamma.y};
                 const float la[kCpt] = {l.x, l.y}, ha[kCpt] = {hi.x, hi.y};
-                CheckBounds<MAXM>(cur, h, L, Grow, 0, col, okc, al, ga, la, ha, err_flag, recip);
+                CheckBounds<MAXM, kStrict>(cur, h, L, Grow, 0, col, okc, al, ga, la, ha, err_flag, recip, ctx,
+                                           offL - colL);
             }
         }
     }
@@ -309,19 +382,19 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
 }
 
 // `table` non-null: the paired pass (Dims::pair) over the slots' pair tables.
-template <int MAXM, bool kHi, bool kWide>
+template <int MAXM, bool kHi, bool kWide, bool kStrict>
 __device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
-                                  int check, unsigned int* err, bool recip, const float2* table) {
+                                  int check, unsigned int* err, bool recip, const float2* table, const ExactCtx& ctx) {
 #define STLQ_B200_CHEAP(LL)                                                                          \
     case LL:                                                                                         \
         if constexpr (LL < MAXM) {                                                                   \
             if constexpr (kPairPath<MAXM>)                                                           \
                 if (table)                                                                           \
-                    return CheapPassPair<MAXM, LL, kHi, kWide>(cur, table, curH, K, offL, colL, Grow, Gdiag, xc, lo, \
-                                                        hi_out, check, err, recip);                  \
-            return CheapPass<MAXM, LL, kHi, kWide>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err, \
-                                                   recip);                                           \
+                    return CheapPassPair<MAXM, LL, kHi, kWide, kStrict>(cur, table, curH, K, offL, colL, Grow, Gdiag, \
+                                                                        xc, lo, hi_out, check, err, recip, ctx); \
+            return CheapPass<MAXM, LL, kHi, kWide, kStrict>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, \
+                                                            check, err, recip, ctx);                 \
         }                                                                                            \
         break;
     switch (L) {
@@ -433,6 +506,57 @@ struct Replay {
         }
         return count;
     }
+    // PreScan over candidates [base0, base0 + n) whose bounds src(idx, lo, hi) computes: the indices
+    // of the candidates that can enter are written to list[] (in scan order); returns their count.
+    // Called chunk after chunk, the state carries over, so the chunks together are one pre-scan.
+    template <class Src>
+    __device__ int PreScanFn(Src src, int base0, int n, int* list) {
+        const int lane = threadIdx.x & 31;
+        int count = 0;
+        for (int b = 0; b < n; b += 32) {
+            const bool in = b + lane < n;
+            float l = PosInf(), h = PosInf();
+            if (in) src(base0 + b + lane, l, h);
+            const bool need = in && l < worst;
+            const unsigned nm = __ballot_sync(kFull, need);
+            if (need) list[count + __popc(nm & ((1u << lane) - 1u))] = base0 + b + lane;
+            count += __popc(nm);
+            unsigned mask = __ballot_sync(kFull, h < worst);
+            while (mask) {
+                const int q = __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float hq = __shfl_sync(kFull, h, q);
+                if (hq < worst) {
+                    if (lane == widx) es = hq;
+                    Refresh();
+                }
+            }
+        }
+        return count;
+    }
+    // ScanList with the errors stored by list position (exl[p] is the error of candidate list[p]).
+    __device__ void ScanListPos(const float* exl, const int* list, int n) {
+        const int lane = threadIdx.x & 31;
+        for (int base = 0; base < n; base += 32) {
+            const bool in = base + lane < n;
+            const int idx = in ? list[base + lane] : -1;
+            const float e = in ? exl[base + lane] : PosInf();
+            unsigned mask = __ballot_sync(kFull, e < worst);
+            while (mask) {
+                const int l = __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float el = __shfl_sync(kFull, e, l);
+                const int il = __shfl_sync(kFull, idx, l);
+                if (el < worst) {
+                    if (lane == widx) {
+                        es = el;
+                        cs = il;
+                    }
+                    Refresh();
+                }
+            }
+        }
+    }
     __device__ void Publish(int beam, LayerTable& lt) {
         const int lane = threadIdx.x & 31;
         if (lane < beam) lt.cand[lane] = cs;
@@ -446,11 +570,11 @@ struct Replay {
 // slot), then the reference's replacement scan over the exact errors.  Without room for the upper
 // bounds (his == nullptr: beam x codebook size too large for shared memory) every candidate is
 // evaluated exactly; the scan's result is the same.
-template <int MAXM, bool kWide>
+template <int MAXM, bool kWide, bool kStrict>
 __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                             const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt,
-                            float2* table) {
+                            float2* table, const ExactCtx& ctx) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
     const int n_cand = curH * K;
@@ -462,8 +586,8 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
                 __syncthreads();
             }
         }
-        CheapDispatch<MAXM, true, kWide>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
-                                  dims.large_root != 0, table);
+        CheapDispatch<MAXM, true, kWide, kStrict>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
+                                                  dims.large_root != 0, table, ctx);
         __syncthreads();
         if (tid < 32) {
             Replay rp;
@@ -478,7 +602,8 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
         const int idx = his ? list[p] : p;
         const int h = idx / K, k = idx - h * K;
         errs[idx] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, dims.ldg, colL + k, __ldg(Gdiag + offL + k),
-                                     __ldg(xc + offL + k), nullptr, nullptr, nullptr, nullptr, dims.large_root != 0);
+                                     ExactGamma<kStrict>(ctx, xc, offL + k), nullptr, nullptr, nullptr, nullptr,
+                                     dims.large_root != 0);
     }
     __syncthreads();
     if (tid < 32) {
@@ -493,32 +618,87 @@ __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, 
     if (newH == 0) {
         curH = KeepPrevious<MAXM>(L, offL * dims.ldg, cur, nxt, curH, beam);
     } else {
-        Materialize<MAXM>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc);
+        Materialize<MAXM, kStrict>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc, ctx);
         curH = newH;
     }
+    __syncthreads();
+}
+
+// STRICT mode, layer 0 of the replay: the pre-scan over the layer-0 bounds (computed where they
+// are read, so the root may be of any size), in chunks of `ch` candidates: each chunk's entering
+// candidates are listed (list[0..ch)), evaluated exactly (exl[0..ch)) and scanned.  The two scans'
+// states carry over from chunk to chunk, so the result is the scan over all K0 exact errors.
+// Fills lt.cand / lt.n_slots like Replay::Publish.
+__device__ void ReplayLayer0Strict(const float* __restrict__ Gdiag, const float* __restrict__ xc, float nx2, int K0,
+                                   int beam, int* list, float* exl, int ch, LayerTable& lt, const ExactCtx& ctx) {
+    const int tid = threadIdx.x;
+    Replay pre, scan;  // used by warp 0 only
+    if (tid < 32) {
+        pre.Init(beam);
+        scan.Init(beam);
+    }
+    auto bounds = [&](int k, float& lo, float& hi) { Layer0Bounds(Gdiag, xc, ctx, nx2, k, lo, hi); };
+    for (int base = 0; base < K0; base += ch) {
+        const int n = min(ch, K0 - base);
+        if (tid < 32) {
+            const int cnt = pre.PreScanFn(bounds, base, n, list);
+            if (tid == 0) lt.n_surv = cnt;
+        }
+        __syncthreads();
+        const int cnt = lt.n_surv;
+        for (int p = tid; p < cnt; p += kThreads) exl[p] = Layer0ErrorG(Gdiag, ctx.Gamma(list[p]), nx2, list[p]);
+        __syncthreads();
+        if (tid < 32) scan.ScanListPos(exl, list, cnt);
+        __syncthreads();
+    }
+    if (tid < 32) scan.Publish(beam, lt);
     __syncthreads();
 }
 
 // Encodes the vectors listed in vec_list[0 .. *count) (or 0 .. n when vec_list is null).  kWide
 // (BigCodebooks): a codebook of layers 1..m-1 has more than kMaxK codewords, or layer 0's errors do
 // not fit the candidate array; the other kernels, the common sizes, compile neither case in.
-template <int MAXM, bool kWide>
+template <class T>
+__device__ __forceinline__ T* Align16(void* p) {
+    return reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+}
+
+// STRICT mode: stages vector `vec` as float in xs (d floats) and returns its exact-entry context.
+__device__ __forceinline__ ExactCtx StageVector(const ExactDotArgs& ea, const Dims& dims, int64_t vec,
+                                                const float* xc, float nx2, float* xs, unsigned int* err) {
+    const int d = dims.d;
+    if (ea.x_dtype == 0) {
+        const float* xv = static_cast<const float*>(ea.X) + vec * d;
+        for (int i = threadIdx.x; i < d; i += kThreads) xs[i] = xv[i];
+    } else {
+        const uint8_t* xv = static_cast<const uint8_t*>(ea.X) + vec * d;
+        for (int i = threadIdx.x; i < d; i += kThreads) xs[i] = static_cast<float>(xv[i]);
+    }
+    return ExactCtx{ea.C, ea.cn, xc, xs, d, StrictKx(ea.kappa, nx2), err};
+}
+
+template <int MAXM, bool kWide, bool kStrict>
 __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const float* __restrict__ Grow,
                                                              const float* __restrict__ Gdiag,
                                                              const float* __restrict__ xnorm2,
                                                              const float* __restrict__ xC, int64_t n, int beam,
                                                              void* __restrict__ Bout, const int* vec_list,
-                                                             const int* count, bool prescan) {
+                                                             const int* count, bool prescan, ExactDotArgs ea,
+                                                             unsigned int* err_flag) {
     extern __shared__ __align__(16) unsigned char smem[];
     const size_t sv = SlotView<MAXM>::Bytes(beam);
     size_t off = (2 * sv + 15) & ~size_t(15);
     LayerTable& lt = *reinterpret_cast<LayerTable*>(smem + off);
     float* errs = reinterpret_cast<float*>(smem + ((off + sizeof(LayerTable) + 15) & ~size_t(15)));
-    float* his = prescan ? errs + beam * dims.maxKs : nullptr;
+    const int nc = ReplayCandFloats(beam, dims.maxKs);
+    float* his = prescan ? errs + nc : nullptr;
+    float* after = errs + (prescan ? 2 : 1) * nc;
     float2* table = nullptr;  // pair tables after the candidate arrays (Dims::pair, pre-scan only)
-    if (dims.pair && prescan)
-        table = reinterpret_cast<float2*>(
-            (reinterpret_cast<uintptr_t>(errs + 2 * beam * dims.maxKs) + 15) & ~uintptr_t(15));
+    if (dims.pair && prescan) {
+        table = Align16<float2>(after);
+        after = reinterpret_cast<float*>(table + beam * PairTableStride<MAXM>());
+    }
+    float* xs = Align16<float>(after);  // STRICT: the vector being encoded
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     const int64_t total = vec_list ? static_cast<int64_t>(*count) : n;
@@ -526,26 +706,33 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         const int64_t vec = vec_list ? vec_list[i] : i;
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
-        // Layer 0 keeps its errors in errs[] when they fit (beam x maxKs floats), else recomputes them.
-        const bool stored0 = !kWide || K0 <= beam * dims.maxKs;
-        if (stored0)
-            for (int k = tid; k < K0; k += kThreads) errs[k] = Layer0Error(Gdiag, xc, nx2, k);
-        __syncthreads();
-        if (tid < 32) {
-            Replay rp;
-            rp.Init(beam);
-            if constexpr (kWide) {
-                if (stored0) rp.Scan(ArraySource{errs}, K0);
-                else rp.Scan(Layer0Source{Gdiag, xc, nx2}, K0);
-            } else {
-                rp.Scan(ArraySource{errs}, K0);
+        ExactCtx ctx{};
+        if constexpr (kStrict) {
+            ctx = StageVector(ea, dims, vec, xc, nx2, xs, err_flag);
+            ReplayLayer0Strict(Gdiag, xc, nx2, K0, beam, reinterpret_cast<int*>(errs), errs + (nc / 2 & ~31),
+                               nc / 2 & ~31, lt, ctx);
+        } else {
+            // Layer 0 keeps its errors in errs[] when they fit (beam x maxKs floats), else recomputes them.
+            const bool stored0 = !kWide || K0 <= beam * dims.maxKs;
+            if (stored0)
+                for (int k = tid; k < K0; k += kThreads) errs[k] = Layer0Error(Gdiag, xc, nx2, k);
+            __syncthreads();
+            if (tid < 32) {
+                Replay rp;
+                rp.Init(beam);
+                if constexpr (kWide) {
+                    if (stored0) rp.Scan(ArraySource{errs}, K0);
+                    else rp.Scan(Layer0Source{Gdiag, xc, nx2}, K0);
+                } else {
+                    rp.Scan(ArraySource{errs}, K0);
+                }
+                rp.Publish(beam, lt);
             }
-            rp.Publish(beam, lt);
+            __syncthreads();
         }
-        __syncthreads();
         int curH = lt.n_slots;
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.ldg, Gdiag, xc, nx2);
+        if (tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.ldg, Gdiag, ExactGamma<kStrict>(ctx, xc, lt.cand[tid]), nx2);
         if (curH == 0) {
             DeadSlot0<MAXM>(dims, s0);
             curH = 1;
@@ -553,9 +740,9 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         __syncthreads();
         int ci = 0;
         for (int L = 1; L < m; ++L) {
-            ReplayLayer<MAXM, kWide>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
-                              SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, errs, his,
-                              lt, table);
+            ReplayLayer<MAXM, kWide, kStrict>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
+                                              SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc,
+                                              beam, errs, his, lt, table, ctx);
             ci ^= 1;
         }
         if (tid < 32) {  // first slot with the smallest error (beam_search.cpp:409-416)
@@ -715,11 +902,12 @@ __device__ __noinline__ int RankSurvivors(const float* ex, const uint16_t* surv,
     return min(n_valid, beam);
 }
 
-template <int MAXM, bool kWide>
+// gex (STRICT): the survivors' exact xC entries by survivor position, for Materialize.
+template <int MAXM, bool kWide, bool kStrict>
 __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
                          const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
                          int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, uint64_t* keys, float* keep,
-                         int check, unsigned int* err_flag, float2* table) {
+                         int check, unsigned int* err_flag, float2* table, const ExactCtx& ctx, float* gex) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
     if constexpr (kPairPath<MAXM>) {
@@ -728,9 +916,8 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
             __syncthreads();
         }
     }
-    const uint32_t hmin =
-        CheapDispatch<MAXM, false, kWide>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag,
-                                   dims.large_root != 0, table);
+    const uint32_t hmin = CheapDispatch<MAXM, false, kWide, kStrict>(
+        L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag, dims.large_root != 0, table, ctx);
     const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     for (int p = tid; p < S; p += kThreads) {
@@ -738,8 +925,10 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
         const int h = idx / K, k = idx - h * K;
         float* st = keep + p * KeepStride<MAXM>();
         const bool kp = p < kKeep;
+        const float gamma = ExactGamma<kStrict>(ctx, xc, offL + k);
+        if constexpr (kStrict) gex[p] = gamma;
         ex[p] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, dims.ldg, colL + k, __ldg(Gdiag + offL + k),
-                                 __ldg(xc + offL + k), kp ? st : nullptr, kp ? st + MAXM : nullptr,
+                                 gamma, kp ? st : nullptr, kp ? st + MAXM : nullptr,
                                  kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr, dims.large_root != 0);
     }
     __syncthreads();
@@ -750,19 +939,19 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
         __syncthreads();
         return kept;
     }
-    Materialize<MAXM>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc, keep, ex);
+    Materialize<MAXM, kStrict>(dims, L, cur, nxt, lt, newH, Grow, Gdiag, xc, ctx, keep, ex, kStrict ? gex : nullptr);
     __syncthreads();
     return newH;
 }
 
-template <int MAXM, bool kWide>
+template <int MAXM, bool kWide, bool kStrict>
 __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Dims dims, const float* __restrict__ Grow,
                                                            const float* __restrict__ Gdiag,
                                                            const float* __restrict__ xnorm2,
                                                            const float* __restrict__ xC, int64_t n, int beam,
                                                            void* __restrict__ Bout, int* redo_list, int* redo_count,
                                                            int check, unsigned int* err_flag,
-                                                           unsigned long long* stats) {
+                                                           unsigned long long* stats, ExactDotArgs ea) {
     extern __shared__ __align__(16) unsigned char smem[];
     const size_t sv = SlotView<MAXM>::Bytes(beam);
     size_t off = (2 * sv + 15) & ~size_t(15);
@@ -773,38 +962,74 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     float* ex = lo + beam * dims.maxKs;
     float* keep = ex + kSurvCap;
     uint16_t* surv = reinterpret_cast<uint16_t*>(keep + kKeep * KeepStride<MAXM>());
-    float2* table = dims.pair ? reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(surv + kSurvCap) + 15) &
-                                                          ~uintptr_t(15))
-                              : nullptr;
+    float2* table = dims.pair ? Align16<float2>(surv + kSurvCap) : nullptr;
+    // STRICT: the vector being encoded, then the survivors' exact xC entries.
+    float* xs = Align16<float>(table ? static_cast<void*>(table + beam * PairTableStride<MAXM>())
+                                     : static_cast<void*>(surv + kSurvCap));
+    float* gex = xs + Align4(dims.d);
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
     unsigned long long n_surv = 0, n_layers = 0, n_vec = 0, n_redo = 0;  // thread 0's tallies
     for (int64_t vec = blockIdx.x; vec < n; vec += gridDim.x) {
         const float* xc = xC + vec * dims.H;
         const float nx2 = __ldg(xnorm2 + vec);
-        // Layer 0: exact errors are cheap; they serve as their own bounds.  They are kept in lo[]
-        // when they fit (beam x maxKs floats), else recomputed where the selection reads them.
+        // Layer 0 errors are kept in lo[] when they fit (beam x maxKs floats), else recomputed
+        // where the selection reads them.
         const bool stored0 = !kWide || K0 <= beam * dims.maxKs;
         uint32_t hmin = 0xffffffffu;
-        for (int k = tid; k < K0; k += kThreads) {
-            const float e1 = Layer0Error(Gdiag, xc, nx2, k);
-            if (stored0) lo[k] = e1;
-            hmin = min(hmin, OrderKey(e1));
-        }
+        ExactCtx ctx{};
         int curH;
-        if constexpr (kWide)
-            curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
-                           : SelectSurvivors(Layer0Source{Gdiag, xc, nx2}, K0, hmin, beam, lt, surv);
-        else
-            curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
-        if (curH >= 0) {
-            for (int p = tid; p < curH; p += kThreads)
-                ex[p] = stored0 ? lo[surv[p]] : Layer0Error(Gdiag, xc, nx2, surv[p]);
-            __syncthreads();
-            curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
+        if constexpr (kStrict) {
+            // Bounds from the tensor-core entries; the survivors' errors exactly.
+            ctx = StageVector(ea, dims, vec, xc, nx2, xs, err_flag);
+            if (check) __syncthreads();  // the self-check below reads the staged vector
+            for (int k = tid; k < K0; k += kThreads) {
+                float l, h;
+                Layer0Bounds(Gdiag, xc, ctx, nx2, k, l, h);
+                if (stored0) lo[k] = l;
+                hmin = min(hmin, OrderKey(h));
+                if (check) {
+                    const float e = Layer0ErrorG(Gdiag, ctx.Gamma(k), nx2, k);
+                    if (e < PosInf() && !(e >= l && e <= h)) atomicOr(err_flag, kErrFilterMiss);
+                }
+            }
+            if constexpr (kWide)
+                curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
+                               : SelectSurvivors(Layer0LoSource{Gdiag, xc, ctx, nx2}, K0, hmin, beam, lt, surv);
+            else
+                curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
+            if (curH >= 0) {
+                for (int p = tid; p < curH; p += kThreads) {
+                    const float g = ctx.Gamma(surv[p]);
+                    gex[p] = g;
+                    ex[p] = Layer0ErrorG(Gdiag, g, nx2, surv[p]);
+                }
+                __syncthreads();
+                curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
+            }
+        } else {
+            // Exact errors are cheap here; they serve as their own bounds.
+            for (int k = tid; k < K0; k += kThreads) {
+                const float e1 = Layer0Error(Gdiag, xc, nx2, k);
+                if (stored0) lo[k] = e1;
+                hmin = min(hmin, OrderKey(e1));
+            }
+            if constexpr (kWide)
+                curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
+                               : SelectSurvivors(Layer0Source{Gdiag, xc, nx2}, K0, hmin, beam, lt, surv);
+            else
+                curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
+            if (curH >= 0) {
+                for (int p = tid; p < curH; p += kThreads)
+                    ex[p] = stored0 ? lo[surv[p]] : Layer0Error(Gdiag, xc, nx2, surv[p]);
+                __syncthreads();
+                curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
+            }
         }
         const SlotView<MAXM> s0 = SlotView<MAXM>::At(smem, beam);
-        if (curH > 0 && tid < curH) InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.ldg, Gdiag, xc, nx2);
+        if (curH > 0 && tid < curH)
+            InitSlot0<MAXM>(s0, tid, lt.cand[tid], dims.ldg, Gdiag,
+                            kStrict ? gex[lt.candp[tid]] : __ldg(xc + lt.cand[tid]), nx2);
         if (curH == 0) {
             DeadSlot0<MAXM>(dims, s0);
             curH = 1;
@@ -812,9 +1037,10 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         __syncthreads();
         int ci = 0;
         for (int L = 1; L < m && curH > 0; ++L) {
-            curH = FastLayer<MAXM, kWide>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
-                                   SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc, beam, lo, lt,
-                                   surv, ex, keys, keep, check, err_flag, table);
+            curH = FastLayer<MAXM, kWide, kStrict>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
+                                                   SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag,
+                                                   xc, beam, lo, lt, surv, ex, keys, keep, check, err_flag, table, ctx,
+                                                   gex);
             ci ^= 1;
             n_surv += lt.n_surv;
             ++n_layers;
@@ -845,20 +1071,28 @@ size_t PairTableBytes(int beam) {
     return 16 + sizeof(float2) * static_cast<size_t>(beam) * PairTableStride<MAXM>();
 }
 
+// STRICT mode's shared arrays: the staged vector (strict_d floats, 0 when not STRICT) and, in the
+// fast kernel, the survivors' exact xC entries; with alignment slack.
+size_t StrictBytes(int strict_d, bool fast) {
+    return strict_d > 0 ? 16 + sizeof(float) * (Align4(strict_d) + (fast ? kSurvCap : 0)) : 0;
+}
+
 template <int MAXM>
-size_t FastSmemBytes(int beam, int maxK, bool pair = false) {
+size_t FastSmemBytes(int beam, int maxK, bool pair = false, int strict_d = 0) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
     return b + sizeof(uint64_t) * kSurvCap + sizeof(float) * beam * maxK + (sizeof(float) + sizeof(uint16_t)) * kSurvCap +
-           sizeof(float) * kKeep * KeepStride<MAXM>() + 16 + (pair ? PairTableBytes<MAXM>(beam) : 0);
+           sizeof(float) * kKeep * KeepStride<MAXM>() + 16 + (pair ? PairTableBytes<MAXM>(beam) : 0) +
+           StrictBytes(strict_d, true);
 }
 
 // With the pre-scan: errors (lower bounds first) and upper bounds; without: errors only.
 template <int MAXM>
-size_t ReplaySmemBytes(int beam, int maxK, bool prescan, bool pair = false) {
+size_t ReplaySmemBytes(int beam, int maxK, bool prescan, bool pair = false, int strict_d = 0) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
-    return b + (prescan ? 2 : 1) * sizeof(float) * beam * maxK + 16 + (pair && prescan ? PairTableBytes<MAXM>(beam) : 0);
+    return b + (prescan ? 2 : 1) * sizeof(float) * ReplayCandFloats(beam, maxK) + 16 +
+           (pair && prescan ? PairTableBytes<MAXM>(beam) : 0) + StrictBytes(strict_d, false);
 }
 
 // The largest dynamic shared memory a block of the current device may opt into.
@@ -890,8 +1124,8 @@ bool PairKeepsOccupancy(KernelT kernel, size_t smem_scalar, size_t smem_pair) {
 
 // The replay runs its pre-scan whenever the upper bounds fit beside the errors.
 template <int MAXM>
-bool ReplayPrescan(int beam, int maxK) {
-    return ReplaySmemBytes<MAXM>(beam, maxK, true) <= MaxBlockSmem();
+bool ReplayPrescan(int beam, int maxK, int strict_d = 0) {
+    return ReplaySmemBytes<MAXM>(beam, maxK, true, false, strict_d) <= MaxBlockSmem();
 }
 
 // Sets the kernel's shared-memory size, finds how many CTAs fit on an SM, then asks for the
@@ -928,33 +1162,35 @@ cudaError_t Prepare(KernelT kernel, size_t smem, int num_sms, int64_t n, int* gr
     return cudaSuccess;
 }
 
-template <int MAXM, bool kWide>
+// strict_d: STRICT mode (ea.X non-null): the vector dimension, for the staged vector.
+template <int MAXM, bool kWide, bool kStrict>
 cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2, const float* xC,
                         int64_t n, int beam, void* Bout, int* redo, int check, unsigned int* err_flag,
-                        unsigned long long* stats, int num_sms, cudaStream_t stream) {
+                        unsigned long long* stats, int num_sms, cudaStream_t stream, const ExactDotArgs& ea) {
+    const int sd = kStrict ? dims.d : 0;
     int grid = 0;
     Dims df = dims;
     df.pair = kPairPath<MAXM> && dims.pair &&
-              PairKeepsOccupancy(BeamFastKernel<MAXM, kWide>, FastSmemBytes<MAXM>(beam, dims.maxKs),
-                                 FastSmemBytes<MAXM>(beam, dims.maxKs, true));
-    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs, df.pair != 0);
-    cudaError_t e = Prepare(BeamFastKernel<MAXM, kWide>, fsm, num_sms, n, &grid);
+              PairKeepsOccupancy(BeamFastKernel<MAXM, kWide, kStrict>, FastSmemBytes<MAXM>(beam, dims.maxKs, false, sd),
+                                 FastSmemBytes<MAXM>(beam, dims.maxKs, true, sd));
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs, df.pair != 0, sd);
+    cudaError_t e = Prepare(BeamFastKernel<MAXM, kWide, kStrict>, fsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
-    BeamFastKernel<MAXM, kWide><<<grid, kThreads, fsm, stream>>>(df, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1, redo,
-                                                          check, err_flag, stats);
+    BeamFastKernel<MAXM, kWide, kStrict><<<grid, kThreads, fsm, stream>>>(df, Grow, Gdiag, xnorm2, xC, n, beam, Bout,
+                                                                          redo + 1, redo, check, err_flag, stats, ea);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
+    const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs, sd);
     Dims dr = dims;
     dr.pair = kPairPath<MAXM> && dims.pair && prescan &&
-              ReplaySmemBytes<MAXM>(beam, dims.maxKs, true, true) <= MaxBlockSmem();
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, dr.pair != 0);
-    e = Prepare(BeamReplayKernel<MAXM, kWide>, rsm, num_sms, n, &grid);
+              ReplaySmemBytes<MAXM>(beam, dims.maxKs, true, true, sd) <= MaxBlockSmem();
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, dr.pair != 0, sd);
+    e = Prepare(BeamReplayKernel<MAXM, kWide, kStrict>, rsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
-    BeamReplayKernel<MAXM, kWide><<<grid, kThreads, rsm, stream>>>(dr, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo + 1,
-                                                            redo, prescan);
+    BeamReplayKernel<MAXM, kWide, kStrict><<<grid, kThreads, rsm, stream>>>(dr, Grow, Gdiag, xnorm2, xC, n, beam, Bout,
+                                                                            redo + 1, redo, prescan, ea, err_flag);
     return cudaGetLastError();
 }
 
@@ -967,17 +1203,18 @@ cudaError_t PrepareT(const Dims& dims, int beam) {
     const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
     const size_t r1 = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, pair);
     const size_t rsm = r1 <= MaxBlockSmem() ? r1 : ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
-    cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM, kWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(fsm));
+    cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM, kWide, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(fsm));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(BeamReplayKernel<MAXM, kWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(BeamReplayKernel<MAXM, kWide, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(rsm));
 }
 
 }  // namespace
 
-size_t BeamFastSmemBytes(const Dims& dims, int beam) {
-    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxKs) : FastSmemBytes<16>(beam, dims.maxKs);
+size_t BeamFastSmemBytes(const Dims& dims, int beam, bool strict) {
+    const int sd = strict ? dims.d : 0;
+    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxKs, false, sd) : FastSmemBytes<16>(beam, dims.maxKs, false, sd);
 }
 
 // The kWide kernels: a codebook of layers 1..m-1 above kMaxK codewords (chunked cheap passes) or
@@ -996,11 +1233,14 @@ cudaError_t PrepareBeamKernels(const Dims& dims, int beam) {
 // no later launch of any beam kernel variant does that first-use work.
 cudaError_t LoadAllBeamKernels() {
     cudaFuncAttributes a{};
-    const void* kernels[] = {
-        reinterpret_cast<const void*>(BeamFastKernel<8, false>),    reinterpret_cast<const void*>(BeamFastKernel<8, true>),
-        reinterpret_cast<const void*>(BeamFastKernel<16, false>),   reinterpret_cast<const void*>(BeamFastKernel<16, true>),
-        reinterpret_cast<const void*>(BeamReplayKernel<8, false>),  reinterpret_cast<const void*>(BeamReplayKernel<8, true>),
-        reinterpret_cast<const void*>(BeamReplayKernel<16, false>), reinterpret_cast<const void*>(BeamReplayKernel<16, true>)};
+    const void* kernels[] = {reinterpret_cast<const void*>(BeamFastKernel<8, false, false>),
+                             reinterpret_cast<const void*>(BeamFastKernel<8, true, false>),
+                             reinterpret_cast<const void*>(BeamFastKernel<16, false, false>),
+                             reinterpret_cast<const void*>(BeamFastKernel<16, true, false>),
+                             reinterpret_cast<const void*>(BeamReplayKernel<8, false, false>),
+                             reinterpret_cast<const void*>(BeamReplayKernel<8, true, false>),
+                             reinterpret_cast<const void*>(BeamReplayKernel<16, false, false>),
+                             reinterpret_cast<const void*>(BeamReplayKernel<16, true, false>)};
     for (const void* k : kernels) {
         const cudaError_t e = cudaFuncGetAttributes(&a, k);
         if (e != cudaSuccess) return e;
@@ -1009,17 +1249,25 @@ cudaError_t LoadAllBeamKernels() {
 }
 
 // redo: n + 1 ints of scratch (a count, then vector ids handed from the fast to the replay kernel).
+// ea (may be null): STRICT mode's exact-entry inputs; with ea->X non-null the kStrict kernels run.
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
                              const float* xC, int64_t n, int beam, void* Bout, int* redo, int check,
-                             unsigned int* err_flag, int num_sms, cudaStream_t stream) {
+                             unsigned int* err_flag, int num_sms, cudaStream_t stream, const ExactDotArgs* ea) {
     if (n <= 0) return cudaSuccess;
     // The encoder's flag word is followed by four 64-bit counters (BeamStats).
     unsigned long long* stats = err_flag ? reinterpret_cast<unsigned long long*>(err_flag + 4) : nullptr;
     const bool wide = BigCodebooks(dims, beam);  // separate kernels: the common sizes keep the simple paths
-#define STLQ_B200_LAUNCH(MM, WW) \
-    LaunchBeamT<MM, WW>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms, stream)
-    if (dims.m <= 8) return wide ? STLQ_B200_LAUNCH(8, true) : STLQ_B200_LAUNCH(8, false);
-    return wide ? STLQ_B200_LAUNCH(16, true) : STLQ_B200_LAUNCH(16, false);
+    const bool strict = ea && ea->X;
+    const ExactDotArgs none{};
+    const ExactDotArgs& a = strict ? *ea : none;
+#define STLQ_B200_LAUNCH(MM, WW, SS) \
+    LaunchBeamT<MM, WW, SS>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout, redo, check, err_flag, stats, num_sms, stream, a)
+    if (strict) {
+        if (dims.m <= 8) return wide ? STLQ_B200_LAUNCH(8, true, true) : STLQ_B200_LAUNCH(8, false, true);
+        return wide ? STLQ_B200_LAUNCH(16, true, true) : STLQ_B200_LAUNCH(16, false, true);
+    }
+    if (dims.m <= 8) return wide ? STLQ_B200_LAUNCH(8, true, false) : STLQ_B200_LAUNCH(8, false, false);
+    return wide ? STLQ_B200_LAUNCH(16, true, false) : STLQ_B200_LAUNCH(16, false, false);
 #undef STLQ_B200_LAUNCH
 }
 

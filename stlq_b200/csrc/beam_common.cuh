@@ -177,9 +177,11 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 // The error bounds of one candidate from its cheap delta, eta and seta (see CheapBounds).
 // lof: the lower bound of a forced candidate: -inf, or +inf for a zero codeword, which is always
 // forced (its cheap denominator is -0 - 0) and which the reference always skips.
-template <int L>
+// kStrict: gamma is a tensor-core value within dg of the exact one, so the exact diff lies within
+// dg of this one and e' = E_old - diff^2/denom moves by at most (2|diff| + dg) dg / denom.
+template <int L, bool kStrict>
 __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta, float eta, float seta, float Eo,
-                                           bool ill, float lof, float& lo, float& hi) {
+                                           bool ill, float lof, float dg, float& lo, float& hi) {
     // Half-width w = 16 * de with de as documented at CheapBounds; the factor 16 is folded into the
     // constants.
     constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
@@ -189,8 +191,8 @@ __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta
     const float rden = __fdividef(1.0f, denom);  // approximate: only bounds depend on it
     const float r = diff * diff * rden;
     const float ep = fmaxf(Eo - r, 0.0f);
-    const float w = fmaf(2.0f * fabsf(diff) * seta + fabsf(r) * (alpha + delta), u16 * fabsf(rden),
-                         e16 * (Eo + fabsf(r)));
+    float w = fmaf(2.0f * fabsf(diff) * seta + fabsf(r) * (alpha + delta), u16 * fabsf(rden), e16 * (Eo + fabsf(r)));
+    if constexpr (kStrict) w = fmaf((2.0f * fabsf(diff) + dg) * dg, 1.001f * fabsf(rden), w);
     const bool force = ill || !(denom > kDenomGuard * alpha) || !(w < PosInf()) || !(ep < PosInf());
     lo = force ? lof : ep - w;
     hi = force ? PosInf() : ep + w;
@@ -207,11 +209,12 @@ __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta
 // whose cheap value is unreliable (ill-conditioned slot, denom <= kDenomGuard * alpha, NaN)
 // gets [-inf, +inf].  A codeword whose whole Gram column is zero (alpha is -0.0f in the beam's
 // diagonal, see IsZeroColumn) gets [+inf, +inf]: the reference always skips it.
-template <int MAXM, int L>
+template <int MAXM, int L, bool kStrict>
 __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* const (&gq)[kCpt],
                                             const bool (&ok)[kCpt],
                                             const float (&alpha)[kCpt], const float (&gamma)[kCpt],
-                                            const float (&lof)[kCpt], float (&lo)[kCpt], float (&hi)[kCpt]) {
+                                            const float (&lof)[kCpt], const float (&dg)[kCpt], float (&lo)[kCpt],
+                                            float (&hi)[kCpt]) {
     const float* Rh = cur.Rh(h);
     const float* rinv = cur.rinvh(h);
     const float* ah = cur.ah(h);
@@ -250,7 +253,7 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     const bool ill = cur.ill[h] != 0;
 #pragma unroll
     for (int q = 0; q < kCpt; ++q)
-        BoundsTail<L>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, lof[q], lo[q], hi[q]);
+        BoundsTail<L, kStrict>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, lof[q], dg[q], lo[q], hi[q]);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -283,10 +286,10 @@ __device__ void BuildPairTable(const SlotView<MAXM>& cur, int curH, int L, float
     }
 }
 
-template <int MAXM, int L>
+template <int MAXM, int L, bool kStrict>
 __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, const int* rw, float Eo, bool ill,
                                                 const float* gq, bool ok, float2 alpha, float2 gamma, float2 lof,
-                                                float2& lo, float2& hi) {
+                                                float2 dg, float2& lo, float2& hi) {
     float2 A[L], y[L];
 #pragma unroll
     for (int i = 0; i < L; ++i)
@@ -306,8 +309,8 @@ __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, 
         seta0 = fmaf(fabsf(A[i].x), fabsf(ai.x), seta0);
         seta1 = fmaf(fabsf(A[i].y), fabsf(ai.x), seta1);
     }
-    BoundsTail<L>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, lof.x, lo.x, hi.x);
-    BoundsTail<L>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, lof.y, lo.y, hi.y);
+    BoundsTail<L, kStrict>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, lof.x, dg.x, lo.x, hi.x);
+    BoundsTail<L, kStrict>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, lof.y, dg.y, lo.y, hi.y);
 }
 
 }  // namespace beam

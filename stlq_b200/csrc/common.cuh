@@ -35,4 +35,79 @@ __device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, 
 __device__ __forceinline__ float sub_rn(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
 
+// K-block split of the reference's CPU BLAS (OpenBLAS 0.3.15 SkylakeX SGEMM, single thread): blocks
+// of 448, a remainder in (448, 896) halved and rounded up to 16.  Every block length is a multiple
+// of 4 when d is.
+__host__ __device__ __forceinline__ int NextKBlock(int rem) {
+    const int Q = 448, U = 16;
+    if (rem >= 2 * Q) return Q;
+    if (rem > Q) return ((rem / 2) + U - 1) & ~(U - 1);
+    return rem;
+}
+
+// One xC entry c . x exactly as the exact GEMM (XcGemmExactKernel) computes it: per K block an
+// FMA chain from zero, folded as t = fma(1, chain, t) from t = 0 in block order.  d % 4 == 0 and
+// the codeword row 16-byte aligned.  x is float or uint8 (converted exactly); with kVecX it is read
+// four at a time (a 16-byte aligned float row: the beam kernels' staged copy), otherwise one
+// element at a time (a caller's row, whatever its alignment).
+template <bool kVecX>
+__device__ __forceinline__ float4 Load4(const float* p) {
+    if constexpr (kVecX) return *reinterpret_cast<const float4*>(p);
+    else return make_float4(p[0], p[1], p[2], p[3]);
+}
+template <bool kVecX>
+__device__ __forceinline__ float4 Load4(const uint8_t* p) {
+    return make_float4(p[0], p[1], p[2], p[3]);
+}
+template <typename TX, bool kVecX = false>
+__device__ __noinline__ float ExactDot(const float* __restrict__ c, const TX* __restrict__ x, int d) {
+    float t = 0.0f;
+    for (int k0 = 0; k0 < d;) {
+        const int kb = NextKBlock(d - k0);
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int i = k0; i < k0 + kb; i += 4) {
+            const float4 cv = __ldg(reinterpret_cast<const float4*>(c + i));
+            const float4 xv = Load4<kVecX>(x + i);
+            acc = __fmaf_rn(cv.x, xv.x, acc);
+            acc = __fmaf_rn(cv.y, xv.y, acc);
+            acc = __fmaf_rn(cv.z, xv.z, acc);
+            acc = __fmaf_rn(cv.w, xv.w, acc);
+        }
+        t = __fmaf_rn(1.0f, acc, t);
+        k0 += kb;
+    }
+    return t;
+}
+
+// STRICT mode: xC comes from the tensor cores (3xTF32), which differ from the exact GEMM's entries
+// by at most kappa * ||c_h|| * ||x||.  Decisions are bounded from the tensor-core values and every
+// value a decision or an output depends on is recomputed with ExactDot, so codes, coefficients and
+// costs equal the exact mode's.  The bound is checked on every entry computed exactly:
+// CheckTcBound sets kErrTcBound when |g - ga| exceeds dg (both values finite).
+__device__ __forceinline__ void CheckTcBound(float g, float ga, float dg, unsigned int* err) {
+    if (isfinite(g) && isfinite(ga) && !(fabsf(g - ga) <= dg)) atomicOr(err, kErrTcBound);
+}
+
+// Per vector, in the beam kernels: x staged as float in shared memory.
+struct ExactCtx {
+    const float* C;      // codeword rows (H x d)
+    const float* cn;     // upper bounds of ||c_h||
+    const float* xc;     // the vector's tensor-core xC row
+    const float* xs;     // the vector, float, 16-byte aligned (shared memory)
+    int d;
+    float kx;            // kappa * (upper bound of ||x||)
+    unsigned int* err;
+    __device__ float Bound(int flat) const { return kx * __ldg(cn + flat); }
+    __device__ float Gamma(int flat) const {
+        const float g = ExactDot<float, true>(C + static_cast<size_t>(flat) * d, xs, d);
+        CheckTcBound(g, xc[flat], Bound(flat), err);
+        return g;
+    }
+};
+
+// kx for a vector with float ||x||^2 = nx2 (its square root, rounded up by far more than its
+// rounding error).
+__device__ __forceinline__ float StrictKx(float kappa, float nx2) { return kappa * sqrtf(fmaxf(nx2, 0.0f)) * 1.0001f; }
+
 }  // namespace stlq_b200

@@ -22,11 +22,14 @@ cudaError_t LaunchSplitTf32(const void* x, int x_dtype, int64_t count, float* hi
 // ||x||^2 per vector in float (the reference's 4-lane SIMD order) and in double; either may be null.
 cudaError_t LaunchNorms(const void* X, int x_dtype, int64_t n, int d, float* xn, double* xnd, cudaStream_t stream);
 
-// Dynamic shared memory of the fast beam kernel (the larger of the two beam kernels).
-size_t BeamFastSmemBytes(const Dims& dims, int beam);
+// Dynamic shared memory of the fast beam kernel (the larger of the two beam kernels); strict: its
+// STRICT-mode instantiation.
+size_t BeamFastSmemBytes(const Dims& dims, int beam, bool strict = false);
+// ea (null, or ea->X null: xC is exact): STRICT mode's inputs for exact xC entries on demand.
 cudaError_t LaunchBeamSearch(const Dims& dims, const float* Grow, const float* Gdiag, const float* xnorm2,
                              const float* xC, int64_t n, int beam, void* Bout, int* redo, int check,
-                             unsigned int* err_flag, int num_sms, cudaStream_t stream);
+                             unsigned int* err_flag, int num_sms, cudaStream_t stream,
+                             const ExactDotArgs* ea = nullptr);
 
 struct RefineArgs {
     Dims dims;
@@ -49,6 +52,11 @@ struct RefineArgs {
     float* a;
     float* cost;
     double* partials;  // [grid][2] (beam SSE, final SSE) or null
+    // STRICT mode (ex.X non-null, mode 1): xC holds tensor-core entries; the kernel writes the exact
+    // entry of every codeword an LS solve or a cost reads into xC (which must be writable) before
+    // reading it, and resolves ICM choices from bounds plus exact scores (see refine.cu).
+    ExactDotArgs ex;
+    unsigned int* err_flag;  // STRICT: kErrTcBound is raised here
 };
 
 cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream);
@@ -82,6 +90,8 @@ cudaError_t LaunchInvnorm(const float* C, int H, int d, float* invnorm, cudaStre
 cudaError_t LaunchBeamDiag(const Dims& dims, const float* Gcol, const float* Gdiag, float* Bdiag,
                            cudaStream_t stream);
 cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStream_t stream);
+// cn[h] >= ||c_h|| for the H codewords of C (H x d): STRICT mode's tensor-core error bounds.
+cudaError_t LaunchNormBounds(const float* C, int H, int d, float* cn, cudaStream_t stream);
 // Large-root precompute: invnorm from the SIMD-order norms; Gdiag = norm0 for the h0 root codewords
 // and the compact Gram's diagonal (G[h * Hs + h - h0]) for the others.
 cudaError_t LaunchLargeRootPrecomp(const float* norms, int h0, int H, const float* G, float* Gdiag, float* invnorm,

@@ -86,7 +86,26 @@ __global__ void U8ToF32Kernel(const uint8_t* __restrict__ x, int64_t count, floa
         out[i] = static_cast<float>(x[i]);
 }
 
+// Upper bounds of ||c_h||: the norm in double, rounded to float and raised by 2^-20 (far above
+// the roundings), one warp per codeword.
+__global__ void NormBoundKernel(const float* __restrict__ C, int H, int d, float* __restrict__ cn) {
+    const int h = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (h >= H) return;
+    double s = 0.0;
+    for (int i = lane; i < d; i += 32) {
+        const double v = C[static_cast<size_t>(h) * d + i];
+        s += v * v;
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) cn[h] = static_cast<float>(sqrt(s)) * (1.0f + 0x1p-20f);
+}
+
 }  // namespace
+
+cudaError_t LaunchNormBounds(const float* C, int H, int d, float* cn, cudaStream_t stream) {
+    NormBoundKernel<<<(H + 7) / 8, 256, 0, stream>>>(C, H, d, cn);
+    return cudaGetLastError();
+}
 
 cudaError_t LaunchU8ToF32(const uint8_t* x, int64_t count, float* out, cudaStream_t stream) {
     if (count <= 0) return cudaSuccess;

@@ -35,6 +35,8 @@ constexpr int kRefineThreads = 32 * kWarps;
 // spills of the serial routines.
 constexpr int kRefineBlocksPerSm = 8;
 
+__device__ __forceinline__ float PosInfF() { return __int_as_float(0x7f800000); }
+
 // The codes and coefficients of the vector the warp is scoring, staged by the lane that holds it.
 struct WarpStage {
     int code[kMaxM];
@@ -390,13 +392,159 @@ __device__ __forceinline__ int ScoreLayer(const Dims& dims, const GramRef& Gr, c
     return (best_s > __int_as_float(0xff800000)) ? best_t : code[j];
 }
 
+// ---------------------------------------------------------------------------------------------
+// STRICT mode: xC holds tensor-core entries, within kx ||c_t|| of the exact ones (kx = kappa ||x||).
+// A lane writes the exact entry of a codeword into its vector's xC row before an LS solve or a
+// cost reads it (FixEntry), and an ICM choice is made from bounds on the scores, with exact
+// scores only where the bounds cannot decide (ScoreLayerStrict).
+
+// The exact xC entry of flat codeword `flat` for vector row `xrow` (the exact GEMM's order).
+__device__ __noinline__ float LaneExact(const ExactDotArgs& ex, int d, const void* xrow, int flat) {
+    const float* c = ex.C + static_cast<size_t>(flat) * d;
+    return ex.x_dtype ? ExactDot(c, static_cast<const uint8_t*>(xrow), d) : ExactDot(c, static_cast<const float*>(xrow), d);
+}
+
+__device__ __forceinline__ void FixEntry(const ExactDotArgs& ex, int d, const void* xrow, float* xcw, int flat, float kx,
+                                         unsigned int* err) {
+    const float g = LaneExact(ex, d, xrow, flat);
+    CheckTcBound(g, xcw[flat], kx * __ldg(ex.cn + flat), err);
+    xcw[flat] = g;
+}
+
+// The ICM choice for layer j of the staged vector, like ScoreLayer, from the tensor-core row xc of
+// that vector.  Each score s_t = |val_t| (or val_t) with val_t = (xc_t - sum_l a_l G(t, flat_l)) *
+// invnorm_t in the reference's order moves by at most
+//   r_t = (dg_t + 2 m u (|xc_t| + dg_t + ||c_t|| A)) invnorm_t (1 + 1e-4) + 3 u |val_t|,
+// dg_t = kx ||c_t||, A >= sum_l |a_l| ||c_{flat_l}||, when the exact xc_t replaces the tensor-core
+// one (the first term is the input's own error, the second the roundings of both chains, the last
+// the final product's).  With LB = max_t (s_t - r_t), every codeword with s_t + r_t < LB scores
+// below the exact maximum, so only the others (the contenders) can be chosen: one contender is the
+// choice; with several, their exact scores decide (first maximum in t order, as the reference).
+// xrow: the staged vector's row of X, for the exact entries.
+__device__ __noinline__ int ScoreLayerStrict(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc,
+                                             int j, const int* code, const float* a, bool use_abs,
+                                             const ExactDotArgs& ex, const void* xrow, float kx) {
+    const int lane = threadIdx.x & 31;
+    const int m = dims.m, hj = dims.h_vec[j], startf = dims.off[j];
+    constexpr float u = 5.9604645e-8f;  // 2^-24
+    float A = 0.0f;
+    for (int l = 0; l < m; ++l)
+        if (l != j) A = fmaf(fabsf(a[l]), __ldg(ex.cn + dims.off[l] + code[l]), A);
+    A *= 1.001f;
+    const float cm = 2.0f * m * u;
+    // Score and radius of this lane's kScoreT codewords of chunk t0.
+    auto score = [&](int t0, float (&s)[kScoreT], float (&r)[kScoreT]) {
+        float v[kScoreT];
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) {
+            const int t = t0 + lane + 32 * i;
+            v[i] = t < hj ? xc[startf + t] : 0.0f;
+        }
+        float xa[kScoreT];
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) xa[i] = fabsf(v[i]);
+        for (int l = 0; l < m; ++l) {
+            if (l == j) continue;
+            const float al = a[l];
+            const float* grow =
+                Gr.g + static_cast<size_t>(dims.off[l] + code[l]) * Gr.ldg + (startf - Gr.c0) + t0 + lane;
+            float g[kScoreT];
+#pragma unroll
+            for (int i = 0; i < kScoreT; ++i) g[i] = t0 + lane + 32 * i < hj ? __ldg(grow + 32 * i) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < kScoreT; ++i) v[i] = sub_rn(v[i], mul_rn(al, g[i]));
+        }
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) {
+            const int t = t0 + lane + 32 * i;
+            if (t >= hj) {
+                s[i] = -PosInfF();
+                r[i] = 0.0f;
+                continue;
+            }
+            const float inv = __ldg(invnorm + startf + t), cnt = __ldg(ex.cn + startf + t);
+            const float val = mul_rn(v[i], inv);
+            const float dg = kx * cnt;
+            s[i] = use_abs ? fabsf(val) : val;
+            r[i] = (dg + cm * (xa[i] + dg + cnt * A)) * inv * 1.0001f + 3.0f * u * fabsf(val);
+        }
+    };
+    // The exact score of codeword t (its exact entry, then the same sequence as ScoreLayer).
+    auto exact = [&](int t) {
+        float v = LaneExact(ex, dims.d, xrow, startf + t);
+        for (int l = 0; l < m; ++l) {
+            if (l == j) continue;
+            v = sub_rn(v, mul_rn(a[l], __ldg(Gr.g + static_cast<size_t>(dims.off[l] + code[l]) * Gr.ldg +
+                                             (startf - Gr.c0) + t)));
+        }
+        const float val = mul_rn(v, __ldg(invnorm + startf + t));
+        return use_abs ? fabsf(val) : val;
+    };
+    const int nchunk = (hj + 32 * kScoreT - 1) / (32 * kScoreT);
+    float s[kScoreT], r[kScoreT];
+    // LB over every chunk (the last chunk's scores stay in registers).
+    float lb = -PosInfF();
+    for (int c = 0; c < nchunk; ++c) {
+        score(c * 32 * kScoreT, s, r);
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) lb = fmaxf(lb, s[i] - r[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lb = fmaxf(lb, __shfl_xor_sync(0xffffffffu, lb, o));
+    // Contenders: t < hj with !(s + r < LB).  Count them and find the first.
+    int count = 0, first = 0x7fffffff;
+    for (int c = nchunk - 1; c >= 0; --c) {
+        if (c != nchunk - 1) score(c * 32 * kScoreT, s, r);
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) {
+            const int t = c * 32 * kScoreT + lane + 32 * i;
+            const bool cont = t < hj && !(s[i] + r[i] < lb);
+            const unsigned bal = __ballot_sync(0xffffffffu, cont);
+            count += __popc(bal);
+            if (bal) first = min(first, c * 32 * kScoreT + (__ffs(bal) - 1) + 32 * i);
+        }
+    }
+    if (count == 1 && lb > -PosInfF()) return first;
+    // Exact scores of the contenders; first strict maximum in t order.
+    float best_s = -PosInfF();
+    int best_t = 0x7fffffff;
+    for (int c = 0; c < nchunk; ++c) {
+        score(c * 32 * kScoreT, s, r);
+#pragma unroll
+        for (int i = 0; i < kScoreT; ++i) {
+            const int t = c * 32 * kScoreT + lane + 32 * i;
+            if (t < hj && !(s[i] + r[i] < lb)) {
+                const float se = exact(t);
+                if (se > best_s) {
+                    best_s = se;
+                    best_t = t;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float s2 = __shfl_xor_sync(0xffffffffu, best_s, o);
+        const int t2 = __shfl_xor_sync(0xffffffffu, best_t, o);
+        if (s2 > best_s || (s2 == best_s && t2 < best_t)) {
+            best_s = s2;
+            best_t = t2;
+        }
+    }
+    return (best_s > -PosInfF()) ? best_t : code[j];
+}
+
 // One lane's trial change of layer j to `best` for its own vector (icm.cpp:300-340): LS for the
 // new codes and their cost; the change is kept only if the cost drops by more than kIcmEps,
-// otherwise code and a are restored.  Returns whether it was kept.
+// otherwise code and a are restored.  Returns whether it was kept.  STRICT (ex.X non-null): the
+// new codeword's exact xC entry is written into the row first.
+template <bool kStrict>
 __device__ __noinline__ bool TryChange(const Dims& dims, const GramRef& Gr, const float* xc, float xn2, int j, int best,
-                                       int* code, float* a, float* cost, LaneScratch& sc) {
+                                       int* code, float* a, float* cost, LaneScratch& sc, const ExactDotArgs& ex,
+                                       const void* xrow, float kx, unsigned int* err) {
     const int m = dims.m;
     const int old_code = code[j];
+    if constexpr (kStrict) FixEntry(ex, dims.d, xrow, const_cast<float*>(xc), dims.off[j] + best, kx, err);
     float backup[kMaxM];
     for (int l = 0; l < m; ++l) backup[l] = a[l];
     code[j] = best;
@@ -414,9 +562,9 @@ __device__ __noinline__ bool TryChange(const Dims& dims, const GramRef& Gr, cons
     return keep;
 }
 
-__device__ __forceinline__ const float* ShflPtr(const float* ptr, int src) {
-    return reinterpret_cast<const float*>(
-        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ptr), src));
+template <typename T>
+__device__ __forceinline__ const T* ShflPtr(const T* ptr, int src) {
+    return reinterpret_cast<const T*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(ptr), src));
 }
 
 // RunIcm's sweeps (icm.cpp:116-344) for the vectors of a warp's group after its first step: lane
@@ -424,9 +572,13 @@ __device__ __forceinline__ const float* ShflPtr(const float* ptr, int src) {
 // layer of the order, the warp scores the active vectors one at a time from the codes their lanes
 // stage in `st`; then every lane tries its own vector's change at once.  A vector stops after a
 // sweep without a kept change, as RunIcm does.
+// kStrict: xc is the lane's tensor-core row (exact at its codes), xrow its vector's row of X and
+// kx its bound factor (see ScoreLayerStrict, FixEntry).
+template <bool kStrict>
 __device__ __noinline__ void RunIcmGroup(const Dims& dims, const GramRef& Gr, const float* invnorm, const float* xc,
                                          float xn2, int ng, int icm_iters, const int* orders, bool use_abs,
-                                         int* code, float* a, float* cost, WarpStage& st, LaneScratch& sc) {
+                                         int* code, float* a, float* cost, WarpStage& st, LaneScratch& sc,
+                                         const ExactDotArgs& ex, const void* xrow, float kx, unsigned int* err) {
     const int lane = threadIdx.x & 31;
     const int m = dims.m;
     bool active = lane < ng;
@@ -447,10 +599,16 @@ __device__ __noinline__ void RunIcmGroup(const Dims& dims, const GramRef& Gr, co
                     }
                 const float* xg = ShflPtr(xc, gi);
                 __syncwarp();
-                const int best = ScoreLayer(dims, Gr, invnorm, xg, j, st.code, st.a, use_abs);
+                int best;
+                if constexpr (kStrict)
+                    best = ScoreLayerStrict(dims, Gr, invnorm, xg, j, st.code, st.a, use_abs, ex, ShflPtr(xrow, gi),
+                                            __shfl_sync(0xffffffffu, kx, gi));
+                else
+                    best = ScoreLayer(dims, Gr, invnorm, xg, j, st.code, st.a, use_abs);
                 if (lane == gi) mine = best;
             }
-            if (active && mine != code[j]) changed |= TryChange(dims, Gr, xc, xn2, j, mine, code, a, cost, sc);
+            if (active && mine != code[j])
+                changed |= TryChange<kStrict>(dims, Gr, xc, xn2, j, mine, code, a, cost, sc, ex, xrow, kx, err);
         }
         active = active && changed;
     }
@@ -458,6 +616,10 @@ __device__ __noinline__ void RunIcmGroup(const Dims& dims, const GramRef& Gr, co
 
 }  // namespace
 
+// kStrict: STRICT mode (p.ex.X non-null, mode 1): the lane's xC row holds tensor-core entries and
+// is made exact at every codeword an LS solve or a cost reads (FixEntry); ICM choices come from
+// ScoreLayerStrict.  The codes, coefficients and costs equal the exact mode's.
+template <bool kStrict>
 __global__ void __launch_bounds__(kRefineThreads, kRefineBlocksPerSm) RefineKernel(RefineArgs p) {
     __shared__ WarpStage stage[kWarps];
     __shared__ double sse_w[kWarps][2];
@@ -479,9 +641,19 @@ __global__ void __launch_bounds__(kRefineThreads, kRefineBlocksPerSm) RefineKern
         LaneScratch sc;
         float cost = 0.0f, xn2 = 0.0f;
         double tb = 0.0, tf = 0.0;
+        const void* xrow = nullptr;  // STRICT: this lane's vector (row of X) and its bound factor
+        float kx = 0.0f;
         if (own) {
             // RunIcm's first step (icm.cpp:109-114), or with mode 0 the whole LS stage.
             for (int l = 0; l < m; ++l) code[l] = LoadCode(p.B, vec * m + l, dims.wide);
+            if constexpr (kStrict) {
+                // The beam codes' exact entries (a large-root encoder's root entry is already the
+                // reference's own dot product, written by LaunchRootDot).
+                xrow = static_cast<const char*>(p.ex.X) + vec * dims.d * (p.ex.x_dtype ? 1 : 4);
+                kx = StrictKx(p.ex.kappa, p.xnorm2[vec]);
+                for (int l = dims.large_root ? 1 : 0; l < m; ++l)
+                    FixEntry(p.ex, dims.d, xrow, const_cast<float*>(xc), dims.off[l] + code[l], kx, p.err_flag);
+            }
             const GramGlobal G{Gr, dims.off, code};
             if (!SolveLs(dims, G, xc, code, sc, a))
                 for (int l = 0; l < m; ++l) a[l] = 0.0f;
@@ -501,7 +673,8 @@ __global__ void __launch_bounds__(kRefineThreads, kRefineBlocksPerSm) RefineKern
         if (p.mode == 0) continue;
         WarpStage& st = stage[warp];
         if (p.icm_iters > 0)
-            RunIcmGroup(dims, Gr, p.invnorm, xc, xn2, ng, p.icm_iters, p.orders, p.use_abs, code, a, &cost, st, sc);
+            RunIcmGroup<kStrict>(dims, Gr, p.invnorm, xc, xn2, ng, p.icm_iters, p.orders, p.use_abs, code, a, &cost,
+                                 st, sc, p.ex, xrow, kx, p.err_flag);
         const int ksel = min(p.perturb_k, m);
         for (int outer = 0; outer < p.n_ils; ++outer) {
             int cand[kMaxM];
@@ -521,15 +694,19 @@ __global__ void __launch_bounds__(kRefineThreads, kRefineBlocksPerSm) RefineKern
                     const int raw = static_cast<int>(UniformBelow(r, static_cast<uint32_t>(h - 1)));
                     cand[layer] = raw >= old_code ? raw + 1 : raw;
                 }
+                if constexpr (kStrict)
+                    for (int l = 1; l < m; ++l)
+                        if (cand[l] != code[l])
+                            FixEntry(p.ex, dims.d, xrow, const_cast<float*>(xc), dims.off[l] + cand[l], kx, p.err_flag);
                 const GramGlobal G{Gr, dims.off, cand};
                 if (!SolveLs(dims, G, xc, cand, sc, acand))
                     for (int l = 0; l < m; ++l) acand[l] = 0.0f;
                 ccost = Cost(dims, G, xc, cand, acand, xn2);
             }
             if (p.icm_iters > 0)
-                RunIcmGroup(dims, Gr, p.invnorm, xc, xn2, ng, p.icm_iters,
-                            p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, cand, acand,
-                            &ccost, st, sc);
+                RunIcmGroup<kStrict>(dims, Gr, p.invnorm, xc, xn2, ng, p.icm_iters,
+                                     p.orders + static_cast<size_t>(outer + 1) * p.icm_iters * m, p.use_abs, cand,
+                                     acand, &ccost, st, sc, p.ex, xrow, kx, p.err_flag);
             if (own && add_rn(ccost, kIcmEps) < cost) {  // icm.cpp:979-990
                 for (int l = 0; l < m; ++l) {
                     code[l] = cand[l];
@@ -641,7 +818,8 @@ __global__ void SseKernel(Dims dims, const float* Gcol, const float* Gdiag, cons
 
 cudaError_t LaunchRefine(const RefineArgs& args, int grid, cudaStream_t stream) {
     if (args.n <= 0) return cudaSuccess;
-    RefineKernel<<<grid, kRefineThreads, 0, stream>>>(args);
+    if (args.ex.X && args.mode == 1) RefineKernel<true><<<grid, kRefineThreads, 0, stream>>>(args);
+    else RefineKernel<false><<<grid, kRefineThreads, 0, stream>>>(args);
     return cudaGetLastError();
 }
 

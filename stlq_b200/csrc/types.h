@@ -19,6 +19,17 @@ enum DeviceError : unsigned int {
     kErrBadShape = 1u << 1,
     kErrFilterMiss = 1u << 2,  // self-check: a candidate the beam pre-filter dropped would have entered
     kErrWaitTimeout = 1u << 3,  // a bounded barrier wait of the tensor-core GEMM ran out
+    kErrTcBound = 1u << 4,      // STRICT: a tensor-core xC entry was outside its error bound
+};
+
+// STRICT mode inputs of the exact xC entries computed on demand (see ExactCtx in common.cuh).
+// X == nullptr: the kernels take xC as exact (EXACT and FAST modes, the stage entry points).
+struct ExactDotArgs {
+    const float* C;      // C_all, codeword h at C + h * d
+    const void* X;       // the slice's vectors as encoded (rotated when a rotation is set)
+    int x_dtype;         // 0 float32, 1 uint8
+    const float* cn;     // upper bounds of ||c_h||
+    float kappa;         // |xC_tensor - xC_exact| <= kappa ||c_h|| ||x||
 };
 
 // Encoder constants shared by every kernel, passed by value.

@@ -33,13 +33,6 @@ namespace {
 
 constexpr int kTM = 128, kTN = 128, kBK = 16, kGemmThreads = 256;
 
-__host__ __device__ __forceinline__ int NextKBlock(int rem) {
-    const int Q = 448, U = 16;
-    if (rem >= 2 * Q) return Q;
-    if (rem > Q) return ((rem / 2) + U - 1) & ~(U - 1);
-    return rem;
-}
-
 // Loads rows [row0, row0 + 128) x k [k0, k0 + 16) of a row-major matrix with `d` columns into
 // registers: thread t holds rows t/4 and t/4 + 64, columns 4*(t%4)..+3 (zero outside).
 template <typename T>
