@@ -64,6 +64,20 @@ def dist_env():
     return rank, world, local
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo) and its logical core count."""
+    name = "unknown CPU"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{name}, {os.cpu_count()} logical cores"
+
+
 def load_measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -235,7 +249,9 @@ def run_reference(args):
                                f"{per_step}-vector sample per step",
                    "cache": "sample per step"},
         "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": ref.threads, "kind": "reference",
-                         "sample": f"{per_step} vectors per step x {args.steps} steps; BLAS core {ref.blas_core()}"},
+                         "cpu_model": cpu_model(),
+                         "sample": f"{per_step} vectors per step x {args.steps} steps on {ref.threads} threads of "
+                                   f"{cpu_model()}; BLAS core {ref.blas_core()}"},
         "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -450,9 +466,9 @@ def run_ours(args):
         try:
             v, cores, ns, code_match, ref_sample = cpu_reference_sample(C_np, h_vec, X_np, args, args.cpu_seconds,
                                                                gpu_codes=B.cpu().numpy())
-            cpu = {"value": v, "unit": "vectors/s", "cores": cores, "kind": "reference",
+            cpu = {"value": v, "unit": "vectors/s", "cores": cores, "kind": "reference", "cpu_model": cpu_model(),
                    "sample": f"first {ns} vectors of rank 0's shard, same codebooks and settings, "
-                             f"reference CPU encoder (oracle/_ref) with {cores} threads, "
+                             f"reference CPU encoder (oracle/_ref) with {cores} threads of {cpu_model()}, "
                              f"OpenBLAS core {(code_match or {}).get('reference_blas_core')}"}
             if code_match is not None:  # the remaining parity metrics: coefficients, costs, MSE
                 a_gpu = a[:ns].cpu().numpy()

@@ -56,6 +56,15 @@ __device__ __forceinline__ float ExactGamma(const ExactCtx& ctx, const float* xc
     else return __ldg(xc + flat);
 }
 
+// STRICT mode: the exact xC entries of the codewords flat_of(p), p < S, into gex[p], entry p by
+// thread p % kThreads (the thread that uses it next).  Staging the rows in shared memory for
+// coalesced loads was measured slower: the larger carve-out costs the cheap pass's Gram gathers
+// their L1 hits.
+template <class FlatOf>
+__device__ __forceinline__ void SurvivorGammas(const ExactCtx& ctx, int S, FlatOf flat_of, float* gex) {
+    for (int p = threadIdx.x; p < S; p += kThreads) gex[p] = ctx.Gamma(flat_of(p));
+}
+
 // Per kept survivor: y[MAXM], v[MAXM], denom, a_last.
 template <int MAXM>
 __host__ __device__ constexpr int KeepStride() { return 2 * MAXM + 2; }
@@ -298,7 +307,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
     // Codebooks above 256 codewords (the kWide kernels) are walked in chunks of kMaxK, kCpt
     // codewords per thread; the other kernels make one pass with kc = 0 known at compile time.
     for (int kc = 0; kc < (kWide ? K : 1); kc += kMaxK) {
-        float alpha[kCpt], gamma[kCpt], lof[kCpt], dg[kCpt];
+        float alpha[kCpt], gamma[kCpt], dg[kCpt];
         int col[kCpt];
         bool ok[kCpt];
 #pragma unroll
@@ -308,7 +317,6 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
             col[c] = colL + k;  // Gram column; Gdiag and xc are indexed by the flat index
             alpha[c] = ok[c] ? __ldg(Gdiag + offL + k) : 0.0f;
             gamma[c] = ok[c] ? __ldg(xc + offL + k) : 0.0f;
-            lof[c] = IsZeroColumn(alpha[c]) ? PosInf() : -PosInf();
             dg[c] = (kStrict && ok[c]) ? ctx.Bound(offL + k) : 0.0f;
         }
         const float* gq[kCpt];
@@ -316,7 +324,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
         for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
         for (int h = 0; h < curH; ++h) {
             float l[kCpt], hi[kCpt];
-            CheapBounds<MAXM, L, kStrict>(cur, h, gq, ok, alpha, gamma, lof, dg, l, hi);
+            CheapBounds<MAXM, L, kStrict>(cur, h, gq, ok, alpha, gamma, dg, l, hi);
 #pragma unroll
             for (int c = 0; c < kCpt; ++c) {
                 if (ok[c]) {
@@ -354,15 +362,13 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
         const bool ok = k < K;  // K is even: k + 1 < K as well
         const float2 alpha = ok ? __ldg(reinterpret_cast<const float2*>(Gdiag + offL + k)) : make_float2(0.0f, 0.0f);
         const float2 gamma = ok ? __ldg(reinterpret_cast<const float2*>(xc + offL + k)) : make_float2(0.0f, 0.0f);
-        const float2 lof = make_float2(IsZeroColumn(alpha.x) ? PosInf() : -PosInf(),
-                                       IsZeroColumn(alpha.y) ? PosInf() : -PosInf());
         const float2 dg = (kStrict && ok) ? make_float2(ctx.Bound(offL + k), ctx.Bound(offL + k + 1))
                                           : make_float2(0.0f, 0.0f);
         const float* gq = Grow + colL + k;
         for (int h = 0; h < curH; ++h) {
             float2 l, hi;
             CheapBoundsPair<MAXM, L, kStrict>(table + h * PairTableStride<MAXM>(), cur.rowh(h), cur.E[h],
-                                              cur.ill[h] != 0, gq, ok, alpha, gamma, lof, dg, l, hi);
+                                              cur.ill[h] != 0, gq, ok, alpha, gamma, dg, l, hi);
             if (ok) {
                 *reinterpret_cast<float2*>(lo + h * K + k) = l;
                 if (kHi) *reinterpret_cast<float2*>(hi_out + h * K + k) = hi;
@@ -920,13 +926,14 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
         L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag, dims.large_root != 0, table, ctx);
     const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
+    if constexpr (kStrict)
+        SurvivorGammas(ctx, S, [&](int p) { return offL + surv[p] % K; }, gex);
     for (int p = tid; p < S; p += kThreads) {
         const int idx = surv[p];
         const int h = idx / K, k = idx - h * K;
         float* st = keep + p * KeepStride<MAXM>();
         const bool kp = p < kKeep;
-        const float gamma = ExactGamma<kStrict>(ctx, xc, offL + k);
-        if constexpr (kStrict) gex[p] = gamma;
+        const float gamma = kStrict ? gex[p] : __ldg(xc + offL + k);
         ex[p] = EvalExactL<MAXM>(cur, h, L, RowsOf<MAXM>(cur, h, L), Grow, dims.ldg, colL + k, __ldg(Gdiag + offL + k),
                                  gamma, kp ? st : nullptr, kp ? st + MAXM : nullptr,
                                  kp ? st + 2 * MAXM : nullptr, kp ? st + 2 * MAXM + 1 : nullptr, dims.large_root != 0);
@@ -999,11 +1006,8 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
             else
                 curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
             if (curH >= 0) {
-                for (int p = tid; p < curH; p += kThreads) {
-                    const float g = ctx.Gamma(surv[p]);
-                    gex[p] = g;
-                    ex[p] = Layer0ErrorG(Gdiag, g, nx2, surv[p]);
-                }
+                SurvivorGammas(ctx, curH, [&](int p) { return static_cast<int>(surv[p]); }, gex);
+                for (int p = tid; p < curH; p += kThreads) ex[p] = Layer0ErrorG(Gdiag, gex[p], nx2, surv[p]);
                 __syncthreads();
                 curH = RankSurvivors(ex, surv, curH, beam, lt, keys);
             }

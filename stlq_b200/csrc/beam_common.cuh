@@ -181,7 +181,8 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 // dg of this one and e' = E_old - diff^2/denom moves by at most (2|diff| + dg) dg / denom.
 template <int L, bool kStrict>
 __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta, float eta, float seta, float Eo,
-                                           bool ill, float lof, float dg, float& lo, float& hi) {
+                                           bool ill, float dg, float& lo, float& hi) {
+    const float lof = IsZeroColumn(alpha) ? PosInf() : -PosInf();  // derived here: one register less per codeword
     // Half-width w = 16 * de with de as documented at CheapBounds; the factor 16 is folded into the
     // constants.
     constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
@@ -213,8 +214,7 @@ template <int MAXM, int L, bool kStrict>
 __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* const (&gq)[kCpt],
                                             const bool (&ok)[kCpt],
                                             const float (&alpha)[kCpt], const float (&gamma)[kCpt],
-                                            const float (&lof)[kCpt], const float (&dg)[kCpt], float (&lo)[kCpt],
-                                            float (&hi)[kCpt]) {
+                                            const float (&dg)[kCpt], float (&lo)[kCpt], float (&hi)[kCpt]) {
     const float* Rh = cur.Rh(h);
     const float* rinv = cur.rinvh(h);
     const float* ah = cur.ah(h);
@@ -253,7 +253,7 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     const bool ill = cur.ill[h] != 0;
 #pragma unroll
     for (int q = 0; q < kCpt; ++q)
-        BoundsTail<L, kStrict>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, lof[q], dg[q], lo[q], hi[q]);
+        BoundsTail<L, kStrict>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, dg[q], lo[q], hi[q]);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -288,8 +288,8 @@ __device__ void BuildPairTable(const SlotView<MAXM>& cur, int curH, int L, float
 
 template <int MAXM, int L, bool kStrict>
 __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, const int* rw, float Eo, bool ill,
-                                                const float* gq, bool ok, float2 alpha, float2 gamma, float2 lof,
-                                                float2 dg, float2& lo, float2& hi) {
+                                                const float* gq, bool ok, float2 alpha, float2 gamma, float2 dg,
+                                                float2& lo, float2& hi) {
     float2 A[L], y[L];
 #pragma unroll
     for (int i = 0; i < L; ++i)
@@ -309,8 +309,8 @@ __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, 
         seta0 = fmaf(fabsf(A[i].x), fabsf(ai.x), seta0);
         seta1 = fmaf(fabsf(A[i].y), fabsf(ai.x), seta1);
     }
-    BoundsTail<L, kStrict>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, lof.x, dg.x, lo.x, hi.x);
-    BoundsTail<L, kStrict>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, lof.y, dg.y, lo.y, hi.y);
+    BoundsTail<L, kStrict>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, dg.x, lo.x, hi.x);
+    BoundsTail<L, kStrict>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, dg.y, lo.y, hi.y);
 }
 
 }  // namespace beam

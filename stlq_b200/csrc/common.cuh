@@ -80,6 +80,41 @@ __device__ __noinline__ float ExactDot(const float* __restrict__ c, const TX* __
     return t;
 }
 
+// ExactDot for R codeword rows at once (rows[r], results out[r]): R independent chains advanced
+// together, each exactly ExactDot's sequence.  x read one element at a time (any alignment).
+template <int R, typename TX>
+__device__ __noinline__ void ExactDotRows(const float* const (&rows)[R], const TX* __restrict__ x, int d, float (&out)[R]) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+        for (int i = 0; i < d; i += 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(rows[r] + i));
+    float t[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) t[r] = 0.0f;
+    for (int k0 = 0; k0 < d;) {
+        const int kb = NextKBlock(d - k0);
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+#pragma unroll 2
+        for (int i = k0; i < k0 + kb; i += 4) {
+            const float4 xv = Load4<false>(x + i);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const float4 cv = __ldg(reinterpret_cast<const float4*>(rows[r] + i));
+                acc[r] = __fmaf_rn(cv.x, xv.x, acc[r]);
+                acc[r] = __fmaf_rn(cv.y, xv.y, acc[r]);
+                acc[r] = __fmaf_rn(cv.z, xv.z, acc[r]);
+                acc[r] = __fmaf_rn(cv.w, xv.w, acc[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) t[r] = __fmaf_rn(1.0f, acc[r], t[r]);
+        k0 += kb;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) out[r] = t[r];
+}
+
 // STRICT mode: xC comes from the tensor cores (3xTF32), which differ from the exact GEMM's entries
 // by at most kappa * ||c_h|| * ||x||.  Decisions are bounded from the tensor-core values and every
 // value a decision or an output depends on is recomputed with ExactDot, so codes, coefficients and

@@ -411,6 +411,31 @@ __device__ __forceinline__ void FixEntry(const ExactDotArgs& ex, int d, const vo
     xcw[flat] = g;
 }
 
+// FixEntry for the codes of layers l0..m-1, four chains at a time.
+__device__ __noinline__ void FixCodes(const ExactDotArgs& ex, const Dims& dims, const void* xrow, float* xcw,
+                                      const int* code, int l0, float kx, unsigned int* err) {
+    const int m = dims.m, d = dims.d;
+    for (int l = l0; l < m; l += 4) {
+        int f[4];
+        const float* rows[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int lr = min(l + r, m - 1);  // past the last layer: a repeat, not written
+            f[r] = dims.off[lr] + code[lr];
+            rows[r] = ex.C + static_cast<size_t>(f[r]) * d;
+        }
+        float g[4];
+        if (ex.x_dtype) ExactDotRows<4>(rows, static_cast<const uint8_t*>(xrow), d, g);
+        else ExactDotRows<4>(rows, static_cast<const float*>(xrow), d, g);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            if (l + r >= m) break;
+            CheckTcBound(g[r], xcw[f[r]], kx * __ldg(ex.cn + f[r]), err);
+            xcw[f[r]] = g[r];
+        }
+    }
+}
+
 // The ICM choice for layer j of the staged vector, like ScoreLayer, from the tensor-core row xc of
 // that vector.  Each score s_t = |val_t| (or val_t) with val_t = (xc_t - sum_l a_l G(t, flat_l)) *
 // invnorm_t in the reference's order moves by at most
@@ -651,8 +676,7 @@ __global__ void __launch_bounds__(kRefineThreads, kRefineBlocksPerSm) RefineKern
                 // reference's own dot product, written by LaunchRootDot).
                 xrow = static_cast<const char*>(p.ex.X) + vec * dims.d * (p.ex.x_dtype ? 1 : 4);
                 kx = StrictKx(p.ex.kappa, p.xnorm2[vec]);
-                for (int l = dims.large_root ? 1 : 0; l < m; ++l)
-                    FixEntry(p.ex, dims.d, xrow, const_cast<float*>(xc), dims.off[l] + code[l], kx, p.err_flag);
+                FixCodes(p.ex, dims, xrow, const_cast<float*>(xc), code, dims.large_root ? 1 : 0, kx, p.err_flag);
             }
             const GramGlobal G{Gr, dims.off, code};
             if (!SolveLs(dims, G, xc, code, sc, a))
