@@ -78,6 +78,19 @@ def cpu_model() -> str:
     return f"{name}, {os.cpu_count()} logical cores"
 
 
+def beam_traffic_from_profile():
+    """DRAM bytes of one 65,536-vector launch of the beam kernel at the headline shape, read from the
+    committed capture summary (its `dram_bytes_per_65536_vectors=` line), or None."""
+    import re
+
+    try:
+        with open(os.path.join(ROOT, "profiles", "beam_fast_d128_m8_k256_b16.md")) as f:
+            m = re.search(r"dram_bytes_per_65536_vectors=(\d+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
 def load_measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -496,11 +509,13 @@ def run_ours(args):
         F_cand = cand_flops_per_vector(args.m, args.k, args.beam)
         beam_bytes = S * (4 * H + 4 + args.m)
         achieved_gbs = beam_bytes / beam_s / 1e9
-        # DRAM traffic of BeamFastKernel<8>, measured by ncu (dram__bytes_read.sum +
-        # dram__bytes_write.sum) on one launch of 65,536 vectors of the headline shape: 544.7 MB
-        # read, 5.1 MB written; it grows with the vectors a launch processes, so it is scaled to S.
+        # DRAM traffic of the beam kernel, from the committed ncu capture summary of the headline
+        # shape (dram__bytes_read.sum + dram__bytes_write.sum of one 65,536-vector launch); the
+        # traffic grows with the vectors a launch processes (each xC row is read once), so it is
+        # scaled to the S vectors timed here.
         headline_shape = (args.d, args.m, args.k, args.beam) == (128, 8, 256, 16)
-        traffic = S * (544.7e6 + 5.1e6) / 65536 if headline_shape else None
+        traffic_65536 = beam_traffic_from_profile() if headline_shape else None
+        traffic = S * traffic_65536 / 65536 if traffic_65536 else None
         F_gemm = 2 * args.d * H
         hbm_bytes_vec = 4 * args.d + args.m + 4 * args.m
         t_gemm = F_gemm / (peaks["bf16_tflops"] * 1e12)
@@ -520,16 +535,20 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "mse": total_mse,
             "roofline": {
-                "bound": "hbm", "kernel": "BeamFastKernel<8>", "achieved": achieved_gbs,
-                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / peaks["hbm_gbs"],
-                "traffic": traffic, "peak_source": peaks_src,
-                "traffic_source": "ncu capture of one 65,536-vector launch of the same shape, scaled to the "
-                                  "launch's vectors" if traffic else "not captured for this shape",
-                "note": "algorithmic bytes per vector = xC row (4H) + ||x||^2 (4) + codes (M); the kernel is "
-                        "bound by FP32 issue, see simt",
-                "simt": {"achieved": F_cand * S / beam_s / 1e12, "peak": fp32_peak, "unit": "TFLOP/s",
-                         "frac": F_cand * S / beam_s / 1e12 / fp32_peak, "flops_per_vector": F_cand,
-                         "peak_source": "cuBLAS SGEMM (TF32 off) measured in this run"},
+                # The beam kernel (93% of the step) is bound by FP32 issue of its candidate
+                # arithmetic, not by HBM or tensor cores: the fraction is against the FP32 SIMT
+                # peak (cuBLAS SGEMM with TF32 off, measured in this run); HBM alongside.
+                "bound": "simt", "kernel": "BeamFastKernel<8, 0, 0>",
+                "achieved": F_cand * S / beam_s / 1e12, "peak": fp32_peak, "unit": "TFLOP/s",
+                "frac": F_cand * S / beam_s / 1e12 / fp32_peak, "flops_per_vector": F_cand,
+                "peak_source": "cuBLAS SGEMM (TF32 off) measured in this run",
+                "traffic": traffic,
+                "traffic_source": ("profiles/beam_fast_d128_m8_k256_b16.md: ncu dram bytes of one 65,536-vector "
+                                   "launch, scaled to the launch's vectors") if traffic else "not captured for this shape",
+                "hbm": {"achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": achieved_gbs / peaks["hbm_gbs"], "peak_source": peaks_src,
+                        "bytes_per_vector": 4 * H + 4 + args.m,
+                        "note": "algorithmic bytes per vector = xC row (4H) + ||x||^2 (4) + codes (M)"},
                 "beam_ms_per_262144": beam_s * 1e3, "gemm_ms_per_262144": gemm_s * 1e3,
                 "beam_exact_per_layer": beam_stats["exact_per_layer"],
                 "beam_replayed_fraction": beam_stats["replayed_fraction"],

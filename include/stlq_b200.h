@@ -212,6 +212,41 @@ int stlq_b200_encode_base_large_root_device(stlq_b200_encoder* enc, const void* 
                                             uint8_t* B_small_dev, float* a_dev, float* cost_dev,
                                             double* cost_sums_dev, void* stream);
 
+/* ---- Multi-GPU encode (one process, several GPUs of one node) ----
+ * The reference encodes the base set on one device (RunStlq -> EncodeBase, src/stlq.cpp:48-55;
+ * EncodeBase is declared in include/stlq/quantizer/encoder.h:66-74).  Base vectors are
+ * independent, so a sharded encoder holds one encoder per device and splits the vectors into
+ * contiguous shards (vector j of n on device floor-split: the first n % N shards one larger), one
+ * host thread per device, each shard with its global sample ids (ILS is keyed by them,
+ * icm.cpp:950-960): the codes, coefficients and costs equal one device's, bit for bit.  Only two
+ * things cross GPUs: the codebook set (C_all, and G / invnorm when given), uploaded to devices[0]
+ * and replicated by one NCCL broadcast, and the per-shard MSE sums, combined by one NCCL reduce
+ * onto devices[0].  NCCL (libnccl.so.2) is loaded at run time by the first call; without it these
+ * calls fail with STLQ_B200_ECUDA.  Collective waits are bounded (the communicators are aborted
+ * and STLQ_B200_EDEVICE returned on expiry).  devices: n_devices distinct ordinals.  The other
+ * arguments are stlq_b200_create's / stlq_b200_create_large_root's. */
+typedef struct stlq_b200_sharded stlq_b200_sharded;
+int stlq_b200_sharded_create(int n_devices, const int* devices, int d, int m, const int* h_vec, const float* C_all,
+                             const float* G, const float* invnorm, int gemm_mode, stlq_b200_sharded** out);
+int stlq_b200_sharded_create_large_root(int n_devices, const int* devices, int d, int m, const int* h_vec,
+                                        const float* C_all, int gemm_mode, stlq_b200_sharded** out);
+int stlq_b200_sharded_destroy(stlq_b200_sharded* sh);
+/* The per-device encoder i (owned by the sharded handle), e.g. for stlq_b200_set_rotation. */
+int stlq_b200_sharded_encoder(stlq_b200_sharded* sh, int i, stlq_b200_encoder** out);
+/* stlq_b200_encode_base / _u16 / stlq_b200_encode_base_large_root over all devices at once (host
+ * buffers, same arguments and outputs; sse_out / cost_sums_out: the NCCL-reduced sums). */
+int stlq_b200_encode_sharded(stlq_b200_sharded* sh, const void* X, int x_dtype, int64_t n, int beam, int icm_iters,
+                             int ils_iters, int perturb_k, int use_abs, uint32_t seed, uint64_t sample_id_offset,
+                             uint8_t* B_out, float* a_out, float* cost_out, double* sse_out);
+int stlq_b200_encode_sharded_u16(stlq_b200_sharded* sh, const void* X, int x_dtype, int64_t n, int beam,
+                                 int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                 uint64_t sample_id_offset, uint16_t* B_out, float* a_out, float* cost_out,
+                                 double* sse_out);
+int stlq_b200_encode_sharded_large_root(stlq_b200_sharded* sh, const void* X, int x_dtype, int64_t n, int beam,
+                                        int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                        uint64_t sample_id_offset, uint32_t* cluster_out, uint8_t* B_small_out,
+                                        float* a_out, float* cost_out, double* cost_sums_out);
+
 /* ---- Kernel-provider primitives ----
  * The device operations behind StreamKernelProvider (include/stlq/core/kernel_provider.h:28-221,
  * the reference's GPU backend seam; its CUDA implementation is src/core/kernel_provider_cuda_stream*

@@ -532,15 +532,18 @@ class AdapterHarness:
         return dict(cluster=cluster, B_small=B_small, a=a, cost=cost, beam_mse=float(mse[0]),
                     final_mse=float(mse[1]))
 
-    def encode_base(self, pre, m, X, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, device=0):
+    def encode_base(self, pre, m, X, beam, icm, ils=0, perturb=0, use_abs=True, seed=38251450, device=0,
+                    n_devices=0):
+        """stlq::b200::EncodeBase, or with n_devices > 0 stlq::b200::EncodeBaseSharded on devices
+        0 .. n_devices-1."""
         X = _f32(X)
         n = X.shape[0]
         B = np.empty((n, m), np.uint8)
         a = np.empty((n, m), np.float32)
         mse = np.zeros(2, np.float32)
         err = ctypes.create_string_buffer(512)
-        rc = self.lib.adapter_encode_base(pre, _p(X, _f32p), n, beam, icm, ils, perturb, int(bool(use_abs)), seed,
-                                          device, _p(B, _u8p), _p(a, _f32p), _p(mse, _f32p), err, 512)
+        rc = self.lib.adapter_encode_base_on(pre, _p(X, _f32p), n, beam, icm, ils, perturb, int(bool(use_abs)), seed,
+                                             device, n_devices, _p(B, _u8p), _p(a, _f32p), _p(mse, _f32p), err, 512)
         if rc:
             raise RuntimeError(err.value.decode())
         return B, a, mse

@@ -12,9 +12,21 @@
 #include "stlq/common/types.h"
 #include "stlq_b200_encoder.h"
 
+// n_devices > 0: stlq::b200::EncodeBaseSharded on devices 0 .. n_devices-1 instead of EncodeBase.
+extern "C" int adapter_encode_base_on(void* pre_h, const float* X, int n, int beam, int icm, int ils, int perturb,
+                                      int use_abs, int seed, int device, int n_devices, std::uint8_t* B_out,
+                                      float* a_out, float* mse_out, char* err, int errlen);
+
 extern "C" int adapter_encode_base(void* pre_h, const float* X, int n, int beam, int icm, int ils, int perturb,
                                    int use_abs, int seed, int device, std::uint8_t* B_out, float* a_out,
                                    float* mse_out, char* err, int errlen) {
+    return adapter_encode_base_on(pre_h, X, n, beam, icm, ils, perturb, use_abs, seed, device, 0, B_out, a_out,
+                                  mse_out, err, errlen);
+}
+
+extern "C" int adapter_encode_base_on(void* pre_h, const float* X, int n, int beam, int icm, int ils, int perturb,
+                                      int use_abs, int seed, int device, int n_devices, std::uint8_t* B_out,
+                                      float* a_out, float* mse_out, char* err, int errlen) {
     const auto* pre = static_cast<const stlq::Precomp*>(pre_h);
     stlq::Config cfg;
     cfg.base.encode.H_beam = beam;
@@ -35,7 +47,11 @@ extern "C" int adapter_encode_base(void* pre_h, const float* X, int n, int beam,
     stlq::BaseEncoding base;
     std::string e;
     float bm = 0.0f, fm = 0.0f;
-    const bool ok = stlq::b200::EncodeBase(cfg, ds, books, *pre, nullptr, &base, &bm, &fm, &e);
+    std::vector<int> devices;
+    for (int i = 0; i < n_devices; ++i) devices.push_back(i);
+    const bool ok = n_devices > 0
+                        ? stlq::b200::EncodeBaseSharded(cfg, ds, books, *pre, devices, &base, &bm, &fm, &e)
+                        : stlq::b200::EncodeBase(cfg, ds, books, *pre, nullptr, &base, &bm, &fm, &e);
     if (!ok) {
         std::strncpy(err, e.c_str(), static_cast<size_t>(errlen) - 1);
         err[errlen - 1] = 0;

@@ -10,6 +10,7 @@ from .encoder import (  # noqa: F401
     GEMM_FAST,
     GEMM_STRICT,
     Encoder,
+    ShardedEncoder,
     StlqB200Error,
     library_path,
     load_library,

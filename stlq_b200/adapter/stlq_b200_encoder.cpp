@@ -183,6 +183,77 @@ bool EncodeBase(const Config& config, const Dataset& dataset, const CodebookPack
     return true;
 }
 
+namespace {
+
+// Sharded encoders cached per (thread, device list, Precomp), like the single-device ones.
+struct CachedSharded {
+    std::vector<int> devices;
+    std::uint64_t build_tag;
+    const float* c_all;
+    int H, d;
+    stlq_b200_sharded* handle;
+};
+struct ThreadSharded {
+    std::vector<CachedSharded> items;
+    ~ThreadSharded() {
+        for (auto& e : items) stlq_b200_sharded_destroy(e.handle);
+    }
+};
+
+stlq_b200_sharded* ShardedFor(const Precomp& pre, const std::vector<int>& devices) {
+    static thread_local ThreadSharded cache;
+    for (auto& e : cache.items)
+        if (e.devices == devices && e.build_tag == pre.build_tag && e.c_all == pre.C_all.data.data() && e.H == pre.H &&
+            e.d == pre.d)
+            return e.handle;
+    stlq_b200_sharded* h = nullptr;
+    Check(stlq_b200_sharded_create(static_cast<int>(devices.size()), devices.data(), pre.d, pre.m, pre.h_vec.data(),
+                                   pre.C_all.data.data(), pre.G.data.data(), pre.invnorm_flat.data(),
+                                   STLQ_B200_GEMM_EXACT, &h),
+          "stlq_b200_sharded_create");
+    cache.items.push_back({devices, pre.build_tag, pre.C_all.data.data(), pre.H, pre.d, h});
+    return h;
+}
+
+}  // namespace
+
+bool EncodeBaseSharded(const Config& config, const Dataset& dataset, const CodebookPack& codebooks,
+                       const Precomp& precomp, const std::vector<int>& devices, BaseEncoding* base,
+                       float* out_beam_mse, float* out_final_mse, std::string* error) {
+    if (!base) {
+        if (error) *error = "BaseEncoding output is null.";
+        return false;
+    }
+    const int d = dataset.Xb.rows, n = dataset.Xb.cols;
+    if (d <= 0 || n <= 0) {
+        if (error) *error = "Empty base dataset.";
+        return false;
+    }
+    if (precomp.d != d || precomp.m != static_cast<int>(codebooks.books.size())) {
+        if (error) *error = "Precomp dimensions do not match codebooks or dataset.";
+        return false;
+    }
+    try {
+        const std::vector<int> devs = devices.empty() ? std::vector<int>{config.runtime.cuda_device} : devices;
+        stlq_b200_sharded* sh = ShardedFor(precomp, devs);
+        const auto& e = config.base.encode;
+        const int m = precomp.m;
+        base->B = ColMajorMatrix<FullCode>(m, n);
+        base->a = ColMajorMatrix<float>(m, n);
+        double sse[2] = {0.0, 0.0};
+        Check(stlq_b200_encode_sharded(sh, dataset.Xb.data.data(), STLQ_B200_F32, n, std::max(1, e.H_beam), e.icm_iters,
+                                       e.ils_iters, e.perturb_k, e.use_abs ? 1 : 0, static_cast<std::uint32_t>(e.seed),
+                                       0, base->B.data.data(), base->a.data.data(), nullptr, sse),
+              "stlq_b200_encode_sharded");
+        if (out_beam_mse) *out_beam_mse = static_cast<float>(sse[0] / n);
+        if (out_final_mse) *out_final_mse = static_cast<float>(sse[1] / n);
+    } catch (const std::exception& ex) {
+        if (error) *error = ex.what();
+        return false;
+    }
+    return true;
+}
+
 void BeamSearchPrefixLS(const ColMajorMatrix<float>& X, const Precomp& precomp, const ColMajorMatrix<float>& xC,
                         int H_beam, ColMajorMatrix<FullCode>* B, int device) {
     const int n = X.cols, d = X.rows, m = precomp.m, H = precomp.H;

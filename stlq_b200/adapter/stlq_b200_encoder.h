@@ -33,6 +33,15 @@ bool EncodeBase(const Config& config, const Dataset& dataset, const CodebookPack
                 KernelProvider* kernels, BaseEncoding* base, float* out_beam_mse, float* out_final_mse,
                 std::string* error);
 
+// EncodeBase on several GPUs of this process (stlq_b200_encode_sharded): the base vectors split into
+// contiguous shards, one per device, with the codebooks replicated by one NCCL broadcast and the MSE
+// sums combined by one NCCL reduce.  Same inputs and outputs as EncodeBase, bit for bit; `devices`
+// lists the GPUs (empty: config.runtime.cuda_device alone).  No counterpart in the reference, whose
+// EncodeBase runs on one device.
+bool EncodeBaseSharded(const Config& config, const Dataset& dataset, const CodebookPack& codebooks,
+                       const Precomp& precomp, const std::vector<int>& devices, BaseEncoding* base,
+                       float* out_beam_mse, float* out_final_mse, std::string* error);
+
 void BeamSearchPrefixLS(const ColMajorMatrix<float>& X, const Precomp& precomp, const ColMajorMatrix<float>& xC,
                         int H_beam, ColMajorMatrix<FullCode>* B, int device = 0);
 

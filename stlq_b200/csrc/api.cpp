@@ -466,7 +466,7 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
         if (e == cudaSuccess) return 0;
         return Fail(STLQ_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
     };
-    if ((rc = ck(cudaMemcpyAsync(enc->C.p, C_all, sizeof(float) * H * d, cudaMemcpyHostToDevice, s), "upload C_all")))
+    if ((rc = ck(cudaMemcpyAsync(enc->C.p, C_all, sizeof(float) * H * d, cudaMemcpyDefault, s), "upload C_all")))
         return fail(rc);
     if (large_root) {
         // G(r, h0 + j) = C_all[r] . C_small[j] at Gcol[r * Hs + j], the GEMM's summation order
@@ -475,7 +475,7 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
                                              STLQ_B200_F32, H, enc->Gcol.as<float>(), Hs, nullptr, nullptr, s),
                 "G0S / G_small gemm");
     } else if (G) {
-        rc = ck(cudaMemcpyAsync(enc->Gcol.p, G, sizeof(float) * HH, cudaMemcpyHostToDevice, s), "upload G");
+        rc = ck(cudaMemcpyAsync(enc->Gcol.p, G, sizeof(float) * HH, cudaMemcpyDefault, s), "upload G");
     } else {
         // G = C_all^T C_all in the same summation order as xC (BuildPrecomp calls the same Gemm).
         rc = ck(stlq_b200::LaunchXcGemmExact(enc->C.as<float>(), H, d, enc->C.p, STLQ_B200_F32, H, enc->Gcol.as<float>(),
@@ -511,7 +511,7 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
         if (rc) return fail(rc);
     } else {
         if (invnorm) {
-            rc = ck(cudaMemcpyAsync(enc->invnorm.p, invnorm, sizeof(float) * H, cudaMemcpyHostToDevice, s),
+            rc = ck(cudaMemcpyAsync(enc->invnorm.p, invnorm, sizeof(float) * H, cudaMemcpyDefault, s),
                     "upload invnorm");
         } else {
             rc = ck(stlq_b200::LaunchInvnorm(enc->C.as<float>(), H, d, enc->invnorm.as<float>(), s), "invnorm");
@@ -958,3 +958,12 @@ int stlq_b200_sse(stlq_b200_encoder* enc, const void* X_dev, int x_dtype, const 
 }
 
 }  // extern "C"
+
+namespace stlq_b200 {
+
+// For the multi-GPU entry points (sharded.cpp): the encoder's device-side sums of the last
+// host-buffer encode (2 doubles, written on its compute stream) and that stream.
+double* EncoderSseDevice(stlq_b200_encoder* enc) { return enc ? enc->sse_d.as<double>() : nullptr; }
+cudaStream_t EncoderStream(stlq_b200_encoder* enc) { return enc ? enc->compute : nullptr; }
+
+}  // namespace stlq_b200

@@ -138,27 +138,32 @@ __device__ float PotfLeftover(float y, const float* a, const float* x, int m1, i
     return add_rn(y, e);
 }
 
-__device__ __noinline__ bool CholLapack(float* A, int m) {  // column-major A[r + c*m], upper triangle
+// The LAPACK path keeps only the upper triangle, packed by columns: element (r, c), r <= c, at
+// c (c + 1) / 2 + r (column c's first c + 1 rows contiguous).  Fewer words per lane than a full
+// m x m column-major array, so the lanes' scratch stays in L1; the arithmetic is unchanged.
+__device__ __forceinline__ int Pk(int r, int c) { return c * (c + 1) / 2 + r; }
+
+__device__ __noinline__ bool CholLapack(float* A, int m) {  // packed upper triangle (Pk)
     for (int j = 0; j < m; ++j) {
-        const float* xj = A + j * m;
+        const float* xj = A + Pk(0, j);
         double acc = 0.0;
         for (int k = 0; k < j; ++k) acc = __dadd_rn(acc, static_cast<double>(mul_rn(xj[k], xj[k])));
-        float ajj = sub_rn(A[j + j * m], static_cast<float>(acc));
+        float ajj = sub_rn(A[Pk(j, j)], static_cast<float>(acc));
         if (ajj <= 0.0f) return false;
         ajj = __fsqrt_rn(ajj);
-        A[j + j * m] = ajj;
+        A[Pk(j, j)] = ajj;
         const float r = div_rn(1.0f, ajj);
         const int ncol = m - j - 1, m3 = j & 3, m1 = j - m3, n1 = (ncol >> 2) * 4;
         for (int ci = 0; ci < ncol; ++ci) {
             const int c = j + 1 + ci;
-            const float* ac = A + c * m;
-            float y = A[j + c * m];
+            const float* ac = A + Pk(0, c);
+            float y = A[Pk(j, c)];
             if (m1 > 0) {
                 const float K = ci < n1 ? PotfBlockAvx(ac, xj, m1) : PotfBlockSse(ac, xj, m1);
                 y = __fmaf_rn(K, -1.0f, y);
             }
             y = PotfLeftover(y, ac, xj, m1, m3);
-            A[j + c * m] = mul_rn(y, r);
+            A[Pk(j, c)] = mul_rn(y, r);
         }
     }
     return true;
@@ -169,24 +174,24 @@ __device__ __noinline__ bool CholLapack(float* A, int m) {  // column-major A[r 
 __device__ void TrsmUpdate(const float* A, int m, float* c, int r0, int nr, int t0, int t1, bool fwd) {
     for (int r = r0; r < r0 + nr; ++r) {
         float acc = 0.0f;
-        for (int t = t0; t < t1; ++t) acc = __fmaf_rn(fwd ? A[t + r * m] : A[r + t * m], c[t], acc);
+        for (int t = t0; t < t1; ++t) acc = __fmaf_rn(fwd ? A[Pk(t, r)] : A[Pk(r, t)], c[t], acc);
         c[r] = __fmaf_rn(acc, -1.0f, c[r]);
     }
 }
 
 __device__ void TrsmFwdBlock(const float* A, int m, float* c, int r0, int bs) {
     for (int i = r0; i < r0 + bs; ++i) {
-        const float bb = mul_rn(c[i], div_rn(1.0f, A[i + i * m]));
+        const float bb = mul_rn(c[i], div_rn(1.0f, A[Pk(i, i)]));
         c[i] = bb;
-        for (int k = i + 1; k < r0 + bs; ++k) c[k] = __fmaf_rn(-bb, A[i + k * m], c[k]);
+        for (int k = i + 1; k < r0 + bs; ++k) c[k] = __fmaf_rn(-bb, A[Pk(i, k)], c[k]);
     }
 }
 
 __device__ void TrsmBwdBlock(const float* A, int m, float* c, int r0, int bs) {
     for (int i = r0 + bs - 1; i >= r0; --i) {
-        const float bb = mul_rn(c[i], div_rn(1.0f, A[i + i * m]));
+        const float bb = mul_rn(c[i], div_rn(1.0f, A[Pk(i, i)]));
         c[i] = bb;
-        for (int k = r0; k < i; ++k) c[k] = __fmaf_rn(-bb, A[k + i * m], c[k]);
+        for (int k = r0; k < i; ++k) c[k] = __fmaf_rn(-bb, A[Pk(k, i)], c[k]);
     }
 }
 
@@ -240,10 +245,10 @@ __device__ __noinline__ bool SolveLs(const Dims& dims, const Gram& G, const floa
             for (int k = 0; k <= j; ++k) {
                 const float g = G(k, j);
                 if (fixed) ws.A[k * m + j] = g;
-                else ws.A[k + j * m] = g;
+                else ws.A[Pk(k, j)] = g;
             }
             if (fixed) ws.A[j * m + j] = add_rn(ws.A[j * m + j], lambda);
-            else ws.A[j + j * m] = add_rn(ws.A[j + j * m], lambda);
+            else ws.A[Pk(j, j)] = add_rn(ws.A[Pk(j, j)], lambda);
         }
         const bool ok = fixed ? CholFixed(ws.A, m) : CholLapack(ws.A, m);
         if (ok) {
@@ -354,7 +359,7 @@ __device__ __forceinline__ int ScoreLayer(const Dims& dims, const GramRef& Gr, c
 #pragma unroll
         for (int i = 0; i < kScoreT; ++i) {
             const int t = t0 + lane + 32 * i;
-            v[i] = t < hj ? xc[startf + t] : 0.0f;
+            v[i] = t < hj ? __ldcs(xc + startf + t) : 0.0f;  // streamed once: evict first
         }
         for (int l = 0; l < m; ++l) {
             if (l == j) continue;
@@ -463,7 +468,7 @@ __device__ __noinline__ int ScoreLayerStrict(const Dims& dims, const GramRef& Gr
 #pragma unroll
         for (int i = 0; i < kScoreT; ++i) {
             const int t = t0 + lane + 32 * i;
-            v[i] = t < hj ? xc[startf + t] : 0.0f;
+            v[i] = t < hj ? __ldcs(xc + startf + t) : 0.0f;
         }
         float xa[kScoreT];
 #pragma unroll

@@ -67,6 +67,13 @@ def load_library():
                                                             c_u32, c_u64, vp, vp, vp, vp, vp, vp]
     lib.stlq_b200_set_rotation.argtypes = [vp, vp]
     lib.stlq_b200_rotate.argtypes = [vp, vp, c_int, c_i64, vp, vp]
+    lib.stlq_b200_sharded_create.argtypes = [c_int, vp, c_int, c_int, vp, vp, vp, vp, c_int, ctypes.POINTER(vp)]
+    lib.stlq_b200_sharded_create_large_root.argtypes = [c_int, vp, c_int, c_int, vp, vp, c_int, ctypes.POINTER(vp)]
+    lib.stlq_b200_sharded_destroy.argtypes = [vp]
+    lib.stlq_b200_sharded_encoder.argtypes = [vp, c_int, ctypes.POINTER(vp)]
+    lib.stlq_b200_encode_sharded.argtypes = lib.stlq_b200_encode_base.argtypes
+    lib.stlq_b200_encode_sharded_u16.argtypes = lib.stlq_b200_encode_base.argtypes
+    lib.stlq_b200_encode_sharded_large_root.argtypes = lib.stlq_b200_encode_base_large_root.argtypes
     _LIB = lib
     return lib
 
@@ -357,3 +364,83 @@ class Encoder:
 
         s = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
         _check(self.lib, self.lib.stlq_b200_sync(self.handle, ctypes.c_void_p(s)), "stlq_b200_sync")
+
+
+class ShardedEncoder:
+    """One codebook set on several GPUs of this process (stlq_b200_sharded_create): the codebooks
+    are replicated from the first device by one NCCL broadcast, every encode splits the vectors
+    into contiguous shards (one host thread per device, global sample ids) and the MSE sums are
+    combined by one NCCL reduce.  Results equal a single device's bit for bit."""
+
+    def __init__(self, C_all, h_vec, devices, G=None, invnorm=None, gemm_mode="exact", large_root: bool = False):
+        self.lib = load_library()
+        self.C_all = np.ascontiguousarray(C_all, np.float32)
+        self.h_vec = np.ascontiguousarray(h_vec, np.int32)
+        self.H, self.d = self.C_all.shape
+        self.m = len(self.h_vec)
+        self.devices = np.ascontiguousarray(list(devices), np.int32)
+        self.wide = self.m > 0 and int(self.h_vec.max()) > 256
+        self.large_root = bool(large_root)
+        mode = _MODES[gemm_mode] if isinstance(gemm_mode, str) else int(gemm_mode)
+        h = ctypes.c_void_p()
+        if self.large_root:
+            rc = self.lib.stlq_b200_sharded_create_large_root(len(self.devices), _np_ptr(self.devices), self.d, self.m,
+                                                              _np_ptr(self.h_vec), _np_ptr(self.C_all), mode,
+                                                              ctypes.byref(h))
+            _check(self.lib, rc, "stlq_b200_sharded_create_large_root")
+        else:
+            Gc = None if G is None else np.ascontiguousarray(G, np.float32)
+            inv = None if invnorm is None else np.ascontiguousarray(invnorm, np.float32)
+            rc = self.lib.stlq_b200_sharded_create(len(self.devices), _np_ptr(self.devices), self.d, self.m,
+                                                   _np_ptr(self.h_vec), _np_ptr(self.C_all), _np_ptr(Gc), _np_ptr(inv),
+                                                   mode, ctypes.byref(h))
+            _check(self.lib, rc, "stlq_b200_sharded_create")
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.stlq_b200_sharded_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode_base(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,
+                    seed: int = 38251450, sample_id_offset: int = 0, out=None):
+        """Like Encoder.encode_base, over every device; beam_mse / final_mse from the reduced sums."""
+        X = np.ascontiguousarray(X)
+        n = X.shape[0]
+        out = dict(out or {})
+        B = out.get("B")
+        B = np.empty((n, self.m), np.uint16 if self.wide else np.uint8) if B is None else B
+        a = out.get("a")
+        a = np.empty((n, self.m), np.float32) if a is None else a
+        cost = out.get("cost")
+        cost = np.empty(n, np.float32) if cost is None else cost
+        sse = np.zeros(2, np.float64)
+        name = "stlq_b200_encode_sharded_u16" if self.wide else "stlq_b200_encode_sharded"
+        rc = getattr(self.lib, name)(self.handle, _np_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters,
+                                     perturb_k, int(bool(use_abs)), seed & 0xFFFFFFFF, sample_id_offset, _np_ptr(B),
+                                     _np_ptr(a), _np_ptr(cost), _np_ptr(sse))
+        _check(self.lib, rc, name)
+        nn = max(n, 1)
+        return dict(B=B, a=a, cost=cost, beam_mse=sse[0] / nn, final_mse=sse[1] / nn, sse=sse)
+
+    def encode_base_large_root(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0,
+                               use_abs=True, seed: int = 38251450, sample_id_offset: int = 0):
+        X = np.ascontiguousarray(X)
+        n = X.shape[0]
+        cluster = np.empty(n, np.uint32)
+        B_small = np.empty((n, self.m - 1), np.uint8)
+        a = np.empty((n, self.m), np.float32)
+        cost = np.empty(n, np.float32)
+        sums = np.zeros(2, np.float64)
+        rc = self.lib.stlq_b200_encode_sharded_large_root(
+            self.handle, _np_ptr(X), _dtype_code(X), n, beam, icm_iters, ils_iters, perturb_k, int(bool(use_abs)),
+            seed & 0xFFFFFFFF, sample_id_offset, _np_ptr(cluster), _np_ptr(B_small), _np_ptr(a), _np_ptr(cost),
+            _np_ptr(sums))
+        _check(self.lib, rc, "stlq_b200_encode_sharded_large_root")
+        return dict(cluster=cluster, B_small=B_small, a=a, cost=cost, sums=sums)

@@ -120,3 +120,22 @@ def test_noalloc_python_layer_rejects_bad_tensors_before_launch():
     for x_c, x_n, out, msg in bad:
         with pytest.raises(ValueError, match=msg):
             enc_mod._check_noalloc_args(x_n, x_c, out, H, m)
+
+
+def test_sharded_entries_reject_bad_arguments():
+    """The multi-GPU entry points validate on the host: no devices, repeated devices, null handle
+    (before any NCCL or CUDA work)."""
+    lib = stlq_b200.load_library()
+    vp = ctypes.c_void_p
+    h = np.array([4, 4], np.int32)
+    C = np.zeros((8, 4), np.float32)
+    out = vp()
+    assert lib.stlq_b200_sharded_create(0, None, 4, 2, vp(h.ctypes.data), vp(C.ctypes.data), None, None, 0,
+                                        ctypes.byref(out)) == 1
+    assert b"n_devices" in lib.stlq_b200_last_error()
+    dup = np.array([0, 0], np.int32)
+    assert lib.stlq_b200_sharded_create(2, vp(dup.ctypes.data), 4, 2, vp(h.ctypes.data), vp(C.ctypes.data), None,
+                                        None, 0, ctypes.byref(out)) == 1
+    assert b"distinct" in lib.stlq_b200_last_error() and not out.value
+    assert lib.stlq_b200_encode_sharded(None, None, 0, 0, 4, 0, 0, 0, 1, 0, 0, None, None, None, None) == 1
+    assert lib.stlq_b200_sharded_destroy(None) == 0

@@ -35,6 +35,20 @@ def test_adapter_encode_base(harness, name):
     assert abs(mse[1] - c["final_mse"]) <= 1e-6 * abs(c["final_mse"])
 
 
+@pytest.mark.parametrize("name", ["d96_m8_k256_b16_ils", "ragged_h"])
+def test_adapter_encode_base_sharded(harness, name):
+    """stlq::b200::EncodeBaseSharded (every GPU of the box) on the reference's Precomp: the
+    reference's golden outputs, like EncodeBase."""
+    import torch
+
+    c = load_case(name)
+    pre, m, H = harness.precomp(c["h_vec"], c["C_all"])
+    B, a, mse = harness.encode_base(pre, m, c["X"], c["beam"], c["icm_iters"], c["ils_iters"], c["perturb_k"],
+                                    bool(c["use_abs"]), c["seed"], n_devices=torch.cuda.device_count())
+    assert np.array_equal(B, c["B"]) and np.array_equal(a, c["a"])
+    assert abs(mse[1] - c["final_mse"]) <= 1e-6 * abs(c["final_mse"])
+
+
 @pytest.mark.parametrize("name", ["d128_m8_k256_b16", "m16_k64_b16", "ref_test_shape"])
 def test_adapter_stage_seams(harness, name):
     c = load_case(name)
