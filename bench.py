@@ -48,6 +48,9 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-fp32-peak", action="store_true", help="skip the SGEMM FP32 peak measurement")
     p.add_argument("--no-strict", action="store_true", help="skip the STRICT (tensor-core GEMM) mode leg")
+    p.add_argument("--gemm-mode", choices=["exact", "strict"], default="exact",
+                   help="xC GEMM of the timed encode: exact (SIMT, the reference BLAS's order) or strict (tcgen05 "
+                        "3xTF32 with the exact entries recomputed where they decide anything); both bit-identical")
     p.add_argument("--sweep", action="store_true",
                    help="config 4's grid (M in {8,16}, K in {256,1024}, beam in {1,4,16,32}, ICM 0/1): one JSON "
                         "line with every point's throughput and code agreement")
@@ -369,7 +372,7 @@ def run_ours(args):
         dist.broadcast(C, src=0)
     C_np = C.cpu().numpy()
     h_vec = [args.k] * args.m
-    enc = stlq_b200.Encoder(C_np, h_vec, device=local)
+    enc = stlq_b200.Encoder(C_np, h_vec, device=local, gemm_mode=args.gemm_mode)
     n = args.n
     offset = rank * n
     X_np = base_vectors(args, n, 4, start=offset)
@@ -449,32 +452,55 @@ def run_ours(args):
         assert np.array_equal(r["B"], B.cpu().numpy()), "host and device paths disagree"
 
     # Dominant kernel (beam search) timed alone on a 262,144-vector slice, CUDA events on the
-    # launching stream, L2 holds none of its 2 GiB xC input between launches.
+    # launching stream, L2 holds none of its 2 GiB xC input between launches.  The GEMM alone is
+    # timed into a preallocated output.  In STRICT mode the beam needs the vectors (its exact
+    # entries), which the stage entry point does not take: its time is the ICM-0 stage's minus the
+    # GEMM's (the LS and norms left in it are under 3% of it).
     S = min(n, 262_144)
-    xC = enc.xc_gemm(X[:S])
-    xn = enc.xnorm2(X[:S])
-    for _ in range(2):
-        enc.beam_search(xn, xC, args.beam)
-    enc.beam_stats(reset=True)
-    enc.beam_search(xn, xC, args.beam)
-    beam_stats = enc.beam_stats(reset=True)
     reps = 3
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    xC = torch.empty((S, H), dtype=torch.float32, device=device)
+
+    def gemm():
+        import ctypes
+
+        from stlq_b200.encoder import _t_ptr
+
+        rc = enc.lib.stlq_b200_xc_gemm(enc.handle, _t_ptr(X), 0, S, _t_ptr(xC),
+                                       ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+        assert rc == 0, enc.lib.stlq_b200_last_error()
+
+    for _ in range(2):
+        gemm()
     torch.cuda.synchronize()
     e0.record()
     for _ in range(reps):
-        enc.beam_search(xn, xC, args.beam)
+        gemm()
+    e1.record()
+    torch.cuda.synchronize()
+    gemm_s = e0.elapsed_time(e1) / 1e3 / reps
+    xn = enc.xnorm2(X[:S])
+    if args.gemm_mode == "strict":
+        def beam_once():
+            enc.encode_base_device(X[:S], args.beam, 0, 0, 0, True, 38251450, offset)
+    else:
+        def beam_once():
+            enc.beam_search(xn, xC, args.beam)
+    for _ in range(2):
+        beam_once()
+    torch.cuda.synchronize()
+    enc.beam_stats(reset=True)
+    beam_once()
+    beam_stats = enc.beam_stats(reset=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        beam_once()
     e1.record()
     torch.cuda.synchronize()
     beam_s = e0.elapsed_time(e1) / 1e3 / reps
-    # GEMM alone on the same slice.
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record()
-    for _ in range(reps):
-        enc.xc_gemm(X[:S])
-    g1.record()
-    torch.cuda.synchronize()
-    gemm_s = g0.elapsed_time(g1) / 1e3 / reps
+    if args.gemm_mode == "strict":
+        beam_s -= gemm_s
     del xC
 
     cpu = None
@@ -533,7 +559,7 @@ def run_ours(args):
             "data": f"synthetic (seeded {args.data.upper()}-like D={args.d}; codebooks: seeded residual k-means)",
             "config": {"workload": f"{n} x D={args.d} f32 per GPU, M={args.m}, K={args.k}, beam={args.beam}, "
                                    f"ICM={args.icm}, ILS=0, use_abs, seed 38251450",
-                       "vectors_per_gpu": n, "gemm_mode": "exact",
+                       "vectors_per_gpu": n, "gemm_mode": args.gemm_mode,
                        "cache": f"inputs larger than L2 (X {X_np.nbytes / 2**20:.0f} MiB per GPU, xC up to 2 GiB "
                                 "per slice)",
                        "parallelism": f"dp{world} (shards of base vectors)"},
@@ -543,7 +569,8 @@ def run_ours(args):
                 # The beam kernel (93% of the step) is bound by FP32 issue of its candidate
                 # arithmetic, not by HBM or tensor cores: the fraction is against the FP32 SIMT
                 # peak (cuBLAS SGEMM with TF32 off, measured in this run); HBM alongside.
-                "bound": "simt", "kernel": "BeamFastKernel<8, 0, 0>",
+                "bound": "simt",
+                "kernel": f"BeamFastKernel<{8 if args.m <= 8 else 16}, 0, {int(args.gemm_mode == 'strict')}>",
                 "achieved": F_cand * S / beam_s / 1e12, "peak": fp32_peak, "unit": "TFLOP/s",
                 "frac": F_cand * S / beam_s / 1e12 / fp32_peak, "flops_per_vector": F_cand,
                 "peak_source": "cuBLAS SGEMM (TF32 off) measured in this run",
