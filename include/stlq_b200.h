@@ -247,6 +247,33 @@ int stlq_b200_encode_sharded_large_root(stlq_b200_sharded* sh, const void* X, in
                                         uint64_t sample_id_offset, uint32_t* cluster_out, uint8_t* B_small_out,
                                         float* a_out, float* cost_out, double* cost_sums_out);
 
+/* ---- Base-store writer fed from device buffers ----
+ * Writes the reference's basic base store (BaseBasicWriter, include/stlq/io/base_store.h:29-97;
+ * src/io/base_store.cpp): meta.json, meta.bin, cluster_id.u32, codes_shard_NNNN.bin,
+ * coeffs_shard_NNNN.bin and bucket_NNNN.bin, byte for byte as the reference writes them for the
+ * same blocks (Open, then AppendBlock / AppendBlockRawU8 / AppendBlockRawF32 per block, Close).
+ * The parameters are BaseBasicStoreConfig's; raw_bytes_per_vec 0 means d (uint8 vectors), d * 4 for
+ * float vectors.  device >= 0: blocks may sit in device memory (outputs of the encode entry points);
+ * an append enqueues their copy into a pinned staging slot on the store's own copy stream, after the
+ * work already enqueued on `stream`, and returns; one writer thread writes blocks in append order
+ * as their copies complete (an append waits only when three blocks are in flight).  device < 0:
+ * host buffers only, no CUDA call.  max_block: the largest block (vectors) an append may pass.
+ * One host thread per store.  Errors of the writer thread are returned by the next call. */
+typedef struct stlq_b200_store stlq_b200_store;
+int stlq_b200_store_open(const char* dir, int d, int m, const int* h_vec, int shard_size, int bucket_size,
+                         int bucket_flush_mb, int write_vector_bucket, int write_basic_to_bucket, int raw_bytes_per_vec,
+                         int device, int64_t max_block, stlq_b200_store** out);
+/* One block of n vectors with global ids start_id..: cluster (n root codes), B_small ((m-1) x n
+ * codes), a (m x n coefficients), x_raw (vector i at x_raw + i * ld_x_bytes; only read with
+ * write_vector_bucket).  Host or device pointers (device stores). */
+int stlq_b200_store_append(stlq_b200_store* st, uint64_t start_id, int64_t n, const uint32_t* cluster,
+                           const uint8_t* B_small, const float* a, const void* x_raw, int64_t ld_x_bytes,
+                           void* stream);
+/* Writes everything appended so far (BaseBasicWriter::Flush). */
+int stlq_b200_store_flush(stlq_b200_store* st);
+/* Flushes, closes the files and frees the store (BaseBasicWriter::Close); returns the first error. */
+int stlq_b200_store_close(stlq_b200_store* st);
+
 /* ---- Kernel-provider primitives ----
  * The device operations behind StreamKernelProvider (include/stlq/core/kernel_provider.h:28-221,
  * the reference's GPU backend seam; its CUDA implementation is src/core/kernel_provider_cuda_stream*

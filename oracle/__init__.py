@@ -238,6 +238,10 @@ class Reference:
         self.lib.ref_set_threads(self.threads)
         return out
 
+    def store_write(self, dir, d, m, h_vec, blocks, **kw):
+        """BaseBasicWriter (src/io/base_store.cpp) writing `blocks`; see ref_store_write."""
+        ref_store_write(self, dir, d, m, h_vec, blocks, **kw)
+
     def rotate(self, R, X):
         """ApplyRotationInPlace's GEMM: R (d x d) given as numpy R_np[col, row] (column-major), X (n, d)."""
         R, X = _f32(R), _f32(X)
@@ -268,6 +272,35 @@ class Reference:
         if rc != 0:
             raise RuntimeError(f"ref_large_root_encode failed ({rc})")
         return dict(cluster=cluster, B_small=B_small, a=a, cost_beam=cost_beam, cost=cost)
+
+
+def ref_store_write(ref, dir, d, m, h_vec, blocks, shard_size=2_000_000, bucket_size=256, bucket_flush_mb=256,
+                    write_vector_bucket=True, write_basic_to_bucket=True, raw_bytes_per_vec=0, x_kind=1):
+    """The reference's BaseBasicWriter (src/io/base_store.cpp) writing `blocks`: a list of dicts with
+    start (global id of the first vector), cluster (n,) uint32, B_small (n, m-1) uint8, a (n, m) float32
+    and, for x_kind 1 / 2, x (n, d) uint8 / float32 (AppendBlockRawU8 / AppendBlockRawF32)."""
+    lib = ref.lib
+    lib.ref_store_write.restype = ctypes.c_int
+    n = np.array([len(b["cluster"]) for b in blocks], np.int64)
+    st = np.array([b["start"] for b in blocks], np.uint64)
+    cl = np.ascontiguousarray(np.concatenate([b["cluster"] for b in blocks]), np.uint32)
+    Bs = np.ascontiguousarray(np.concatenate([b["B_small"].reshape(len(b["cluster"]), -1) for b in blocks]), np.uint8)
+    A = np.ascontiguousarray(np.concatenate([b["a"] for b in blocks]), np.float32)
+    X = None
+    if x_kind:
+        X = np.ascontiguousarray(np.concatenate([b["x"] for b in blocks]))
+        X = X.view(np.uint8)
+    err = ctypes.create_string_buffer(512)
+    h = np.asarray(h_vec, np.int32)
+    vp = ctypes.c_void_p
+    rc = lib.ref_store_write(
+        str(dir).encode(), ctypes.c_int(d), ctypes.c_int(m), vp(h.ctypes.data), ctypes.c_int(shard_size),
+        ctypes.c_int(bucket_size), ctypes.c_int(bucket_flush_mb), ctypes.c_int(int(write_vector_bucket)),
+        ctypes.c_int(int(write_basic_to_bucket)), ctypes.c_int(raw_bytes_per_vec), ctypes.c_int(len(blocks)),
+        vp(n.ctypes.data), vp(st.ctypes.data), vp(cl.ctypes.data), vp(Bs.ctypes.data), vp(A.ctypes.data),
+        vp(X.ctypes.data) if X is not None else None, ctypes.c_int(x_kind), err, ctypes.c_int(512))
+    if rc:
+        raise RuntimeError(err.value.decode())
 
 
 class RefPrecomp:

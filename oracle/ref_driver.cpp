@@ -319,3 +319,61 @@ int ref_large_root_encode(int d, int m, const int* h_vec, const float* C_all, co
 }
 
 }  // extern "C"
+
+// The reference's own base-store writer (src/io/base_store.cpp, BaseBasicWriter): Open, one append
+// per block (x_kind 0: AppendBlock without raw vectors; 1: AppendBlockRawU8; 2: AppendBlockRawF32),
+// Close.  Block b has block_n[b] vectors starting at global id block_start[b]; the arrays hold the
+// blocks one after another (cluster ids, (m-1) x n codes, m x n coefficients, raw vectors).
+#include "stlq/io/base_store.h"
+
+extern "C" int ref_store_write(const char* dir, int d, int m, const int* h_vec, int shard_size, int bucket_size,
+                               int bucket_flush_mb, int write_vector_bucket, int write_basic_to_bucket,
+                               int raw_bytes_per_vec, int nblocks, const std::int64_t* block_n,
+                               const std::uint64_t* block_start, const std::uint32_t* cluster,
+                               const std::uint8_t* B_small, const float* a, const std::uint8_t* x_raw, int x_kind,
+                               char* err, int errlen) {
+    stlq::io::BaseBasicStoreConfig cfg;
+    cfg.dir = dir;
+    cfg.d = d;
+    cfg.m = m;
+    cfg.h_vec.assign(h_vec, h_vec + m);
+    cfg.shard_size = shard_size;
+    cfg.bucket_size = bucket_size;
+    cfg.bucket_flush_mb = bucket_flush_mb;
+    cfg.write_vector_bucket = write_vector_bucket != 0;
+    cfg.write_basic_to_bucket = write_basic_to_bucket != 0;
+    cfg.raw_bytes_per_vec = raw_bytes_per_vec;
+    stlq::io::BaseBasicWriter w;
+    std::string e;
+    auto fail = [&] {
+        std::strncpy(err, e.c_str(), static_cast<size_t>(errlen) - 1);
+        err[errlen - 1] = 0;
+        return 1;
+    };
+    if (!w.Open(cfg, &e)) return fail();
+    const int mc = std::max(0, m - 1);
+    const int raw = write_vector_bucket ? (raw_bytes_per_vec > 0 ? raw_bytes_per_vec : d) : 0;
+    for (int b = 0; b < nblocks; ++b) {
+        const int n = static_cast<int>(block_n[b]);
+        std::vector<std::uint32_t> cid(cluster, cluster + n);
+        ColMajorMatrix<stlq::Code> B(mc, n);
+        std::memcpy(B.data.data(), B_small, static_cast<size_t>(mc) * n);
+        ColMajorMatrix<float> A(m, n);
+        std::memcpy(A.data.data(), a, sizeof(float) * static_cast<size_t>(m) * n);
+        bool ok;
+        if (x_kind == 1) {
+            ok = w.AppendBlockRawU8(block_start[b], cid, B, A, x_raw, raw, &e);
+        } else if (x_kind == 2) {
+            ok = w.AppendBlockRawF32(block_start[b], cid, B, A, reinterpret_cast<const float*>(x_raw), raw / 4, &e);
+        } else {
+            ok = w.AppendBlock(block_start[b], cid, B, A, nullptr, &e);
+        }
+        if (!ok) return fail();
+        cluster += n;
+        B_small += static_cast<size_t>(mc) * n;
+        a += static_cast<size_t>(m) * n;
+        if (x_raw) x_raw += static_cast<size_t>(raw) * n;
+    }
+    if (!w.Close(&e)) return fail();
+    return 0;
+}

@@ -11,6 +11,7 @@ from .encoder import (  # noqa: F401
     GEMM_STRICT,
     Encoder,
     ShardedEncoder,
+    BaseStore,
     StlqB200Error,
     library_path,
     load_library,

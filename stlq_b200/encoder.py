@@ -9,6 +9,7 @@ run on the tensor's current stream.
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import os
 
@@ -444,3 +445,75 @@ class ShardedEncoder:
             _np_ptr(sums))
         _check(self.lib, rc, "stlq_b200_encode_sharded_large_root")
         return dict(cluster=cluster, B_small=B_small, a=a, cost=cost, sums=sums)
+
+
+class BaseStore:
+    """The reference's basic base store written from device or host buffers (stlq_b200_store_*):
+    the same files, byte for byte, as its BaseBasicWriter for the same blocks.  device < 0: host
+    arrays only (no CUDA).  Append blocks in order; close() returns once everything is written."""
+
+    def __init__(self, dir, d, m, h_vec, shard_size=2_000_000, bucket_size=256, bucket_flush_mb=256,
+                 write_vector_bucket=True, write_basic_to_bucket=True, raw_bytes_per_vec=0, device=0,
+                 max_block=262_144):
+        self.lib = load_library()
+        lib = self.lib
+        vp, ci = ctypes.c_void_p, ctypes.c_int
+        lib.stlq_b200_store_open.argtypes = [ctypes.c_char_p, ci, ci, vp, ci, ci, ci, ci, ci, ci, ci, ctypes.c_int64,
+                                             ctypes.POINTER(vp)]
+        lib.stlq_b200_store_append.argtypes = [vp, ctypes.c_uint64, ctypes.c_int64, vp, vp, vp, vp, ctypes.c_int64, vp]
+        lib.stlq_b200_store_flush.argtypes = [vp]
+        lib.stlq_b200_store_close.argtypes = [vp]
+        self.m, self.d, self.device = int(m), int(d), int(device)
+        h = np.ascontiguousarray(h_vec, np.int32)
+        if h.ndim != 1 or len(h) != int(m):
+            raise StlqB200Error("h_vec must hold m codebook sizes")
+        out = vp()
+        _check(lib, lib.stlq_b200_store_open(str(dir).encode(), d, m, _np_ptr(h), shard_size, bucket_size,
+                                             bucket_flush_mb, int(bool(write_vector_bucket)),
+                                             int(bool(write_basic_to_bucket)), raw_bytes_per_vec, self.device,
+                                             max_block, ctypes.byref(out)), "stlq_b200_store_open")
+        self.handle = out
+        # The last appended blocks stay referenced until their staging copies have run: an append
+        # waits for a free slot (3 on a device store), so a block four appends back has been copied.
+        self._keep = collections.deque(maxlen=4)
+
+    def append(self, start_id, cluster, B_small, a, x=None, stream=None):
+        """cluster (n,) uint32/int32, B_small (n, m-1) uint8, a (n, m) float32, x (n, ...) raw vectors;
+        numpy arrays or CUDA tensors."""
+        def ptr(t):
+            if t is None:
+                return None
+            if hasattr(t, "data_ptr"):
+                return _t_ptr(t)
+            return _np_ptr(t)
+
+        n = int(cluster.shape[0])
+        ld = 0
+        if x is not None:
+            ld = int(x.nbytes // max(n, 1)) if not hasattr(x, "element_size") else int(x.stride(0) * x.element_size())
+        if stream is None and hasattr(cluster, "data_ptr") and cluster.is_cuda:
+            import torch
+
+            stream = torch.cuda.current_stream(cluster.device).cuda_stream
+        self._keep.append((cluster, B_small, a, x))
+        _check(self.lib, self.lib.stlq_b200_store_append(self.handle, int(start_id), n, ptr(cluster), ptr(B_small),
+                                                         ptr(a), ptr(x), ld, ctypes.c_void_p(stream or 0)),
+               "stlq_b200_store_append")
+
+    def flush(self):
+        _check(self.lib, self.lib.stlq_b200_store_flush(self.handle), "stlq_b200_store_flush")
+        self._keep.clear()
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            rc = self.lib.stlq_b200_store_close(self.handle)
+            self.handle = None
+            self._keep.clear()
+            _check(self.lib, rc, "stlq_b200_store_close")
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
