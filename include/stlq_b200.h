@@ -274,6 +274,32 @@ int stlq_b200_store_flush(stlq_b200_store* st);
 /* Flushes, closes the files and frees the store (BaseBasicWriter::Close); returns the first error. */
 int stlq_b200_store_close(stlq_b200_store* st);
 
+/* ---- Vector-file reader (input side of the large pipeline's block loop) ----
+ * The reference's BvecsReader / FvecsReader / FbinReader (include/stlq/io/{bvecs,fvecs,fbin}_reader.h)
+ * and its block prefetcher (AsyncBasicBlockPrefetcher, src/quantizer/encode_base_streaming.cpp:72-230).
+ * format: STLQ_B200_FMT_AUTO takes it from the suffix (.bvecs/.siftbin, .fbin, .fvecs), as the
+ * reference's dataset reader factory does.  A prefetch thread reads blocks of `block` vectors of
+ * [begin, end) (end 0: the file's n) into `depth` (>= 2) pinned slots with io_threads parallel
+ * reads.  device >= 0: next() copies a block to device memory on `stream` and strips the records'
+ * dimension prefixes there; device < 0: host-only, no CUDA call.  Every record's prefix is checked
+ * against d (a mismatch of a device block is returned by a later call).  Blocks are row-major
+ * count x d (the reference's column-major d x count), uint8 for .bvecs, float32 otherwise. */
+enum { STLQ_B200_FMT_AUTO = 0, STLQ_B200_FMT_BVECS = 1, STLQ_B200_FMT_FVECS = 2, STLQ_B200_FMT_FBIN = 3 };
+typedef struct stlq_b200_reader stlq_b200_reader;
+int stlq_b200_reader_open(const char* path, int format, uint64_t begin, uint64_t end, int64_t block, int depth,
+                          int io_threads, int device, stlq_b200_reader** out);
+/* d, n (vectors in the file) and the element type (STLQ_B200_U8 or STLQ_B200_F32). */
+int stlq_b200_reader_info(const stlq_b200_reader* rd, int* d, uint64_t* n, int* x_dtype);
+/* The next block, in file order: *start = its first vector, *count = its size (0 once the range is
+ * done).  dst: device memory (device readers) or host memory of at least block * d * element bytes;
+ * asynchronous on `stream` for device readers. */
+int stlq_b200_reader_next(stlq_b200_reader* rd, void* dst, size_t dst_bytes, void* stream, uint64_t* start,
+                          int64_t* count);
+/* ReadBlockInto: vectors start..start+count-1 (clipped to n) into host memory, synchronously. */
+int stlq_b200_reader_read(stlq_b200_reader* rd, uint64_t start, int64_t count, void* dst, size_t dst_bytes,
+                          int64_t* nread);
+int stlq_b200_reader_close(stlq_b200_reader* rd);
+
 /* ---- Kernel-provider primitives ----
  * The device operations behind StreamKernelProvider (include/stlq/core/kernel_provider.h:28-221,
  * the reference's GPU backend seam; its CUDA implementation is src/core/kernel_provider_cuda_stream*

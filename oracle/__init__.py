@@ -238,6 +238,26 @@ class Reference:
         self.lib.ref_set_threads(self.threads)
         return out
 
+    def read_block(self, path, format, start, count):
+        """The reference's BvecsReader / FvecsReader / FbinReader (format 1 / 2 / 3): Open, then
+        ReadBlockInto(start, count).  Returns (d, n, block (nread, d))."""
+        L = self.lib
+        L.ref_read_block.restype = ctypes.c_int
+        probe_d, probe_n, got = ctypes.c_int(), ctypes.c_uint64(), ctypes.c_int64()
+        err = ctypes.create_string_buffer(512)
+        # First call with count 0 learns d and n; the second reads.
+        for pass_ in range(2):
+            dt = np.uint8 if format == 1 else np.float32
+            cnt = count if pass_ else 0
+            buf = np.empty((max(cnt, 1), max(probe_d.value, 1)), dt)
+            rc = L.ref_read_block(str(path).encode(), ctypes.c_int(format), ctypes.c_uint64(start),
+                                  ctypes.c_uint32(cnt), ctypes.c_void_p(buf.ctypes.data), ctypes.c_size_t(buf.nbytes),
+                                  ctypes.byref(probe_d), ctypes.byref(probe_n), ctypes.byref(got), err,
+                                  ctypes.c_int(512))
+            if rc:
+                raise RuntimeError(err.value.decode())
+        return probe_d.value, probe_n.value, buf[: got.value]
+
     def store_write(self, dir, d, m, h_vec, blocks, **kw):
         """BaseBasicWriter (src/io/base_store.cpp) writing `blocks`; see ref_store_write."""
         ref_store_write(self, dir, d, m, h_vec, blocks, **kw)

@@ -377,3 +377,39 @@ extern "C" int ref_store_write(const char* dir, int d, int m, const int* h_vec, 
     if (!w.Close(&e)) return fail();
     return 0;
 }
+
+// The reference's vector-file readers (src/io/{bvecs,fvecs,fbin}_reader.cpp): Open, then
+// ReadBlockInto(start, count) into dst (d x count column-major).  format 1 bvecs, 2 fvecs, 3 fbin.
+// *nread = min(count, n - start) (0 past the end).
+#include "stlq/io/bvecs_reader.h"
+#include "stlq/io/fbin_reader.h"
+#include "stlq/io/fvecs_reader.h"
+
+extern "C" int ref_read_block(const char* path, int format, std::uint64_t start, std::uint32_t count, void* dst,
+                              std::size_t dst_bytes, int* d_out, std::uint64_t* n_out, std::int64_t* nread,
+                              char* err, int errlen) {
+    std::string e;
+    auto fail = [&] {
+        std::strncpy(err, e.c_str(), static_cast<size_t>(errlen) - 1);
+        err[errlen - 1] = 0;
+        return 1;
+    };
+    auto run = [&](auto& r, auto* p) {
+        if (!r.Open(path, &e)) return fail();
+        *d_out = r.d();
+        *n_out = r.n();
+        *nread = (count == 0 || start >= r.n()) ? 0 : static_cast<std::int64_t>(std::min<std::uint64_t>(r.n() - start, count));
+        if (!r.ReadBlockInto(start, count, p, dst_bytes, &e)) return fail();
+        return 0;
+    };
+    if (format == 1) {
+        stlq::io::BvecsReader r;
+        return run(r, static_cast<std::uint8_t*>(dst));
+    }
+    if (format == 2) {
+        stlq::io::FvecsReader r;
+        return run(r, static_cast<float*>(dst));
+    }
+    stlq::io::FbinReader r;
+    return run(r, static_cast<float*>(dst));
+}

@@ -12,6 +12,7 @@ from .encoder import (  # noqa: F401
     Encoder,
     ShardedEncoder,
     BaseStore,
+    VectorReader,
     StlqB200Error,
     library_path,
     load_library,

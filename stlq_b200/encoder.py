@@ -517,3 +517,82 @@ class BaseStore:
             self.close()
         except Exception:
             pass
+
+
+class VectorReader:
+    """The reference's .bvecs / .fvecs / .fbin readers with its block prefetcher (stlq_b200_reader_*).
+    device >= 0: next_block() returns device tensors; device < 0: numpy arrays (no CUDA)."""
+
+    FORMATS = {"auto": 0, "bvecs": 1, "fvecs": 2, "fbin": 3}
+
+    def __init__(self, path, format="auto", begin=0, end=0, block=262_144, depth=3, io_threads=4, device=0):
+        self.lib = load_library()
+        lib = self.lib
+        vp, ci, u64, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_int64
+        lib.stlq_b200_reader_open.argtypes = [ctypes.c_char_p, ci, u64, u64, i64, ci, ci, ci, ctypes.POINTER(vp)]
+        lib.stlq_b200_reader_info.argtypes = [vp, ctypes.POINTER(ci), ctypes.POINTER(u64), ctypes.POINTER(ci)]
+        lib.stlq_b200_reader_next.argtypes = [vp, vp, ctypes.c_size_t, vp, ctypes.POINTER(u64), ctypes.POINTER(i64)]
+        lib.stlq_b200_reader_read.argtypes = [vp, u64, i64, vp, ctypes.c_size_t, ctypes.POINTER(i64)]
+        lib.stlq_b200_reader_close.argtypes = [vp]
+        out = vp()
+        fmt = self.FORMATS[format] if isinstance(format, str) else int(format)
+        _check(lib, lib.stlq_b200_reader_open(str(path).encode(), fmt, int(begin), int(end), int(block), int(depth),
+                                              int(io_threads), int(device), ctypes.byref(out)), "stlq_b200_reader_open")
+        self.handle = out
+        self.device, self.block = int(device), int(block)
+        d, n, dt = ci(), u64(), ci()
+        _check(lib, lib.stlq_b200_reader_info(out, ctypes.byref(d), ctypes.byref(n), ctypes.byref(dt)),
+               "stlq_b200_reader_info")
+        self.d, self.n = d.value, n.value
+        self.dtype = np.uint8 if dt.value == 1 else np.float32
+
+    def read(self, start, count):
+        """ReadBlockInto: host array of vectors start..start+count-1 (clipped to n)."""
+        buf = np.empty((max(int(count), 0), self.d), self.dtype)
+        got = ctypes.c_int64()
+        _check(self.lib, self.lib.stlq_b200_reader_read(self.handle, int(start), int(count), _np_ptr(buf), buf.nbytes,
+                                                        ctypes.byref(got)), "stlq_b200_reader_read")
+        return buf[: got.value]
+
+    def next_block(self, out=None, stream=None):
+        """(start, block) of the next block in file order, or None at the end.  Device readers copy
+        asynchronously on `stream` (default: torch's current stream) into `out` (or a new tensor)."""
+        start, cnt = ctypes.c_uint64(), ctypes.c_int64()
+        if self.device < 0:
+            buf = np.empty((self.block, self.d), self.dtype) if out is None else out
+            _check(self.lib, self.lib.stlq_b200_reader_next(self.handle, _np_ptr(buf), buf.nbytes, None,
+                                                            ctypes.byref(start), ctypes.byref(cnt)),
+                   "stlq_b200_reader_next")
+        else:
+            import torch
+
+            tdt = torch.uint8 if self.dtype == np.uint8 else torch.float32
+            buf = torch.empty((self.block, self.d), dtype=tdt, device=f"cuda:{self.device}") if out is None else out
+            s = torch.cuda.current_stream(buf.device).cuda_stream if stream is None else stream
+            _check(self.lib, self.lib.stlq_b200_reader_next(self.handle, _t_ptr(buf),
+                                                            buf.numel() * buf.element_size(), ctypes.c_void_p(s),
+                                                            ctypes.byref(start), ctypes.byref(cnt)),
+                   "stlq_b200_reader_next")
+        if cnt.value == 0:
+            return None
+        return start.value, buf[: cnt.value]
+
+    def __iter__(self):
+        while True:
+            b = self.next_block()
+            if b is None:
+                return
+            yield b
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            rc = self.lib.stlq_b200_reader_close(self.handle)
+            self.handle = None
+            _check(self.lib, rc, "stlq_b200_reader_close")
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
