@@ -35,8 +35,11 @@ enum {
  *   STLQ_B200_GEMM_EXACT  FP32 FMA chains in the order of the reference's CPU BLAS backend
  *                         (OpenBLAS SkylakeX SGEMM: one chain per 448-deep K block, blocks summed);
  *                         xC and therefore the codes are bit-identical to the reference's.
- *   STLQ_B200_GEMM_STRICT tcgen05 tensor cores, 3xTF32 split: FP32-accurate, not bit-identical
- *                         (the reference's runtime.cuda_mode=strict accuracy class).
+ *   STLQ_B200_GEMM_STRICT tcgen05 tensor cores, 3xTF32 split, with error bounds carried through
+ *                         the beam and the refinement: every xC entry a decision or an output
+ *                         depends on is recomputed in the CPU BLAS's order, so the results are
+ *                         bit-identical to EXACT's (a tensor-core entry outside its bound is
+ *                         reported as an error, never used).
  *   STLQ_B200_GEMM_FAST   tcgen05 tensor cores, 1xTF32 (the reference's TF32 fast mode). */
 enum {
     STLQ_B200_GEMM_EXACT = 0,
@@ -265,7 +268,9 @@ int stlq_b200_store_open(const char* dir, int d, int m, const int* h_vec, int sh
                          int device, int64_t max_block, stlq_b200_store** out);
 /* One block of n vectors with global ids start_id..: cluster (n root codes), B_small ((m-1) x n
  * codes), a (m x n coefficients), x_raw (vector i at x_raw + i * ld_x_bytes; only read with
- * write_vector_bucket).  Host or device pointers (device stores). */
+ * write_vector_bucket).  Host or device pointers (device stores).  Device stores: work enqueued on
+ * `stream` after the append waits for the block's staging copy, so the caller may reuse or free
+ * its buffers in that stream's order. */
 int stlq_b200_store_append(stlq_b200_store* st, uint64_t start_id, int64_t n, const uint32_t* cluster,
                            const uint8_t* B_small, const float* a, const void* x_raw, int64_t ld_x_bytes,
                            void* stream);

@@ -377,6 +377,9 @@ int stlq_b200_store_append(stlq_b200_store* st, uint64_t start_id, int64_t n, co
             e = cudaMemcpy2DAsync(s.x, xrow, x_raw, static_cast<size_t>(ld_x_bytes), xrow, static_cast<size_t>(n),
                                   cudaMemcpyDefault, st->copy);
         if (e == cudaSuccess) e = cudaEventRecord(s.copied, st->copy);
+        // Later work on the caller's stream (which may reuse or free the block's buffers) waits
+        // for the staging copy.
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), s.copied, 0);
         if (e != cudaSuccess) {
             cudaGetLastError();
             std::lock_guard<std::mutex> lock(st->mu);

@@ -9,7 +9,6 @@ run on the tensor's current stream.
 """
 from __future__ import annotations
 
-import collections
 import ctypes
 import os
 
@@ -473,9 +472,6 @@ class BaseStore:
                                              int(bool(write_basic_to_bucket)), raw_bytes_per_vec, self.device,
                                              max_block, ctypes.byref(out)), "stlq_b200_store_open")
         self.handle = out
-        # The last appended blocks stay referenced until their staging copies have run: an append
-        # waits for a free slot (3 on a device store), so a block four appends back has been copied.
-        self._keep = collections.deque(maxlen=4)
 
     def append(self, start_id, cluster, B_small, a, x=None, stream=None):
         """cluster (n,) uint32/int32, B_small (n, m-1) uint8, a (n, m) float32, x (n, ...) raw vectors;
@@ -495,20 +491,17 @@ class BaseStore:
             import torch
 
             stream = torch.cuda.current_stream(cluster.device).cuda_stream
-        self._keep.append((cluster, B_small, a, x))
         _check(self.lib, self.lib.stlq_b200_store_append(self.handle, int(start_id), n, ptr(cluster), ptr(B_small),
                                                          ptr(a), ptr(x), ld, ctypes.c_void_p(stream or 0)),
                "stlq_b200_store_append")
 
     def flush(self):
         _check(self.lib, self.lib.stlq_b200_store_flush(self.handle), "stlq_b200_store_flush")
-        self._keep.clear()
 
     def close(self):
         if getattr(self, "handle", None) is not None and self.handle.value:
             rc = self.lib.stlq_b200_store_close(self.handle)
             self.handle = None
-            self._keep.clear()
             _check(self.lib, rc, "stlq_b200_store_close")
         self.handle = None
 
