@@ -59,6 +59,8 @@ def parse_args():
                    help="config 3: uint8 slices streamed from pinned host memory through the large-root encoder")
     p.add_argument("--c3-slice", type=int, default=1_000_000, help="config 3: vectors per slice")
     p.add_argument("--c3-slices", type=int, default=16, help="config 3: slices in the timed call")
+    p.add_argument("--c3-file-slices", type=int, default=0,
+                   help="config 3: also run the block loop from a .bvecs file of this many slices into a base store")
     p.add_argument("--c3-check", type=int, default=1500, help="config 3: vectors per checked slice")
     p.add_argument("--gemm-only", choices=["exact", "strict", "fast"], default=None,
                    help="profiling aid: run only the xC GEMM of this mode on one 262,144-vector slice")
@@ -852,8 +854,58 @@ def run_config3(args):
                              "cost 4) on the other direction"},
         "parity": parity, "clocks": clock_info, "cpu_baseline": cpu,
     }
+    if args.c3_file_slices > 0:
+        line["file_to_store"] = run_config3_file(args, enc, Xh[:min(n, args.c3_file_slices * slice_n)], beam)
     print(json.dumps(line), flush=True)
     enc.close()
+
+
+def run_config3_file(args, enc, Xh, beam):
+    """Config 3 through the large pipeline's whole block loop: the vectors written as a .bvecs file
+    (local temporary directory; the file was just written, so it is read from the page cache), then
+    stlq_b200_encode_file_large_root reads it in 262,144-vector blocks (prefetch thread, pinned
+    slots, prefixes stripped on the device), encodes each block and appends it to a basic base store
+    (the reference's default layout: shards of 2,000,000, buckets of 256 root codes with the raw
+    vector and the codes per record).  Timed: the call plus the store's close (files written to the
+    page cache), wall clock."""
+    import shutil
+    import tempfile
+
+    import stlq_b200
+
+    n, d = Xh.shape
+    h_vec = [int(v) for v in enc.h_vec]
+    tmp = tempfile.mkdtemp(prefix="stlq_b200_c3_")
+    try:
+        path = os.path.join(tmp, "base.bvecs")
+        rec = np.empty((n, 4 + d), np.uint8)
+        rec[:, :4] = np.frombuffer(np.int32(d).tobytes(), np.uint8)
+        rec[:, 4:] = Xh.numpy()
+        rec.tofile(path)
+        del rec
+        block = 262_144
+
+        def once(store_dir):
+            rd = stlq_b200.VectorReader(path, device=0, block=block, depth=3, io_threads=8)
+            st = stlq_b200.BaseStore(store_dir, d, len(h_vec), h_vec, device=0, max_block=block)
+            t0 = time.perf_counter()
+            out = enc.encode_file_large_root(rd, st, beam, 0)
+            st.close()
+            dt = time.perf_counter() - t0
+            rd.close()
+            return out, dt
+
+        once(os.path.join(tmp, "warm"))  # warm-up (page cache, pinned slots)
+        shutil.rmtree(os.path.join(tmp, "warm"))
+        out, dt = once(os.path.join(tmp, "store"))
+        store_bytes = sum(os.path.getsize(os.path.join(tmp, "store", f)) for f in os.listdir(os.path.join(tmp, "store")))
+        return {"value": out["vectors"] / dt, "unit": "vectors/s", "vectors": out["vectors"], "seconds": dt,
+                "file_bytes": os.path.getsize(path), "store_bytes": store_bytes,
+                "mse_final": out["mse_sum_final"] / max(out["vectors"], 1),
+                "note": "file -> pinned slots -> device -> large-root encode -> base store, one call; the .bvecs "
+                        "file and the store files in the page cache of a local temporary directory"}
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
 
 
 def run_gemm_only(args):

@@ -305,6 +305,19 @@ int stlq_b200_reader_read(stlq_b200_reader* rd, uint64_t start, int64_t count, v
                           int64_t* nread);
 int stlq_b200_reader_close(stlq_b200_reader* rd);
 
+/* The large pipeline's block loop (src/quantizer/encode_base_streaming.cpp:640-1310, basic encode):
+ * every block of the reader's range is copied to the device, encoded by the large-root encoder
+ * `enc` (sample ids = global vector ids) and, when `st` is not NULL, appended to the store, the
+ * next block's copy and the store's copies overlapping the encode.  The reader must be a device
+ * reader on the encoder's device; the store a device store there with d and m of the encoder and
+ * max_block >= the reader's block.  mse_sums_out (2 doubles, may be NULL): sum over blocks of
+ * float(mean beam cost of the block) x block size, and the same for the final cost (the reference's
+ * mse_sum_beam / mse_sum_final, 1303-1304).  vectors_out: vectors encoded.  Returns when every
+ * block is encoded and handed to the store (the store's files are complete after its close). */
+int stlq_b200_encode_file_large_root(stlq_b200_encoder* enc, stlq_b200_reader* rd, stlq_b200_store* st, int beam,
+                                     int icm_iters, int ils_iters, int perturb_k, int use_abs, uint32_t seed,
+                                     double* mse_sums_out, int64_t* vectors_out);
+
 /* ---- Kernel-provider primitives ----
  * The device operations behind StreamKernelProvider (include/stlq/core/kernel_provider.h:28-221,
  * the reference's GPU backend seam; its CUDA implementation is src/core/kernel_provider_cuda_stream*

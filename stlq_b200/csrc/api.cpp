@@ -966,4 +966,12 @@ namespace stlq_b200 {
 double* EncoderSseDevice(stlq_b200_encoder* enc) { return enc ? enc->sse_d.as<double>() : nullptr; }
 cudaStream_t EncoderStream(stlq_b200_encoder* enc) { return enc ? enc->compute : nullptr; }
 
+// For the block loop (pipeline.cpp): the encoder's device, dimension, codebooks and kind.
+void EncoderShape(const stlq_b200_encoder* enc, int* device, int* d, int* m, int* large_root) {
+    *device = enc->device;
+    *d = enc->dims.d;
+    *m = enc->dims.m;
+    *large_root = enc->dims.large_root;
+}
+
 }  // namespace stlq_b200

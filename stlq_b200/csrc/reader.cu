@@ -287,6 +287,21 @@ void Destroy(stlq_b200_reader* rd) {
 
 }  // namespace
 
+namespace stlq_b200 {
+
+// For the block loop (pipeline.cpp).
+void ReaderShape(const stlq_b200_reader* rd, int* device, int* d, int* x_dtype, int64_t* block, uint64_t* begin,
+                 uint64_t* end) {
+    *device = rd->device;
+    *d = rd->d;
+    *x_dtype = rd->elem == 1 ? STLQ_B200_U8 : STLQ_B200_F32;
+    *block = rd->block;
+    *begin = rd->begin;
+    *end = rd->end;
+}
+
+}  // namespace stlq_b200
+
 extern "C" {
 
 int stlq_b200_reader_open(const char* path, int format, uint64_t begin, uint64_t end, int64_t block, int depth,

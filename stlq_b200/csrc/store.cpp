@@ -252,6 +252,19 @@ int Drain(stlq_b200_store* st) {
 
 }  // namespace
 
+namespace stlq_b200 {
+
+// For the block loop (pipeline.cpp).
+void StoreShape(const stlq_b200_store* st, int* device, int* d, int* m, int* raw_bytes, int64_t* max_block) {
+    *device = st->device;
+    *d = st->d;
+    *m = st->m;
+    *raw_bytes = st->raw_bytes;
+    *max_block = st->slots.empty() ? 0 : st->slots[0].cap;
+}
+
+}  // namespace stlq_b200
+
 extern "C" {
 
 int stlq_b200_store_open(const char* dir, int d, int m, const int* h_vec, int shard_size, int bucket_size,

@@ -237,6 +237,23 @@ class Encoder:
         _check(self.lib, rc, "stlq_b200_encode_base_large_root_device")
         return cluster, B_small, a, cost, sums
 
+    def encode_file_large_root(self, reader, store, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0,
+                               use_abs=True, seed: int = 38251450):
+        """The large pipeline's block loop (stlq_b200_encode_file_large_root): every block of a device
+        VectorReader encoded and appended to a device BaseStore (or None).  Returns dict(vectors,
+        mse_sum_beam, mse_sum_final)."""
+        lib = self.lib
+        vp = ctypes.c_void_p
+        lib.stlq_b200_encode_file_large_root.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                         ctypes.c_int, ctypes.c_int, ctypes.c_uint32, vp, vp]
+        sums = np.zeros(2, np.float64)
+        nvec = ctypes.c_int64()
+        rc = lib.stlq_b200_encode_file_large_root(self.handle, reader.handle, store.handle if store else None, beam,
+                                                  icm_iters, ils_iters, perturb_k, int(bool(use_abs)),
+                                                  seed & 0xFFFFFFFF, _np_ptr(sums), ctypes.byref(nvec))
+        _check(lib, rc, "stlq_b200_encode_file_large_root")
+        return dict(vectors=nvec.value, mse_sum_beam=float(sums[0]), mse_sum_final=float(sums[1]))
+
     # ---- whole stage, device tensors -----------------------------------------------------
     def encode_base_device(self, X, beam: int, icm_iters: int, ils_iters: int = 0, perturb_k: int = 0, use_abs=True,
                            seed: int = 38251450, sample_id_offset: int = 0, B=None, a=None, cost=None, sse=None,

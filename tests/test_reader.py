@@ -169,3 +169,71 @@ def test_device_reader_flags_bad_record(tmp_path):
         rd.next_block()
     with pytest.raises(stlq_b200.StlqB200Error, match="dimension mismatch"):
         rd.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not have_cuda(), reason="needs a GPU")
+@pytest.mark.skipif(not ref_available, reason="oracle/_ref not built")
+@pytest.mark.parametrize("fmt,icm,ils", [("bvecs", 1, 0), ("fvecs", 1, 1)])
+def test_file_to_store_block_loop(tmp_path, fmt, icm, ils):
+    """stlq_b200_encode_file_large_root: file -> device -> large-root encode -> store.  The store's
+    files equal the reference writer's for the reference's own large-root encode of the same blocks,
+    and the MSE sums follow the reference's per-block formula on the reference's costs."""
+    import stlq_b200
+
+    rng = np.random.default_rng(9)
+    d, h, n, block, beam = 24, [300, 64, 64, 64], 2500, 1024, 8
+    C = rng.standard_normal((sum(h), d)).astype(np.float32) * 30
+    path, X = make_file(tmp_path, fmt, n, d, seed=4)
+    X = X.astype(np.float32) if fmt == "bvecs" else X * 60
+    if fmt == "fvecs":
+        write_vectors(path, X, fmt)
+    raw = 0 if fmt == "bvecs" else 4 * d
+    kw = dict(shard_size=1800, bucket_size=32, bucket_flush_mb=1, raw_bytes_per_vec=raw)
+    enc = stlq_b200.Encoder(C, h, large_root=True)
+    rd = stlq_b200.VectorReader(path, device=0, block=block, depth=3)
+    st = stlq_b200.BaseStore(tmp_path / "b200", d, len(h), h, device=0, max_block=block, **kw)
+    out = enc.encode_file_large_root(rd, st, beam, icm, ils, perturb_k=2 if ils else 0)
+    st.close()
+    rd.close()
+    assert out["vectors"] == n
+    R = oracle.Reference(threads=4)
+    blocks, mse = [], [0.0, 0.0]
+    for s in range(0, n, block):
+        xb = X[s:s + block]
+        r = R.large_root_encode(h, C, xb, beam, icm, ils, perturb_k=2 if ils else 0, sample_id_offset=s)
+        blk = dict(start=s, cluster=r["cluster"], B_small=r["B_small"], a=r["a"])
+        blk["x"] = np.ascontiguousarray(xb.astype(np.uint8) if fmt == "bvecs" else xb)
+        blocks.append(blk)
+        for j, c in enumerate((r["cost_beam"], r["cost"])):
+            mse[j] += float(np.float32(c.astype(np.float64).sum() / len(c))) * len(c)
+    R.store_write(tmp_path / "ref", d, len(h), h, blocks, x_kind=1 if fmt == "bvecs" else 2, **kw)
+    assert_same_dirs(tmp_path / "b200", tmp_path / "ref")
+    np.testing.assert_allclose([out["mse_sum_beam"], out["mse_sum_final"]], mse, rtol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not have_cuda(), reason="needs a GPU")
+def test_block_loop_rejects_mismatches(tmp_path):
+    import stlq_b200
+
+    rng = np.random.default_rng(1)
+    h = [64, 16, 16]
+    path, _ = make_file(tmp_path, "bvecs", 100, 8)
+    enc = stlq_b200.Encoder(rng.standard_normal((sum(h), 16)).astype(np.float32), h, large_root=True)
+    rd = stlq_b200.VectorReader(path, device=0, block=64)
+    with pytest.raises(stlq_b200.StlqB200Error, match="dimension"):  # file d 8, encoder d 16
+        enc.encode_file_large_root(rd, None, 4, 0)
+    rd.close()
+    enc8 = stlq_b200.Encoder(rng.standard_normal((sum(h), 8)).astype(np.float32), h, large_root=True)
+    rd = stlq_b200.VectorReader(path, device=0, block=64)
+    st = stlq_b200.BaseStore(tmp_path / "s", 8, len(h), h, device=0, max_block=32)
+    with pytest.raises(stlq_b200.StlqB200Error, match="max_block"):
+        enc8.encode_file_large_root(rd, st, 4, 0)
+    st.close()
+    regular = stlq_b200.Encoder(rng.standard_normal((sum(h), 8)).astype(np.float32), h)
+    with pytest.raises(stlq_b200.StlqB200Error, match="large-root"):
+        regular.encode_file_large_root(rd, None, 4, 0)
+    out = enc8.encode_file_large_root(rd, None, 4, 0)  # without a store
+    assert out["vectors"] == 100
+    rd.close()
