@@ -9,6 +9,7 @@ import pytest
 
 import oracle
 from conftest import have_cuda
+from test_store import assert_same_dirs
 
 ref_available = os.path.exists(oracle.REF_SO)
 FMT = {"bvecs": 1, "fvecs": 2, "fbin": 3}
