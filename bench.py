@@ -899,8 +899,32 @@ def run_config3_file(args, enc, Xh, beam):
         shutil.rmtree(os.path.join(tmp, "warm"))
         out, dt = once(os.path.join(tmp, "store"))
         store_bytes = sum(os.path.getsize(os.path.join(tmp, "store", f)) for f in os.listdir(os.path.join(tmp, "store")))
+        # Each end alone: the reader feeding a device buffer, and the store fed one device block over
+        # and over (the outputs of the last encoded block).
+        import torch
+
+        rd = stlq_b200.VectorReader(path, device=0, block=block, depth=3, io_threads=8)
+        buf = torch.empty((block, d), dtype=torch.uint8, device="cuda:0")
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        while rd.next_block(out=buf) is not None:
+            pass
+        torch.cuda.synchronize()
+        t_read = time.perf_counter() - t0
+        rd.close()
+        Xd = Xh[:block].to("cuda:0")
+        cl, Bs, a, _, _ = enc.encode_base_large_root_device(Xd, beam, 0)
+        torch.cuda.synchronize()
+        st = stlq_b200.BaseStore(os.path.join(tmp, "store_only"), d, len(h_vec), h_vec, device=0, max_block=block)
+        t0 = time.perf_counter()
+        for s0 in range(0, n, block):
+            c = min(block, n - s0)
+            st.append(s0, cl[:c], Bs[:c], a[:c], Xd[:c])
+        st.close()
+        t_store = time.perf_counter() - t0
         return {"value": out["vectors"] / dt, "unit": "vectors/s", "vectors": out["vectors"], "seconds": dt,
                 "file_bytes": os.path.getsize(path), "store_bytes": store_bytes,
+                "reader_alone_vps": n / t_read, "store_alone_vps": n / t_store,
                 "mse_final": out["mse_sum_final"] / max(out["vectors"], 1),
                 "note": "file -> pinned slots -> device -> large-root encode -> base store, one call; the .bvecs "
                         "file and the store files in the page cache of a local temporary directory"}

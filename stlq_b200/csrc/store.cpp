@@ -148,6 +148,10 @@ bool WriteBlock(stlq_b200_store* st, const Slot& s, std::string* err) {
     }
     if (!st->vec_bucket && !st->basic_bucket) return true;
     const int bsize = std::max(1, st->bucket_size);
+    const size_t xb = st->vec_bucket ? static_cast<size_t>(st->raw_bytes) : 0;
+    const size_t cb = st->basic_bucket ? static_cast<size_t>(mc) : 0;
+    const size_t ab = st->basic_bucket ? sizeof(float) * st->m : 0;
+    const size_t rec = 8 + xb + cb + ab;
     for (int64_t i = 0; i < n; ++i) {
         const uint32_t gid = static_cast<uint32_t>(s.start_id + static_cast<uint64_t>(i));
         const uint32_t cid = s.cluster[i];
@@ -158,17 +162,20 @@ bool WriteBlock(stlq_b200_store* st, const Slot& s, std::string* err) {
         }
         if (!OpenBucket(st, b, err)) return false;
         auto& buf = st->bucket_buf[b];
-        auto put = [&](const void* p, size_t bytes) {
-            const auto* q = static_cast<const uint8_t*>(p);
-            buf.insert(buf.end(), q, q + bytes);
-        };
-        put(&gid, 4);
-        put(&cid, 4);
-        if (st->vec_bucket) put(s.x + static_cast<size_t>(i) * st->raw_bytes, st->raw_bytes);
-        if (st->basic_bucket) {
-            put(s.codes + static_cast<size_t>(i) * mc, mc);
-            put(s.a + static_cast<size_t>(i) * st->m, sizeof(float) * st->m);
-        }
+        // One record: id, root code, [raw vector], [small codes, coefficients].
+        if (buf.capacity() - buf.size() < rec)
+            buf.reserve(std::max(buf.size() + rec, std::max<size_t>(buf.capacity() * 3 / 2, 1u << 20)));
+        const size_t at = buf.size();
+        buf.resize(at + rec);
+        uint8_t* p = buf.data() + at;
+        std::memcpy(p, &gid, 4);
+        std::memcpy(p + 4, &cid, 4);
+        p += 8;
+        if (xb) std::memcpy(p, s.x + static_cast<size_t>(i) * xb, xb);
+        p += xb;
+        if (cb) std::memcpy(p, s.codes + static_cast<size_t>(i) * mc, cb);
+        p += cb;
+        if (ab) std::memcpy(p, s.a + static_cast<size_t>(i) * st->m, ab);
         if (buf.size() >= st->flush_bytes && !FlushBucket(st, b, err)) return false;
     }
     return true;
