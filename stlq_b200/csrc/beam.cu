@@ -81,7 +81,6 @@ struct LayerTable {
     int n_surv;
     uint32_t key_b;       // fast kernel: error keys ranked B-1 and B (boundary tie test)
     uint32_t key_n;
-    int wsum[kWarps];     // survivors found by each warp
     uint32_t mins[kWarps * kMaxBeam];  // each warp's B smallest per-thread upper bounds, sorted
 };
 
@@ -270,6 +269,11 @@ struct Layer0Source {
     __device__ const float* v0() const { return nullptr; }  // no array: never read four at a time
 };
 
+// A thread's two smallest upper bounds as selection keys: the smallest in the low word.
+__device__ __forceinline__ uint64_t BoundKeys(float h1, float h2) {
+    return (static_cast<uint64_t>(OrderKey(h2)) << 32) | OrderKey(h1);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Cheap pass shared by both kernels.
 
@@ -294,16 +298,17 @@ __device__ __forceinline__ void CheckBounds(const SlotView<MAXM> cur, int h, int
 }
 
 // The cheap pass of layer L over every live slot: lower bounds into lo[h * K + k] (with kHi also
-// the upper bounds into hi_out), and the thread's smallest upper bound as the return value.  One copy per layer, inlined (with L a
-// compile-time constant the loop is fully unrolled; each copy is a few KB, and out of line the
-// call boundary costs more than the copies save).
-template <int MAXM, int L, bool kHi, bool kWide, bool kStrict>
-__device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH, int K, int offL, int colL,
+// the upper bounds into hi_out), and the thread's smallest upper bound as the return value.  One
+// inlined copy serves every layer (L at run time): per-layer copies, fully unrolled, ran 11%
+// slower at M = 8 because together they overflow the instruction cache; out of line, the call
+// boundary's register saves cost more still.
+template <int MAXM, bool kHi, bool kWide, bool kStrict>
+__device__ __forceinline__ uint64_t CheapPass(const SlotView<MAXM> cur, int L, int curH, int K, int offL, int colL,
                                            const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                                            const float* __restrict__ xc, float* lo, float* hi_out, int check,
                                            unsigned int* err_flag, bool recip, const ExactCtx& ctx) {
     const int tid = threadIdx.x;
-    float hmin = PosInf();  // never NaN: a bound is finite or +-inf
+    float hmin = PosInf(), hmin2 = PosInf();  // never NaN: a bound is finite or +-inf
     // Codebooks above 256 codewords (the kWide kernels) are walked in chunks of kMaxK, kCpt
     // codewords per thread; the other kernels make one pass with kc = 0 known at compile time.
     for (int kc = 0; kc < (kWide ? K : 1); kc += kMaxK) {
@@ -324,12 +329,13 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
         for (int c = 0; c < kCpt; ++c) gq[c] = Grow + col[c];
         for (int h = 0; h < curH; ++h) {
             float l[kCpt], hi[kCpt];
-            CheapBounds<MAXM, L, kStrict>(cur, h, gq, ok, alpha, gamma, dg, l, hi);
+            CheapBounds<MAXM, kStrict>(cur, h, L, gq, ok, alpha, gamma, dg, l, hi);
 #pragma unroll
             for (int c = 0; c < kCpt; ++c) {
                 if (ok[c]) {
                     lo[h * K + kc + tid + c * kThreads] = l[c];
                     if (kHi) hi_out[h * K + kc + tid + c * kThreads] = hi[c];
+                    hmin2 = fminf(hmin2, fmaxf(hmin, hi[c]));
                     hmin = fminf(hmin, hi[c]);
                 }
             }
@@ -338,7 +344,7 @@ __device__ __forceinline__ uint32_t CheapPass(const SlotView<MAXM> cur, int curH
                                            offL - colL);
         }
     }
-    return OrderKey(hmin);
+    return BoundKeys(hmin, hmin2);
 }
 
 // CheapPass with each thread's two codewords adjacent (k = kc + 2 t, k + 1): aligned 8-byte
@@ -350,13 +356,13 @@ template <int MAXM>
 constexpr bool kPairPath = MAXM > 8;
 static_assert(kCpt == 2, "the paired cheap pass takes two codewords per thread");
 template <int MAXM, int L, bool kHi, bool kWide, bool kStrict>
-__device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
+__device__ __forceinline__ uint64_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
                                                int offL, int colL, const float* __restrict__ Grow,
                                                const float* __restrict__ Gdiag, const float* __restrict__ xc,
                                                float* lo, float* hi_out, int check, unsigned int* err_flag,
                                                bool recip, const ExactCtx& ctx) {
     const int tid = threadIdx.x;
-    float hmin = PosInf();
+    float hmin = PosInf(), hmin2 = PosInf();
     for (int kc = 0; kc < (kWide ? K : 1); kc += 2 * kThreads) {
         const int k = kc + 2 * tid;
         const bool ok = k < K;  // K is even: k + 1 < K as well
@@ -372,7 +378,10 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
             if (ok) {
                 *reinterpret_cast<float2*>(lo + h * K + k) = l;
                 if (kHi) *reinterpret_cast<float2*>(hi_out + h * K + k) = hi;
-                hmin = fminf(hmin, fminf(hi.x, hi.y));
+                hmin2 = fminf(hmin2, fmaxf(hmin, hi.x));
+                hmin = fminf(hmin, hi.x);
+                hmin2 = fminf(hmin2, fmaxf(hmin, hi.y));
+                hmin = fminf(hmin, hi.y);
             }
             if (check) {
                 const int col[kCpt] = {colL + k, colL + k + 1};
@@ -384,33 +393,33 @@ __device__ __forceinline__ uint32_t CheapPassPair(const SlotView<MAXM> cur, cons
             }
         }
     }
-    return OrderKey(hmin);
+    return BoundKeys(hmin, hmin2);
 }
 
 // `table` non-null: the paired pass (Dims::pair) over the slots' pair tables.
 template <int MAXM, bool kHi, bool kWide, bool kStrict>
-__device__ uint32_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
+__device__ uint64_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
                                   int check, unsigned int* err, bool recip, const float2* table, const ExactCtx& ctx) {
+    if constexpr (kPairPath<MAXM>) {
+        if (table) {
 #define STLQ_B200_CHEAP(LL)                                                                          \
     case LL:                                                                                         \
-        if constexpr (LL < MAXM) {                                                                   \
-            if constexpr (kPairPath<MAXM>)                                                           \
-                if (table)                                                                           \
-                    return CheapPassPair<MAXM, LL, kHi, kWide, kStrict>(cur, table, curH, K, offL, colL, Grow, Gdiag, \
-                                                                        xc, lo, hi_out, check, err, recip, ctx); \
-            return CheapPass<MAXM, LL, kHi, kWide, kStrict>(cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, \
-                                                            check, err, recip, ctx);                 \
-        }                                                                                            \
+        if constexpr (LL < MAXM)                                                                     \
+            return CheapPassPair<MAXM, LL, kHi, kWide, kStrict>(cur, table, curH, K, offL, colL, Grow, Gdiag, xc, lo, \
+                                                                hi_out, check, err, recip, ctx);     \
         break;
-    switch (L) {
-        STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
-        STLQ_B200_CHEAP(6) STLQ_B200_CHEAP(7) STLQ_B200_CHEAP(8) STLQ_B200_CHEAP(9) STLQ_B200_CHEAP(10)
-        STLQ_B200_CHEAP(11) STLQ_B200_CHEAP(12) STLQ_B200_CHEAP(13) STLQ_B200_CHEAP(14) STLQ_B200_CHEAP(15)
-        default: break;
-    }
+            switch (L) {
+                STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
+                STLQ_B200_CHEAP(6) STLQ_B200_CHEAP(7) STLQ_B200_CHEAP(8) STLQ_B200_CHEAP(9) STLQ_B200_CHEAP(10)
+                STLQ_B200_CHEAP(11) STLQ_B200_CHEAP(12) STLQ_B200_CHEAP(13) STLQ_B200_CHEAP(14) STLQ_B200_CHEAP(15)
+                default: break;
+            }
 #undef STLQ_B200_CHEAP
-    return 0u;  // unreachable: 1 <= L < m <= MAXM
+        }
+    }
+    return CheapPass<MAXM, kHi, kWide, kStrict>(cur, L, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err,
+                                                recip, ctx);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -782,20 +791,31 @@ __device__ __forceinline__ uint32_t WarpSortAsc(uint32_t v) {
 
 // Selection shared by every layer of the fast kernel, out of line so that one copy serves every
 // layer.  Inputs: src(idx) (a lower bound of each candidate's exact error; the exact error itself
-// in layer 0) and this thread's smallest upper bound `hmin`.  The 128 per-thread
-// minima belong to distinct candidates, so their B-th smallest, tau, bounds the B-th smallest
+// in layer 0) and `hmin`, this thread's two smallest upper bounds as order keys (BoundKeys).  The
+// 256 values belong to distinct candidates, so their B-th smallest, tau, bounds the B-th smallest
 // exact error from above; every candidate with lo <= tau is a survivor (all others are provably
-// larger than the B-th smallest exact error).  Returns the survivor count, or -1 when the list
-// overflows.
+// larger than the B-th smallest exact error).  Two values per thread rather than one cut the
+// survivors per layer from 44 to 27 at the benchmark shape.  Returns the survivor count, or -1
+// when the list overflows.
 template <class Src>
-__device__ __noinline__ int SelectSurvivors(Src src, int n_cand, uint32_t hmin, int beam, LayerTable& lt,
+__device__ __noinline__ int SelectSurvivors(Src src, int n_cand, uint64_t hmin, int beam, LayerTable& lt,
                                             uint16_t* surv) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Each warp sorts its 32 minima; only a warp's B smallest can be among the B smallest of all
     // 128, so ranking those 4B values (binary search into the other sorted lists) finds tau.  Every
     // warp does it, so tau needs no second barrier.
-    const uint32_t sorted = WarpSortAsc(hmin);
+    // Each thread gives its two smallest upper bounds (distinct candidates): the warp's 32 smallest
+    // of its 64 are min(a[i], b[31 - i]) of the two sorted lists, a bitonic sequence, then sorted.
+    const uint32_t sa = WarpSortAsc(static_cast<uint32_t>(hmin));
+    const uint32_t sb = __shfl_sync(kFull, WarpSortAsc(static_cast<uint32_t>(hmin >> 32)), 31 - lane);
+    uint32_t sorted = min(sa, sb);
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const uint32_t o = __shfl_xor_sync(kFull, sorted, j);
+        sorted = (lane & j) ? max(sorted, o) : min(sorted, o);
+    }
     if (lane < beam) lt.mins[warp * kMaxBeam + lane] = sorted;
+    if (tid == 0) lt.n_surv = 0;
     __syncthreads();
     // Rank of value v (list w, position j) among all 4B values: j plus, in each other list, the
     // number of entries ordered before it (ties broken by list index).  The searches over the
@@ -825,45 +845,55 @@ __device__ __noinline__ int SelectSurvivors(Src src, int n_cand, uint32_t hmin, 
     }
     tb = __reduce_min_sync(kFull, tb);
     const float tau = tb >= OrderKey(PosInf()) ? PosInf() : KeyToFloat(tb);  // < B finite bounds: keep all
-    // Count this thread's survivors (four candidates per 128-bit load), scan the counts across the
-    // block, then write the survivors at their offsets.
+    // One pass: each thread marks its survivors among up to 32 candidates per round (eight 128-bit
+    // loads), the warp scans the counts and reserves its range of the list with one atomic, and
+    // the marked candidates are written there.  The list's order does not matter: survivors are
+    // ranked by (exact error, scan index), which is unique.
     const float4* lo4 = reinterpret_cast<const float4*>(src.v0());
     const int n4 = Src::kVec ? n_cand >> 2 : 0;
-    int cnt = 0;
-    for (int c = tid; c < n4; c += kThreads) {
-        const float4 v = lo4[c];
-        cnt += (v.x <= tau) + (v.y <= tau) + (v.z <= tau) + (v.w <= tau);
-    }
-    for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads) cnt += src(idx) <= tau;
-    int incl = cnt;
+    const auto emit = [&](uint32_t mask, auto idx_of) {
+        const int cnt = __popc(mask);
+        int incl = cnt;
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        const int o = __shfl_up_sync(kFull, incl, d);
-        if (lane >= d) incl += o;
-    }
-    if (lane == 31) lt.wsum[warp] = incl;
-    __syncthreads();
-    int base = 0, S = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-        const int ws = lt.wsum[w];
-        base += w < warp ? ws : 0;
-        S += ws;
-    }
-    if (S <= kSurvCap && cnt > 0) {
-        int p = base + incl - cnt;
-        for (int c = tid; c < n4; c += kThreads) {
-            const float4 v = lo4[c];
-            if (v.x <= tau) surv[p++] = static_cast<uint16_t>(4 * c);
-            if (v.y <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 1);
-            if (v.z <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 2);
-            if (v.w <= tau) surv[p++] = static_cast<uint16_t>(4 * c + 3);
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(kFull, incl, d);
+            if (lane >= d) incl += o;
         }
-        for (int idx = 4 * n4 + tid; idx < n_cand; idx += kThreads)
-            if (src(idx) <= tau) surv[p++] = static_cast<uint16_t>(idx);
+        int base = 0;
+        if (lane == 31 && incl > 0) base = atomicAdd(&lt.n_surv, incl);
+        base = __shfl_sync(kFull, base, 31);
+        int p = base + incl - cnt;
+        if (p + cnt <= kSurvCap) {
+            while (mask) {
+                const int b = __ffs(mask) - 1;
+                mask &= mask - 1;
+                surv[p++] = static_cast<uint16_t>(idx_of(b));
+            }
+        }
+    };
+    // Rounds are warp-uniform: every lane takes part in each round's scan.
+    for (int c0 = warp * 32; c0 < n4; c0 += 8 * kThreads) {
+        uint32_t mask = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = c0 + j * kThreads + lane;
+            if (c < n4) {
+                const float4 v = lo4[c];
+                mask |= ((v.x <= tau) | ((v.y <= tau) << 1) | ((v.z <= tau) << 2) | ((v.w <= tau) << 3)) << (4 * j);
+            }
+        }
+        emit(mask, [&](int b) { return 4 * (c0 + (b >> 2) * kThreads + lane) + (b & 3); });
+    }
+    for (int i0 = 4 * n4 + warp * 32; i0 < n_cand; i0 += 32 * kThreads) {
+        uint32_t mask = 0;
+        for (int j = 0; j < 32; ++j) {
+            const int idx = i0 + j * kThreads + lane;
+            if (idx < n_cand && src(idx) <= tau) mask |= 1u << j;
+        }
+        emit(mask, [&](int b) { return i0 + b * kThreads + lane; });
     }
     __syncthreads();
-    if (tid == 0) lt.n_surv = S;
+    const int S = lt.n_surv;
     return S > kSurvCap ? -1 : S;
 }
 
@@ -922,7 +952,7 @@ __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, con
             __syncthreads();
         }
     }
-    const uint32_t hmin = CheapDispatch<MAXM, false, kWide, kStrict>(
+    const uint64_t hmin = CheapDispatch<MAXM, false, kWide, kStrict>(
         L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag, dims.large_root != 0, table, ctx);
     const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
@@ -983,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         // Layer 0 errors are kept in lo[] when they fit (beam x maxKs floats), else recomputed
         // where the selection reads them.
         const bool stored0 = !kWide || K0 <= beam * dims.maxKs;
-        uint32_t hmin = 0xffffffffu;
+        uint32_t hmin = 0xffffffffu, hmin2 = 0xffffffffu;  // the thread's two smallest bound keys
         ExactCtx ctx{};
         int curH;
         if constexpr (kStrict) {
@@ -994,17 +1024,19 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
                 float l, h;
                 Layer0Bounds(Gdiag, xc, ctx, nx2, k, l, h);
                 if (stored0) lo[k] = l;
+                hmin2 = min(hmin2, max(hmin, OrderKey(h)));
                 hmin = min(hmin, OrderKey(h));
                 if (check) {
                     const float e = Layer0ErrorG(Gdiag, ctx.Gamma(k), nx2, k);
                     if (e < PosInf() && !(e >= l && e <= h)) atomicOr(err_flag, kErrFilterMiss);
                 }
             }
+            const uint64_t keys0 = (static_cast<uint64_t>(hmin2) << 32) | hmin;
             if constexpr (kWide)
-                curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
-                               : SelectSurvivors(Layer0LoSource{Gdiag, xc, ctx, nx2}, K0, hmin, beam, lt, surv);
+                curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, keys0, beam, lt, surv)
+                               : SelectSurvivors(Layer0LoSource{Gdiag, xc, ctx, nx2}, K0, keys0, beam, lt, surv);
             else
-                curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
+                curH = SelectSurvivors(ArraySource{lo}, K0, keys0, beam, lt, surv);
             if (curH >= 0) {
                 SurvivorGammas(ctx, curH, [&](int p) { return static_cast<int>(surv[p]); }, gex);
                 for (int p = tid; p < curH; p += kThreads) ex[p] = Layer0ErrorG(Gdiag, gex[p], nx2, surv[p]);
@@ -1016,13 +1048,15 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
             for (int k = tid; k < K0; k += kThreads) {
                 const float e1 = Layer0Error(Gdiag, xc, nx2, k);
                 if (stored0) lo[k] = e1;
+                hmin2 = min(hmin2, max(hmin, OrderKey(e1)));
                 hmin = min(hmin, OrderKey(e1));
             }
+            const uint64_t keys0 = (static_cast<uint64_t>(hmin2) << 32) | hmin;
             if constexpr (kWide)
-                curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv)
-                               : SelectSurvivors(Layer0Source{Gdiag, xc, nx2}, K0, hmin, beam, lt, surv);
+                curH = stored0 ? SelectSurvivors(ArraySource{lo}, K0, keys0, beam, lt, surv)
+                               : SelectSurvivors(Layer0Source{Gdiag, xc, nx2}, K0, keys0, beam, lt, surv);
             else
-                curH = SelectSurvivors(ArraySource{lo}, K0, hmin, beam, lt, surv);
+                curH = SelectSurvivors(ArraySource{lo}, K0, keys0, beam, lt, surv);
             if (curH >= 0) {
                 for (int p = tid; p < curH; p += kThreads)
                     ex[p] = stored0 ? lo[surv[p]] : Layer0Error(Gdiag, xc, nx2, surv[p]);

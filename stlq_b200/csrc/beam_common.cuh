@@ -179,13 +179,13 @@ __device__ __forceinline__ float EvalExactL(const SlotView<MAXM>& cur, int h, in
 // forced (its cheap denominator is -0 - 0) and which the reference always skips.
 // kStrict: gamma is a tensor-core value within dg of the exact one, so the exact diff lies within
 // dg of this one and e' = E_old - diff^2/denom moves by at most (2|diff| + dg) dg / denom.
-template <int L, bool kStrict>
-__device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta, float eta, float seta, float Eo,
+template <bool kStrict>
+__device__ __forceinline__ void BoundsTail(int L, float alpha, float gamma, float delta, float eta, float seta, float Eo,
                                            bool ill, float dg, float& lo, float& hi) {
     const float lof = IsZeroColumn(alpha) ? PosInf() : -PosInf();  // derived here: one register less per codeword
     // Half-width w = 16 * de with de as documented at CheapBounds; the factor 16 is folded into the
     // constants.
-    constexpr float u16 = 16.0f * 1.2e-7f * (L + 2);
+    const float u16 = 16.0f * 1.2e-7f * static_cast<float>(L + 2);
     constexpr float e16 = 16.0f * 1.2e-7f;
     const float denom = alpha - delta;
     const float diff = gamma - eta;
@@ -201,8 +201,7 @@ __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta
 
 // Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
 // kCpt codewords (Gram column pointers gq[q] = Grow + col[q]; the values of a codeword with !ok[q]
-// are meaningless and unused).  L is a compile-time constant here: this is the hot
-// loop, and each layer's copy is small (see CheapPass in beam.cu).
+// are meaningless and unused).  This is the hot loop (see CheapPass in beam.cu).
 // e' = E_old - diff^2/denom with y from FMA forward substitution, delta = |y|^2, eta = A.a.  The
 // half-width covers the rounding of both this and the exact sequence: relative errors of order
 // L ulp in diff (scale |gamma| + sum|A_t a_t|) and in denom (scale alpha + delta), propagated
@@ -210,8 +209,10 @@ __device__ __forceinline__ void BoundsTail(float alpha, float gamma, float delta
 // whose cheap value is unreliable (ill-conditioned slot, denom <= kDenomGuard * alpha, NaN)
 // gets [-inf, +inf].  A codeword whose whole Gram column is zero (alpha is -0.0f in the beam's
 // diagonal, see IsZeroColumn) gets [+inf, +inf]: the reference always skips it.
-template <int MAXM, int L, bool kStrict>
-__device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, const float* const (&gq)[kCpt],
+// The layer L is a run-time value (loops run to NL = MAXM - 1 with uniform guards): one copy of
+// this code serves every layer, which keeps the kernel's hot code within the instruction cache.
+template <int MAXM, bool kStrict>
+__device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, int L, const float* const (&gq)[kCpt],
                                             const bool (&ok)[kCpt],
                                             const float (&alpha)[kCpt], const float (&gamma)[kCpt],
                                             const float (&dg)[kCpt], float (&lo)[kCpt], float (&hi)[kCpt]) {
@@ -221,9 +222,11 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     const int* rw = cur.rowh(h);
     // Slot values are warp-uniform shared-memory broadcasts, loaded where they are used (loading
     // them ahead into registers costs more in spills than it saves in load instructions).
-    float A[kCpt][L], y[kCpt][L];
+    constexpr int NL = MAXM - 1;
+    float A[kCpt][NL], y[kCpt][NL];
 #pragma unroll
-    for (int i = 0; i < L; ++i) {
+    for (int i = 0; i < NL; ++i) {
+        if (i >= L) break;
         const int r = rw[i];
 #pragma unroll
         for (int q = 0; q < kCpt; ++q) A[q][i] = ok[q] ? __ldg(gq[q] + r) : 0.0f;
@@ -236,7 +239,8 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
         seta[q] = fabsf(gamma[q]);
     }
 #pragma unroll
-    for (int i = 0; i < L; ++i) {
+    for (int i = 0; i < NL; ++i) {
+        if (i >= L) break;
         const float ri = rinv[i], ai = ah[i];
 #pragma unroll
         for (int q = 0; q < kCpt; ++q) {
@@ -253,7 +257,7 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, co
     const bool ill = cur.ill[h] != 0;
 #pragma unroll
     for (int q = 0; q < kCpt; ++q)
-        BoundsTail<L, kStrict>(alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, dg[q], lo[q], hi[q]);
+        BoundsTail<kStrict>(L, alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, dg[q], lo[q], hi[q]);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -309,8 +313,8 @@ __device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, 
         seta0 = fmaf(fabsf(A[i].x), fabsf(ai.x), seta0);
         seta1 = fmaf(fabsf(A[i].y), fabsf(ai.x), seta1);
     }
-    BoundsTail<L, kStrict>(alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, dg.x, lo.x, hi.x);
-    BoundsTail<L, kStrict>(alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, dg.y, lo.y, hi.y);
+    BoundsTail<kStrict>(L, alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, dg.x, lo.x, hi.x);
+    BoundsTail<kStrict>(L, alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, dg.y, lo.y, hi.y);
 }
 
 }  // namespace beam
