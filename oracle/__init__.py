@@ -78,6 +78,7 @@ def build(reference: bool = True) -> None:
         targets.append("ref")
         if os.path.exists(os.path.join(os.path.dirname(HERE), "stlq_b200", "libstlq_b200.so")):
             targets.append("adapter")
+            targets.append("dropin")  # the reference's whole pipeline with the drop-in bound
         if shutil.which("nvcc") or os.path.exists("/usr/local/cuda/bin/nvcc"):
             targets.append("refcuda")  # the reference's own CUDA ICM, for timing against ours
     subprocess.run(["make", "-s", "-C", HERE, "-j8", *targets], check=True, env=env)
@@ -619,3 +620,71 @@ class AdapterHarness:
 
     def release(self):
         self.lib.adapter_release()
+
+
+DROPIN_SO = os.path.join(HERE, "_ref", "libstlq_dropin.so")
+RUN_FULL_PIPELINE, RUN_TRAIN_ONLY, RUN_BUILD_BASE_ONLY = 1, 2, 3  # stlq::StlqRunMode
+
+
+def write_fvecs(path, X):
+    """.fvecs: per vector int32 d, then d float32."""
+    X = np.ascontiguousarray(X, np.float32)
+    n, d = X.shape
+    rec = np.empty((n, d + 1), np.float32)
+    rec[:, 0] = np.frombuffer(np.int32(d).tobytes(), np.float32)[0]
+    rec[:, 1:] = X
+    rec.tofile(path)
+
+
+def write_ivecs(path, I):
+    """.ivecs: per row int32 k, then k int32."""
+    I = np.ascontiguousarray(I, np.int32)
+    n, k = I.shape
+    rec = np.empty((n, k + 1), np.int32)
+    rec[:, 0] = k
+    rec[:, 1:] = I
+    rec.tofile(path)
+
+
+def read_books(path):
+    """The codebooks dropin_driver.cpp dumps (STLQ_B200_DROPIN_BOOKS): (C_all (H, d), h_vec)."""
+    raw = open(path, "rb").read()
+    m, d = np.frombuffer(raw, np.int32, 2)
+    h = np.frombuffer(raw, np.int32, int(m), 8).astype(int).tolist()
+    books = np.frombuffer(raw, np.float32, offset=8 + 4 * int(m))
+    C, off = [], 0
+    for hl in h:
+        C.append(books[off:off + d * hl].reshape(hl, d))  # column-major d x h: row c = codeword c
+        off += d * hl
+    return np.ascontiguousarray(np.concatenate(C), np.float32), h
+
+
+class Dropin:
+    """The reference's whole pipeline (RunStlq, compiled from its sources) with stlq::EncodeBase
+    bound to the B200 drop-in by the linker (oracle/dropin_driver.cpp)."""
+
+    def __init__(self, path: str = DROPIN_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: build it with `make -C oracle REF=<dir> dropin`")
+        self.lib = ctypes.CDLL(path)
+        self.lib.dropin_run_mode.argtypes = [ctypes.c_char_p, ctypes.c_int]
+        self.lib.dropin_run_mode.restype = ctypes.c_int
+
+    def run(self, cfg_path, mode=RUN_FULL_PIPELINE, dropin=None, report=None, books=None):
+        """RunStlq(request) on a configuration file; dropin: None (the reference's EncodeBase),
+        "b200" or "both" (see dropin_driver.cpp).  Returns RunStlq's exit code."""
+        env = {"STLQ_B200_DROPIN": dropin, "STLQ_B200_DROPIN_REPORT": report, "STLQ_B200_DROPIN_BOOKS": books}
+        old = {k: os.environ.get(k) for k in env}
+        try:
+            for k, v in env.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = str(v)
+            return self.lib.dropin_run_mode(str(cfg_path).encode(), int(mode))
+        finally:
+            for k, v in old.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
