@@ -48,6 +48,8 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-fp32-peak", action="store_true", help="skip the SGEMM FP32 peak measurement")
     p.add_argument("--no-strict", action="store_true", help="skip the STRICT (tensor-core GEMM) mode leg")
+    p.add_argument("--books", choices=["auto", "reference", "kmeans"], default="auto",
+                   help="codebooks: frozen from the reference's trainer (auto at D=128, M=8, K=256) or k-means")
     p.add_argument("--gemm-mode", choices=["exact", "strict"], default="exact",
                    help="xC GEMM of the timed encode: exact (SIMT, the reference BLAS's order) or strict (tcgen05 "
                         "3xTF32 with the exact entries recomputed where they decide anything); both bit-identical")
@@ -121,11 +123,35 @@ def base_vectors(args, n, seed, start=0):
     return gen(n, d=args.d, seed=seed + 7919 * (start // max(n, 1)))
 
 
+REF_BOOKS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden",
+                         "ref_books_sift_d128_m8_k256.npz")
+
+
+def books_source(args):
+    """"reference": the codebooks the reference's own trainer produced and that were frozen in
+    tests/golden (gen_ref_books.py: SIFT-like training vectors, D=128, M=8, K=256, no OPQ), used at
+    that shape; "kmeans": a seeded residual k-means on a 50,000-vector subsample (seed 0), the
+    stand-in at every other shape."""
+    if args.books != "auto":
+        return args.books
+    fits = args.data == "sift" and (args.d, args.m, args.k) == (128, 8, 256)
+    return "reference" if fits and os.path.exists(REF_BOOKS) else "kmeans"
+
+
+def books_label(args):
+    return ("frozen from the reference's trainer (RunStlq on seeded SIFT-like vectors)"
+            if books_source(args) == "reference" else "seeded residual k-means")
+
+
 def make_codebooks(args, device):
-    """Seeded residual k-means on a 50,000-vector subsample (seed 0): the stand-in for codebooks
-    frozen from the reference's trainer."""
     from stlq_b200 import synth
 
+    if books_source(args) == "reference":
+        with np.load(REF_BOOKS) as z:
+            C = np.ascontiguousarray(z["C_all"], np.float32)
+        if C.shape != (args.m * args.k, args.d):
+            raise SystemExit(f"{REF_BOOKS} holds {C.shape}, not ({args.m * args.k}, {args.d})")
+        return C
     train = base_vectors(args, 50_000, 0)
     books = synth.train_rvq(train, args.m, args.k, iters=8, seed=0, device=device)
     return synth.flatten_books(books)
@@ -266,7 +292,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "encoded vectors/sec", "value": value, "unit": "vectors/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic (seeded {args.data.upper()}-like D={args.d}; codebooks: {books_label(args)})",
         "config": {"workload": f"{args.n} x D={args.d} f32 ({args.data.upper()}-like, seed 4), M={args.m}, K={args.k}, "
                                f"beam={args.beam}, ICM={args.icm}, ILS=0; reference CPU encoder on a "
                                f"{per_step}-vector sample per step",
@@ -558,7 +585,7 @@ def run_ours(args):
             "metric": "encoded vectors/sec", "value": value, "unit": "vectors/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": f"synthetic (seeded {args.data.upper()}-like D={args.d}; codebooks: seeded residual k-means)",
+            "data": f"synthetic (seeded {args.data.upper()}-like D={args.d}; codebooks: {books_label(args)})",
             "config": {"workload": f"{n} x D={args.d} f32 per GPU, M={args.m}, K={args.k}, beam={args.beam}, "
                                    f"ICM={args.icm}, ILS=0, use_abs, seed 38251450",
                        "vectors_per_gpu": n, "gemm_mode": args.gemm_mode,

@@ -18,7 +18,8 @@ def pytest_configure(config):
 def golden_names():
     """Fixtures of the regular encode stage (EncodeBase)."""
     names = (os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN, "*.npz")))
-    return sorted(n for n in names if not n.startswith("lr_"))
+    # lr_*: large-root cases; ref_books_*: frozen codebooks (inputs, not cases).
+    return sorted(n for n in names if not n.startswith(("lr_", "ref_books_")))
 
 
 def large_root_names():

@@ -19,8 +19,9 @@ BuildPrecompLargeRoot, BeamSearchPrefixLSLargeRoot, SolveLeastSquaresAllLargeRoo
 ComputeCostsLargeRoot, DynamicIcmWithIls*LargeRoot) and store ``cluster``, ``B_small``, ``a``,
 ``cost_beam`` and ``cost``.
 
-The codebooks are a seeded residual k-means stand-in for the reference's trainer (which is outside
-the encode path); the base vectors come from the seeded generators in stlq_b200/synth.py.
+The codebooks are a seeded residual k-means stand-in for the reference's trainer, except in
+``refbooks_*``, whose codebooks the reference's own trainer produced (gen_ref_books.py); the base
+vectors come from the seeded generators in stlq_b200/synth.py.
 """
 from __future__ import annotations
 
@@ -173,6 +174,18 @@ def config_cases():
               icm=0, store_xc=False)
 
 
+def ref_books_cases():
+    # Codebooks frozen from the reference's own trainer (gen_ref_books.py: RunStlq on seeded
+    # SIFT-like vectors, m = 8, K = 256, no OPQ) at the headline encode settings, on base vectors the
+    # trainer did not see.
+    with np.load(os.path.join(HERE, "ref_books_sift_d128_m8_k256.npz")) as z:
+        C, h = z["C_all"], [int(v) for v in z["h_vec"]]
+    offs = np.concatenate([[0], np.cumsum(h)])
+    books = [C[offs[i]:offs[i + 1]] for i in range(len(h))]
+    X = synth.sift_like(500, d=128, seed=44)
+    make_case("refbooks_d128_m8_k256_b16", X[:400], books, beam=16, icm=1, store_xc=False)
+
+
 def main():
     # The reference's own test setup (tests/test_streaming_encode_base.cpp:67-134): m=3, K=16,
     # d=16, beam 2, ICM 2, ILS 3, perturb 2, seed 1234 -- at n=600.
@@ -226,9 +239,13 @@ if __name__ == "__main__":
     if "--config-only" in sys.argv:
         config_cases()
         sys.exit(0)
+    if "--ref-books-only" in sys.argv:
+        ref_books_cases()
+        sys.exit(0)
     if "--large-root-only" not in sys.argv:
         main()
     large_root_cases()
     big_root_cases()
     zero_codeword_cases()
     config_cases()
+    ref_books_cases()
