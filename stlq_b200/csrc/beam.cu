@@ -349,11 +349,11 @@ __device__ __forceinline__ uint64_t CheapPass(const SlotView<MAXM> cur, int L, i
 
 // CheapPass with each thread's two codewords adjacent (k = kc + 2 t, k + 1): aligned 8-byte
 // gathers and packed FP32x2 arithmetic (CheapBoundsPair); `table` holds the slots' pair tables.
-// Only the 16-layer kernel has it: there the L^2 substitution dominates and the pass is 7%
-// faster; the 8-layer kernel is bound by dependency latency and the table's extra barrier per
-// layer, and measured 2% slower with it.
+// Compiled into no kernel: with the scalar pass as one run-time-layer copy, the 16-layer kernel
+// runs 9% faster without it (no table in shared memory, no spills at 2 CTAs per SM; 107 against
+// 118 ms per 65,536 D=960 vectors), and the 8-layer kernel was already faster without it.
 template <int MAXM>
-constexpr bool kPairPath = MAXM > 8;
+constexpr bool kPairPath = false;
 static_assert(kCpt == 2, "the paired cheap pass takes two codewords per thread");
 template <int MAXM, int L, bool kHi, bool kWide, bool kStrict>
 __device__ __forceinline__ uint64_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
