@@ -421,8 +421,6 @@ int CreateImpl(int device, int d, int m, const int* h_vec, const float* C_all, c
     dims.maxKs = maxKs;
     dims.large_root = large_root ? 1 : 0;
     dims.wide = maxK > STLQ_B200_MAX_K;  // large root: only the root can exceed 256
-    dims.pair = 1;
-    for (int l = 0; l < m; ++l) dims.pair &= (h_vec[l] % 2 == 0) ? 1 : 0;
     dims.c0 = large_root ? h_vec[0] : 0;
     dims.ldg = H - dims.c0;
     const int Hs = dims.ldg;

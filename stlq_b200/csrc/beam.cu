@@ -347,77 +347,10 @@ __device__ __forceinline__ uint64_t CheapPass(const SlotView<MAXM> cur, int L, i
     return BoundKeys(hmin, hmin2);
 }
 
-// CheapPass with each thread's two codewords adjacent (k = kc + 2 t, k + 1): aligned 8-byte
-// gathers and packed FP32x2 arithmetic (CheapBoundsPair); `table` holds the slots' pair tables.
-// Compiled into no kernel: with the scalar pass as one run-time-layer copy, the 16-layer kernel
-// runs 9% faster without it (no table in shared memory, no spills at 2 CTAs per SM; 107 against
-// 118 ms per 65,536 D=960 vectors), and the 8-layer kernel was already faster without it.
-template <int MAXM>
-constexpr bool kPairPath = false;
-static_assert(kCpt == 2, "the paired cheap pass takes two codewords per thread");
-template <int MAXM, int L, bool kHi, bool kWide, bool kStrict>
-__device__ __forceinline__ uint64_t CheapPassPair(const SlotView<MAXM> cur, const float2* table, int curH, int K,
-                                               int offL, int colL, const float* __restrict__ Grow,
-                                               const float* __restrict__ Gdiag, const float* __restrict__ xc,
-                                               float* lo, float* hi_out, int check, unsigned int* err_flag,
-                                               bool recip, const ExactCtx& ctx) {
-    const int tid = threadIdx.x;
-    float hmin = PosInf(), hmin2 = PosInf();
-    for (int kc = 0; kc < (kWide ? K : 1); kc += 2 * kThreads) {
-        const int k = kc + 2 * tid;
-        const bool ok = k < K;  // K is even: k + 1 < K as well
-        const float2 alpha = ok ? __ldg(reinterpret_cast<const float2*>(Gdiag + offL + k)) : make_float2(0.0f, 0.0f);
-        const float2 gamma = ok ? __ldg(reinterpret_cast<const float2*>(xc + offL + k)) : make_float2(0.0f, 0.0f);
-        const float2 dg = (kStrict && ok) ? make_float2(ctx.Bound(offL + k), ctx.Bound(offL + k + 1))
-                                          : make_float2(0.0f, 0.0f);
-        const float* gq = Grow + colL + k;
-        for (int h = 0; h < curH; ++h) {
-            float2 l, hi;
-            CheapBoundsPair<MAXM, L, kStrict>(table + h * PairTableStride<MAXM>(), cur.rowh(h), cur.E[h],
-                                              cur.ill[h] != 0, gq, ok, alpha, gamma, dg, l, hi);
-            if (ok) {
-                *reinterpret_cast<float2*>(lo + h * K + k) = l;
-                if (kHi) *reinterpret_cast<float2*>(hi_out + h * K + k) = hi;
-                hmin2 = fminf(hmin2, fmaxf(hmin, hi.x));
-                hmin = fminf(hmin, hi.x);
-                hmin2 = fminf(hmin2, fmaxf(hmin, hi.y));
-                hmin = fminf(hmin, hi.y);
-            }
-            if (check) {
-                const int col[kCpt] = {colL + k, colL + k + 1};
-                const bool okc[kCpt] = {ok, ok};
-                const float al[kCpt] = {alpha.x, alpha.y}, ga[kCpt] = {gamma.x, gamma.y};
-                const float la[kCpt] = {l.x, l.y}, ha[kCpt] = {hi.x, hi.y};
-                CheckBounds<MAXM, kStrict>(cur, h, L, Grow, 0, col, okc, al, ga, la, ha, err_flag, recip, ctx,
-                                           offL - colL);
-            }
-        }
-    }
-    return BoundKeys(hmin, hmin2);
-}
-
-// `table` non-null: the paired pass (Dims::pair) over the slots' pair tables.
 template <int MAXM, bool kHi, bool kWide, bool kStrict>
 __device__ uint64_t CheapDispatch(int L, const SlotView<MAXM>& cur, int curH, int K, int offL, int colL,
                                   const float* Grow, const float* Gdiag, const float* xc, float* lo, float* hi_out,
-                                  int check, unsigned int* err, bool recip, const float2* table, const ExactCtx& ctx) {
-    if constexpr (kPairPath<MAXM>) {
-        if (table) {
-#define STLQ_B200_CHEAP(LL)                                                                          \
-    case LL:                                                                                         \
-        if constexpr (LL < MAXM)                                                                     \
-            return CheapPassPair<MAXM, LL, kHi, kWide, kStrict>(cur, table, curH, K, offL, colL, Grow, Gdiag, xc, lo, \
-                                                                hi_out, check, err, recip, ctx);     \
-        break;
-            switch (L) {
-                STLQ_B200_CHEAP(1) STLQ_B200_CHEAP(2) STLQ_B200_CHEAP(3) STLQ_B200_CHEAP(4) STLQ_B200_CHEAP(5)
-                STLQ_B200_CHEAP(6) STLQ_B200_CHEAP(7) STLQ_B200_CHEAP(8) STLQ_B200_CHEAP(9) STLQ_B200_CHEAP(10)
-                STLQ_B200_CHEAP(11) STLQ_B200_CHEAP(12) STLQ_B200_CHEAP(13) STLQ_B200_CHEAP(14) STLQ_B200_CHEAP(15)
-                default: break;
-            }
-#undef STLQ_B200_CHEAP
-        }
-    }
+                                  int check, unsigned int* err, bool recip, const ExactCtx& ctx) {
     return CheapPass<MAXM, kHi, kWide, kStrict>(cur, L, curH, K, offL, colL, Grow, Gdiag, xc, lo, hi_out, check, err,
                                                 recip, ctx);
 }
@@ -589,20 +522,14 @@ template <int MAXM, bool kWide, bool kStrict>
 __device__ void ReplayLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int& curH,
                             const float* __restrict__ Grow, const float* __restrict__ Gdiag,
                             const float* __restrict__ xc, int beam, float* errs, float* his, LayerTable& lt,
-                            float2* table, const ExactCtx& ctx) {
+                            const ExactCtx& ctx) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
     const int n_cand = curH * K;
     int* list = reinterpret_cast<int*>(his);
     if (his) {
-        if constexpr (kPairPath<MAXM>) {
-            if (table) {
-                BuildPairTable<MAXM>(cur, curH, L, table);
-                __syncthreads();
-            }
-        }
         CheapDispatch<MAXM, true, kWide, kStrict>(L, cur, curH, K, offL, colL, Grow, Gdiag, xc, errs, his, 0, nullptr,
-                                                  dims.large_root != 0, table, ctx);
+                                                  dims.large_root != 0, ctx);
         __syncthreads();
         if (tid < 32) {
             Replay rp;
@@ -708,11 +635,6 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
     const int nc = ReplayCandFloats(beam, dims.maxKs);
     float* his = prescan ? errs + nc : nullptr;
     float* after = errs + (prescan ? 2 : 1) * nc;
-    float2* table = nullptr;  // pair tables after the candidate arrays (Dims::pair, pre-scan only)
-    if (dims.pair && prescan) {
-        table = Align16<float2>(after);
-        after = reinterpret_cast<float*>(table + beam * PairTableStride<MAXM>());
-    }
     float* xs = Align16<float>(after);  // STRICT: the vector being encoded
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
@@ -757,7 +679,7 @@ __global__ void __launch_bounds__(kThreads) BeamReplayKernel(Dims dims, const fl
         for (int L = 1; L < m; ++L) {
             ReplayLayer<MAXM, kWide, kStrict>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
                                               SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag, xc,
-                                              beam, errs, his, lt, table, ctx);
+                                              beam, errs, his, lt, ctx);
             ci ^= 1;
         }
         if (tid < 32) {  // first slot with the smallest error (beam_search.cpp:409-416)
@@ -943,17 +865,11 @@ template <int MAXM, bool kWide, bool kStrict>
 __device__ int FastLayer(const Dims& dims, int L, const SlotView<MAXM>& cur, const SlotView<MAXM>& nxt, int curH,
                          const float* __restrict__ Grow, const float* __restrict__ Gdiag, const float* __restrict__ xc,
                          int beam, float* lo, LayerTable& lt, uint16_t* surv, float* ex, uint64_t* keys, float* keep,
-                         int check, unsigned int* err_flag, float2* table, const ExactCtx& ctx, float* gex) {
+                         int check, unsigned int* err_flag, const ExactCtx& ctx, float* gex) {
     const int tid = threadIdx.x;
     const int K = dims.h_vec[L], offL = dims.off[L], colL = offL - dims.c0;
-    if constexpr (kPairPath<MAXM>) {
-        if (table) {
-            BuildPairTable<MAXM>(cur, curH, L, table);
-            __syncthreads();
-        }
-    }
     const uint64_t hmin = CheapDispatch<MAXM, false, kWide, kStrict>(
-        L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag, dims.large_root != 0, table, ctx);
+        L, cur, curH, K, offL, colL, Grow, Gdiag, xc, lo, nullptr, check, err_flag, dims.large_root != 0, ctx);
     const int S = SelectSurvivors(ArraySource{lo}, curH * K, hmin, beam, lt, surv);
     if (S < 0) return -1;
     if constexpr (kStrict)
@@ -999,10 +915,8 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     float* ex = lo + beam * dims.maxKs;
     float* keep = ex + kSurvCap;
     uint16_t* surv = reinterpret_cast<uint16_t*>(keep + kKeep * KeepStride<MAXM>());
-    float2* table = dims.pair ? Align16<float2>(surv + kSurvCap) : nullptr;
     // STRICT: the vector being encoded, then the survivors' exact xC entries.
-    float* xs = Align16<float>(table ? static_cast<void*>(table + beam * PairTableStride<MAXM>())
-                                     : static_cast<void*>(surv + kSurvCap));
+    float* xs = Align16<float>(surv + kSurvCap);
     float* gex = xs + Align4(dims.d);
     const int tid = threadIdx.x;
     const int m = dims.m, K0 = dims.h_vec[0];
@@ -1077,7 +991,7 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
         for (int L = 1; L < m && curH > 0; ++L) {
             curH = FastLayer<MAXM, kWide, kStrict>(dims, L, SlotView<MAXM>::At(smem + ci * sv, beam),
                                                    SlotView<MAXM>::At(smem + (ci ^ 1) * sv, beam), curH, Grow, Gdiag,
-                                                   xc, beam, lo, lt, surv, ex, keys, keep, check, err_flag, table, ctx,
+                                                   xc, beam, lo, lt, surv, ex, keys, keep, check, err_flag, ctx,
                                                    gex);
             ci ^= 1;
             n_surv += lt.n_surv;
@@ -1103,12 +1017,6 @@ __global__ void __launch_bounds__(kThreads, MAXM <= 8 ? 4 : 2) BeamFastKernel(Di
     }
 }
 
-// The pair tables of every slot (Dims::pair), with 16 bytes of alignment slack.
-template <int MAXM>
-size_t PairTableBytes(int beam) {
-    return 16 + sizeof(float2) * static_cast<size_t>(beam) * PairTableStride<MAXM>();
-}
-
 // STRICT mode's shared arrays: the staged vector (strict_d floats, 0 when not STRICT) and, in the
 // fast kernel, the survivors' exact xC entries; with alignment slack.
 size_t StrictBytes(int strict_d, bool fast) {
@@ -1116,21 +1024,19 @@ size_t StrictBytes(int strict_d, bool fast) {
 }
 
 template <int MAXM>
-size_t FastSmemBytes(int beam, int maxK, bool pair = false, int strict_d = 0) {
+size_t FastSmemBytes(int beam, int maxK, int strict_d = 0) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
     return b + sizeof(uint64_t) * kSurvCap + sizeof(float) * beam * maxK + (sizeof(float) + sizeof(uint16_t)) * kSurvCap +
-           sizeof(float) * kKeep * KeepStride<MAXM>() + 16 + (pair ? PairTableBytes<MAXM>(beam) : 0) +
-           StrictBytes(strict_d, true);
+           sizeof(float) * kKeep * KeepStride<MAXM>() + 16 + StrictBytes(strict_d, true);
 }
 
 // With the pre-scan: errors (lower bounds first) and upper bounds; without: errors only.
 template <int MAXM>
-size_t ReplaySmemBytes(int beam, int maxK, bool prescan, bool pair = false, int strict_d = 0) {
+size_t ReplaySmemBytes(int beam, int maxK, bool prescan, int strict_d = 0) {
     size_t b = (2 * SlotView<MAXM>::Bytes(beam) + 15) & ~size_t(15);
     b = (b + sizeof(LayerTable) + 15) & ~size_t(15);
-    return b + (prescan ? 2 : 1) * sizeof(float) * ReplayCandFloats(beam, maxK) + 16 +
-           (pair && prescan ? PairTableBytes<MAXM>(beam) : 0) + StrictBytes(strict_d, false);
+    return b + (prescan ? 2 : 1) * sizeof(float) * ReplayCandFloats(beam, maxK) + 16 + StrictBytes(strict_d, false);
 }
 
 // The largest dynamic shared memory a block of the current device may opt into.
@@ -1142,28 +1048,10 @@ size_t MaxBlockSmem() {
     return static_cast<size_t>(v);
 }
 
-// The fast kernel takes the pair tables (Dims::pair) when they fit and cost no resident CTA.
-template <typename KernelT>
-bool PairKeepsOccupancy(KernelT kernel, size_t smem_scalar, size_t smem_pair) {
-    if (smem_pair > MaxBlockSmem()) return false;
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_pair)) !=
-        cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    int a = 0, b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, kernel, kThreads, smem_scalar) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kThreads, smem_pair) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    return b > 0 && b >= a;
-}
-
 // The replay runs its pre-scan whenever the upper bounds fit beside the errors.
 template <int MAXM>
 bool ReplayPrescan(int beam, int maxK, int strict_d = 0) {
-    return ReplaySmemBytes<MAXM>(beam, maxK, true, false, strict_d) <= MaxBlockSmem();
+    return ReplaySmemBytes<MAXM>(beam, maxK, true, strict_d) <= MaxBlockSmem();
 }
 
 // Sets the kernel's shared-memory size, finds how many CTAs fit on an SM, then asks for the
@@ -1207,40 +1095,30 @@ cudaError_t LaunchBeamT(const Dims& dims, const float* Grow, const float* Gdiag,
                         unsigned long long* stats, int num_sms, cudaStream_t stream, const ExactDotArgs& ea) {
     const int sd = kStrict ? dims.d : 0;
     int grid = 0;
-    Dims df = dims;
-    df.pair = kPairPath<MAXM> && dims.pair &&
-              PairKeepsOccupancy(BeamFastKernel<MAXM, kWide, kStrict>, FastSmemBytes<MAXM>(beam, dims.maxKs, false, sd),
-                                 FastSmemBytes<MAXM>(beam, dims.maxKs, true, sd));
-    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs, df.pair != 0, sd);
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs, sd);
     cudaError_t e = Prepare(BeamFastKernel<MAXM, kWide, kStrict>, fsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(redo, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
-    BeamFastKernel<MAXM, kWide, kStrict><<<grid, kThreads, fsm, stream>>>(df, Grow, Gdiag, xnorm2, xC, n, beam, Bout,
+    BeamFastKernel<MAXM, kWide, kStrict><<<grid, kThreads, fsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout,
                                                                           redo + 1, redo, check, err_flag, stats, ea);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs, sd);
-    Dims dr = dims;
-    dr.pair = kPairPath<MAXM> && dims.pair && prescan &&
-              ReplaySmemBytes<MAXM>(beam, dims.maxKs, true, true, sd) <= MaxBlockSmem();
-    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, dr.pair != 0, sd);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, sd);
     e = Prepare(BeamReplayKernel<MAXM, kWide, kStrict>, rsm, num_sms, n, &grid);
     if (e != cudaSuccess) return e;
-    BeamReplayKernel<MAXM, kWide, kStrict><<<grid, kThreads, rsm, stream>>>(dr, Grow, Gdiag, xnorm2, xC, n, beam, Bout,
+    BeamReplayKernel<MAXM, kWide, kStrict><<<grid, kThreads, rsm, stream>>>(dims, Grow, Gdiag, xnorm2, xC, n, beam, Bout,
                                                                             redo + 1, redo, prescan, ea, err_flag);
     return cudaGetLastError();
 }
 
 template <int MAXM, bool kWide>
 cudaError_t PrepareT(const Dims& dims, int beam) {
-    // The largest sizes a launch may ask for (the pair tables included when they fit).
-    const bool pair = kPairPath<MAXM> && dims.pair != 0;
-    const size_t f1 = FastSmemBytes<MAXM>(beam, dims.maxKs, pair);
-    const size_t fsm = f1 <= MaxBlockSmem() ? f1 : FastSmemBytes<MAXM>(beam, dims.maxKs);
+    // The sizes a launch asks for.
+    const size_t fsm = FastSmemBytes<MAXM>(beam, dims.maxKs);
     const bool prescan = ReplayPrescan<MAXM>(beam, dims.maxKs);
-    const size_t r1 = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan, pair);
-    const size_t rsm = r1 <= MaxBlockSmem() ? r1 : ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
+    const size_t rsm = ReplaySmemBytes<MAXM>(beam, dims.maxKs, prescan);
     cudaError_t e = cudaFuncSetAttribute(BeamFastKernel<MAXM, kWide, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(fsm));
     if (e != cudaSuccess) return e;
@@ -1252,7 +1130,7 @@ cudaError_t PrepareT(const Dims& dims, int beam) {
 
 size_t BeamFastSmemBytes(const Dims& dims, int beam, bool strict) {
     const int sd = strict ? dims.d : 0;
-    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxKs, false, sd) : FastSmemBytes<16>(beam, dims.maxKs, false, sd);
+    return dims.m <= 8 ? FastSmemBytes<8>(beam, dims.maxKs, sd) : FastSmemBytes<16>(beam, dims.maxKs, sd);
 }
 
 // The kWide kernels: a codebook of layers 1..m-1 above kMaxK codewords (chunked cheap passes) or

@@ -259,62 +259,5 @@ __device__ __forceinline__ void CheapBounds(const SlotView<MAXM>& cur, int h, in
         BoundsTail<kStrict>(L, alpha[q], gamma[q], delta[q], eta[q], seta[q], Eo, ill, dg[q], lo[q], hi[q]);
 }
 
-// ---------------------------------------------------------------------------------------------
-// Paired cheap bounds: a thread's two candidates are adjacent codewords k, k + 1 of one slot, so
-// their Gram gathers, alpha and gamma are single 8-byte loads and the substitution, delta and eta
-// run on packed FP32x2 (two correctly rounded fma / mul per instruction, bit-identical per lane to
-// the scalar CheapBounds).  The slot's scalars reach both lanes as duplicated pairs from a
-// per-layer table built by BuildPairTable.  Used when every codebook has an even number of
-// codewords (so every row offset, column and flat index of a pair is even: 8-byte aligned).
-
-// Table of one slot at layer L, in the order the substitution consumes it: for i = 0..L-1 the
-// entries -R(k, i) for k < i, then 1/R_ii, then a_i, each as the pair {v, v}.  Row i starts at
-// i(i-1)/2 + 2i.
-template <int MAXM>
-__host__ __device__ constexpr int PairTableStride() { return (MAXM - 1) * (MAXM - 2) / 2 + 2 * (MAXM - 1); }
-
-template <int MAXM>
-__device__ void BuildPairTable(const SlotView<MAXM>& cur, int curH, int L, float2* table) {
-    for (int e = threadIdx.x; e < curH * L; e += blockDim.x) {
-        const int h = e / L, i = e - h * L;
-        float2* row = table + h * PairTableStride<MAXM>() + i * (i - 1) / 2 + 2 * i;
-        const float* Rh = cur.Rh(h);
-        for (int k = 0; k < i; ++k) {
-            const float v = -Rh[i * MAXM + k];
-            row[k] = make_float2(v, v);
-        }
-        const float ri = cur.rinvh(h)[i], ai = cur.ah(h)[i];
-        row[i] = make_float2(ri, ri);
-        row[i + 1] = make_float2(ai, ai);
-    }
-}
-
-template <int MAXM, int L, bool kStrict>
-__device__ __forceinline__ void CheapBoundsPair(const float2* __restrict__ tab, const int* rw, float Eo, bool ill,
-                                                const float* gq, bool ok, float2 alpha, float2 gamma, float2 dg,
-                                                float2& lo, float2& hi) {
-    float2 A[L], y[L];
-#pragma unroll
-    for (int i = 0; i < L; ++i)
-        A[i] = ok ? __ldg(reinterpret_cast<const float2*>(gq + rw[i])) : make_float2(0.0f, 0.0f);
-    float2 delta = make_float2(0.0f, 0.0f), eta = make_float2(0.0f, 0.0f);
-    float seta0 = fabsf(gamma.x), seta1 = fabsf(gamma.y);
-#pragma unroll
-    for (int i = 0; i < L; ++i) {
-        const float2* row = tab + i * (i - 1) / 2 + 2 * i;
-        float2 s = A[i];
-#pragma unroll
-        for (int k = 0; k < i; ++k) s = __ffma2_rn(row[k], y[k], s);
-        const float2 ri = row[i], ai = row[i + 1];
-        y[i] = __fmul2_rn(s, ri);
-        delta = __ffma2_rn(y[i], y[i], delta);
-        eta = __ffma2_rn(A[i], ai, eta);
-        seta0 = fmaf(fabsf(A[i].x), fabsf(ai.x), seta0);
-        seta1 = fmaf(fabsf(A[i].y), fabsf(ai.x), seta1);
-    }
-    BoundsTail<kStrict>(L, alpha.x, gamma.x, delta.x, eta.x, seta0, Eo, ill, dg.x, lo.x, hi.x);
-    BoundsTail<kStrict>(L, alpha.y, gamma.y, delta.y, eta.y, seta1, Eo, ill, dg.y, lo.y, hi.y);
-}
-
 }  // namespace beam
 }  // namespace stlq_b200

@@ -55,9 +55,6 @@ struct Dims {
     int large_root;
     // Codes are uint16 (some codebook has more than 256 codewords) instead of uint8.
     int wide;
-    // Every codebook has an even number of codewords: the beam's cheap pass may take its two
-    // codewords per thread as aligned pairs (set per launch where the pair table fits).
-    int pair;
 };
 
 }  // namespace stlq_b200
