@@ -480,6 +480,8 @@ class BaseStore:
         lib.stlq_b200_store_flush.argtypes = [vp]
         lib.stlq_b200_store_close.argtypes = [vp]
         self.m, self.d, self.device = int(m), int(d), int(device)
+        self.vec_bucket = bool(write_vector_bucket)
+        self.raw_bytes = (int(raw_bytes_per_vec) if raw_bytes_per_vec > 0 else int(d)) if self.vec_bucket else 0
         h = np.ascontiguousarray(h_vec, np.int32)
         if h.ndim != 1 or len(h) != int(m):
             raise StlqB200Error("h_vec must hold m codebook sizes")
@@ -501,9 +503,7 @@ class BaseStore:
             return _np_ptr(t)
 
         n = int(cluster.shape[0])
-        ld = 0
-        if x is not None:
-            ld = int(x.nbytes // max(n, 1)) if not hasattr(x, "element_size") else int(x.stride(0) * x.element_size())
+        ld = self._check_block(n, cluster, B_small, a, x)
         if stream is None and hasattr(cluster, "data_ptr") and cluster.is_cuda:
             import torch
 
@@ -511,6 +511,39 @@ class BaseStore:
         _check(self.lib, self.lib.stlq_b200_store_append(self.handle, int(start_id), n, ptr(cluster), ptr(B_small),
                                                          ptr(a), ptr(x), ld, ctypes.c_void_p(stream or 0)),
                "stlq_b200_store_append")
+
+    def _check_block(self, n, cluster, B_small, a, x):
+        """Shapes, types, contiguity and placement of one block's arrays, before any pointer reaches
+        the library (a wrong one would be read out of bounds).  Returns x's row stride in bytes."""
+        def info(t, name):
+            if t is None:
+                raise StlqB200Error(f"{name} is required")
+            if hasattr(t, "data_ptr"):  # torch tensor
+                if t.is_cuda and (self.device < 0 or t.device.index != self.device):
+                    raise StlqB200Error(f"{name} is on {t.device}; this store stages from device {self.device}")
+                return tuple(t.shape), t.element_size(), t.is_contiguous(), t.stride(0) * t.element_size() if t.dim() else 0
+            t = np.asarray(t)
+            return t.shape, t.itemsize, t.flags.c_contiguous, t.strides[0] if t.ndim else 0
+
+        shp, es, contig, _ = info(cluster, "cluster")
+        if len(shp) != 1 or es != 4 or not contig:
+            raise StlqB200Error("cluster must be a contiguous (n,) array of 32-bit root codes")
+        if self.m > 1:
+            shp, es, contig, _ = info(B_small, "B_small")
+            if shp != (n, self.m - 1) or es != 1 or not contig:
+                raise StlqB200Error(f"B_small must be a contiguous ({n}, {self.m - 1}) uint8 array")
+        shp, es, contig, _ = info(a, "a")
+        if shp != (n, self.m) or es != 4 or not contig:
+            raise StlqB200Error(f"a must be a contiguous ({n}, {self.m}) float32 array")
+        if x is None:
+            if self.vec_bucket:
+                raise StlqB200Error("x (the raw vectors) is required when write_vector_bucket is on")
+            return 0
+        shp, es, _, ld = info(x, "x")
+        inner = int(np.prod(shp[1:])) * es if len(shp) > 1 else es
+        if shp[0] != n or (n > 1 and ld < inner) or inner < self.raw_bytes:
+            raise StlqB200Error(f"x must hold {n} rows of at least {self.raw_bytes} contiguous bytes")
+        return int(ld if n > 1 else inner)
 
     def flush(self):
         _check(self.lib, self.lib.stlq_b200_store_flush(self.handle), "stlq_b200_store_flush")
@@ -568,6 +601,8 @@ class VectorReader:
         """(start, block) of the next block in file order, or None at the end.  Device readers copy
         asynchronously on `stream` (default: torch's current stream) into `out` (or a new tensor)."""
         start, cnt = ctypes.c_uint64(), ctypes.c_int64()
+        if out is not None:
+            self._check_out(out)
         if self.device < 0:
             buf = np.empty((self.block, self.d), self.dtype) if out is None else out
             _check(self.lib, self.lib.stlq_b200_reader_next(self.handle, _np_ptr(buf), buf.nbytes, None,
@@ -586,6 +621,23 @@ class VectorReader:
         if cnt.value == 0:
             return None
         return start.value, buf[: cnt.value]
+
+    def _check_out(self, out):
+        """A caller's block buffer: (block, d) rows of the file's element type, contiguous, in host
+        memory for a host-only reader and on the reader's device otherwise."""
+        if hasattr(out, "data_ptr"):
+            import torch
+
+            want = torch.uint8 if self.dtype == np.uint8 else torch.float32
+            ok = (self.device >= 0 and out.is_cuda and out.device.index == self.device and out.dtype == want
+                  and out.is_contiguous() and tuple(out.shape) == (self.block, self.d))
+        else:
+            ok = (self.device < 0 and isinstance(out, np.ndarray) and out.dtype == self.dtype
+                  and out.flags.c_contiguous and out.shape == (self.block, self.d))
+        if not ok:
+            where = "host" if self.device < 0 else f"cuda:{self.device}"
+            raise StlqB200Error(f"out must be a contiguous ({self.block}, {self.d}) {np.dtype(self.dtype).name} "
+                                f"array in {where} memory")
 
     def __iter__(self):
         while True:

@@ -121,6 +121,53 @@ def test_store_rejects_bad_arguments(tmp_path):
         st.close()
 
 
+def test_store_checks_block_arrays(tmp_path):
+    """Arrays of the wrong shape, type or layout are refused before any pointer reaches the library."""
+    import stlq_b200
+
+    st = stlq_b200.BaseStore(tmp_path / "v", 8, 3, [4, 256, 256], device=-1, max_block=16)
+    n = 5
+    c = np.zeros(n, np.uint32)
+    B = np.zeros((n, 2), np.uint8)
+    a = np.zeros((n, 3), np.float32)
+    x = np.zeros((n, 8), np.uint8)
+    bad = [
+        (c.astype(np.int64), B, a, x),            # 64-bit root codes
+        (c, np.zeros((n, 3), np.uint8), a, x),    # m codes instead of m - 1
+        (c, B, a.astype(np.float64), x),          # double coefficients
+        (c, B, np.zeros((n, 2), np.float32), x),  # too few coefficients
+        (c, B, a, np.zeros((n, 4), np.uint8)),    # rows shorter than the raw bytes
+        (c, B, a, np.zeros((n + 1, 8), np.uint8)),  # row count differs
+        (c, np.asfortranarray(np.zeros((n, 2), np.uint8)), a, x),  # not C-contiguous
+    ]
+    for args in bad:
+        with pytest.raises(stlq_b200.StlqB200Error):
+            st.append(0, *args)
+    st.append(0, c, B, a, x)  # the valid block still goes through
+    st.close()
+
+
+def test_reader_checks_out_buffer(tmp_path):
+    import stlq_b200
+
+    path, _ = make_file_f32(tmp_path)
+    rd = stlq_b200.VectorReader(path, device=-1, block=8)
+    for out in (np.empty((8, 5), np.float32), np.empty((8, 4), np.float64), np.empty((4, 8), np.float32).T):
+        with pytest.raises(stlq_b200.StlqB200Error):
+            rd.next_block(out=out)
+    start, blk = rd.next_block(out=np.empty((8, 4), np.float32))
+    assert start == 0 and blk.shape == (8, 4)
+    rd.close()
+
+
+def make_file_f32(tmp_path, n=20, d=4):
+    X = np.arange(n * d, dtype=np.float32).reshape(n, d)
+    path = tmp_path / "v.fbin"
+    with open(path, "wb") as f:
+        f.write(np.array([n, d], np.int32).tobytes() + X.tobytes())
+    return path, X
+
+
 @pytest.mark.gpu
 @pytest.mark.skipif(not have_cuda(), reason="needs a GPU")
 @pytest.mark.skipif(not ref_available, reason="oracle/_ref not built")
