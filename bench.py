@@ -758,26 +758,48 @@ def run_config3(args):
     outputs out (pinned double buffers).  Reported beside it: the same encode on device-resident
     vectors (equal throughput means the copies are hidden), the measured H2D bandwidth and the PCIe
     roofline it sets, and the codes of the first, middle and last slices against the reference's
-    own large-root CPU encoder (bit for bit, on a bounded sample of each)."""
+    own large-root CPU encoder (bit for bit, on a bounded sample of each).
+
+    Under torchrun (N ranks, one GPU each) every rank streams its own --c3-slices slices (rank r
+    holds global slices r * c3_slices onwards: weak scaling, no collective on the data path); the
+    codebooks are trained on rank 0 and broadcast, the timed call is bracketed by barriers and its
+    time is the maximum over ranks.  Parity covers the job's first slice, rank 0's middle and last
+    slices and the job's last slice (on the last rank); the CPU baseline is timed at N=1 only."""
     import torch
+    import torch.distributed as dist
 
     import stlq_b200
     from stlq_b200 import synth
 
-    device = torch.device("cuda", 0)
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
     d, m, k, beam = 128, 8, 256, 16
-    slice_n, n_slices = args.c3_slice, args.c3_slices
+    slice_n, n_slices = args.c3_slice, args.c3_slices  # per rank
     n = slice_n * n_slices
+    first = rank * n_slices  # this rank's first global slice
+    g0 = first * slice_n  # global id of its first vector
     t_gen = time.perf_counter()
     Xh = torch.empty((n, d), dtype=torch.uint8).pin_memory()
     for s in range(n_slices):  # each slice as the generator makes it (its own position in the stream)
         Xh[s * slice_n:(s + 1) * slice_n] = torch.from_numpy(
-            synth.sift_like(slice_n, d=d, seed=3, n_centres=10_000, dtype=np.uint8, start=s * slice_n))
+            synth.sift_like(slice_n, d=d, seed=3, n_centres=10_000, dtype=np.uint8, start=(first + s) * slice_n))
     t_gen = time.perf_counter() - t_gen
-    train = Xh[:50_000].numpy().astype(np.float32)  # codebooks from the first slice
-    C = synth.flatten_books(synth.train_rvq(train, m, k, iters=8, seed=3, device=device))
     h_vec = [k] * m
-    enc = stlq_b200.Encoder(C, h_vec, device=0, large_root=True)
+    if rank == 0:  # codebooks from the job's first slice
+        train = Xh[:50_000].numpy().astype(np.float32)
+        Ct = torch.from_numpy(synth.flatten_books(synth.train_rvq(train, m, k, iters=8, seed=3, device=device)))
+        Ct = Ct.to(device)
+    else:
+        Ct = torch.empty((m * k, d), dtype=torch.float32, device=device)
+    if world > 1:
+        dist.broadcast(Ct, src=0)
+    C = Ct.cpu().numpy()
+    enc = stlq_b200.Encoder(C, h_vec, device=local, large_root=True)
     cluster = torch.empty(n, dtype=torch.int32).pin_memory()
     B_small = torch.empty((n, m - 1), dtype=torch.uint8).pin_memory()
     a = torch.empty((n, m), dtype=torch.float32).pin_memory()
@@ -788,13 +810,15 @@ def run_config3(args):
 
     def stream(count):
         rc = lib.stlq_b200_encode_base_large_root(
-            enc.handle, _t_ptr(Xh), 1, count, beam, 0, 0, 0, 1, 38251450, 0, _t_ptr(cluster), _t_ptr(B_small),
+            enc.handle, _t_ptr(Xh), 1, count, beam, 0, 0, 0, 1, 38251450, g0, _t_ptr(cluster), _t_ptr(B_small),
             _t_ptr(a), _t_ptr(cost), _np_ptr(sums))
         if rc:
             raise stlq_b200.StlqB200Error(lib.stlq_b200_last_error().decode())
 
     stream(slice_n)  # warm-up
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     uuid = None
     try:
         uuid = str(torch.cuda.get_device_properties(device).uuid)
@@ -806,6 +830,10 @@ def run_config3(args):
     stream(n)
     t_stream = time.perf_counter() - t0
     clock_info = clocks.stop()
+    if world > 1:  # the job's time: the slowest rank's
+        tt = torch.tensor([t_stream], dtype=torch.float64, device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_stream = float(tt.item())
     # The same encode on device-resident vectors (no copies), on the first slices.
     nd = min(n, 4 * slice_n)
     Xd = Xh[:nd].to(device)
@@ -832,59 +860,78 @@ def run_config3(args):
     torch.cuda.synchronize()
     h2d_gbs = 3 * hb.numel() / (e0.elapsed_time(e1) / 1e3) / 1e9
     del db
-    # Parity: the first, middle and last slices against the reference's large-root CPU encoder.
-    parity = {}
-    if not args.no_cpu:
+    # Parity: slices against the reference's large-root CPU encoder, a bounded sample of each.
+    ns = min(slice_n, args.c3_check)
+
+    def check(slices, threads):
         import oracle
 
-        ref = oracle.Reference(threads=os.cpu_count())
-        ns = min(slice_n, args.c3_check)
-        t_ref = 0.0
-        for s in sorted({0, n_slices // 2, n_slices - 1}):
+        ref = oracle.Reference(threads=threads)
+        out, t_ref = {}, 0.0
+        for s in slices:
             lo = s * slice_n
             t1 = time.perf_counter()
-            r = ref.large_root_encode(h_vec, C, Xh[lo:lo + ns].numpy(), beam, 0, sample_id_offset=lo)
+            r = ref.large_root_encode(h_vec, C, Xh[lo:lo + ns].numpy(), beam, 0, sample_id_offset=g0 + lo)
             t_ref += time.perf_counter() - t1
             same = (r["cluster"] == cluster[lo:lo + ns].numpy().view(np.uint32)) & \
                 (r["B_small"] == B_small[lo:lo + ns].numpy()).all(1)
-            parity[f"slice_{s}"] = {"vectors": ns, "codes_identical": float(same.mean()),
-                                    "coefficients_identical": bool(np.array_equal(r["a"], a[lo:lo + ns].numpy())),
-                                    "costs_identical": bool(np.array_equal(r["cost"], cost[lo:lo + ns].numpy()))}
-        cpu = {"value": 3 * ns / t_ref, "unit": "vectors/s", "cores": ref.threads, "kind": "reference",
-               "cpu_model": cpu_model(),
-               "sample": f"{ns} vectors of each checked slice, the reference's large-root CPU encoder (oracle/_ref) "
-                         f"on {ref.threads} threads of {cpu_model()}"}
-    else:
-        cpu = None
-    value = n / t_stream
-    in_b, out_b = d, 4 + (m - 1) + 4 * m + 4
-    line = {
-        "metric": "encoded vectors/sec (config 3: uint8 vectors streamed from host memory, large-root encoder)",
-        "value": value, "unit": "vectors/s", "n_gpus": 1, "steps": 1, "warmup": 1,
-        "ms_per_step": 1e3 * t_stream, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8 in, f32 compute", "data": "synthetic (SIFT-like generator, 10,000 centres, seed 3, per 1M slice)",
-        "config": {"workload": f"{n_slices} slices x {slice_n} x D={d} uint8 from pinned host memory, M={m}, K={k} "
-                               f"(root 256), beam {beam}, ICM 0, ILS 0; codebooks: seeded residual k-means on 50,000 "
-                               "vectors of the first slice", "cache": "inputs larger than L2 (streamed)",
-                   "host_generation_s": t_gen},
-        "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": n * in_b, "d2h_bytes_per_step": n * out_b,
-                "timing": "wall clock around the synchronous host-buffer call"},
-        "device_resident": {"value": nd / t_dev, "unit": "vectors/s", "vectors": nd,
-                            "note": "the same encode with the vectors already on the device (no copies)"},
-        "copy_overlap": {"stream_over_device_throughput": value / (nd / t_dev),
-                         "achieved_h2d_gbs": n * in_b / t_stream / 1e9, "achieved_d2h_gbs": n * out_b / t_stream / 1e9},
-        "roofline": {"bound": "pcie", "achieved": n * in_b / t_stream / 1e9, "peak": h2d_gbs, "unit": "GB/s",
-                     "frac": n * in_b / t_stream / 1e9 / h2d_gbs,
-                     "peak_source": "pinned host-to-device copy measured in this run (CUDA events)",
-                     "vectors_per_s_bound": h2d_gbs * 1e9 / in_b,
-                     "note": "PCIe bytes per vector: 128 in (uint8), 47 out (cluster id 4, codes 7, coefficients 32, "
-                             "cost 4) on the other direction"},
-        "parity": parity, "clocks": clock_info, "cpu_baseline": cpu,
-    }
-    if args.c3_file_slices > 0:
-        line["file_to_store"] = run_config3_file(args, enc, Xh[:min(n, args.c3_file_slices * slice_n)], beam)
-    print(json.dumps(line), flush=True)
+            out[f"slice_{first + s}"] = {"vectors": ns, "codes_identical": float(same.mean()),
+                                         "coefficients_identical": bool(np.array_equal(r["a"], a[lo:lo + ns].numpy())),
+                                         "costs_identical": bool(np.array_equal(r["cost"], cost[lo:lo + ns].numpy()))}
+        return out, len(slices) * ns / t_ref, ref.threads
+
+    parity, cpu, last = {}, None, None
+    threads = os.cpu_count() if world == 1 else max(1, os.cpu_count() // world)
+    if not args.no_cpu and rank == 0:
+        parity, v_ref, used = check(sorted({0, n_slices // 2, n_slices - 1}), threads)
+        if world == 1:
+            cpu = {"value": v_ref, "unit": "vectors/s", "cores": used, "kind": "reference", "cpu_model": cpu_model(),
+                   "sample": f"{ns} vectors of each checked slice, the reference's large-root CPU encoder "
+                             f"(oracle/_ref) on {used} threads of {cpu_model()}"}
+    elif not args.no_cpu and rank == world - 1:
+        last = check([n_slices - 1], threads)[0]
+    if world > 1:
+        objs = [None] * world
+        dist.all_gather_object(objs, last)
+        if objs[-1]:
+            parity.update(objs[-1])
+    if rank == 0:
+        value = world * n / t_stream
+        in_b, out_b = d, 4 + (m - 1) + 4 * m + 4
+        h2d_ach = n * in_b / t_stream / 1e9  # per GPU: each streams over its own link
+        line = {
+            "metric": "encoded vectors/sec (config 3: uint8 vectors streamed from host memory, large-root encoder)",
+            "value": value, "unit": "vectors/s", "n_gpus": world, "steps": 1, "warmup": 1,
+            "ms_per_step": 1e3 * t_stream, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8 in, f32 compute",
+            "data": "synthetic (SIFT-like generator, 10,000 centres, seed 3, per 1M slice)",
+            "config": {"workload": f"{n_slices} slices x {slice_n} x D={d} uint8 per GPU from pinned host memory "
+                                   f"({world * n} vectors in all), M={m}, K={k} (root 256), beam {beam}, ICM 0, "
+                                   "ILS 0; codebooks: seeded residual k-means on 50,000 vectors of the first slice",
+                       "cache": "inputs larger than L2 (streamed)", "host_generation_s": t_gen,
+                       "parallelism": f"dp{world} (each GPU streams its own slices)"},
+            "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": world * n * in_b,
+                    "d2h_bytes_per_step": world * n * out_b,
+                    "timing": "wall clock around the synchronous host-buffer call" +
+                              (", max over ranks" if world > 1 else "")},
+            "device_resident": {"value": nd / t_dev, "unit": "vectors/s", "vectors": nd,
+                                "note": "rank 0: the same encode with the vectors already on the device (no copies)"},
+            "copy_overlap": {"stream_over_device_throughput": value / world / (nd / t_dev),
+                             "achieved_h2d_gbs_per_gpu": h2d_ach, "achieved_d2h_gbs_per_gpu": n * out_b / t_stream / 1e9},
+            "roofline": {"bound": "pcie", "achieved": h2d_ach, "peak": h2d_gbs, "unit": "GB/s", "frac": h2d_ach / h2d_gbs,
+                         "peak_source": "rank 0's pinned host-to-device copy measured in this run (CUDA events)",
+                         "vectors_per_s_bound": world * h2d_gbs * 1e9 / in_b,
+                         "note": "per GPU; PCIe bytes per vector: 128 in (uint8), 47 out (cluster id 4, codes 7, "
+                                 "coefficients 32, cost 4) on the other direction"},
+            "parity": parity, "clocks": clock_info, "cpu_baseline": cpu,
+        }
+        if args.c3_file_slices > 0:
+            line["file_to_store"] = run_config3_file(args, enc, Xh[:min(n, args.c3_file_slices * slice_n)], beam)
+        print(json.dumps(line), flush=True)
     enc.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_config3_file(args, enc, Xh, beam):
