@@ -193,9 +193,12 @@ __device__ __forceinline__ void BoundsTail(int L, float alpha, float gamma, floa
     const float ep = fmaxf(Eo - r, 0.0f);
     float w = fmaf(2.0f * fabsf(diff) * seta + fabsf(r) * (alpha + delta), u16 * fabsf(rden), e16 * (Eo + fabsf(r)));
     if constexpr (kStrict) w = fmaf((2.0f * fabsf(diff) + dg) * dg, 1.001f * fabsf(rden), w);
-    const bool force = ill || !(denom > kDenomGuard * alpha) || !(w < PosInf()) || !(ep < PosInf());
+    // One test for both ep and w: their sum is +inf or NaN when either is (ep is never NaN, being a
+    // fmaxf); a finite pair whose sum overflows is forced too, which only costs an exact evaluation.
+    const float hw = ep + w;
+    const bool force = ill || !(denom > kDenomGuard * alpha) || !(hw < PosInf());
     lo = force ? lof : ep - w;
-    hi = force ? PosInf() : ep + w;
+    hi = force ? PosInf() : hw;
 }
 
 // Cheap bounds [lo, hi] on the exact errors of slot h's candidates at layer L for this thread's
